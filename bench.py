@@ -1,0 +1,299 @@
+#!/usr/bin/env python
+"""Benchmark: certified input regions/sec (DeepPoly, whole input box) on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cfgpu|reference] [--workload 2]
+
+One step = one whole DeepPoly pass (input box, property matrix, every layer's
+backsubstitution down to the input, final bounds) over one batch of regions of the
+workload (default: ReLU MLP 784-(200x9)-10, 256 regions per GPU, eps 0.002; seeded
+synthetic network and centres, since no dataset or trained model is available offline).
+Multi-GPU: one process per GPU (torchrun), each certifying its own 256 regions (weak
+scaling; regions are independent, no collective on the data path).  Rank 0 prints one
+JSON line.
+
+--impl reference times the CPU restatement of the reference's algorithm (oracle/, numpy
+float32 with all host threads) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "constraintflow-gpu_b200"))
+sys.path.insert(0, HERE)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from cfgpu import nets  # noqa: E402
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="cfgpu", choices=["cfgpu", "reference"])
+    ap.add_argument("--workload", type=int, default=2)
+    ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def flops_per_region(wl):
+    """Algorithmic backsubstitution FLOPs per region, both bounds, one GEMM per substitution."""
+    widths = [(L.n_out, L.n_in) for L in wl.layers if L.kind in ("linear", "conv")]
+    tot = 0
+    rows = [w[0] for w in widths] + [9]
+    for m in range(1, len(rows)):
+        for j in range(m - 1, -1, -1):
+            if j < len(widths):
+                tot += 2 * rows[m] * widths[j][0] * widths[j][1]
+    return 2 * tot
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (one GPU)."""
+
+    def __init__(self, index, path):
+        self.path = path
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.fh = open(path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}", "--format=csv,noheader",
+                                       "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1].split()[0]))
+                mx = float(f[2].split()[0])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(wl, sample, reps=3):
+    """Oracle (numpy float32, all host threads) on `sample` regions of the workload: regions/s."""
+    from oracle import deeppoly_oracle as O
+    X = nets.centres(wl, sample)
+    y = nets.labels(wl, X)
+    l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
+    W = nets.spec_weight(y).numpy()
+    l0, u0 = l0.numpy(), u0.numpy()
+    O.deeppoly(wl.layers, l0[:1], u0[:1], W[:1])  # warm
+    ts = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        O.deeppoly(wl.layers, l0, u0, W)
+        ts.append(time.perf_counter() - t)
+    return sample / statistics.median(ts), statistics.median(ts)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    wl = nets.workload(args.workload)
+    sample = {0: 1, 1: 16, 2: 8, 3: 4, 4: 1}[args.workload]
+    from oracle import deeppoly_oracle as O
+    X = nets.centres(wl, sample)
+    y = nets.labels(wl, X)
+    l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
+    W = nets.spec_weight(y).numpy()
+    l0, u0 = l0.numpy(), u0.numpy()
+    for _ in range(args.warmup):
+        O.deeppoly(wl.layers, l0, u0, W)
+    ts = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        O.deeppoly(wl.layers, l0, u0, W)
+        ts.append(time.perf_counter() - t)
+    ms = 1000 * statistics.mean(ts)
+    val = sample / (ms / 1000)
+    cores = os.cpu_count()
+    desc = f"oracle port (numpy float32 BLAS, {cores} threads), {sample} regions of {wl.name} per step"
+    print(json.dumps({
+        "impl": "reference", "metric": "certified input regions/sec (DeepPoly, whole box)", "value": val,
+        "unit": "regions/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "regions_per_step": sample, "eps": wl.eps},
+        "cpu_baseline": {"value": val, "unit": "regions/s", "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": val, "unit": "regions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def run_cfgpu(args, rank, world, local):
+    import torch.distributed as dist
+    from cfgpu.engine import DeepPolyEngine, profile_enable, profile_collect
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl = nets.workload(args.workload)
+    B = args.batch or wl.B
+    Xall = nets.centres(wl, B * world)
+    X = Xall[rank * B:(rank + 1) * B].contiguous()
+    y = nets.labels(wl, X)
+    eng = DeepPolyEngine(wl.layers, wl.input_size, dev)
+    Xd, yd = X.to(dev), y.to(dev)
+    lb = torch.empty(B, 9, dtype=torch.float64, device=dev)
+    ub = torch.empty_like(lb)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step():
+        eng.certify(Xd, yd, wl.eps, wl.dataset, out=(lb, ub))
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    # ---- timed region: device events per step, L2 flushed between steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clk = Clocks(local, os.path.join(HERE, "gpurun_out", f"clocks_r{rank}.csv")) if os.path.isdir(
+        os.path.join(HERE, "gpurun_out")) else Clocks(local, f"/tmp/cf_clocks_r{rank}.csv")
+    barrier()
+    torch.cuda.synchronize()
+    profile_enable(True)
+    wall = time.perf_counter()
+    for k in range(args.steps):
+        flush.zero_()
+        starts[k].record()
+        step()
+        ends[k].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall
+    prof = profile_collect()
+    profile_enable(False)
+    barrier()
+    clocks = clk.stop()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = B * world * args.steps / (ms_max / 1000.0)
+    certified = torch.tensor([int((lb >= 0).all(dim=1).sum().item())], device=dev)
+    if world > 1:
+        dist.all_reduce(certified)
+    # ---- end-to-end through the public API with host buffers
+    Xh = X.pin_memory()
+    yh = y.pin_memory()
+    lbh = torch.empty(B, 9, dtype=torch.float64).pin_memory()
+    ubh = torch.empty_like(lbh).pin_memory()
+    Xe = torch.empty_like(Xd)
+    ye = torch.empty_like(yd)
+
+    def e2e_step():
+        Xe.copy_(Xh, non_blocking=True)
+        ye.copy_(yh, non_blocking=True)
+        eng.certify(Xe, ye, wl.eps, wl.dataset, out=(lb, ub))
+        lbh.copy_(lb, non_blocking=True)
+        ubh.copy_(ub, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = B * world * args.steps / (float(te.item()) / 1000.0)
+    if rank != 0:
+        return
+    bf16, hbm, src = peaks()
+    peak_3xtf32 = bf16 / 2.0 / 3.0
+    achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
+    out = {
+        "metric": "certified input regions/sec (DeepPoly, whole box)", "value": value, "unit": "regions/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "regions_per_gpu": B, "global_regions": B * world, "eps": wl.eps,
+                   "parallelism": f"regions sharded over {world} GPU(s)", "l2": "flushed between timed steps",
+                   "certified": int(certified.item())},
+        "e2e": {"value": e2e_val, "unit": "regions/s",
+                "h2d_bytes_per_step": int(X.numel() * 4 + y.numel() * 8),
+                "d2h_bytes_per_step": int(2 * B * 9 * 8)},
+        "gpu_launches": int(prof["kernel_launches"]),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3xtf32, "unit": "TFLOP/s",
+                     "frac": (achieved / peak_3xtf32) if achieved else None, "traffic": None,
+                     "kernel": "backsubstitution step", "peak_source": f"3xTF32 = bf16/2/3 of {src} MEASURED_PEAKS",
+                     "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
+                     "step_launches": prof["step_launches"]},
+        "clocks": clocks,
+        "wall_s_timed": wall,
+    }
+    if world == 1:
+        sample = {0: 1, 1: 16, 2: 8, 3: 4, 4: 1}[args.workload]
+        v, t1 = cpu_baseline(wl, sample)
+        out["cpu_baseline"] = {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"oracle numpy float32, {sample} regions of {wl.name}, median of 3 "
+                                         f"({t1:.2f} s each)"}
+    print(json.dumps(out))
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    try:
+        run_cfgpu(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+"""Host side of the DeepPoly network driver: network upload + one call into libcfgpu.
+
+``DeepPolyEngine`` mirrors what ``Flow(abs_elem, deeppoly(), network).flow()``
+(constraintflow/lib/flow_sparse.py:27-228) computes for a chain network, but runs the
+whole layer loop inside ``cf_deeppoly_run``: one C-ABI call per batch of regions, all
+work stream-ordered on the current torch stream.  Torch only provides device memory
+and the stream handle.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import lib, check, CfLayer, CfNetwork
+
+N_CLASSES = 10
+
+
+class DeepPolyEngine:
+    """A chain network resident on one GPU, ready to certify batches of input regions.
+
+    layers: sequence of objects with ``kind`` in {'linear','conv','relu'} and, for affine
+    layers, ``W`` / ``b`` arrays (Linear W [out, in]; Conv W [Cout, Cin, k, k]) plus
+    ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers.
+    """
+
+    def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DeepPolyEngine runs on a CUDA device only (no CPU fallback)")
+        self.input_size = int(input_size)
+        self.n_spec = int(n_spec)
+        self._keep = []
+        descs = []
+        width = self.input_size
+        for L in layers:
+            d = CfLayer()
+            if L.kind == "relu":
+                d.kind = _lib.CF_LAYER_RELU
+                d.n_in = d.n_out = width
+            else:
+                W = torch.as_tensor(L.W, dtype=torch.float32).to(self.device).contiguous()
+                b = torch.as_tensor(L.b, dtype=torch.float32).to(self.device).contiguous()
+                self._keep += [W, b]
+                d.W_dev, d.b_dev = W.data_ptr(), b.data_ptr()
+                if L.kind == "linear":
+                    d.kind = _lib.CF_LAYER_LINEAR
+                    d.n_out, d.n_in = int(W.shape[0]), int(W.shape[1])
+                elif L.kind == "conv":
+                    d.kind = _lib.CF_LAYER_CONV
+                    d.cout, d.cin, d.kh, d.kw = (int(x) for x in W.shape)
+                    _, d.ih, d.iw = (int(x) for x in L.in_shape)
+                    _, d.oh, d.ow = (int(x) for x in L.out_shape)
+                    d.stride, d.pad = int(L.stride), int(L.pad)
+                    d.n_in = d.cin * d.ih * d.iw
+                    d.n_out = d.cout * d.oh * d.ow
+                else:
+                    raise NotImplementedError(f"layer kind {L.kind}")
+            width = d.n_out
+            descs.append(d)
+        self.n_last = width
+        self._layers = (CfLayer * len(descs))(*descs)
+        self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, _lib.CF_RELAX_DEEPPOLY)
+        self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))
+        if self.N < 0:
+            check(_lib.CF_ERR_SHAPE, "network description")
+        self._ws = None
+
+    def workspace_bytes(self, chunk):
+        return int(lib.cf_deeppoly_workspace_bytes(ctypes.byref(self.net), int(chunk)))
+
+    def _workspace(self, B, budget_bytes):
+        need_full = self.workspace_bytes(max(1, B))
+        need = min(need_full, max(self.workspace_bytes(1), budget_bytes))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def run(self, l0, u0, spec_W, want_state=False, workspace_budget=8 << 30, out=None):
+        """Bounds for B regions.
+
+        l0, u0: [B, n_input] float32 device tensors (normalised input box);
+        spec_W: [B, n_spec, n_last] float32 device tensor (property matrix).
+        Returns (lb, ub) float64 [B, n_spec] and, if want_state, (state_l, state_u)
+        float32 [B, N] with every neuron's bounds in the reference's neuron order.
+        """
+        B = int(l0.shape[0])
+        for t, shp in ((l0, (B, self.input_size)), (u0, (B, self.input_size)),
+                       (spec_W, (B, self.n_spec, self.n_last))):
+            if tuple(t.shape) != shp or t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.device:
+                raise Exception(f"SHAPE MISMATCH: expected contiguous float32 {shp} on {self.device}, "
+                                f"got {tuple(t.shape)} {t.dtype} on {t.device}")
+        if out is None:
+            lb = torch.empty(B, self.n_spec, dtype=torch.float64, device=self.device)
+            ub = torch.empty_like(lb)
+        else:
+            lb, ub = out
+        sl = su = None
+        if want_state:
+            sl = torch.empty(B, self.N, dtype=torch.float32, device=self.device)
+            su = torch.empty_like(sl)
+        ws = self._workspace(B, workspace_budget)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        st = lib.cf_deeppoly_run(ctypes.byref(self.net), B, l0.data_ptr(), u0.data_ptr(), spec_W.data_ptr(),
+                                 sl.data_ptr() if sl is not None else None,
+                                 su.data_ptr() if su is not None else None,
+                                 lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+        check(st, "cf_deeppoly_run")
+        if want_state:
+            return lb, ub, sl, su
+        return lb, ub
+
+    def input_spec(self, X, y, eps, dataset):
+        """Device input box and property matrix from device centres X [B,C,H,W] and labels y [B].
+
+        Same arithmetic as constraintflow/lib/spec.py:21-72 (clip, normalise, e_label - e_k).
+        """
+        from .nets import MNIST_MEAN, MNIST_STD, CIFAR_MEAN, CIFAR_STD
+        B = int(X.shape[0])
+        C = int(X.shape[1])
+        HW = int(X[0, 0].numel())
+        mean, std = (MNIST_MEAN, MNIST_STD) if dataset == "mnist" else (CIFAR_MEAN, CIFAR_STD)
+        if len(mean) == 1:
+            mean, std = mean * C, std * C
+        l0 = torch.empty(B, C * HW, dtype=torch.float32, device=self.device)
+        u0 = torch.empty_like(l0)
+        W = torch.empty(B, self.n_spec, self.n_spec + 1, dtype=torch.float32, device=self.device)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib.cf_input_box(B, C, HW, X.data_ptr(), float(eps), _lib.f32_array(mean), _lib.f32_array(std),
+                               l0.data_ptr(), u0.data_ptr(), stream), "cf_input_box")
+        check(lib.cf_spec_matrix(B, self.n_spec + 1, y.data_ptr(), W.data_ptr(), stream), "cf_spec_matrix")
+        return l0, u0, W
+
+    def certify(self, X, y, eps, dataset, out=None):
+        """Whole pipeline on device tensors: input box, property, DeepPoly -> (lb, ub, verdict)."""
+        l0, u0, W = self.input_spec(X, y, eps, dataset)
+        lb, ub = self.run(l0, u0, W, out=out)
+        return lb, ub
+
+
+def profile_enable(on=True):
+    check(lib.cf_profile_enable(1 if on else 0))
+
+
+def profile_collect():
+    st = _lib.CfProfileStats()
+    check(lib.cf_profile_collect(ctypes.byref(st)), "cf_profile_collect")
+    return dict(kernel_launches=st.kernel_launches, step_launches=st.step_launches, step_ms=st.step_ms,
+                step_flops=st.step_flops, step_bytes=st.step_bytes)

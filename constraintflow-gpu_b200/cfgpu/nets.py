@@ -1,0 +1,229 @@
+"""Seeded synthetic networks and input regions for the five certification workloads.
+
+No public model or dataset is available offline, so every workload is a seeded
+network built in memory plus uniformly drawn input centres:
+
+* weights: ``torch.nn.init.kaiming_normal_`` (fan_in, gain sqrt(2)) drawn from one
+  ``torch.Generator().manual_seed(seed)`` in layer order (weight, then bias);
+* biases: zero, except the 784-(100x6)-10 MLP whose biases are N(0, 0.01);
+* centres: ``torch.rand(B, C, H, W, generator=manual_seed(100 + workload id))``;
+* label: argmax of the float32 forward pass at the *normalised* centre.
+
+The layer list mirrors what the reference's ONNX reader produces
+(constraintflow/lib/parse.py:60-248): Gemm -> Linear, Conv -> Conv2D, Relu -> ReLU,
+with the robustness property appended as a final per-region Linear layer
+(constraintflow/lib/parse.py:230-238, constraintflow/lib/spec.py:61-72).
+"""
+from dataclasses import dataclass, field
+import math
+
+import numpy as np
+import torch
+
+MNIST_MEAN = (0.1307,)
+MNIST_STD = (0.3081,)
+CIFAR_MEAN = (0.4914, 0.4822, 0.4465)
+CIFAR_STD = (0.2023, 0.1994, 0.2010)
+
+
+@dataclass
+class Layer:
+    """One network layer.  ``kind`` is 'linear', 'conv' or 'relu'.
+
+    Linear: W [out, in], b [out].  Conv: W [Cout, Cin, kh, kw], b [Cout], square
+    ``stride``/``pad``; ``in_shape``/``out_shape`` are (C, H, W).
+    """
+    kind: str
+    W: np.ndarray = None
+    b: np.ndarray = None
+    stride: int = 1
+    pad: int = 0
+    in_shape: tuple = None
+    out_shape: tuple = None
+
+    @property
+    def n_in(self):
+        return int(np.prod(self.in_shape))
+
+    @property
+    def n_out(self):
+        return int(np.prod(self.out_shape))
+
+
+@dataclass
+class Workload:
+    wid: int
+    name: str
+    input_shape: tuple
+    layers: list
+    B: int
+    eps: float
+    dataset: str
+    seed: int
+    description: str = ""
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def input_size(self):
+        return int(np.prod(self.input_shape))
+
+
+def _kaiming(shape, g):
+    w = torch.empty(*shape)
+    torch.nn.init.kaiming_normal_(w, generator=g)
+    return w
+
+
+def _mlp(sizes, seed, bias_std):
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for i in range(len(sizes) - 1):
+        w = _kaiming((sizes[i + 1], sizes[i]), g)
+        if bias_std:
+            b = torch.randn(sizes[i + 1], generator=g) * bias_std
+        else:
+            b = torch.zeros(sizes[i + 1])
+        layers.append(Layer('linear', w.numpy(), b.numpy(), in_shape=(sizes[i], 1, 1),
+                            out_shape=(sizes[i + 1], 1, 1)))
+        if i < len(sizes) - 2:
+            layers.append(Layer('relu', in_shape=(sizes[i + 1], 1, 1), out_shape=(sizes[i + 1], 1, 1)))
+    return layers
+
+
+def _convnet(in_shape, convs, fcs, seed):
+    g = torch.Generator().manual_seed(seed)
+    C, H, W = in_shape
+    layers = []
+    for (oc, k, s, p) in convs:
+        w = _kaiming((oc, C, k, k), g)
+        b = torch.zeros(oc)
+        OH, OW = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+        layers.append(Layer('conv', w.numpy(), b.numpy(), stride=s, pad=p, in_shape=(C, H, W),
+                            out_shape=(oc, OH, OW)))
+        layers.append(Layer('relu', in_shape=(oc, OH, OW), out_shape=(oc, OH, OW)))
+        C, H, W = oc, OH, OW
+    sizes = [C * H * W] + list(fcs)
+    for i in range(len(sizes) - 1):
+        w = _kaiming((sizes[i + 1], sizes[i]), g)
+        b = torch.zeros(sizes[i + 1])
+        layers.append(Layer('linear', w.numpy(), b.numpy(), in_shape=(sizes[i], 1, 1),
+                            out_shape=(sizes[i + 1], 1, 1)))
+        if i < len(sizes) - 2:
+            layers.append(Layer('relu', in_shape=(sizes[i + 1], 1, 1), out_shape=(sizes[i + 1], 1, 1)))
+    return layers
+
+
+def workload(wid):
+    """The five certification workloads: id -> Workload (full batch size)."""
+    if wid == 0:
+        return Workload(0, "mlp_784-50x3-10", (1, 28, 28), _mlp([784, 50, 50, 50, 10], 0, None),
+                        1, 0.01, 'mnist', 0, "DeepPoly, ReLU MLP 784-50-50-50-10, 1 region, eps 0.01")
+    if wid == 1:
+        return Workload(1, "mlp_784-100x6-10", (1, 28, 28), _mlp([784] + [100] * 6 + [10], 1, 0.01),
+                        64, 0.005, 'mnist', 1, "DeepPoly, ReLU MLP 784-(100x6)-10, bias N(0,0.01), 64 regions")
+    if wid == 2:
+        return Workload(2, "mlp_784-200x9-10", (1, 28, 28), _mlp([784] + [200] * 9 + [10], 2, None),
+                        256, 0.002, 'mnist', 2, "DeepPoly, ReLU MLP 784-(200x9)-10, 256 regions, eps 0.002")
+    if wid == 3:
+        return Workload(3, "conv_1x28x28_c16c32_fc100_fc10", (1, 28, 28),
+                        _convnet((1, 28, 28), [(16, 4, 2, 0), (32, 4, 2, 0)], [100, 10], 3),
+                        128, 0.02, 'mnist', 3, "DeepPoly, conv net 1x28x28, 128 regions, eps 0.02")
+    if wid == 4:
+        return Workload(4, "conv_3x32x32_c32c32c64c64_fc512x2_fc10", (3, 32, 32),
+                        _convnet((3, 32, 32), [(32, 3, 1, 1), (32, 4, 2, 1), (64, 3, 1, 1), (64, 4, 2, 1)],
+                                 [512, 512, 10], 4),
+                        1024, 2.0 / 255.0, 'cifar', 4, "DeepPoly, conv net 3x32x32, 1024 regions, eps 2/255")
+    raise ValueError(f"unknown workload {wid}")
+
+
+def centres(wl, B=None):
+    """Uniform [0,1] input centres [B, C, H, W] float32 (first B of the seeded draw)."""
+    Bfull = wl.B if B is None else max(B, wl.B)
+    g = torch.Generator().manual_seed(100 + wl.wid)
+    X = torch.rand(Bfull, *wl.input_shape, generator=g)
+    return X[: (wl.B if B is None else B)].contiguous()
+
+
+def _norm(x, dataset):
+    """Dataset normalisation exactly as constraintflow/lib/spec.py:21-47 (float32)."""
+    if dataset == 'mnist':
+        mean = torch.tensor(MNIST_MEAN).reshape(-1, 1)
+        std = torch.tensor(MNIST_STD).reshape(-1, 1)
+        return (x - mean) / std
+    mean = torch.tensor(CIFAR_MEAN).reshape(1, -1, 1, 1)
+    std = torch.tensor(CIFAR_STD).reshape(1, -1, 1, 1)
+    return (x - mean.expand(x.shape)) / std.expand(x.shape)
+
+
+def input_box(X, eps, dataset):
+    """L-inf box clipped to [0,1] then normalised, flattened: (l0, u0) [B, n0] float32.
+
+    Follows constraintflow/lib/spec.py:21-47 (create_l / create_u) op for op.
+    """
+    X = torch.as_tensor(X, dtype=torch.float32)
+    lo = torch.clip(X - eps, min=0., max=1.)
+    hi = torch.clip(X + eps, min=0., max=1.)
+    lo = _norm(lo, dataset).reshape(X.shape[0], -1)
+    hi = _norm(hi, dataset).reshape(X.shape[0], -1)
+    return lo.contiguous(), hi.contiguous()
+
+
+def forward(layers, x):
+    """float32 forward pass of the layer list on [B, C, H, W] inputs -> logits [B, 10]."""
+    h = torch.as_tensor(x, dtype=torch.float32)
+    for L in layers:
+        if L.kind == 'conv':
+            h = torch.nn.functional.conv2d(h, torch.from_numpy(L.W), torch.from_numpy(L.b),
+                                           stride=L.stride, padding=L.pad)
+        elif L.kind == 'linear':
+            h = h.reshape(h.shape[0], -1) @ torch.from_numpy(L.W).T + torch.from_numpy(L.b)
+        else:
+            h = torch.relu(h)
+    return h
+
+
+def labels(wl, X):
+    """Argmax label at the normalised centre, as the robustness property needs."""
+    return forward(wl.layers, _norm(torch.as_tensor(X), wl.dataset)).argmax(-1)
+
+
+def spec_weight(y, num_classes=10):
+    """Per-region property matrix y[label] - y[j], j != label: [B, 9, 10] float32.
+
+    Same construction as constraintflow/lib/spec.py:61-72.
+    """
+    y = torch.as_tensor(y)
+    B = y.shape[0]
+    eye = torch.eye(num_classes)
+    w = eye[y].unsqueeze(1) - eye.unsqueeze(0)
+    keep = ~(y.unsqueeze(1) == torch.arange(num_classes).unsqueeze(0))
+    return w[keep].view(B, num_classes - 1, num_classes).contiguous()
+
+
+def weights_digest(layers):
+    """Order-sensitive float64 checksum of all weights (guards fixture/generator drift)."""
+    s = 0.0
+    for i, L in enumerate(layers):
+        if L.W is not None:
+            s += (i + 1) * float(np.asarray(L.W, np.float64).sum()) + 0.5 * float(np.abs(L.W).astype(np.float64).sum())
+            s += (i + 7) * float(np.asarray(L.b, np.float64).sum())
+    return s
+
+
+def neuron_layout(wl):
+    """Neuron numbering of the reference (input, then each layer, then the 9-row spec layer).
+
+    Returns a list of (kind, start, end) per layer including the input and the
+    property layer, matching constraintflow/lib/parse.py:243-248 and :284-295.
+    """
+    out = [('input', 0, wl.input_size)]
+    pos = wl.input_size
+    for L in wl.layers:
+        out.append((L.kind, pos, pos + L.n_out))
+        pos += L.n_out
+    out.append(('spec', pos, pos + 9))
+    return out
+
+
+def conv_out(h, k, s, p):
+    return math.floor((h + 2 * p - k) / s) + 1

@@ -1,0 +1,252 @@
+// DeepPoly building blocks on CUDA cores: ReLU relaxation, input-box concretisation,
+// the constant update of a backsubstitution step, and a SIMT float32 step GEMM.
+//
+// Row convention of every coefficient kernel: 2*B*R rows, row r = (s, b, i) with
+// s = r / (B*R) the bound (0 lower, 1 upper), b the region and i the row inside the
+// region.  Strides (a_ss, a_bs, a_rs) locate row (s,b,i) of a possibly broadcast input
+// (zero strides), so the first step of every layer reads the shared weight matrix
+// without materialising it per region.
+#include "cf_common.cuh"
+#include "cf_kernels.cuh"
+
+namespace cf {
+
+// ------------------------------------------------------------------ ReLU relaxation
+// Generated deeppoly.Relu (deeppoly.cf:20-24,41):
+//   l' = relu(l), u' = relu(u)
+//   L' = 1[l+u>=0] * x
+//   U' = x if l>=0; 0 if u<=0; else lam*x + mu, lam = u/(u-l), mu = -(u*l)/(u-l)
+// float32 IEEE division, same operation order as the generated code.
+__global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
+                             int64_t ld_in, float* __restrict__ lo, float* __restrict__ uo, int64_t ld_out,
+                             float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu) {
+  int64_t total = B * n;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = t / n, k = t - b * n;
+    float lv = l[b * ld_in + k], uv = u[b * ld_in + k];
+    bool pos = lv >= 0.0f;
+    bool dead = (!pos) && (uv <= 0.0f);
+    float den = uv - lv;
+    float lam_u = __fdiv_rn(uv, den);
+    float mu_u = 0.0f - __fdiv_rn(__fmul_rn(uv, lv), den);
+    if (lo) lo[b * ld_out + k] = pos ? lv : 0.0f;
+    if (uo) uo[b * ld_out + k] = (uv >= 0.0f) ? uv : 0.0f;
+    alpha[t] = (__fadd_rn(lv, uv) >= 0.0f) ? 1.0f : 0.0f;
+    lam[t] = pos ? 1.0f : (dead ? 0.0f : lam_u);
+    mu[t] = (pos || dead) ? 0.0f : mu_u;
+  }
+}
+
+cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
+                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st) {
+  int64_t total = B * n;
+  if (total == 0) return CF_OK;
+  int threads = 256;
+  int64_t blocks = ceil_div(total, threads);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu);
+  return check_launch("k_relu_relax");
+}
+
+// ------------------------------------------------------------------ concretisation
+// bound(s,b,i) = c + sum_n (a>=0 ? a*box_s[n] : a*box_{1-s}[n]), box_0 = l0, box_1 = u0.
+// One warp per row; lanes stride the n0 columns (coalesced), shuffle reduction.
+__global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A, int64_t a_ss,
+                             int64_t a_bs, int64_t a_rs, const float* __restrict__ c, int64_t c_ss, int64_t c_bs,
+                             const float* __restrict__ l0, const float* __restrict__ u0, float* __restrict__ out_l,
+                             float* __restrict__ out_u, int64_t ld_out) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int64_t rows = 2 * B * R;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    int64_t s = r / (B * R), rem = r - s * B * R, b = rem / R, i = rem - b * R;
+    const float* a = A + s * a_ss + b * a_bs + i * a_rs;
+    const float* pos_box = (s == 0 ? l0 : u0) + b * n0;
+    const float* neg_box = (s == 0 ? u0 : l0) + b * n0;
+    float acc = 0.0f;
+    for (int64_t k = lane; k < n0; k += 32) {
+      float v = a[k];
+      acc += v >= 0.0f ? v * pos_box[k] : v * neg_box[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      float cv = c ? c[s * c_ss + b * c_bs + i] : 0.0f;
+      float res = acc + cv;
+      if (s == 0) out_l[b * ld_out + i] = res;
+      else out_u[b * ld_out + i] = res;
+    }
+  }
+}
+
+cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
+                            int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
+                            const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
+  int64_t rows = 2 * B * R;
+  if (rows == 0) return CF_OK;
+  int threads = 256;
+  int64_t blocks = ceil_div(rows * 32, threads);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_concretize<<<(unsigned)blocks, threads, 0, st>>>(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, out_l,
+                                                      out_u, ld_out);
+  return check_launch("k_concretize");
+}
+
+// ------------------------------------------------------------------ step constant
+// c_out = c_in + sum_k mu-term_s(a_k) + sum_k T_s(a_k) * bias[k]
+//   lower (s=0): T(a) = a>=0 ? a*alpha : a*lam,   mu-term = a<0 ? a*mu : 0
+//   upper (s=1): T(a) = a>=0 ? a*lam   : a*alpha, mu-term = a>0 ? a*mu : 0
+__global__ void k_step_const(int64_t B, int64_t R, int64_t K, const float* __restrict__ A, int64_t a_ss,
+                             int64_t a_bs, int64_t a_rs, const float* __restrict__ c_in, int64_t c_ss, int64_t c_bs,
+                             const float* __restrict__ alpha, const float* __restrict__ lam,
+                             const float* __restrict__ mu, const float* __restrict__ bias,
+                             float* __restrict__ c_out) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int64_t rows = 2 * B * R;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    int64_t s = r / (B * R), rem = r - s * B * R, b = rem / R, i = rem - b * R;
+    const float* a = A + s * a_ss + b * a_bs + i * a_rs;
+    float acc_mu = 0.0f, acc_b = 0.0f;
+    for (int64_t k = lane; k < K; k += 32) {
+      float v = a[k];
+      float t = v;
+      if (alpha) {
+        float al = alpha[b * K + k], la = lam[b * K + k], m = mu[b * K + k];
+        if (s == 0) {
+          t = v >= 0.0f ? v * al : v * la;
+          if (v < 0.0f) acc_mu += v * m;
+        } else {
+          t = v >= 0.0f ? v * la : v * al;
+          if (v > 0.0f) acc_mu += v * m;
+        }
+      }
+      if (bias) acc_b += t * bias[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc_mu += __shfl_xor_sync(0xffffffffu, acc_mu, o);
+      acc_b += __shfl_xor_sync(0xffffffffu, acc_b, o);
+    }
+    if (lane == 0) {
+      float cv = c_in ? c_in[s * c_ss + b * c_bs + i] : 0.0f;
+      c_out[r] = (acc_mu + cv) + acc_b;
+    }
+  }
+}
+
+cf_status launch_step_const(int64_t B, int64_t R, int64_t K, const float* A, int64_t a_ss, int64_t a_bs,
+                            int64_t a_rs, const float* c_in, int64_t c_ss, int64_t c_bs, const float* alpha,
+                            const float* lam, const float* mu, const float* bias, float* c_out, cudaStream_t st) {
+  int64_t rows = 2 * B * R;
+  if (rows == 0) return CF_OK;
+  int threads = 256;
+  int64_t blocks = ceil_div(rows * 32, threads);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_step_const<<<(unsigned)blocks, threads, 0, st>>>(B, R, K, A, a_ss, a_bs, a_rs, c_in, c_ss, c_bs, alpha, lam, mu,
+                                                      bias, c_out);
+  return check_launch("k_step_const");
+}
+
+// ------------------------------------------------------------------ SIMT step GEMM
+// A_out[r, :] = T_s(A_in[r, :]) @ W,  W [K, N] row-major.  64x64 output tile per CTA,
+// K staged 16 at a time in shared memory, 4x4 register tile per thread.  This is the
+// CUDA-core path (exact float32 FMA); the tensor-core path replaces it on B200.
+constexpr int SB_M = 64, SB_N = 64, SB_K = 16;
+
+__global__ void __launch_bounds__(256) k_step_gemm_simt(int64_t B, int64_t R, int64_t K, int64_t N,
+                                                         const float* __restrict__ A, int64_t a_ss, int64_t a_bs,
+                                                         int64_t a_rs, const float* __restrict__ alpha,
+                                                         const float* __restrict__ lam,
+                                                         const float* __restrict__ W, float* __restrict__ out) {
+  __shared__ float As[SB_K][SB_M + 4];
+  __shared__ float Ws[SB_K][SB_N + 4];
+  const int64_t rows = 2 * B * R;
+  const int64_t m0 = (int64_t)blockIdx.y * SB_M;
+  const int64_t n0 = (int64_t)blockIdx.x * SB_N;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][4] = {};
+  // per-thread A-load coordinates: 4 elements (rows lr + 16*q, column lk)
+  const int lk = tid & 15, lr = tid >> 4;
+  int64_t rbase[4];
+  int64_t rb[4];
+  int rs[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    int64_t r = m0 + lr + 16 * q;
+    if (r < rows) {
+      int64_t s = r / (B * R), rem = r - s * B * R, b = rem / R, i = rem - b * R;
+      rbase[q] = s * a_ss + b * a_bs + i * a_rs;
+      rb[q] = b;
+      rs[q] = (int)s;
+    } else {
+      rbase[q] = -1;
+      rb[q] = 0;
+      rs[q] = 0;
+    }
+  }
+  for (int64_t k0 = 0; k0 < K; k0 += SB_K) {
+    int64_t k = k0 + lk;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v = 0.0f;
+      if (rbase[q] >= 0 && k < K) {
+        v = A[rbase[q] + k];
+        if (alpha) {
+          float al = alpha[rb[q] * K + k], la = lam[rb[q] * K + k];
+          float pf = rs[q] == 0 ? al : la, nf = rs[q] == 0 ? la : al;
+          v = v >= 0.0f ? v * pf : v * nf;
+        }
+      }
+      As[lk][lr + 16 * q] = v;
+    }
+    // W tile: 16 x 64, 4 elements per thread
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int e = tid + 256 * q;
+      int kk = e >> 6, nn = e & 63;
+      int64_t kg = k0 + kk, ng = n0 + nn;
+      Ws[kk][nn] = (kg < K && ng < N) ? W[kg * N + ng] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SB_K; ++kk) {
+      float a4[4], w4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a4[q] = As[kk][ty * 4 + q];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) w4[q] = Ws[kk][tx * 4 + q];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a4[i], w4[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t r = m0 + ty * 4 + i;
+    if (r >= rows) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t n = n0 + tx * 4 + j;
+      if (n < N) out[r * N + n] = acc[i][j];
+    }
+  }
+}
+
+cf_status launch_step_gemm_simt(int64_t B, int64_t R, int64_t K, int64_t N, const float* A, int64_t a_ss,
+                                int64_t a_bs, int64_t a_rs, const float* alpha, const float* lam, const float* W,
+                                float* out, cudaStream_t st) {
+  int64_t rows = 2 * B * R;
+  if (rows == 0 || N == 0) return CF_OK;
+  dim3 grid((unsigned)ceil_div(N, SB_N), (unsigned)ceil_div(rows, SB_M));
+  CF_REQUIRE(grid.y <= 65535u, CF_ERR_SHAPE, "step gemm: %lld rows exceed the grid limit", (long long)rows);
+  k_step_gemm_simt<<<grid, 256, 0, st>>>(B, R, K, N, A, a_ss, a_bs, a_rs, alpha, lam, W, out);
+  return check_launch("k_step_gemm_simt");
+}
+
+}  // namespace cf

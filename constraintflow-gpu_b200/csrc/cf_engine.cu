@@ -1,0 +1,316 @@
+// Network driver of libcfgpu: runs DeepPoly over a chain network for a batch of input
+// regions, region chunk by region chunk, entirely stream-ordered on the caller's stream.
+//
+// Per chunk the abstract state is a pair of [Bc, N] float32 arrays (every neuron's lower
+// and upper bound, the dense view of the reference's abs_elem.d['l'|'u']), plus the ReLU
+// relaxations (alpha, lam, mu) of every ReLU layer.  An affine layer m is bounded by
+// backsubstitution: its coefficient rows start as W_m (shared by every region: zero
+// region stride) and are pushed through ReLU_j + affine_j for j = m-1 .. 0 by one step
+// kernel each, then folded into the input box.  Follows the generated deeppoly.Affine
+// while-loop and Flow.flow (constraintflow/lib/flow_sparse.py:27-228).
+#include <stdarg.h>
+
+#include <vector>
+
+#include "cf_common.cuh"
+#include "cf_kernels.cuh"
+#include "cf_step.cuh"
+
+namespace cf {
+
+static thread_local char g_err[512] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+void clear_error() { g_err[0] = 0; }
+
+bool fault_injected(const char* site) {
+  const char* env = getenv("CF_FAULT");
+  if (!env || !*env) return false;
+  size_t n = strlen(site);
+  const char* p = env;
+  while (*p) {
+    const char* q = strchr(p, ',');
+    size_t len = q ? (size_t)(q - p) : strlen(p);
+    if (len == n && strncmp(p, site, n) == 0) return true;
+    if (!q) break;
+    p = q + 1;
+  }
+  return false;
+}
+
+// ------------------------------------------------------------------ small kernels
+__global__ void k_to_f64(int64_t B, int64_t n, const float* __restrict__ src, int64_t ld, double* __restrict__ dst) {
+  int64_t total = B * n;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = t / n, k = t - b * n;
+    dst[t] = (double)src[b * ld + k];
+  }
+}
+
+cf_status launch_to_f64(int64_t B, int64_t n, const float* src, int64_t ld_src, double* dst, cudaStream_t st) {
+  if (B * n == 0) return CF_OK;
+  int64_t blocks = ceil_div(B * n, 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  k_to_f64<<<(unsigned)blocks, 256, 0, st>>>(B, n, src, ld_src, dst);
+  return check_launch("k_to_f64");
+}
+
+cf_status launch_copy_rows(int64_t B, int64_t n, const float* src, int64_t ld_src, float* dst, int64_t ld_dst,
+                           cudaStream_t st) {
+  if (B * n == 0) return CF_OK;
+  cudaError_t e = cudaMemcpy2DAsync(dst, ld_dst * sizeof(float), src, ld_src * sizeof(float), n * sizeof(float), B,
+                                    cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) {
+    set_error("copy_rows: %s", cudaGetErrorString(e));
+    return CF_ERR_CUDA;
+  }
+  return CF_OK;
+}
+
+// ------------------------------------------------------------------ network plan
+struct Plan {
+  std::vector<int> affine;      // layer indices of affine layers, in order
+  std::vector<int> relu_after;  // per affine index: layer index of the ReLU that follows, or -1
+  std::vector<int64_t> col;     // per layer: first state column (input = 0)
+  int64_t n_out_last = 0;       // width of the last affine layer (property matrix columns)
+  int64_t N = 0;                // total neurons incl. input and property rows
+  int64_t spec_col = 0;
+  int64_t r_max = 0, k_max = 0, n_max = 0, relu_total = 0;
+};
+
+static cf_status make_plan(const cf_network* net, Plan& p) {
+  CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
+  CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
+  int64_t pos = net->n_input, prev_width = net->n_input;
+  p.col.assign(net->n_layers, 0);
+  p.relu_after.clear();
+  p.affine.clear();
+  for (int li = 0; li < net->n_layers; ++li) {
+    const cf_layer& L = net->layers[li];
+    CF_REQUIRE(L.n_in == prev_width, CF_ERR_SHAPE, "layer %d: n_in %d != previous width %lld", li, L.n_in,
+               (long long)prev_width);
+    if (L.kind == CF_LAYER_RELU) {
+      CF_REQUIRE(!p.affine.empty() && p.relu_after.back() == -1 && net->layers[li - 1].kind != CF_LAYER_RELU,
+                 CF_ERR_UNSUPPORTED, "layer %d: ReLU must follow an affine layer", li);
+      CF_REQUIRE(L.n_out == L.n_in, CF_ERR_SHAPE, "layer %d: ReLU width mismatch", li);
+      p.relu_after.back() = li;
+      p.relu_total += L.n_out;
+    } else if (L.kind == CF_LAYER_LINEAR) {
+      CF_REQUIRE(L.W_dev && L.b_dev, CF_ERR_NULL, "layer %d: weights missing", li);
+      p.affine.push_back(li);
+      p.relu_after.push_back(-1);
+    } else if (L.kind == CF_LAYER_CONV) {
+      set_error("layer %d: convolution layers are not supported by this build of the driver", li);
+      return CF_ERR_UNSUPPORTED;
+    } else {
+      set_error("layer %d: unknown kind %d", li, L.kind);
+      return CF_ERR_UNSUPPORTED;
+    }
+    p.col[li] = pos;
+    pos += L.n_out;
+    prev_width = L.n_out;
+  }
+  CF_REQUIRE(net->layers[net->n_layers - 1].kind != CF_LAYER_RELU, CF_ERR_UNSUPPORTED,
+             "network must end with an affine layer");
+  p.n_out_last = prev_width;
+  p.spec_col = pos;
+  p.N = pos + net->n_spec;
+  p.r_max = net->n_spec;
+  for (size_t a = 0; a < p.affine.size(); ++a) {
+    const cf_layer& L = net->layers[p.affine[a]];
+    if (a > 0 && L.n_out > p.r_max) p.r_max = L.n_out;
+    if (L.n_in > p.n_max) p.n_max = L.n_in;
+    if (L.n_out > p.k_max) p.k_max = L.n_out;
+  }
+  return CF_OK;
+}
+
+static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct WsLayout {
+  size_t A[2], C[2], relu, state, total;
+};
+
+static WsLayout ws_layout(const Plan& p, int64_t Bc) {
+  WsLayout w;
+  size_t off = 0;
+  size_t a_bytes = align256((size_t)2 * Bc * p.r_max * p.n_max * sizeof(float));
+  size_t c_bytes = align256((size_t)2 * Bc * p.r_max * sizeof(float));
+  w.A[0] = off; off += a_bytes;
+  w.A[1] = off; off += a_bytes;
+  w.C[0] = off; off += c_bytes;
+  w.C[1] = off; off += c_bytes;
+  w.relu = off; off += align256((size_t)3 * Bc * p.relu_total * sizeof(float));
+  w.state = off; off += align256((size_t)2 * Bc * p.N * sizeof(float));
+  off += step_scratch_bytes(Bc, p.r_max);
+  w.total = off;
+  return w;
+}
+
+// A step with optional profiling events around it.  Algorithmic work of one step:
+// 2*rows*K*N FLOPs (one useful GEMM; the sign split adds none) and bytes = A in (unless
+// broadcast) + A out + W + the relaxation vectors.
+static cf_status timed_step(int64_t B, int64_t R, int64_t K, int64_t N, const float* A, int64_t a_ss, int64_t a_bs,
+                            int64_t a_rs, const float* c_in, int64_t c_ss, int64_t c_bs, const float* alpha,
+                            const float* lam, const float* mu, const float* W, const float* bias, float* A_out,
+                            float* c_out, char* scratch, cudaStream_t st) {
+  const double rows = 2.0 * B * R;
+  prof_step_begin(st);
+  cf_status s = run_step(B, R, K, N, A, a_ss, a_bs, a_rs, c_in, c_ss, c_bs, alpha, lam, mu, W, bias, A_out, c_out,
+                         scratch, st);
+  double a_in = (a_ss == 0 && a_bs == 0) ? (double)R * K : (a_ss == 0 ? (double)B * R * K : rows * K);
+  double bytes = 4.0 * (a_in + rows * N + (double)K * N + (alpha ? 3.0 * B * K : 0.0) + rows);
+  prof_step_end(st, 2.0 * rows * K * N, bytes);
+  return s;
+}
+
+// One chunk of Bc regions.  All pointers already offset to the chunk.
+static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
+                           const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
+                           const WsLayout& w, cudaStream_t st) {
+  const int64_t N = p.N, n0 = net->n_input;
+  float* Abuf[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
+  float* Cbuf[2] = {reinterpret_cast<float*>(ws + w.C[0]), reinterpret_cast<float*>(ws + w.C[1])};
+  float* relu_base = reinterpret_cast<float*>(ws + w.relu);
+  char* scratch = ws + w.state + align256((size_t)2 * Bc * N * sizeof(float));
+  // relaxation arrays per affine index
+  std::vector<float*> ra(p.affine.size(), nullptr), rl(p.affine.size(), nullptr), rm(p.affine.size(), nullptr);
+  {
+    float* q = relu_base;
+    for (size_t a = 0; a < p.affine.size(); ++a) {
+      if (p.relu_after[a] < 0) continue;
+      int64_t n = net->layers[p.relu_after[a]].n_out;
+      ra[a] = q; q += Bc * n;
+      rl[a] = q; q += Bc * n;
+      rm[a] = q; q += Bc * n;
+    }
+  }
+  CF_TRY(launch_copy_rows(Bc, n0, l0, n0, st_l, N, st));
+  CF_TRY(launch_copy_rows(Bc, n0, u0, n0, st_u, N, st));
+
+  // bound one affine-type layer: rows R, coefficient source (A0 strides), bias c0
+  auto bound_layer = [&](size_t ma, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs, const float* c0,
+                         int64_t col) -> cf_status {
+    const float* cur = A0;
+    int64_t ss = 0, bs = a_bs, rs = a_rs;
+    const float* c = c0;
+    int64_t c_ss = 0, c_bs = 0;
+    int t = 0;
+    for (int64_t j = (int64_t)ma - 1; j >= 0; --j, ++t) {
+      const cf_layer& Lj = net->layers[p.affine[j]];
+      int64_t K = Lj.n_out, Nn = Lj.n_in;
+      float* Aout = Abuf[t & 1];
+      float* cout_ = Cbuf[t & 1];
+      CF_TRY(timed_step(Bc, R, K, Nn, cur, ss, bs, rs, c, c_ss, c_bs, ra[j], rl[j], rm[j], Lj.W_dev, Lj.b_dev, Aout,
+                        cout_, scratch, st));
+      cur = Aout;
+      ss = Bc * R * Nn;
+      bs = R * Nn;
+      rs = Nn;
+      c = cout_;
+      c_ss = Bc * R;
+      c_bs = R;
+    }
+    return launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + col, st_u + col, N, st);
+  };
+
+  for (size_t a = 0; a < p.affine.size(); ++a) {
+    const cf_layer& L = net->layers[p.affine[a]];
+    int64_t col = p.col[p.affine[a]];
+    CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
+    if (p.relu_after[a] >= 0) {
+      const cf_layer& Rl = net->layers[p.relu_after[a]];
+      int64_t rcol = p.col[p.relu_after[a]];
+      CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a], rl[a],
+                               rm[a], st));
+    }
+  }
+  // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
+  {
+    const int64_t R = net->n_spec, K = p.n_out_last;
+    // treat it as affine index affine.size(): substitutes every affine layer below it
+    const float* cur = specW;
+    int64_t ss = 0, bs = R * K, rs = K;
+    const float* c = nullptr;
+    int64_t c_ss = 0, c_bs = 0;
+    int t = 0;
+    for (int64_t j = (int64_t)p.affine.size() - 1; j >= 0; --j, ++t) {
+      const cf_layer& Lj = net->layers[p.affine[j]];
+      int64_t Kj = Lj.n_out, Nn = Lj.n_in;
+      float* Aout = Abuf[t & 1];
+      float* cout_ = Cbuf[t & 1];
+      CF_TRY(timed_step(Bc, R, Kj, Nn, cur, ss, bs, rs, c, c_ss, c_bs, ra[j], rl[j], rm[j], Lj.W_dev, Lj.b_dev,
+                        Aout, cout_, scratch, st));
+      cur = Aout;
+      ss = Bc * R * Nn;
+      bs = R * Nn;
+      rs = Nn;
+      c = cout_;
+      c_ss = Bc * R;
+      c_bs = R;
+    }
+    CF_TRY(launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + p.spec_col,
+                             st_u + p.spec_col, N, st));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
+    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+  }
+  return CF_OK;
+}
+
+}  // namespace cf
+
+using namespace cf;
+
+extern "C" int64_t cf_network_neurons(const cf_network* net) {
+  Plan p;
+  if (make_plan(net, p) != CF_OK) return -1;
+  return p.N;
+}
+
+extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk) {
+  Plan p;
+  if (make_plan(net, p) != CF_OK || chunk < 1) return 0;
+  return ws_layout(p, chunk).total;
+}
+
+extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
+                                     const float* specW, float* state_l, float* state_u, double* lb, double* ub,
+                                     void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  CF_INJECT("deeppoly_run");
+  Plan p;
+  CF_TRY(make_plan(net, p));
+  CF_REQUIRE(B >= 0, CF_ERR_SHAPE, "B < 0");
+  if (B == 0) return CF_OK;
+  CF_REQUIRE(l0 && u0 && specW && lb && ub && workspace, CF_ERR_NULL, "deeppoly_run: NULL argument");
+  // largest chunk that fits the workspace
+  size_t base = ws_layout(p, 1).total;
+  CF_REQUIRE(ws_bytes >= base, CF_ERR_WORKSPACE, "workspace %zu < %zu bytes needed for one region", ws_bytes, base);
+  int64_t lo = 1, hi = B;
+  while (lo < hi) {
+    int64_t mid = (lo + hi + 1) / 2;
+    if (ws_layout(p, mid).total <= ws_bytes) lo = mid;
+    else hi = mid - 1;
+  }
+  const int64_t Bc = lo;
+  const WsLayout w = ws_layout(p, Bc);
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
+  for (int64_t b0 = 0; b0 < B; b0 += Bc) {
+    int64_t nb = (B - b0 < Bc) ? (B - b0) : Bc;
+    float* sl = state_l ? state_l + b0 * N : reinterpret_cast<float*>(ws + w.state);
+    float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
+    CF_TRY(run_chunk(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su, lb + b0 * ns,
+                     ub + b0 * ns, ws, w, st));
+  }
+  return CF_OK;
+}
+
+extern "C" const char* cf_last_error(void) { return g_err; }
+extern "C" const char* cf_version(void) { return "cfgpu 0.1 (sm_100a)"; }

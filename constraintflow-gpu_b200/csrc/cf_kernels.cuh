@@ -1,0 +1,26 @@
+// Internal launcher declarations shared between the kernel files and the C ABI.
+#pragma once
+#include "cf_common.cuh"
+
+namespace cf {
+
+cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
+                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st);
+
+cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
+                            int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
+                            const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
+
+cf_status launch_step_const(int64_t B, int64_t R, int64_t K, const float* A, int64_t a_ss, int64_t a_bs,
+                            int64_t a_rs, const float* c_in, int64_t c_ss, int64_t c_bs, const float* alpha,
+                            const float* lam, const float* mu, const float* bias, float* c_out, cudaStream_t st);
+
+cf_status launch_step_gemm_simt(int64_t B, int64_t R, int64_t K, int64_t N, const float* A, int64_t a_ss,
+                                int64_t a_bs, int64_t a_rs, const float* alpha, const float* lam, const float* W,
+                                float* out, cudaStream_t st);
+
+cf_status launch_to_f64(int64_t B, int64_t n, const float* src, int64_t ld_src, double* dst, cudaStream_t st);
+cf_status launch_copy_rows(int64_t B, int64_t n, const float* src, int64_t ld_src, float* dst, int64_t ld_dst,
+                           cudaStream_t st);
+
+}  // namespace cf

@@ -1,0 +1,217 @@
+/*
+ * cfgpu.h -- C ABI of libcfgpu.so, the B200 (sm_100a) runtime for the tensor code that
+ * ConstraintFlow emits for DeepPoly-style certifiers.
+ *
+ * Conventions
+ *   - Every pointer argument named *_dev is device memory; sizes are element counts.
+ *   - All calls are stream-ordered on `stream` (a cudaStream_t passed as void*), never
+ *     synchronise, never allocate or free memory, and never free caller memory.
+ *     Scratch space is a caller-provided `workspace` of the size the *_workspace_bytes
+ *     query returns.
+ *   - Return value: cf_status (0 = CF_OK).  cf_last_error() gives a message for the
+ *     last failing call on the calling host thread.
+ *   - float32 everywhere (the reference forces every block to float32,
+ *     constraintflow/gbcsr/sparse_block.py:141-147); final property bounds are also
+ *     produced as float64 as Flow.flow returns them (constraintflow/gbcsr/
+ *     sparse_tensor.py:627-654).
+ *
+ * The functions and the reference interface each one replaces:
+ *   cf_relu_relax        generated deeppoly.Relu body (examples/compiler_examples/deeppoly.cf:20-24,41;
+ *                        constraintflow/lib/llist.py:764 convert_to_poly)
+ *   cf_backsub_step      one substitution iteration of the generated deeppoly.Affine while-loop:
+ *                        clamp sign split (constraintflow/gbcsr/tensor_ops.py:765) + inner_prod
+ *                        (tensor_ops.py:370 -> SparseTensor.matmul sparse_tensor.py:1671 ->
+ *                        DenseBlock.matmul_equal_dims sparse_block.py:748) + binary add
+ *                        (tensor_ops.py:163), for a ReLU layer followed by an affine layer
+ *   cf_concretize        the input-layer substitution + final bound (generated Affine tail;
+ *                        DenseBlock.matmul_unequal_dims sparse_block.py:964)
+ *   cf_deeppoly_run      Flow.flow over a chain network (constraintflow/lib/flow_sparse.py:27-228)
+ *                        with the generated deeppoly transformer
+ *   cf_ew_binary / cf_ew_unary / cf_ew_where / cf_ew_clamp / cf_ew_any
+ *                        block kernels of the gbcsr elementwise ops: SparseBlock.binary
+ *                        (sparse_block.py:181), unary_operation (:60), where_block (:104),
+ *                        SparseBlock.clamp (:542), SparseTensor.any (sparse_tensor.py:1597)
+ */
+#ifndef CFGPU_H
+#define CFGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t cf_status;
+enum {
+  CF_OK = 0,
+  CF_ERR_SHAPE = 1,        /* inconsistent sizes ("SHAPE MISMATCH", tensor_ops.py:53-77) */
+  CF_ERR_UNSUPPORTED = 2,  /* layer / op combination not implemented (NotImplementedError) */
+  CF_ERR_CUDA = 3,         /* a CUDA launch or runtime call failed */
+  CF_ERR_TIMEOUT = 4,      /* a bounded device-side wait gave up */
+  CF_ERR_NULL = 5,         /* required pointer was NULL */
+  CF_ERR_WORKSPACE = 6,    /* workspace smaller than cf_deeppoly_workspace_bytes reports */
+  CF_ERR_INJECTED = 7      /* host-side fault injection (env CF_FAULT=<site>) fired */
+};
+
+/* Layer kinds of a chain network (constraintflow/lib/network.py:75-87). */
+enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
+
+/* Relaxations the ReLU transformer can use. */
+enum { CF_RELAX_DEEPPOLY = 0 };
+
+/* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
+ * Conv: W_dev [cout, cin, kh, kw], b_dev [cout]; neurons in (c, y, x) order,
+ * n_in = cin*ih*iw, n_out = cout*oh*ow (constraintflow/lib/parse.py:89-126).
+ * ReLU: no weights, n_in == n_out. */
+typedef struct cf_layer {
+  int32_t kind;
+  int32_t n_in, n_out;
+  int32_t cin, ih, iw, cout, oh, ow, kh, kw, stride, pad;
+  const float* W_dev;
+  const float* b_dev;
+} cf_layer;
+
+/* A chain network Input -> layers[0] -> ... -> layers[n_layers-1] -> property layer.
+ * The property layer (y[label] - y[j], constraintflow/lib/spec.py:61-72) is given per
+ * region at run time. */
+typedef struct cf_network {
+  int32_t n_layers;
+  const cf_layer* layers;  /* host array */
+  int32_t n_input;
+  int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
+  int32_t relaxation;      /* CF_RELAX_DEEPPOLY */
+} cf_network;
+
+/* Total neuron count N of the abstract state: input + every layer + property rows
+ * (constraintflow/lib/parse.py:243-248). */
+int64_t cf_network_neurons(const cf_network* net);
+
+/* Workspace needed to run `chunk` regions at a time (regions beyond it are processed
+ * in further chunks inside one cf_deeppoly_run call). */
+size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk);
+
+/* Whole DeepPoly pass over B regions.
+ *   l0_dev, u0_dev   [B, n_input]   normalised input box
+ *   spec_W_dev       [B, n_spec, n_out(last layer)]  per-region property matrix (bias 0)
+ *   state_l_dev, state_u_dev  [B, N] or NULL: every neuron's bounds in the reference's
+ *                    neuron order, input columns included (abs_elem.d['l'|'u'] dense view)
+ *   lb_dev, ub_dev   [B, n_spec] float64: the property bounds Flow.flow returns
+ *   workspace_dev / workspace_bytes: scratch, >= cf_deeppoly_workspace_bytes(net, chunk)
+ *                    for some chunk >= 1 */
+cf_status cf_deeppoly_run(const cf_network* net, int64_t B,
+                          const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
+                          float* state_l_dev, float* state_u_dev,
+                          double* lb_dev, double* ub_dev,
+                          void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* Input boundary (constraintflow/lib/spec.py:21-47, 61-72).
+ * cf_input_box: l0 = (clip(X - eps, 0, 1) - mean[c]) / std[c], u0 likewise with +eps, for
+ * X [B, C, HW] float32 (C mean/std values given on the host, C <= 4).
+ * cf_spec_matrix: per-region property matrix W [B, n_classes-1, n_classes] with row j
+ * = e_label - e_k for the k-th class k != label, from labels [B] int64. */
+cf_status cf_input_box(int64_t B, int32_t C, int64_t HW, const float* X_dev, float eps,
+                       const float* mean_host, const float* std_host,
+                       float* l0_dev, float* u0_dev, void* stream);
+cf_status cf_spec_matrix(int64_t B, int32_t n_classes, const int64_t* labels_dev, float* W_dev,
+                         void* stream);
+
+/* Profiling: while enabled (per host thread), cf_deeppoly_run records CUDA events around
+ * every backsubstitution-step launch on the caller's stream and counts every kernel it
+ * launches; cf_profile_collect waits for those events and returns the totals since the
+ * last collect. */
+typedef struct cf_profile_stats {
+  int64_t kernel_launches;   /* all kernels launched by cf_deeppoly_run */
+  int64_t step_launches;     /* backsubstitution steps (the dominant kernel) */
+  double step_ms;            /* summed device time of the steps */
+  double step_flops;         /* algorithmic FLOPs of those steps: 2*rows*K*N each */
+  double step_bytes;         /* algorithmic bytes: A in + A out + W + relaxation vectors */
+} cf_profile_stats;
+cf_status cf_profile_enable(int32_t on);
+cf_status cf_profile_collect(cf_profile_stats* out);
+
+/* ReLU transformer on pre-activation bounds l, u [B, n] (row stride ld_in):
+ * l' = relu(l), u' = relu(u) (row stride ld_out), and the relaxation
+ * L' = alpha*x, U' = lam*x + mu as compact [B, n] arrays. */
+cf_status cf_relu_relax(int64_t B, int64_t n, const float* l_dev, const float* u_dev, int64_t ld_in,
+                        float* l_out_dev, float* u_out_dev, int64_t ld_out,
+                        float* alpha_dev, float* lam_dev, float* mu_dev, int32_t relaxation,
+                        void* stream);
+
+/* One backsubstitution step for 2*B*R coefficient rows (bound s in {0 lower, 1 upper},
+ * region b, row i).  Row (s,b,i) of A_in is at A_in_dev + s*a_ss + b*a_bs + i*a_rs,
+ * K contiguous columns over the output of affine layer j (after its ReLU if
+ * alpha/lam/mu are given).  The step substitutes that ReLU (sign split with the
+ * per-region relaxation) and then the affine layer:
+ *   A_out[s,b,i,:] = T_s(A_in[s,b,i,:]) @ W     (W_dev [K, N] row-major = layer weight)
+ *   c_out[s,b,i]   = c_in + sum_k mu-terms + T_s(A_in) . bias
+ * A_out_dev is [2, B, R, N] compact, c_out_dev [2, B, R].  c_in may be NULL (zero). */
+cf_status cf_backsub_step(int64_t B, int64_t R, int64_t K, int64_t N,
+                          const float* A_in_dev, int64_t a_ss, int64_t a_bs, int64_t a_rs,
+                          const float* c_in_dev, int64_t c_ss, int64_t c_bs,
+                          const float* alpha_dev, const float* lam_dev, const float* mu_dev,
+                          const float* W_dev, const float* bias_dev,
+                          float* A_out_dev, float* c_out_dev, void* stream);
+
+/* Fold the input box into the constant: for row (s,b,i) with coefficients over the
+ * input, bound = c + sum_n (a>=0 ? a*box_s : a*box_{1-s}) where box_0 = l0, box_1 = u0.
+ * Lower rows go to out_l_dev[b*ld_out + i], upper rows to out_u_dev[b*ld_out + i]. */
+cf_status cf_concretize(int64_t B, int64_t R, int64_t n0,
+                        const float* A_dev, int64_t a_ss, int64_t a_bs, int64_t a_rs,
+                        const float* c_dev, int64_t c_ss, int64_t c_bs,
+                        const float* l0_dev, const float* u0_dev,
+                        float* out_l_dev, float* out_u_dev, int64_t ld_out, void* stream);
+
+/* ---- gbcsr block kernels ----------------------------------------------------------
+ * Elementwise kernels over one output block of `ndim` (<= CF_MAX_DIMS) dims with sizes
+ * shape[], written contiguously (row-major).  Each input has its own element strides
+ * (0 = broadcast along that dim), so the broadcast views the reference builds with
+ * RepeatBlock / unsqueeze (sparse_block.py:3797) are read in place. */
+#define CF_MAX_DIMS 6
+enum {
+  CF_OP_ADD = 0, CF_OP_SUB = 1, CF_OP_MUL = 2, CF_OP_DIV = 3,
+  CF_OP_GE = 4, CF_OP_GT = 5, CF_OP_LE = 6, CF_OP_LT = 7, CF_OP_EQ = 8, CF_OP_NE = 9,
+  CF_OP_AND = 10, CF_OP_OR = 11, CF_OP_MAX = 12, CF_OP_MIN = 13
+};
+enum { CF_UOP_NEG = 0, CF_UOP_NOT = 1, CF_UOP_SIGMOID = 2, CF_UOP_RELU = 3, CF_UOP_TO_F32 = 4 };
+/* dtype codes of a block: 0 float32, 1 bool (one byte, 0/1) */
+enum { CF_F32 = 0, CF_BOOL = 1 };
+
+/* out = x op y.  Arithmetic in float32 (bool reads as 0/1); comparisons, and, or give
+ * bool; the result is converted to out_dtype (bool: value != 0). */
+cf_status cf_ew_binary(int32_t op, int32_t ndim, const int64_t* shape,
+                       const void* x_dev, int32_t x_dtype, const int64_t* x_strides,
+                       const void* y_dev, int32_t y_dtype, const int64_t* y_strides,
+                       void* out_dev, int32_t out_dtype, void* stream);
+/* out = op(x) (neg, logical not, sigmoid, relu, or plain conversion to out_dtype). */
+cf_status cf_ew_unary(int32_t op, int32_t ndim, const int64_t* shape,
+                      const void* x_dev, int32_t x_dtype, const int64_t* x_strides,
+                      void* out_dev, int32_t out_dtype, void* stream);
+/* out = cond ? y : z  (cond bool, y and z of out_dtype). */
+cf_status cf_ew_where(int32_t ndim, const int64_t* shape,
+                      const uint8_t* cond_dev, const int64_t* c_strides,
+                      const void* y_dev, const int64_t* y_strides,
+                      const void* z_dev, const int64_t* z_strides,
+                      void* out_dev, int32_t out_dtype, void* stream);
+/* min_true != 0: out = max(x, c) (clamp(min=c)); else out = min(x, c) (clamp(max=c)). */
+cf_status cf_ew_clamp(int32_t ndim, const int64_t* shape, const float* x_dev, const int64_t* x_strides,
+                      float c, int32_t min_true, float* out_dev, void* stream);
+/* *flag_dev |= 1 if any element of x is nonzero (flag is a device uint32). */
+cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x_dev, int32_t x_dtype,
+                    const int64_t* x_strides, uint32_t* flag_dev, void* stream);
+
+/* Message for the last non-OK status on this host thread ("" if none). */
+const char* cf_last_error(void);
+/* Library version string. */
+const char* cf_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif /* CFGPU_H */

@@ -1,0 +1,238 @@
+"""CPU oracle for the DeepPoly certification hot path (numpy, float32).
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of bench.py may import this module,
+and only as the checker or as the timed CPU restatement.  The product path
+(cfgpu) never imports it and has no CPU fallback.
+
+What it restates.  The reference compiles examples/compiler_examples/deeppoly.cf
+into per-layer transformer code (constraintflow/compiler/codeGen.py) that the layer
+loop constraintflow/lib/flow_sparse.py:27-228 calls.  On a chain network
+(Input, [Linear|Conv, ReLU]*, Linear, property layer) the arithmetic that code
+performs is:
+
+* Affine (deeppoly.cf:14-15, 39): the coefficient matrix of layer m starts as
+  W_m (per-region property matrix for the appended spec layer) with constant
+  b_m.  A backward traversal (priority2 = -layer, deeppoly.cf:10) substitutes one
+  earlier layer per while-iteration.  Each substitution is the sign split
+  ``clamp(A,0,True)@L + clamp(A,0,False)@U`` (replace_lower/replace_upper,
+  deeppoly.cf:6-7, turned into clamps by constraintflow/compiler/optimizations/
+  rewrite.py:116) with inner_prod (constraintflow/gbcsr/tensor_ops.py:370) and
+  clamp (tensor_ops.py:765); the constant accumulates
+  ``((A+@Lc + A-@Uc) + 0) + c`` (tensor_ops.py:616-687 split the stop / not-stop
+  parts).  The input layer's L/U are (empty matrix, constant l0 / u0)
+  (constraintflow/lib/spec.py:86-104), so the final substitution folds the
+  input box into the constant and the bound is that constant.
+* Relu (deeppoly.cf:20-24, 41): l' = relu(l), u' = relu(u);
+  L' = 1[l+u>=0] x;  U' = x if l>=0, 0 if u<=0, else lam x + mu with
+  lam = u/(u-l), mu = -(u*l)/(u-l) (all float32, same operation order).
+* Affine substitution of a conv layer is the transposed convolution of the
+  coefficient rows (constraintflow/gbcsr/sparse_block.py:839-928, 1364-1730).
+* Input box: clip(X -/+ eps, 0, 1) then dataset normalisation (spec.py:21-47).
+* Output: Flow.flow returns the property layer's l/u via get_dense, float64
+  (constraintflow/gbcsr/sparse_tensor.py:627-654).
+
+Pinned against: the reference's own outputs on the same seeded networks, stored
+by tests/golden/gen_golden.py in tests/golden/*.npz.
+"""
+import numpy as np
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------- relaxation
+def relu_relax(l, u, force=None):
+    """DeepPoly ReLU transformer (deeppoly.cf:20-24,41; generated Relu body).
+
+    Returns (l', u', alpha, lam, mu): L' = alpha*x, U' = lam*x + mu.
+
+    ``force`` = (l_dec, u_dec) optionally supplies the bounds from which the three
+    discrete decisions (l>=0, u<=0, l+u>=0) are taken, while the continuous values
+    (lam, mu, relu) still come from (l, u).  A test uses it to replay another
+    implementation's decisions: those comparisons are discontinuous, so a bound a
+    few ulps from a threshold can flip them and every later layer then differs.
+    """
+    l = l.astype(F32, copy=False)
+    u = u.astype(F32, copy=False)
+    ld, ud = (l, u) if force is None else (force[0].astype(F32), force[1].astype(F32))
+    zero = F32(0.0)
+    l_new = np.where(ld >= zero, l, zero).astype(F32)
+    u_new = np.where(ud >= zero, u, zero).astype(F32)
+    alpha = ((ld + ud) >= zero).astype(F32)
+    with np.errstate(divide='ignore', invalid='ignore'):
+        den = (u - l).astype(F32)
+        lam_unst = (u / den).astype(F32)
+        mu_unst = (zero - (u * l).astype(F32) / den).astype(F32)
+    pos = ld >= zero
+    dead = (~pos) & (ud <= zero)
+    lam = np.where(pos, F32(1.0), np.where(dead, zero, lam_unst)).astype(F32)
+    mu = np.where(pos | dead, zero, mu_unst).astype(F32)
+    return l_new, u_new, alpha, lam, mu
+
+
+# ---------------------------------------------------------------- substitutions
+def _split(A):
+    zero = F32(0.0)
+    return np.maximum(A, zero), np.minimum(A, zero)
+
+
+def subst_relu(A, c, alpha, lam, mu, lower):
+    """Substitute a ReLU layer: A [B,R,n], c [B,R]; per-region vectors [B,n].
+
+    Lower bound: coeff>=0 -> coeff*L (alpha x), else coeff*U (lam x + mu).
+    Upper bound: coeff>=0 -> coeff*U, else coeff*L (deeppoly.cf:6-7).
+    """
+    Ap, An = _split(A)
+    if lower:
+        A_new = Ap * alpha[:, None, :] + An * lam[:, None, :]
+        dc = np.einsum('brn,bn->br', An, mu, dtype=F32)
+    else:
+        A_new = Ap * lam[:, None, :] + An * alpha[:, None, :]
+        dc = np.einsum('brn,bn->br', Ap, mu, dtype=F32)
+    return A_new.astype(F32), ((dc + F32(0.0)) + c).astype(F32)
+
+
+def _conv_T(A, layer):
+    """Rows of A over the conv output [.., Cout*OH*OW] -> rows over its input.
+
+    Transposed convolution (the adjoint of the conv forward) computed as a
+    col2im scatter: out[:, ci, s*oy+i-p, s*ox+j-p] += sum_co A[:, co, oy, ox] W[co, ci, i, j].
+    """
+    Cout, Cin, kh, kw = layer.W.shape
+    _, OH, OW = layer.out_shape
+    _, IH, IW = layer.in_shape
+    s, p = layer.stride, layer.pad
+    R = A.shape[0]
+    Ahw = A.reshape(R, Cout, OH, OW).transpose(0, 2, 3, 1).reshape(R * OH * OW, Cout)
+    Hp, Wp = (OH - 1) * s + kh, (OW - 1) * s + kw
+    outp = np.zeros((R, max(Hp, IH + p), max(Wp, IW + p), Cin), F32)
+    for i in range(kh):
+        for j in range(kw):
+            contrib = (Ahw @ layer.W[:, :, i, j]).reshape(R, OH, OW, Cin)
+            outp[:, i:i + s * (OH - 1) + 1:s, j:j + s * (OW - 1) + 1:s, :] += contrib
+    out = outp[:, p:p + IH, p:p + IW, :]
+    return np.ascontiguousarray(out.transpose(0, 3, 1, 2)).reshape(R, Cin * IH * IW)
+
+
+def _conv_bias(layer):
+    _, OH, OW = layer.out_shape
+    return np.repeat(layer.b.astype(F32), OH * OW)
+
+
+def layer_bias(layer):
+    return _conv_bias(layer) if layer.kind == 'conv' else layer.b.astype(F32)
+
+
+def apply_affine_T(A2d, layer):
+    """A2d [R, n_out] @ W (Linear) or transposed conv (Conv) -> [R, n_in]."""
+    if layer.kind == 'conv':
+        return _conv_T(A2d, layer)
+    return (A2d @ layer.W.astype(F32)).astype(F32)
+
+
+def subst_affine(A, c, layer):
+    """Substitute an affine layer whose L = U = W x + b: A+@W + A-@W, c + A+@b + A-@b."""
+    B, R, n = A.shape
+    Ap, An = _split(A)
+    W2 = lambda M: apply_affine_T(M.reshape(B * R, n), layer).reshape(B, R, -1)
+    A_new = (W2(Ap) + W2(An)).astype(F32)
+    b = layer_bias(layer)
+    dc = (Ap @ b + An @ b).astype(F32)
+    return A_new, ((dc + F32(0.0)) + c).astype(F32)
+
+
+def concretize(A, c, l0, u0, lower):
+    """Fold the input box into the constant (input layer L/U = const l0/u0)."""
+    Ap, An = _split(A)
+    if lower:
+        dc = np.einsum('brn,bn->br', Ap, l0, dtype=F32) + np.einsum('brn,bn->br', An, u0, dtype=F32)
+    else:
+        dc = np.einsum('brn,bn->br', Ap, u0, dtype=F32) + np.einsum('brn,bn->br', An, l0, dtype=F32)
+    return ((dc.astype(F32) + F32(0.0)) + c).astype(F32)
+
+
+# ---------------------------------------------------------------- network
+def _affine_rows(layer, row_lo, row_hi, B):
+    """Initial coefficient rows [B, r, n_in] of an affine layer: rows of W (or of the conv Toeplitz)."""
+    if layer.kind == 'linear':
+        W = layer.W.astype(F32)[row_lo:row_hi]
+        return np.broadcast_to(W, (B,) + W.shape)
+    n_out = layer.n_out
+    E = np.zeros((row_hi - row_lo, n_out), F32)
+    E[np.arange(row_hi - row_lo), np.arange(row_lo, row_hi)] = 1.0
+    rows = _conv_T(E, layer)
+    return np.broadcast_to(rows, (B,) + rows.shape)
+
+
+def deeppoly(layers, l0, u0, spec_W, row_chunk=4096, force=None):
+    """Run DeepPoly over a chain network.
+
+    layers : list of cfgpu.nets.Layer (linear / conv / relu), property layer excluded.
+    l0, u0 : [B, n0] float32 normalised input box.
+    spec_W : [B, 9, 10] per-region property matrix (bias 0).
+    force  : optional (l_all, u_all) [B, N-n0] in the same per-layer order as the
+             returned bounds; the ReLU decisions are then taken from them (see relu_relax).
+    Returns (bounds, lb, ub): bounds is a list, per layer (excluding input,
+    including the property layer), of (l [B,n], u [B,n]); lb/ub float64 [B, 9].
+    """
+    l0 = np.asarray(l0, F32)
+    u0 = np.asarray(u0, F32)
+    B = l0.shape[0]
+    affine = []       # (layer, relu-after (alpha, lam, mu) or None)
+    bounds = []
+    relax = {}
+    pos = 0
+    for idx, L in enumerate(layers + ['spec']):
+        if L == 'spec':
+            kind = 'spec'
+        else:
+            kind = L.kind
+        if kind == 'relu':
+            l_prev, u_prev = bounds[-1]
+            n = l_prev.shape[1]
+            fz = None if force is None else (force[0][:, pos - n:pos], force[1][:, pos - n:pos])
+            ln, un, alpha, lam, mu = relu_relax(l_prev, u_prev, fz)
+            pos += n
+            relax[len(affine) - 1] = (alpha, lam, mu)
+            bounds.append((ln, un))
+            continue
+        # affine-type layer: backsubstitute to the input, chunked over rows
+        n_rows = 9 if kind == 'spec' else L.n_out
+        lo_all = np.empty((B, n_rows), F32)
+        up_all = np.empty((B, n_rows), F32)
+        for r0 in range(0, n_rows, row_chunk):
+            r1 = min(n_rows, r0 + row_chunk)
+            if kind == 'spec':
+                A0 = spec_W[:, r0:r1, :].astype(F32)
+                c0 = np.zeros((B, r1 - r0), F32)
+            else:
+                A0 = _affine_rows(L, r0, r1, B)
+                c0 = np.broadcast_to(layer_bias(L)[r0:r1], (B, r1 - r0)).astype(F32)
+            for lower in (True, False):
+                A, c = np.array(A0, F32), np.array(c0, F32)
+                for j in range(len(affine) - 1, -1, -1):
+                    if j in relax:
+                        alpha, lam, mu = relax[j]
+                        A, c = subst_relu(A, c, alpha, lam, mu, lower)
+                    A, c = subst_affine(A, c, affine[j])
+                    if not np.any(A):
+                        A = None
+                        break
+                if A is None:
+                    res = c
+                else:
+                    res = concretize(A, c, l0, u0, lower)
+                (lo_all if lower else up_all)[:, r0:r1] = res
+        bounds.append((lo_all, up_all))
+        pos += n_rows
+        if kind != 'spec':
+            affine.append(L)
+    lb, ub = bounds[-1]
+    return bounds, lb.astype(np.float64), ub.astype(np.float64)
+
+
+def flatten_bounds(wl_input_size, bounds, B):
+    """Concatenate per-layer bounds into the reference's [B, N] neuron order (input excluded)."""
+    ls = [b[0] for b in bounds]
+    us = [b[1] for b in bounds]
+    return np.concatenate(ls, axis=1), np.concatenate(us, axis=1)

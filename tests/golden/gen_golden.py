@@ -1,0 +1,183 @@
+"""Generate the golden vectors under tests/golden/ by running the REFERENCE itself.
+
+This script is test infrastructure.  It runs only in a container that has the
+reference checkout (ConstraintFlow, pure Python + PyTorch) at REF_ROOT; the GPU
+box never runs it.  Usage::
+
+    python tests/golden/gen_golden.py            # all cases
+    python tests/golden/gen_golden.py dp_w0      # cases whose name starts with dp_w0
+
+For every case it
+  1. compiles the reference's own certifier program
+     (examples/compiler_examples/deeppoly.cf or crown.cf) with the reference
+     compiler (constraintflow/compiler/compile.py:66-97) into a scratch dir;
+  2. builds the seeded synthetic network in memory (cfgpu/nets.py) and hands it
+     to the reference's ONNX reader through the in-memory onnx stand-in
+     (refshim/stubs/onnx), exactly the fields constraintflow/lib/parse.py reads;
+  3. runs the generated ``main.run`` body (network + spec, Abs_elem_sparse,
+     Flow(...).flow(), as emitted by constraintflow/compiler/codeGen.py:26-36)
+     on CPU, the way constraintflow/cli.py:344-354 calls it (no dataset download);
+  4. stores the inputs, the final bounds (float64, as Flow.flow returns them) and
+     the full per-neuron l/u state of the abstract element into ``<case>.npz``.
+
+Shims (refshim/): an ANTLR v3-ATN loader (the generated parser predates the
+installed antlr4 runtime) and stub plotting/graphviz modules that the reference
+imports but never calls on this path.
+"""
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
+PKG = os.path.join(REPO, "constraintflow-gpu_b200")
+
+# name -> (program, workload id, batch, eps)
+CASES = {
+    "dp_w0_b1_e1e-2": ("deeppoly", 0, 1, 0.01),
+    "dp_w0_b4_e1e-3": ("deeppoly", 0, 4, 0.001),
+    "dp_w0_b4_e0": ("deeppoly", 0, 4, 0.0),
+    "dp_w1_b16_e5e-3": ("deeppoly", 1, 16, 0.005),
+    "dp_w1_b16_e5e-4": ("deeppoly", 1, 16, 0.0005),
+    "dp_w1_b16_e5e-5": ("deeppoly", 1, 16, 0.00005),
+    "dp_w2_b8_e2e-3": ("deeppoly", 2, 8, 0.002),
+    "dp_w2_b8_e2e-4": ("deeppoly", 2, 8, 0.0002),
+    "dp_w2_b8_e2e-5": ("deeppoly", 2, 8, 0.00002),
+    "dp_w3_b4_e2e-2": ("deeppoly", 3, 4, 0.02),
+    "dp_w3_b4_e2e-3": ("deeppoly", 3, 4, 0.002),
+    "dp_w3_b4_e2e-4": ("deeppoly", 3, 4, 0.0002),
+    "dp_w4_b1_e2o255": ("deeppoly", 4, 1, 2.0 / 255.0),
+    "dp_w4_b1_e2o2550": ("deeppoly", 4, 1, 2.0 / 2550.0),
+    "crown_w0_b4_e1e-2": ("crown", 0, 4, 0.01),
+    "crown_w0_b4_e1e-3": ("crown", 0, 4, 0.001),
+    "crown_w2_b4_e2e-3": ("crown", 2, 4, 0.002),
+    "crown_w2_b4_e2e-4": ("crown", 2, 4, 0.0002),
+}
+
+
+def _load_nets():
+    spec = importlib.util.spec_from_file_location("cfgpu_nets", os.path.join(PKG, "cfgpu", "nets.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _onnx_graph(nets, wl):
+    """In-memory graph with the fields constraintflow/lib/parse.py:60-143 reads.
+
+    Conv attributes are positional in torch-export order
+    (dilations, group, kernel_shape, pads, strides): parse.py:110-112.  A leading
+    Flatten (skipped by the reader as identity, parse.py:240-247) keeps the
+    4-D input shape for the first Gemm (parse.py:137).
+    """
+    import types
+    NS = types.SimpleNamespace
+    inits, nodes = [], []
+    prev = "input"
+    conv_i = fc_i = relu_i = 0
+    flattened = False
+    for L in wl.layers:
+        if L.kind == "conv":
+            k = L.W.shape[2]
+            inits += [NS(name=f"c{conv_i}.weight", array=L.W), NS(name=f"c{conv_i}.bias", array=L.b)]
+            nodes.append(NS(op_type="Conv", input=[prev, f"c{conv_i}.weight", f"c{conv_i}.bias"],
+                            output=[f"cv{conv_i}"],
+                            attribute=[NS(ints=[1, 1]), NS(ints=[1]), NS(ints=[k, k]),
+                                       NS(ints=[L.pad] * 4), NS(ints=[L.stride] * 2)]))
+            prev = f"cv{conv_i}"
+            conv_i += 1
+        elif L.kind == "linear":
+            if not flattened:
+                nodes.append(NS(op_type="Flatten", input=[prev], output=["flat"], attribute=[]))
+                prev = "flat"
+                flattened = True
+            inits += [NS(name=f"fc{fc_i}.weight", array=L.W), NS(name=f"fc{fc_i}.bias", array=L.b)]
+            nodes.append(NS(op_type="Gemm", input=[prev, f"fc{fc_i}.weight", f"fc{fc_i}.bias"],
+                            output=[f"g{fc_i}"], attribute=[]))
+            prev = f"g{fc_i}"
+            fc_i += 1
+        else:
+            nodes.append(NS(op_type="Relu", input=[prev], output=[f"r{relu_i}"], attribute=[]))
+            prev = f"r{relu_i}"
+            relu_i += 1
+    C, H, W = wl.input_shape
+    dims = [NS(dim_value=v) for v in (1, C, H, W)]
+    return NS(input=[NS(name="input", type=NS(tensor_type=NS(shape=NS(dim=dims))))],
+              node=nodes, initializer=inits)
+
+
+def worker(program, outdir, case_names):
+    """Runs inside a fresh interpreter: the reference package on sys.path first."""
+    sys.argv = ["x"]
+    sys.path.insert(0, os.path.join(HERE, "refshim", "stubs"))
+    sys.path.insert(0, os.path.join(HERE, "refshim"))
+    sys.path.insert(0, REF_ROOT)
+    import numpy as np
+    import torch
+    import antlr_v3_shim  # noqa: F401  (must precede the reference's parser import)
+    import onnx
+    from constraintflow.compiler import compile as cfcompile
+    nets = _load_nets()
+
+    src = os.path.join(REF_ROOT, "examples", "compiler_examples", f"{program}.cf")
+    os.makedirs(outdir, exist_ok=True)
+    cfcompile.compile(src, outdir)
+    sys.path.insert(0, outdir)
+    import constraintflow.lib.flow_sparse as fs
+    captured = {}
+    orig_flow = fs.Flow.flow
+
+    def flow_and_keep(self):
+        res = orig_flow(self)
+        captured["abs_elem"] = self.abs_elem
+        captured["model"] = self.model
+        return res
+    fs.Flow.flow = flow_and_keep
+    import main as cfmain
+
+    for name in case_names:
+        prog, wid, B, eps = CASES[name]
+        wl = nets.workload(wid)
+        X = nets.centres(wl, B)
+        y = nets.labels(wl, X)
+        net_name = f"{name}.onnx"
+        onnx.register(net_name, _onnx_graph(nets, wl))
+        torch.set_num_threads(os.cpu_count())
+        t0 = time.perf_counter()
+        lb, ub = cfmain.run(net_name, B, eps, X, y, wl.dataset, False, False, False)
+        dt = time.perf_counter() - t0
+        ae = captured["abs_elem"]
+        l_all = ae.d["l"].get_dense().to(torch.float32).numpy()
+        u_all = ae.d["u"].get_dense().to(torch.float32).numpy()
+        layout = [(str(layer.type).split(".")[-1], int(layer.start), int(layer.end)) for layer in captured["model"]]
+        np.savez_compressed(
+            os.path.join(HERE, f"{name}.npz"),
+            program=program, wid=wid, B=B, eps=eps, dataset=wl.dataset,
+            X=X.numpy(), y=y.numpy().astype(np.int64),
+            weights_digest=nets.weights_digest(wl.layers),
+            lb=lb.numpy(), ub=ub.numpy(), l_all=l_all, u_all=u_all,
+            layout=json.dumps(layout), ref_seconds=dt)
+        print(json.dumps({"case": name, "seconds": round(dt, 2), "lb_dtype": str(lb.dtype),
+                          "certified": int((lb >= 0).all(dim=1).sum()), "B": B}), flush=True)
+
+
+def main():
+    sel = sys.argv[1:]
+    names = [n for n in CASES if not sel or any(n.startswith(s) for s in sel)]
+    by_prog = {}
+    for n in names:
+        by_prog.setdefault(CASES[n][0], []).append(n)
+    for prog, case_names in by_prog.items():
+        with tempfile.TemporaryDirectory() as tmp:
+            code = ("import sys; sys.path.insert(0, %r); import gen_golden as g; g.worker(%r, %r, %r)"
+                    % (HERE, prog, os.path.join(tmp, "out"), case_names))
+            subprocess.run([sys.executable, "-c", code], cwd=tmp, check=True)
+
+
+if __name__ == "__main__":
+    main()

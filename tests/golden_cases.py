@@ -1,0 +1,43 @@
+"""Loader for the reference-generated golden vectors (tests/golden/*.npz)."""
+import glob
+import os
+
+import numpy as np
+
+from cfgpu import nets
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def names(program="deeppoly", max_wid=4):
+    out = []
+    for f in sorted(glob.glob(os.path.join(GOLDEN, "*.npz"))):
+        z = np.load(f)
+        if str(z["program"]) == program and int(z["wid"]) <= max_wid:
+            out.append(os.path.basename(f)[:-4])
+    return out
+
+
+class Case:
+    def __init__(self, name):
+        z = np.load(os.path.join(GOLDEN, name + ".npz"))
+        self.name = name
+        self.program = str(z["program"])
+        self.wid = int(z["wid"])
+        self.B = int(z["B"])
+        self.eps = float(z["eps"])
+        self.wl = nets.workload(self.wid)
+        assert abs(nets.weights_digest(self.wl.layers) - float(z["weights_digest"])) < 1e-6 * max(
+            1.0, abs(float(z["weights_digest"]))), "synthetic network drifted from the golden vectors"
+        self.X = z["X"]
+        self.y = z["y"]
+        self.lb, self.ub = z["lb"], z["ub"]
+        n0 = self.wl.input_size
+        self.l_all, self.u_all = z["l_all"][:, n0:], z["u_all"][:, n0:]
+        self.l0_ref, self.u0_ref = z["l_all"][:, :n0], z["u_all"][:, :n0]
+        l0, u0 = nets.input_box(self.X, self.eps, self.wl.dataset)
+        self.l0, self.u0 = l0.numpy(), u0.numpy()
+        self.spec_W = nets.spec_weight(self.y).numpy()
+        self.sizes = [L.n_out for L in self.wl.layers] + [9]
+        kinds = [L.kind for L in self.wl.layers]
+        self.relu_layers = [i for i in range(len(kinds) - 1) if kinds[i + 1] == "relu"]
