@@ -58,6 +58,7 @@ def _load():
         "cf_network_neurons": (_i64, [P(CfNetwork)]),
         "cf_deeppoly_workspace_bytes": (_sz, [P(CfNetwork), _i64]),
         "cf_deeppoly_run": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+        "cf_deeppoly_check": (_i32, [_vp, _vp]),
         "cf_relu_relax": (_i32, [_i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp]),
         "cf_backsub_step": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -86,7 +87,8 @@ def _load():
 lib = _load()
 
 # Every symbol the C header declares (checked by the CPU test suite).
-EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_relu_relax",
+EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_deeppoly_check",
+            "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",
             "cf_ew_any", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",
             "cf_last_error", "cf_version")

@@ -76,13 +76,14 @@ class DeepPolyEngine:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def run(self, l0, u0, spec_W, want_state=False, workspace_budget=8 << 30, out=None):
+    def run(self, l0, u0, spec_W, want_state=False, workspace_budget=8 << 30, out=None, check_device=False):
         """Bounds for B regions.
 
         l0, u0: [B, n_input] float32 device tensors (normalised input box);
         spec_W: [B, n_spec, n_last] float32 device tensor (property matrix).
         Returns (lb, ub) float64 [B, n_spec] and, if want_state, (state_l, state_u)
         float32 [B, N] with every neuron's bounds in the reference's neuron order.
+        check_device=True synchronises and raises if a bounded device wait gave up.
         """
         B = int(l0.shape[0])
         for t, shp in ((l0, (B, self.input_size)), (u0, (B, self.input_size)),
@@ -106,6 +107,8 @@ class DeepPolyEngine:
                                  su.data_ptr() if su is not None else None,
                                  lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         check(st, "cf_deeppoly_run")
+        if check_device:
+            check(lib.cf_deeppoly_check(ws.data_ptr(), stream), "device status")
         if want_state:
             return lb, ub, sl, su
         return lb, ub

@@ -1,0 +1,42 @@
+// Chained tensor-core backsubstitution (cf_chain.cu): parameters and host entry points.
+#pragma once
+#include "cf_common.cuh"
+
+namespace cf {
+
+constexpr int kChainStages = 2;     // shared-memory pipeline depth
+constexpr int kChainMaxSteps = 24;  // substitutions per launch (affine layers below the bounded one)
+
+// One substitution: ReLU_j (if alpha != nullptr) then affine layer j, W_j [K, N].
+struct ChainStep {
+  const uint8_t* wimg;  // chain_prep_weights image of W_j
+  const float* alpha;   // [B, K] relaxation of the ReLU after layer j, or nullptr
+  const float* lam;
+  const float* mu;
+  const float* bias;    // [K] bias of layer j
+  int32_t K, N, tile_n, n_tiles, kchunks;
+};
+
+struct ChainParams {
+  ChainStep st[kChainMaxSteps];
+  int32_t S;
+  int64_t B, R, rows;                   // rows = 2*B*R, row = (bound, region, i)
+  const float* A0;                      // first coefficient rows (row (s,b,i) at s*a_ss + b*a_bs + i*a_rs)
+  int64_t a_ss, a_bs, a_rs;
+  const float* c0;                      // [R] constant of the bounded layer (its bias) or nullptr
+  const float* l0;                      // [B, n0] input box
+  const float* u0;
+  int64_t n0;
+  float* out_l;                         // bound of row (0,b,i) -> out_l[b*ld_out + i]
+  float* out_u;
+  int64_t ld_out;
+  int* err;                             // device error word (bounded-wait timeouts)
+  uint32_t stage_bytes, w_lo_off;       // filled by chain_launch
+};
+
+void chain_tile(int N, int& tile_n, int& n_tiles);
+size_t chain_wimg_bytes(int K, int N);
+cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStream_t st);
+cf_status chain_launch(const ChainParams& P, cudaStream_t st);
+
+}  // namespace cf

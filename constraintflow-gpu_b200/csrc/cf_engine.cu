@@ -12,6 +12,7 @@
 
 #include <vector>
 
+#include "cf_chain.cuh"
 #include "cf_common.cuh"
 #include "cf_kernels.cuh"
 #include "cf_step.cuh"
@@ -133,12 +134,21 @@ static cf_status make_plan(const cf_network* net, Plan& p) {
 static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t A[2], C[2], relu, state, total;
+  size_t err, wimg, A[2], C[2], relu, state, total;
+  std::vector<size_t> wimg_off;  // per affine index
 };
 
-static WsLayout ws_layout(const Plan& p, int64_t Bc) {
+static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   WsLayout w;
   size_t off = 0;
+  w.err = off; off += 256;
+  w.wimg = off;
+  w.wimg_off.assign(p.affine.size(), 0);
+  for (size_t a = 0; a < p.affine.size(); ++a) {
+    const cf_layer& L = net->layers[p.affine[a]];
+    w.wimg_off[a] = off;
+    off += align256(chain_wimg_bytes(L.n_out, L.n_in));
+  }
   size_t a_bytes = align256((size_t)2 * Bc * p.r_max * p.n_max * sizeof(float));
   size_t c_bytes = align256((size_t)2 * Bc * p.r_max * sizeof(float));
   w.A[0] = off; off += a_bytes;
@@ -169,10 +179,79 @@ static cf_status timed_step(int64_t B, int64_t R, int64_t K, int64_t N, const fl
   return s;
 }
 
+// Tensor-core chain (cf_chain.cu) unless CF_STEP_IMPL=simt selects the CUDA-core steps.
+static bool use_chain() {
+  const char* e = getenv("CF_STEP_IMPL");
+  return !(e && strcmp(e, "simt") == 0);
+}
+
+// The chain keeps the coefficient rows in TMEM: every substitution except the last must
+// be at most 256 wide, and every layer below the bounded one must be linear.
+static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below) {
+  if (!use_chain() || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
+  for (size_t j = 0; j < n_below; ++j) {
+    const cf_layer& L = net->layers[p.affine[j]];
+    if (L.kind != CF_LAYER_LINEAR) return false;
+    if (j + 2 <= n_below && L.n_out > 256) return false;
+  }
+  return true;
+}
+
+static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const WsLayout& w, char* ws, int64_t Bc,
+                                    size_t n_below, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs,
+                                    const float* c0, const float* l0, const float* u0, float* out_l, float* out_u,
+                                    const std::vector<float*>& ra, const std::vector<float*>& rl,
+                                    const std::vector<float*>& rm, cudaStream_t st) {
+  ChainParams P;
+  memset(&P, 0, sizeof(P));
+  P.S = (int32_t)n_below;
+  for (int s = 0; s < P.S; ++s) {
+    const size_t j = n_below - 1 - s;
+    const cf_layer& L = net->layers[p.affine[j]];
+    ChainStep& S = P.st[s];
+    S.wimg = reinterpret_cast<const uint8_t*>(ws + w.wimg_off[j]);
+    S.alpha = ra[j];
+    S.lam = rl[j];
+    S.mu = rm[j];
+    S.bias = L.b_dev;
+    S.K = L.n_out;
+    S.N = L.n_in;
+    chain_tile(S.N, S.tile_n, S.n_tiles);
+    S.kchunks = (S.K + 31) / 32;
+  }
+  P.B = Bc;
+  P.R = R;
+  P.rows = 2 * Bc * R;
+  P.A0 = A0;
+  P.a_ss = 0;
+  P.a_bs = a_bs;
+  P.a_rs = a_rs;
+  P.c0 = c0;
+  P.l0 = l0;
+  P.u0 = u0;
+  P.n0 = net->n_input;
+  P.out_l = out_l;
+  P.out_u = out_u;
+  P.ld_out = p.N;
+  P.err = reinterpret_cast<int*>(ws + w.err);
+  const double rows = 2.0 * Bc * R;
+  double flops = 0.0, bytes = 4.0 * rows;
+  for (int s = 0; s < P.S; ++s) {
+    flops += 2.0 * rows * P.st[s].K * P.st[s].N;
+    bytes += (double)P.st[s].n_tiles * chain_wimg_bytes(P.st[s].K, P.st[s].N) + (P.st[s].alpha ? 12.0 * Bc * P.st[s].K : 0);
+  }
+  bytes += 8.0 * Bc * net->n_input;
+  prof_step_begin(st);
+  cf_status s = chain_launch(P, st);
+  prof_step_end(st, flops, bytes);
+  return s;
+}
+
 // One chunk of Bc regions.  All pointers already offset to the chunk.
 static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
                            const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
                            const WsLayout& w, cudaStream_t st) {
+  (void)w.wimg;
   const int64_t N = p.N, n0 = net->n_input;
   float* Abuf[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
   float* Cbuf[2] = {reinterpret_cast<float*>(ws + w.C[0]), reinterpret_cast<float*>(ws + w.C[1])};
@@ -222,7 +301,11 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
-    CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
+    if (chain_applicable(net, p, a))
+      CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
+                                st_u + col, ra, rl, rm, st));
+    else
+      CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
     if (p.relu_after[a] >= 0) {
       const cf_layer& Rl = net->layers[p.relu_after[a]];
       int64_t rcol = p.col[p.relu_after[a]];
@@ -231,7 +314,13 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
     }
   }
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
-  {
+  if (chain_applicable(net, p, p.affine.size())) {
+    const int64_t R = net->n_spec, K = p.n_out_last;
+    CF_TRY(launch_chain_layer(net, p, w, ws, Bc, p.affine.size(), R, specW, R * K, K, nullptr, l0, u0,
+                              st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
+    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+  } else {
     const int64_t R = net->n_spec, K = p.n_out_last;
     // treat it as affine index affine.size(): substitutes every affine layer below it
     const float* cur = specW;
@@ -275,7 +364,7 @@ extern "C" int64_t cf_network_neurons(const cf_network* net) {
 extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk) {
   Plan p;
   if (make_plan(net, p) != CF_OK || chunk < 1) return 0;
-  return ws_layout(p, chunk).total;
+  return ws_layout(net, p, chunk).total;
 }
 
 extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
@@ -289,18 +378,28 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
   if (B == 0) return CF_OK;
   CF_REQUIRE(l0 && u0 && specW && lb && ub && workspace, CF_ERR_NULL, "deeppoly_run: NULL argument");
   // largest chunk that fits the workspace
-  size_t base = ws_layout(p, 1).total;
+  size_t base = ws_layout(net, p, 1).total;
   CF_REQUIRE(ws_bytes >= base, CF_ERR_WORKSPACE, "workspace %zu < %zu bytes needed for one region", ws_bytes, base);
   int64_t lo = 1, hi = B;
   while (lo < hi) {
     int64_t mid = (lo + hi + 1) / 2;
-    if (ws_layout(p, mid).total <= ws_bytes) lo = mid;
+    if (ws_layout(net, p, mid).total <= ws_bytes) lo = mid;
     else hi = mid - 1;
   }
   const int64_t Bc = lo;
-  const WsLayout w = ws_layout(p, Bc);
+  const WsLayout w = ws_layout(net, p, Bc);
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = as_stream(stream);
+  if (cudaMemsetAsync(ws + w.err, 0, 256, st) != cudaSuccess) {
+    set_error("deeppoly_run: cudaMemsetAsync failed");
+    return CF_ERR_CUDA;
+  }
+  if (use_chain()) {
+    for (size_t a = 0; a < p.affine.size(); ++a) {
+      const cf_layer& L = net->layers[p.affine[a]];
+      CF_TRY(chain_prep_weights(L.W_dev, L.n_out, L.n_in, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
+    }
+  }
   const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
   for (int64_t b0 = 0; b0 < B; b0 += Bc) {
     int64_t nb = (B - b0 < Bc) ? (B - b0) : Bc;
@@ -308,6 +407,24 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
     float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
     CF_TRY(run_chunk(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su, lb + b0 * ns,
                      ub + b0 * ns, ws, w, st));
+  }
+  return CF_OK;
+}
+
+extern "C" cf_status cf_deeppoly_check(const void* workspace, void* stream) {
+  clear_error();
+  CF_REQUIRE(workspace, CF_ERR_NULL, "deeppoly_check: NULL workspace");
+  int h = 0;
+  cudaStream_t st = as_stream(stream);
+  cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error("deeppoly_check: %s", cudaGetErrorString(e));
+    return CF_ERR_CUDA;
+  }
+  if (h != 0) {
+    set_error("a bounded device wait gave up (site %d)", h);
+    return CF_ERR_TIMEOUT;
   }
   return CF_OK;
 }

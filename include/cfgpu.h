@@ -133,6 +133,10 @@ typedef struct cf_profile_stats {
 cf_status cf_profile_enable(int32_t on);
 cf_status cf_profile_collect(cf_profile_stats* out);
 
+/* Synchronise `stream` and report whether a bounded device-side wait of the last
+ * cf_deeppoly_run that used `workspace_dev` gave up (CF_ERR_TIMEOUT) instead of hanging. */
+cf_status cf_deeppoly_check(const void* workspace_dev, void* stream);
+
 /* ReLU transformer on pre-activation bounds l, u [B, n] (row stride ld_in):
  * l' = relu(l), u' = relu(u) (row stride ld_out), and the relaxation
  * L' = alpha*x, U' = lam*x + mu as compact [B, n] arrays. */
