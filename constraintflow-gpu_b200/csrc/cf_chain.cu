@@ -20,8 +20,9 @@
 //   in N tiles, each drained by the transform warps straight into the concretisation
 //   sum_n (a>=0 ? a*box_s : a*box_{1-s}).  Only one float per row is written to HBM.
 //
-// Warp roles (192 threads): warps 0-3 transform/epilogue (thread t <-> TMEM lane t <->
-// tile row t), warp 4 allocates TMEM and streams W chunks, warp 5 issues the MMAs.
+// Warp roles (320 threads): warps 0-7 transform/epilogue (thread t <-> TMEM lane t%128 <->
+// tile row t%128; threads t and t+128 take the two 16-column halves of every chunk),
+// warp 8 allocates TMEM and streams W chunks, warp 9 issues the MMAs.
 // Every mbarrier wait is bounded (cf_tc.cuh); a timeout is recorded in the device error
 // word and all roles unwind.
 #include "cf_chain.cuh"
@@ -32,7 +33,10 @@ namespace cf {
 using namespace tc;
 
 constexpr uint32_t kAImg = 128 * 128;  // bytes of one 128-row x 32-fp32 A plane
-constexpr int kThreads = 192;
+constexpr int kTransformThreads = 256; // warps 0-7
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
 
 void chain_tile(int N, int& tile_n, int& n_tiles) {
   n_tiles = (N + 255) / 256;
@@ -86,6 +90,25 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
 
+// 16 consecutive floats p[k0 .. k0+16) with zeros at k >= K; four 16-byte loads when
+// `vec` (16-byte aligned rows and K % 4 == 0), scalar loads otherwise.
+__device__ __forceinline__ void load16(const float* __restrict__ p, int k0, int K, bool vec, float (&o)[16]) {
+  if (vec && k0 + 16 <= K) {
+    const float4* q = reinterpret_cast<const float4*>(p + k0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4 v = __ldg(q + j);
+      o[4 * j] = v.x;
+      o[4 * j + 1] = v.y;
+      o[4 * j + 2] = v.z;
+      o[4 * j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o[e] = (k0 + e < K) ? __ldg(p + k0 + e) : 0.0f;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ ChainParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -96,12 +119,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   uint64_t* acc_full = empty + kChainStages;
   uint64_t* mma_done = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [128] partial sums of the second half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = P.err;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kChainStages; ++i) {
-      mbar_init(&full_a[i], 128);
+      mbar_init(&full_a[i], kTransformThreads);
       mbar_init(&full_w[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -109,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -118,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- W producer
     if (lane == 0) {
       uint32_t g = 0;
@@ -144,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         mbar_wait(&full_w[stage], round & 1, err, 12);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       uint32_t g = 0;
@@ -180,8 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     }
   } else {
     // ---------------------------------------------------------------- transform warps
-    const int tid = threadIdx.x;  // 0..127: tile row and TMEM lane
-    const int64_t row = (int64_t)blockIdx.x * 128 + tid;
+    // thread -> tile row (TMEM lane) `r`; the two halves split each 32-column chunk
+    const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
+    const int64_t row = (int64_t)blockIdx.x * 128 + r;
     const bool valid = row < P.rows;
     int64_t sb_ = 0, b = 0, i = 0;
     if (valid) {
@@ -191,9 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       i = rem - b * P.R;
     }
     const bool lower = sb_ == 0;
-    float cacc = (valid && P.c0) ? P.c0[i] : 0.0f;
+    float cacc = (valid && P.c0 && half == 0) ? P.c0[i] : 0.0f;
     float conc = 0.0f;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t g = 0, nacc = 0;
     const float* a0row = P.A0 + sb_ * P.a_ss + b * P.a_bs + i * P.a_rs;
     const float* pos_box = (lower ? P.l0 : P.u0) + b * P.n0;
@@ -202,60 +227,58 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     for (int s = 0; s < P.S && ok; ++s) {
       const ChainStep& S = P.st[s];
       const int K = S.K;
+      const bool cvec = (K & 3) == 0;
       if (s > 0) {
         if (!mbar_wait(acc_full, nacc & 1, err, 31)) { ok = false; break; }
         ++nacc;
         tc_fence_after();
       }
       const uint32_t src_acc = tbase + (uint32_t)((s - 1) & 1) * 256u + lane_off;
-      const float* pf = nullptr;
-      const float* nf = nullptr;
-      const float* muv = nullptr;
-      if (S.alpha && valid) {
-        pf = (lower ? S.alpha : S.lam) + b * K;
-        nf = (lower ? S.lam : S.alpha) + b * K;
-        muv = S.mu + b * K;
-      }
+      const bool relu = S.alpha != nullptr;
+      const float* pf = (lower ? S.alpha : S.lam) + b * K;
+      const float* nf = (lower ? S.lam : S.alpha) + b * K;
+      const float* muv = S.mu + b * K;
       for (int t = 0; t < S.n_tiles && ok; ++t) {
         for (int c = 0; c < S.kchunks; ++c, ++g) {
           const uint32_t stage = g % kChainStages, round = g / kChainStages;
-          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, err, 32)) { ok = false; break; }
-          float v[32];
+          const int k0 = c * 32 + half * 16;
+          // coefficient loads first: they depend on nothing the barriers protect
+          float pv[16], nv[16], mv[16], bv[16];
+          if (relu) {
+            load16(pf, k0, K, cvec, pv);
+            load16(nf, k0, K, cvec, nv);
+            if (t == 0) load16(muv, k0, K, cvec, mv);
+          }
+          if (t == 0) load16(S.bias, k0, K, cvec, bv);
+          float v[16];
           if (s == 0) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              int k = c * 32 + e;
-              v[e] = (valid && k < K) ? a0row[k] : 0.0f;
-            }
-          } else {
-            float h0[16], h1[16];
-            tmem_ld16(src_acc + (uint32_t)(c * 32), h0);
-            tmem_ld16(src_acc + (uint32_t)(c * 32 + 16), h1);
+            load16(a0row, k0, valid ? K : 0, P.a0_vec, v);
+          }
+          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, err, 32)) { ok = false; break; }
+          if (s > 0) {
+            tmem_ld16(src_acc + (uint32_t)k0, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              v[e] = (c * 32 + e < K) ? h0[e] : 0.0f;
-              v[16 + e] = (c * 32 + 16 + e < K) ? h1[e] : 0.0f;
-            }
+            for (int e = 0; e < 16; ++e) v[e] = (valid && k0 + e < K) ? v[e] : 0.0f;
           }
-          uint8_t* sbase = smem + stage * stage_bytes;
-          float hi[32], lo[32];
+          float hi[16], lo[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int k = c * 32 + e;
-            float a = valid ? v[e] : 0.0f;
+          for (int e = 0; e < 16; ++e) {
+            const float a = v[e];
             float tr = a;
-            if (pf && k < K) {
-              tr = a >= 0.0f ? a * pf[k] : a * nf[k];
-              if (t == 0 && (lower ? (a < 0.0f) : (a > 0.0f))) cacc = fmaf(a, muv[k], cacc);
+            if (relu) {
+              tr = a >= 0.0f ? a * pv[e] : a * nv[e];
+              if (t == 0) cacc = fmaf((lower ? (a < 0.0f) : (a > 0.0f)) ? a : 0.0f, mv[e], cacc);
             }
-            if (t == 0 && k < K && valid) cacc = fmaf(tr, S.bias[k], cacc);
+            if (t == 0) cacc = fmaf(tr, bv[e], cacc);
             hi[e] = to_tf32(tr);
             lo[e] = to_tf32(tr - hi[e]);
           }
+          uint8_t* sbase = smem + stage * stage_bytes;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint32_t off = (uint32_t)tid * 128u + ((((uint32_t)q) ^ ((uint32_t)tid & 7u)) << 4);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t qq = (uint32_t)(half * 4 + q);
+            const uint32_t off = (uint32_t)r * 128u + ((qq ^ ((uint32_t)r & 7u)) << 4);
             *reinterpret_cast<float4*>(sbase + off) = make_float4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
             *reinterpret_cast<float4*>(sbase + kAImg + off) =
                 make_float4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
@@ -266,30 +289,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         }
         if (!ok) break;
         if (s == P.S - 1) {
-          // drain output tile t straight into the concretisation
+          // drain output tile t straight into the concretisation; halves take alternate 16-column groups
           if (!mbar_wait(acc_full, nacc & 1, err, 33)) { ok = false; break; }
           ++nacc;
           tc_fence_after();
           const uint32_t dst = tbase + (uint32_t)(s & 1) * 256u + lane_off;
-          for (int q = 0; q < S.tile_n / 16; ++q) {
-            float x[16];
+          for (int q = half; q < S.tile_n / 16; q += 2) {
+            const int n0 = t * S.tile_n + q * 16;
+            float pb[16], nb[16], x[16];
+            load16(pos_box, n0, valid ? S.N : 0, P.box_vec, pb);
+            load16(neg_box, n0, valid ? S.N : 0, P.box_vec, nb);
             tmem_ld16(dst + (uint32_t)(q * 16), x);
             tmem_ld_wait();
-            const int n_base = t * S.tile_n + q * 16;
-            if (valid) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const int n = n_base + e;
-                if (n < S.N) conc += x[e] >= 0.0f ? x[e] * pos_box[n] : x[e] * neg_box[n];
-              }
-            }
+            for (int e = 0; e < 16; ++e) conc += x[e] >= 0.0f ? x[e] * pb[e] : x[e] * nb[e];
           }
           tc_fence_before();
         }
       }
     }
-    if (valid && ok) {
-      const float res = conc + cacc;
+    // combine the two halves of every row
+    if (half == 1) red[r] = conc + cacc;
+    asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
+    if (half == 0 && valid && ok) {
+      const float res = (conc + cacc) + red[r];
       (lower ? P.out_l : P.out_u)[b * P.ld_out + i] = res;
     }
   }
@@ -297,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) tmem_dealloc(tbase, 512);
+  if (warp == kProducerWarp) tmem_dealloc(tbase, 512);
 }
 
 cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
@@ -315,7 +338,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   ChainParams Q = P;
   Q.w_lo_off = 2 * kAImg + (uint32_t)tn_max * 128u;
   Q.stage_bytes = (2 * kAImg + 2u * (uint32_t)tn_max * 128u + 1023u) & ~1023u;
-  size_t smem = 1024 + (size_t)kChainStages * Q.stage_bytes + (3 * kChainStages + 2) * 8 + 16;
+  size_t smem = 1024 + (size_t)kChainStages * Q.stage_bytes + (3 * kChainStages + 2) * 8 + 16 + 128 * 4;
   // at least 116 KB so that one CTA (which holds all 512 TMEM columns) runs per SM
   if (smem < 116 * 1024) smem = 116 * 1024;
   cudaError_t e = cudaFuncSetAttribute(k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);

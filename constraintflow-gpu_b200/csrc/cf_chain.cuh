@@ -31,6 +31,7 @@ struct ChainParams {
   float* out_u;
   int64_t ld_out;
   int* err;                             // device error word (bounded-wait timeouts)
+  int32_t a0_vec, box_vec;              // 16-byte loads allowed for A0 rows / the input box
   uint32_t stage_bytes, w_lo_off;       // filled by chain_launch
 };
 

@@ -234,6 +234,9 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
   P.out_u = out_u;
   P.ld_out = p.N;
   P.err = reinterpret_cast<int*>(ws + w.err);
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  P.a0_vec = (a_bs % 4 == 0) && (a_rs % 4 == 0) && al16(A0);
+  P.box_vec = (net->n_input % 4 == 0) && al16(l0) && al16(u0);
   const double rows = 2.0 * Bc * R;
   double flops = 0.0, bytes = 4.0 * rows;
   for (int s = 0; s < P.S; ++s) {
