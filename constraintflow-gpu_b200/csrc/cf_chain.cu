@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         tc_fence_after();
       }
       const uint32_t src_acc = tbase + (uint32_t)((s - 1) & 1) * 256u + lane_off;
+      const int src_cols = s > 0 ? P.st[s - 1].tile_n : 0;
       const bool relu = S.alpha != nullptr;
       const float* pf = (lower ? S.alpha : S.lam) + b * K;
       const float* nf = (lower ? S.lam : S.alpha) + b * K;
@@ -251,28 +252,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           }
           if (t == 0) load16(S.bias, k0, K, cvec, bv);
           float v[16];
-          if (s == 0) {
-            load16(a0row, k0, valid ? K : 0, P.a0_vec, v);
-          }
+          if (s == 0) load16(a0row, k0, valid ? K : 0, P.a0_vec, v);
           if (!mbar_wait(&empty[stage], (round & 1) ^ 1, err, 32)) { ok = false; break; }
           if (s > 0) {
-            tmem_ld16(src_acc + (uint32_t)k0, v);
-            tmem_ld_wait();
+            // columns [K, tile_n) of the previous accumulator are exact zeros (zero-padded
+            // W); a half-chunk past tile_n was never written and is skipped
+            if (k0 < src_cols) {
+              tmem_ld16(src_acc + (uint32_t)k0, v);
+              tmem_ld_wait();
+            } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = (valid && k0 + e < K) ? v[e] : 0.0f;
+              for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+            }
           }
           float hi[16], lo[16];
+          if (relu && t == 0) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float a = v[e];
-            float tr = a;
-            if (relu) {
-              tr = a >= 0.0f ? a * pv[e] : a * nv[e];
-              if (t == 0) cacc = fmaf((lower ? (a < 0.0f) : (a > 0.0f)) ? a : 0.0f, mv[e], cacc);
+            for (int e = 0; e < 16; ++e) {
+              const float pos = fmaxf(v[e], 0.0f), neg = fminf(v[e], 0.0f);
+              const float tr = fmaf(pos, pv[e], neg * nv[e]);
+              cacc = fmaf(lower ? neg : pos, mv[e], cacc);
+              cacc = fmaf(tr, bv[e], cacc);
+              split_tf32(tr, hi[e], lo[e]);
             }
-            if (t == 0) cacc = fmaf(tr, bv[e], cacc);
-            hi[e] = to_tf32(tr);
-            lo[e] = to_tf32(tr - hi[e]);
+          } else if (relu) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float tr = fmaf(fmaxf(v[e], 0.0f), pv[e], fminf(v[e], 0.0f) * nv[e]);
+              split_tf32(tr, hi[e], lo[e]);
+            }
+          } else if (t == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              cacc = fmaf(v[e], bv[e], cacc);
+              split_tf32(v[e], hi[e], lo[e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) split_tf32(v[e], hi[e], lo[e]);
           }
           uint8_t* sbase = smem + stage * stage_bytes;
 #pragma unroll
@@ -302,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             tmem_ld16(dst + (uint32_t)(q * 16), x);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) conc += x[e] >= 0.0f ? x[e] * pb[e] : x[e] * nb[e];
+            for (int e = 0; e < 16; ++e) conc = fmaf(x[e], x[e] >= 0.0f ? pb[e] : nb[e], conc);
           }
           tc_fence_before();
         }

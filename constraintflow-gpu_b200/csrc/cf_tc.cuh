@@ -141,6 +141,16 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// 3xTF32 operand split: hi = x rounded to the 10-bit tf32 mantissa (round half away
+// from zero on the magnitude bits), lo = the tf32 rounding of the exact remainder x - hi.
+__device__ __forceinline__ float tf32_round_bits(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = tf32_round_bits(x);
+  lo = tf32_round_bits(x - hi);
+}
+
 // Byte offset of element (row, k) (k in [0,32), fp32) inside a K-major SW128 image whose
 // rows are 128 B: 16-byte chunk (k/4) is stored at chunk position (k/4) ^ (row % 8).
 __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t k) {
