@@ -138,19 +138,48 @@ struct WsLayout {
   std::vector<size_t> wimg_off;  // per affine index
 };
 
+// Tensor-core chain (cf_chain.cu) unless CF_STEP_IMPL=simt selects the CUDA-core steps.
+static bool use_chain() {
+  const char* e = getenv("CF_STEP_IMPL");
+  return !(e && strcmp(e, "simt") == 0);
+}
+
+// The chain keeps the coefficient rows in TMEM: every substitution except the last must
+// be at most 256 wide, and every layer below the bounded one must be linear.
+static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below) {
+  if (!use_chain() || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
+  for (size_t j = 0; j < n_below; ++j) {
+    const cf_layer& L = net->layers[p.affine[j]];
+    if (L.kind != CF_LAYER_LINEAR) return false;
+    if (j + 2 <= n_below && L.n_out > 256) return false;
+  }
+  return true;
+}
+
+// True when some layer is bounded with the unchained steps, which materialise the
+// coefficient matrices in the workspace (ping-pong A and constant buffers).
+static bool needs_step_buffers(const cf_network* net, const Plan& p) {
+  for (size_t a = 1; a <= p.affine.size(); ++a)
+    if (!chain_applicable(net, p, a)) return true;
+  return false;
+}
+
 static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   WsLayout w;
   size_t off = 0;
   w.err = off; off += 256;
   w.wimg = off;
   w.wimg_off.assign(p.affine.size(), 0);
-  for (size_t a = 0; a < p.affine.size(); ++a) {
-    const cf_layer& L = net->layers[p.affine[a]];
-    w.wimg_off[a] = off;
-    off += align256(chain_wimg_bytes(L.n_out, L.n_in));
+  if (use_chain()) {
+    for (size_t a = 0; a < p.affine.size(); ++a) {
+      const cf_layer& L = net->layers[p.affine[a]];
+      w.wimg_off[a] = off;
+      off += align256(chain_wimg_bytes(L.n_out, L.n_in));
+    }
   }
-  size_t a_bytes = align256((size_t)2 * Bc * p.r_max * p.n_max * sizeof(float));
-  size_t c_bytes = align256((size_t)2 * Bc * p.r_max * sizeof(float));
+  const bool steps = needs_step_buffers(net, p);
+  size_t a_bytes = steps ? align256((size_t)2 * Bc * p.r_max * p.n_max * sizeof(float)) : 0;
+  size_t c_bytes = steps ? align256((size_t)2 * Bc * p.r_max * sizeof(float)) : 0;
   w.A[0] = off; off += a_bytes;
   w.A[1] = off; off += a_bytes;
   w.C[0] = off; off += c_bytes;
@@ -177,24 +206,6 @@ static cf_status timed_step(int64_t B, int64_t R, int64_t K, int64_t N, const fl
   double bytes = 4.0 * (a_in + rows * N + (double)K * N + (alpha ? 3.0 * B * K : 0.0) + rows);
   prof_step_end(st, 2.0 * rows * K * N, bytes);
   return s;
-}
-
-// Tensor-core chain (cf_chain.cu) unless CF_STEP_IMPL=simt selects the CUDA-core steps.
-static bool use_chain() {
-  const char* e = getenv("CF_STEP_IMPL");
-  return !(e && strcmp(e, "simt") == 0);
-}
-
-// The chain keeps the coefficient rows in TMEM: every substitution except the last must
-// be at most 256 wide, and every layer below the bounded one must be linear.
-static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below) {
-  if (!use_chain() || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
-  for (size_t j = 0; j < n_below; ++j) {
-    const cf_layer& L = net->layers[p.affine[j]];
-    if (L.kind != CF_LAYER_LINEAR) return false;
-    if (j + 2 <= n_below && L.n_out > 256) return false;
-  }
-  return true;
 }
 
 static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const WsLayout& w, char* ws, int64_t Bc,
