@@ -15,6 +15,7 @@ CF_OK, CF_ERR_SHAPE, CF_ERR_UNSUPPORTED, CF_ERR_CUDA, CF_ERR_TIMEOUT, CF_ERR_NUL
 CF_LAYER_LINEAR, CF_LAYER_CONV, CF_LAYER_RELU = 1, 2, 3
 CF_RELAX_DEEPPOLY = 0
 CF_MAX_DIMS = 6
+CF_STATIC_SCRATCH_BYTES = 32 << 20
 CF_F32, CF_BOOL = 0, 1
 OPS = dict(add=0, sub=1, mul=2, truediv=3, ge=4, gt=5, le=6, lt=7, eq=8, ne=9, and_=10, or_=11, max=12, min=13)
 UOPS = dict(neg=0, not_=1, sigmoid=2, relu=3, to_f32=4)
@@ -59,6 +60,7 @@ def _load():
         "cf_deeppoly_workspace_bytes": (_sz, [P(CfNetwork), _i64]),
         "cf_deeppoly_run": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
         "cf_deeppoly_check": (_i32, [_vp, _vp]),
+        "cf_deeppoly_run_static": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
         "cf_relu_relax": (_i32, [_i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp]),
         "cf_backsub_step": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -88,6 +90,7 @@ lib = _load()
 
 # Every symbol the C header declares (checked by the CPU test suite).
 EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_deeppoly_check",
+            "cf_deeppoly_run_static",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",
             "cf_ew_any", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",

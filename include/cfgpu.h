@@ -133,6 +133,22 @@ typedef struct cf_profile_stats {
 cf_status cf_profile_enable(int32_t on);
 cf_status cf_profile_collect(cf_profile_stats* out);
 
+/* No counterpart in the reference.  cf_deeppoly_run for callers that cannot allocate
+ * device memory (a plugin inside another framework's allocator, a service that must not
+ * touch the allocator on its request path): the workspace is a fixed device array of
+ * CF_STATIC_SCRATCH_BYTES inside libcfgpu, held on every GPU that loads the library
+ * until exit.  The caller passes inputs and outputs as for cf_deeppoly_run.  The first
+ * call on a device looks the array up (cudaGetSymbolAddress with that device current):
+ * make it before any stream capture.  All calls share the array, so calls that overlap
+ * on the GPU race and must be serialised by the caller.  A network whose scratch for one
+ * region exceeds the array is rejected with CF_ERR_WORKSPACE; larger batches are run in
+ * region chunks that fit. */
+#define CF_STATIC_SCRATCH_BYTES (32u << 20)
+cf_status cf_deeppoly_run_static(const cf_network* net, int64_t B,
+                                 const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
+                                 float* state_l_dev, float* state_u_dev,
+                                 double* lb_dev, double* ub_dev, void* stream);
+
 /* Synchronise `stream` and report whether a bounded device-side wait of the last
  * cf_deeppoly_run that used `workspace_dev` gave up (CF_ERR_TIMEOUT) instead of hanging. */
 cf_status cf_deeppoly_check(const void* workspace_dev, void* stream);
