@@ -16,6 +16,7 @@
 #include "cf_common.cuh"
 #include "cf_kernels.cuh"
 #include "cf_step.cuh"
+#include "cf_window.cuh"
 
 namespace cf {
 
@@ -74,15 +75,25 @@ cf_status launch_copy_rows(int64_t B, int64_t n, const float* src, int64_t ld_sr
 }
 
 // ------------------------------------------------------------------ network plan
+struct Img {
+  int32_t C, H, W;
+};
+
 struct Plan {
   std::vector<int> affine;      // layer indices of affine layers, in order
+  std::vector<Img> in_img, out_img;  // per affine index: input / output image (linear: (n,1,1) out)
+  bool has_conv = false;
+  int64_t win_floats = 0;       // window path: per region, max rows*window floats of one buffer
   std::vector<int> relu_after;  // per affine index: layer index of the ReLU that follows, or -1
   std::vector<int64_t> col;     // per layer: first state column (input = 0)
   int64_t n_out_last = 0;       // width of the last affine layer (property matrix columns)
   int64_t N = 0;                // total neurons incl. input and property rows
   int64_t spec_col = 0;
   int64_t r_max = 0, k_max = 0, n_max = 0, relu_total = 0;
+  int64_t r_max_all = 0;        // rows of the widest bounded layer, first layer and property included
 };
+
+static void window_sizing(const cf_network* net, Plan& p);
 
 static cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
@@ -91,6 +102,12 @@ static cf_status make_plan(const cf_network* net, Plan& p) {
   p.col.assign(net->n_layers, 0);
   p.relu_after.clear();
   p.affine.clear();
+  p.in_img.clear();
+  p.out_img.clear();
+  p.has_conv = false;
+  // image carried between layers: the input is (n_input,1,1) unless the first layer is a conv
+  Img img{net->n_input, 1, 1};
+  if (net->layers[0].kind == CF_LAYER_CONV) img = Img{net->layers[0].cin, net->layers[0].ih, net->layers[0].iw};
   for (int li = 0; li < net->n_layers; ++li) {
     const cf_layer& L = net->layers[li];
     CF_REQUIRE(L.n_in == prev_width, CF_ERR_SHAPE, "layer %d: n_in %d != previous width %lld", li, L.n_in,
@@ -103,11 +120,29 @@ static cf_status make_plan(const cf_network* net, Plan& p) {
       p.relu_total += L.n_out;
     } else if (L.kind == CF_LAYER_LINEAR) {
       CF_REQUIRE(L.W_dev && L.b_dev, CF_ERR_NULL, "layer %d: weights missing", li);
+      CF_REQUIRE((int64_t)img.C * img.H * img.W == L.n_in, CF_ERR_SHAPE, "layer %d: input image mismatch", li);
       p.affine.push_back(li);
       p.relu_after.push_back(-1);
+      p.in_img.push_back(img);
+      img = Img{L.n_out, 1, 1};
+      p.out_img.push_back(img);
     } else if (L.kind == CF_LAYER_CONV) {
-      set_error("layer %d: convolution layers are not supported by this build of the driver", li);
-      return CF_ERR_UNSUPPORTED;
+      CF_REQUIRE(L.W_dev && L.b_dev, CF_ERR_NULL, "layer %d: weights missing", li);
+      CF_REQUIRE(L.cin == img.C && L.ih == img.H && L.iw == img.W, CF_ERR_SHAPE,
+                 "layer %d: conv input (%d,%d,%d) != previous image (%d,%d,%d)", li, L.cin, L.ih, L.iw, img.C,
+                 img.H, img.W);
+      CF_REQUIRE(L.stride >= 1 && L.kh >= 1 && L.kw >= 1 && L.pad >= 0 && L.cout >= 1, CF_ERR_SHAPE,
+                 "layer %d: bad conv geometry", li);
+      CF_REQUIRE(L.oh == (L.ih + 2 * L.pad - L.kh) / L.stride + 1 && L.ow == (L.iw + 2 * L.pad - L.kw) / L.stride + 1,
+                 CF_ERR_SHAPE, "layer %d: conv output size", li);
+      CF_REQUIRE(L.n_in == L.cin * L.ih * L.iw && L.n_out == L.cout * L.oh * L.ow, CF_ERR_SHAPE,
+                 "layer %d: conv neuron counts", li);
+      p.affine.push_back(li);
+      p.relu_after.push_back(-1);
+      p.in_img.push_back(img);
+      img = Img{L.cout, L.oh, L.ow};
+      p.out_img.push_back(img);
+      p.has_conv = true;
     } else {
       set_error("layer %d: unknown kind %d", li, L.kind);
       return CF_ERR_UNSUPPORTED;
@@ -122,19 +157,89 @@ static cf_status make_plan(const cf_network* net, Plan& p) {
   p.spec_col = pos;
   p.N = pos + net->n_spec;
   p.r_max = net->n_spec;
+  p.r_max_all = net->n_spec;
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
+    if (L.n_out > p.r_max_all) p.r_max_all = L.n_out;
     if (a > 0 && L.n_out > p.r_max) p.r_max = L.n_out;
     if (L.n_in > p.n_max) p.n_max = L.n_in;
     if (L.n_out > p.k_max) p.k_max = L.n_out;
   }
+  window_sizing(net, p);
   return CF_OK;
+}
+
+// Windows of the bounded layer with affine index a (a == affine.size(): the property
+// layer) at levels a-1, a-2, ..., 0 and finally the input image: geoms[0] is the window
+// over layer a's input, geoms.back() the window over the network input.
+static void window_chain(const cf_network* net, const Plan& p, size_t a, std::vector<WinGeom>& geoms) {
+  geoms.clear();
+  const bool spec = a == p.affine.size();
+  const Img lvl = a == 0 ? p.in_img[0] : p.out_img[a - 1];
+  WinGeom g;
+  g.C = lvl.C;
+  g.H = lvl.H;
+  g.W = lvl.W;
+  if (!spec && net->layers[p.affine[a]].kind == CF_LAYER_CONV) {
+    const cf_layer& L = net->layers[p.affine[a]];
+    g.Ph = L.kh;
+    g.Pw = L.kw;
+    g.sig_h = g.sig_w = L.stride;
+    g.pi_h = g.pi_w = L.pad;
+  } else {
+    g.Ph = lvl.H;
+    g.Pw = lvl.W;
+    g.sig_h = g.sig_w = 0;
+    g.pi_h = g.pi_w = 0;
+  }
+  geoms.push_back(g);
+  for (int64_t j = (int64_t)a - 1; j >= 0; --j) {
+    const cf_layer& Lj = net->layers[p.affine[j]];
+    const Img in = p.in_img[j];
+    WinGeom h;
+    h.C = in.C;
+    h.H = in.H;
+    h.W = in.W;
+    if (Lj.kind == CF_LAYER_CONV && g.sig_h > 0) {
+      h.Ph = (g.Ph - 1) * Lj.stride + Lj.kh;
+      h.Pw = (g.Pw - 1) * Lj.stride + Lj.kw;
+      h.sig_h = g.sig_h * Lj.stride;
+      h.sig_w = g.sig_w * Lj.stride;
+      h.pi_h = g.pi_h * Lj.stride + Lj.pad;
+      h.pi_w = g.pi_w * Lj.stride + Lj.pad;
+    } else {  // a single position: the whole image below (exact, outside is zero)
+      h.Ph = in.H;
+      h.Pw = in.W;
+      h.sig_h = h.sig_w = 0;
+      h.pi_h = h.pi_w = 0;
+    }
+    geoms.push_back(h);
+    g = h;
+  }
+}
+
+static int64_t window_rows(const cf_network* net, const Plan& p, size_t a) {
+  return a == p.affine.size() ? net->n_spec : net->layers[p.affine[a]].n_out;
+}
+
+static void window_sizing(const cf_network* net, Plan& p) {
+  p.win_floats = 0;
+  if (!p.has_conv) return;
+  std::vector<WinGeom> gs;
+  for (size_t a = 0; a <= p.affine.size(); ++a) {
+    window_chain(net, p, a, gs);
+    const int64_t R = window_rows(net, p, a);
+    for (const WinGeom& g : gs) {
+      const int64_t f = 2 * R * (int64_t)g.C * g.Ph * g.Pw;
+      if (f > p.win_floats) p.win_floats = f;
+    }
+  }
 }
 
 static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t err, wimg, A[2], C[2], relu, state, total;
+  size_t err, wimg, A[2], C[2], X[2], relu, state, total;
   std::vector<size_t> wimg_off;  // per affine index
 };
 
@@ -147,7 +252,7 @@ static bool use_chain() {
 // The chain keeps the coefficient rows in TMEM: every substitution except the last must
 // be at most 256 wide, and every layer below the bounded one must be linear.
 static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below) {
-  if (!use_chain() || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
+  if (!use_chain() || p.has_conv || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
   for (size_t j = 0; j < n_below; ++j) {
     const cf_layer& L = net->layers[p.affine[j]];
     if (L.kind != CF_LAYER_LINEAR) return false;
@@ -159,6 +264,7 @@ static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_belo
 // True when some layer is bounded with the unchained steps, which materialise the
 // coefficient matrices in the workspace (ping-pong A and constant buffers).
 static bool needs_step_buffers(const cf_network* net, const Plan& p) {
+  if (p.has_conv) return false;
   for (size_t a = 1; a <= p.affine.size(); ++a)
     if (!chain_applicable(net, p, a)) return true;
   return false;
@@ -170,7 +276,7 @@ static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   w.err = off; off += 256;
   w.wimg = off;
   w.wimg_off.assign(p.affine.size(), 0);
-  if (use_chain()) {
+  if (use_chain() && !p.has_conv) {  // weight images for the tensor-core chain
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
       w.wimg_off[a] = off;
@@ -184,6 +290,14 @@ static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   w.A[1] = off; off += a_bytes;
   w.C[0] = off; off += c_bytes;
   w.C[1] = off; off += c_bytes;
+  const size_t x_bytes = p.has_conv ? align256((size_t)Bc * p.win_floats * sizeof(float)) : 0;
+  const size_t cw_bytes = p.has_conv ? align256((size_t)2 * Bc * p.r_max_all * sizeof(float)) : 0;
+  w.X[0] = off; off += x_bytes;
+  w.X[1] = off; off += x_bytes;
+  if (p.has_conv) {
+    w.C[0] = off; off += cw_bytes;
+    w.C[1] = off; off += cw_bytes;
+  }
   w.relu = off; off += align256((size_t)3 * Bc * p.relu_total * sizeof(float));
   w.state = off; off += align256((size_t)2 * Bc * p.N * sizeof(float));
   off += step_scratch_bytes(Bc, p.r_max);
@@ -312,10 +426,62 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
     return launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + col, st_u + col, N, st);
   };
 
+  // receptive-field windows (conv networks): bound layer a (a == affine.size(): property)
+  float* Xbuf[2] = {reinterpret_cast<float*>(ws + w.X[0]), reinterpret_cast<float*>(ws + w.X[1])};
+  auto bound_window = [&](size_t a, int64_t col) -> cf_status {
+    const bool spec = a == p.affine.size();
+    std::vector<WinGeom> gs;
+    window_chain(net, p, a, gs);
+    RowGeom rg;
+    rg.B = Bc;
+    rg.R = window_rows(net, p, a);
+    const Img oimg = spec ? Img{net->n_spec, 1, 1} : p.out_img[a];
+    rg.Hm = oimg.H;
+    rg.Wm = oimg.W;
+    const bool conv_m = !spec && net->layers[p.affine[a]].kind == CF_LAYER_CONV;
+    const float* Wm = spec ? specW : net->layers[p.affine[a]].W_dev;
+    const int64_t w_bs = spec ? rg.R * p.n_out_last : 0;
+    float* X = Xbuf[0];
+    float* Y = Xbuf[1];
+    float* c = Cbuf[0];
+    float* c2 = Cbuf[1];
+    CF_TRY(win_init(rg, gs[0], Wm, w_bs, conv_m, X, st));
+    CF_TRY(win_row_bias(rg, spec ? nullptr : net->layers[p.affine[a]].b_dev, conv_m, c, st));
+    for (int64_t j = (int64_t)a - 1, k = 0; j >= 0; --j, ++k) {
+      const cf_layer& Lj = net->layers[p.affine[j]];
+      const WinGeom& g = gs[k];
+      const WinGeom& h = gs[k + 1];
+      prof_step_begin(st);
+      CF_TRY(win_relu_bias(rg, g, X, c, Bc * rg.R, rg.R, ra[j], rl[j], rm[j], Lj.b_dev, c2, st));
+      if (Lj.kind == CF_LAYER_CONV) {
+        ConvGeom cv{Lj.cin, Lj.kh, Lj.kw, Lj.stride, Lj.pad};
+        CF_TRY(win_convT(rg, g, h, cv, X, Lj.W_dev, Y, st));
+      } else {
+        const int64_t K = Lj.n_out, Nn = Lj.n_in;
+        CF_TRY(launch_step_gemm_simt(Bc, rg.R, K, Nn, X, Bc * rg.R * K, rg.R * K, K, nullptr, nullptr, Lj.W_dev, Y,
+                                     st));
+      }
+      const double rows = 2.0 * Bc * rg.R;
+      const double macs = Lj.kind == CF_LAYER_CONV ? (double)h.C * h.Ph * h.Pw * g.C * Lj.kh * Lj.kw /
+                                                         ((double)Lj.stride * Lj.stride)
+                                                   : (double)Lj.n_out * Lj.n_in;
+      prof_step_end(st, 2.0 * rows * macs, 4.0 * rows * ((double)g.C * g.Ph * g.Pw * 2 + (double)h.C * h.Ph * h.Pw));
+      float* tX = X;
+      X = Y;
+      Y = tX;
+      float* tc = c;
+      c = c2;
+      c2 = tc;
+    }
+    return win_concretize(rg, gs.back(), X, c, l0, u0, st_l + col, st_u + col, N, st);
+  };
+
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
-    if (chain_applicable(net, p, a))
+    if (p.has_conv)
+      CF_TRY(bound_window(a, col));
+    else if (chain_applicable(net, p, a))
       CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
                                 st_u + col, ra, rl, rm, st));
     else
@@ -328,7 +494,12 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
     }
   }
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
-  if (chain_applicable(net, p, p.affine.size())) {
+  if (p.has_conv) {
+    const int64_t R = net->n_spec;
+    CF_TRY(bound_window(p.affine.size(), p.spec_col));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
+    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+  } else if (chain_applicable(net, p, p.affine.size())) {
     const int64_t R = net->n_spec, K = p.n_out_last;
     CF_TRY(launch_chain_layer(net, p, w, ws, Bc, p.affine.size(), R, specW, R * K, K, nullptr, l0, u0,
                               st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st));
@@ -408,7 +579,7 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
     set_error("deeppoly_run: cudaMemsetAsync failed");
     return CF_ERR_CUDA;
   }
-  if (use_chain()) {
+  if (use_chain() && !p.has_conv) {
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
       CF_TRY(chain_prep_weights(L.W_dev, L.n_out, L.n_in, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));

@@ -1,0 +1,36 @@
+// Receptive-field window backsubstitution (cf_window.cu): geometry and launchers.
+#pragma once
+#include "cf_common.cuh"
+
+namespace cf {
+
+// Rows 2*B*R of a bounded layer whose output image is (., Hm, Wm): row (s, b, i) with
+// i = co*Hm*Wm + oy*Wm + ox.
+struct RowGeom {
+  int64_t B, R;
+  int32_t Hm, Wm;
+};
+
+// A window at one level: image (C, H, W) of that level, window Ph x Pw over all C
+// channels, origin (oy*sig_h - pi_h, ox*sig_w - pi_w).  Element order (c, u, v).
+struct WinGeom {
+  int32_t C, H, W, Ph, Pw, sig_h, sig_w, pi_h, pi_w;
+};
+
+// The convolution substituted by k_win_convT: weights [Cout, cin, kh, kw], stride s, pad.
+struct ConvGeom {
+  int32_t cin, kh, kw, s, pad;
+};
+
+cf_status win_init(const RowGeom& rg, const WinGeom& g, const float* W, int64_t w_bs, bool conv, float* out,
+                   cudaStream_t st);
+cf_status win_row_bias(const RowGeom& rg, const float* bias, bool conv, float* c_out, cudaStream_t st);
+cf_status win_relu_bias(const RowGeom& rg, const WinGeom& g, float* A, const float* c_in, int64_t c_ss, int64_t c_bs,
+                        const float* alpha, const float* lam, const float* mu, const float* bias, float* c_out,
+                        cudaStream_t st);
+cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
+                    const float* W, float* out, cudaStream_t st);
+cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, const float* c, const float* l0,
+                         const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
+
+}  // namespace cf
