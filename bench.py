@@ -32,6 +32,9 @@ import torch  # noqa: E402
 from cfgpu import nets  # noqa: E402
 
 L2_BYTES = 126 * 2 ** 20
+# DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu capture of
+# the default command (profiles/k_chain_mlp784-200x9_b256.txt); per workload id.
+NCU_TRAFFIC = {2: 10.85e6}
 
 
 def parse():
@@ -162,8 +165,10 @@ def run_cfgpu(args, rank, world, local):
     torch.cuda.set_device(dev)
     wl = nets.workload(args.workload)
     B = args.batch or wl.B
+    from cfgpu import dist as cdist
     Xall = nets.centres(wl, B * world)
-    X = Xall[rank * B:(rank + 1) * B].contiguous()
+    lo, hi = cdist.shard_range(B * world, rank, world)
+    X = Xall[lo:hi].contiguous()
     y = nets.labels(wl, X)
     eng = DeepPolyEngine(wl.layers, wl.input_size, dev)
     Xd, yd = X.to(dev), y.to(dev)
@@ -207,9 +212,12 @@ def run_cfgpu(args, rank, world, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     value = B * world * args.steps / (ms_max / 1000.0)
-    certified = torch.tensor([int((lb >= 0).all(dim=1).sum().item())], device=dev)
+    # the one collective of the path, after the timed region: gather every region's bounds
     if world > 1:
-        dist.all_reduce(certified)
+        lb_all, _ = cdist.gather_bounds(lb, ub, B * world, rank, world)
+    else:
+        lb_all = lb
+    certified = (lb_all >= 0).all(dim=1).sum()
     # ---- end-to-end through the public API with host buffers
     Xh = X.pin_memory()
     yh = y.pin_memory()
@@ -257,7 +265,10 @@ def run_cfgpu(args, rank, world, local):
                 "d2h_bytes_per_step": int(2 * B * 9 * 8)},
         "gpu_launches": int(prof["kernel_launches"]),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_3xtf32, "unit": "TFLOP/s",
-                     "frac": (achieved / peak_3xtf32) if achieved else None, "traffic": None,
+                     "frac": (achieved / peak_3xtf32) if achieved else None,
+                     "traffic": NCU_TRAFFIC.get(args.workload),
+                     "traffic_source": "dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
+                                       "CTAs) from one ncu --set full capture of this command",
                      "kernel": "backsubstitution step", "peak_source": f"3xTF32 = bf16/2/3 of {src} MEASURED_PEAKS",
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
                      "step_launches": prof["step_launches"]},
