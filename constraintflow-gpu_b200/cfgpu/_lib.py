@@ -71,6 +71,7 @@ def _load():
         "cf_ew_where": (_i32, [_i32, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _i32, _vp]),
         "cf_ew_clamp": (_i32, [_i32, _p64, _vp, _p64, _f32, _i32, _vp, _vp]),
         "cf_ew_any": (_i32, [_i32, _p64, _vp, _i32, _p64, _vp, _vp]),
+        "cf_bmm": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _vp]),
         "cf_input_box": (_i32, [_i64, _i32, _i64, _vp, _f32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp, _vp,
                                 _vp]),
         "cf_spec_matrix": (_i32, [_i64, _i32, _vp, _vp, _vp]),
@@ -93,7 +94,7 @@ EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_ru
             "cf_deeppoly_run_static",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",
-            "cf_ew_any", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",
+            "cf_ew_any", "cf_bmm", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",
             "cf_last_error", "cf_version")
 
 

@@ -110,6 +110,62 @@ __global__ void k_ew_any(Geo g, const void* x, int32_t xdt, uint32_t* flag) {
   if (__any_sync(0xffffffffu, found) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u);
 }
 
+// C[b] (+)= A[b] @ B[b] with arbitrary element strides (broadcast views included).
+// 64x64 output tile per CTA, K staged 16 at a time, 4x4 register tile per thread.
+constexpr int BM_M = 64, BM_N = 64, BM_K = 16;
+
+__global__ void __launch_bounds__(256) k_bmm(int64_t nb, int64_t M, int64_t N, int64_t K, const float* __restrict__ A,
+                                             int64_t a_bs, int64_t a_ms, int64_t a_ks, const float* __restrict__ B,
+                                             int64_t b_bs, int64_t b_ks, int64_t b_ns, float* __restrict__ C,
+                                             int accumulate) {
+  __shared__ float As[BM_K][BM_M + 4];
+  __shared__ float Bs[BM_K][BM_N + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  for (int64_t bt = blockIdx.z; bt < nb; bt += gridDim.z) {
+    const float* Ab = A + bt * a_bs;
+    const float* Bb = B + bt * b_bs;
+    const int64_t m0 = (int64_t)blockIdx.y * BM_M, n0 = (int64_t)blockIdx.x * BM_N;
+    float acc[4][4] = {};
+    for (int64_t k0 = 0; k0 < K; k0 += BM_K) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int e = tid + 256 * q;
+        const int kk = e & 15, mm = e >> 4;
+        const int64_t mg = m0 + mm, kg = k0 + kk;
+        As[kk][mm] = (mg < M && kg < K) ? Ab[mg * a_ms + kg * a_ks] : 0.0f;
+        const int kk2 = e >> 6, nn = e & 63;
+        const int64_t kg2 = k0 + kk2, ng = n0 + nn;
+        Bs[kk2][nn] = (kg2 < K && ng < N) ? Bb[kg2 * b_ks + ng * b_ns] : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < BM_K; ++kk) {
+        float a4[4], b4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) a4[q] = As[kk][ty * 4 + q];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) b4[q] = Bs[kk][tx * 4 + q];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a4[i], b4[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+    float* Cb = C + bt * M * N;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + ty * 4 + i;
+      if (m >= M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = n0 + tx * 4 + j;
+        if (n < N) Cb[m * N + n] = accumulate ? Cb[m * N + n] + acc[i][j] : acc[i][j];
+      }
+    }
+  }
+}
+
 static cf_status make_geo(Geo& g, int32_t ndim, const int64_t* shape, const int64_t* sx, const int64_t* sy,
                           const int64_t* sz) {
   CF_REQUIRE(ndim >= 0 && ndim <= CF_MAX_DIMS, CF_ERR_SHAPE, "ew: ndim %d out of range", ndim);
@@ -200,4 +256,20 @@ extern "C" cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x
   CF_REQUIRE(x && flag, CF_ERR_NULL, "ew_any: NULL argument");
   k_ew_any<<<grid_for(g.total), 256, 0, as_stream(stream)>>>(g, x, xdt, flag);
   return check_launch("k_ew_any");
+}
+
+extern "C" cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K, const float* A, int64_t a_bs, int64_t a_ms,
+                            int64_t a_ks, const float* B, int64_t b_bs, int64_t b_ks, int64_t b_ns, float* C,
+                            int32_t accumulate, void* stream) {
+  clear_error();
+  CF_INJECT("bmm");
+  CF_REQUIRE(nb >= 0 && M >= 0 && N >= 0 && K >= 0, CF_ERR_SHAPE, "bmm: negative size");
+  if (nb * M * N == 0) return CF_OK;
+  CF_REQUIRE(C && (K == 0 || (A && B)), CF_ERR_NULL, "bmm: NULL argument");
+  const int64_t gx = ceil_div(N, BM_N), gy = ceil_div(M, BM_M);
+  CF_REQUIRE(gx <= 0x7fffffff && gy <= 65535, CF_ERR_SHAPE, "bmm: %lld x %lld too large", (long long)M,
+             (long long)N);
+  dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(nb < 65535 ? nb : 65535));
+  k_bmm<<<grid, 256, 0, as_stream(stream)>>>(nb, M, N, K, A, a_bs, a_ms, a_ks, B, b_bs, b_ks, b_ns, C, accumulate);
+  return check_launch("k_bmm");
 }

@@ -219,6 +219,14 @@ cf_status cf_ew_where(int32_t ndim, const int64_t* shape,
 /* min_true != 0: out = max(x, c) (clamp(min=c)); else out = min(x, c) (clamp(max=c)). */
 cf_status cf_ew_clamp(int32_t ndim, const int64_t* shape, const float* x_dev, const int64_t* x_strides,
                       float c, int32_t min_true, float* out_dev, void* stream);
+/* C[b] (+)= A[b] @ B[b], b < nb: A [M, K] with element strides (a_bs, a_ms, a_ks), B [K, N]
+ * with (b_bs, b_ks, b_ns) (zero strides broadcast), C contiguous [nb, M, N]; float32.
+ * The block-pair product of SparseTensor.matmul (constraintflow/gbcsr/sparse_tensor.py:1671-2060,
+ * DenseBlock.matmul_equal_dims sparse_block.py:748, matmul_unequal_dims :964). */
+cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K,
+                 const float* A_dev, int64_t a_bs, int64_t a_ms, int64_t a_ks,
+                 const float* B_dev, int64_t b_bs, int64_t b_ks, int64_t b_ns,
+                 float* C_dev, int32_t accumulate, void* stream);
 /* *flag_dev |= 1 if any element of x is nonzero (flag is a device uint32). */
 cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x_dev, int32_t x_dtype,
                     const int64_t* x_strides, uint32_t* flag_dev, void* stream);
