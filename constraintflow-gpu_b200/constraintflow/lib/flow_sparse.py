@@ -1,0 +1,115 @@
+"""Flow: the layer loop of a certifier over a network (reference:
+constraintflow/lib/flow_sparse.py:15-228).
+
+The reference calls the generated transformer's Affine / Relu on every layer and does
+the arithmetic op by op.  Here the whole loop of a recognised certifier runs in one call
+of the B200 network driver (cf_deeppoly_run through cfgpu.engine), which computes the
+same abstract state: every neuron's l/u is written back into abs_elem.d['l'|'u'] and the
+property layer's bounds are returned as float64 (lb, ub), as Flow.flow returns them.
+
+Recognition: the compiler emits a class with Affine and Relu methods; the DeepPoly
+program (examples/compiler_examples/deeppoly.cf) is identified from the operations its
+generated Relu and Affine perform (the triangle relaxation: convert_to_poly, the
+u/(u-l) slope, the l>=0 / u<=0 cases; the backward traversal: clamp sign split,
+inner_prod, get_max_priority).  A transformer object may also declare itself with a
+``cf_certifier = "deeppoly"`` attribute.  Other programs raise NotImplementedError.
+"""
+import inspect
+
+import torch
+
+from constraintflow.gbcsr.sparse_block import DenseBlock
+from constraintflow.gbcsr.sparse_tensor import SparseTensor
+
+from .network import LayerType
+
+_DEEPPOLY_RELU = ("convert_to_poly(", "operator.truediv", "operator.le", "operator.ge", "where(")
+_DEEPPOLY_AFFINE = ("clamp(", "inner_prod(", "get_max_priority(", "filter_trav_exp_not_stop(")
+_CROWN_RELU = ("operator.gt",)
+
+
+def certifier_of(transformer):
+    """'deeppoly' for the DeepPoly program's generated transformer, else raises."""
+    declared = getattr(transformer, "cf_certifier", None)
+    if declared is not None:
+        return declared
+    cls = type(transformer)
+    try:
+        relu = inspect.getsource(cls.Relu)
+        affine = inspect.getsource(cls.Affine)
+    except (AttributeError, OSError, TypeError) as e:
+        raise NotImplementedError(f"cannot read the generated transformer: {e}")
+    if all(k in relu for k in _DEEPPOLY_RELU) and all(k in affine for k in _DEEPPOLY_AFFINE) \
+            and not any(k in relu for k in _CROWN_RELU):
+        return "deeppoly"
+    raise NotImplementedError("this runtime runs the DeepPoly certifier program; the given transformer "
+                              f"({cls.__name__}) is a different program")
+
+
+class _EngineLayer:
+    def __init__(self, kind, W=None, b=None, in_shape=None, out_shape=None, stride=1, pad=0):
+        self.kind, self.W, self.b = kind, W, b
+        self.in_shape, self.out_shape, self.stride, self.pad = in_shape, out_shape, stride, pad
+
+
+def engine_layers(model):
+    """The network as the driver's chain of linear / conv / relu layers (property layer excluded)."""
+    out = []
+    for i, layer in enumerate(model):
+        if layer.type == LayerType.Input or i == len(model) - 1:
+            continue
+        if layer.type == LayerType.Linear:
+            out.append(_EngineLayer("linear", layer.weight.float(), layer.bias.float()))
+        elif layer.type == LayerType.Conv2D:
+            parent = model[layer.parents[0]]
+            bias = getattr(layer, "bias_channel", None)
+            if bias is None:
+                bias = layer.bias.reshape(layer.weight.shape[0], -1)[:, 0]
+            out.append(_EngineLayer("conv", layer.weight.float(), bias.float(), in_shape=tuple(parent.shape[1:]),
+                                    out_shape=tuple(layer.shape[1:]), stride=layer.stride[0], pad=layer.padding[0]))
+        elif layer.type == LayerType.ReLU:
+            out.append(_EngineLayer("relu"))
+        else:
+            raise NotImplementedError(f"layer type {layer.type} (the driver runs chains of Linear/Conv2D/ReLU)")
+        if len(layer.parents) != 1:
+            raise NotImplementedError("non-chain networks (Add / Concat)")
+    return out
+
+
+class Flow:
+    def __init__(self, abs_elem, transformer, model, print_intermediate_results=False, no_sparsity=False):
+        self.abs_elem = abs_elem
+        self.transformer = transformer
+        self.model = model
+        self.input_size = model.input_size
+        self.batch_size = abs_elem.batch_size
+        self.print_intermediate_results = print_intermediate_results
+        self.no_sparsity = no_sparsity
+
+    def flow(self):
+        from cfgpu.engine import DeepPolyEngine
+        certifier_of(self.transformer)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        n0 = self.input_size
+        B = self.batch_size
+        l_in = self.abs_elem.d["l"]
+        u_in = self.abs_elem.d["u"]
+        l0 = l_in.get_dense_device()[:, :n0].contiguous()
+        u0 = u_in.get_dense_device()[:, :n0].contiguous()
+        spec = self.model[-1]
+        W = torch.as_tensor(spec.weight, dtype=torch.float32).to(dev).contiguous()
+        eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]))
+        lb, ub, sl, su = eng.run(l0, u0, W, want_state=True)
+        total = torch.tensor([B, self.model.size])
+        self.abs_elem.d["l"] = SparseTensor([torch.tensor([0, 0])], [DenseBlock(sl)], 2, total,
+                                            dense_const=float("-inf"))
+        self.abs_elem.d["u"] = SparseTensor([torch.tensor([0, 0])], [DenseBlock(su)], 2, total,
+                                            dense_const=float("inf"))
+        self.abs_elem.d["llist"][:] = True
+        lb, ub = lb.cpu(), ub.cpu()
+        if self.print_intermediate_results:
+            for i, layer in enumerate(self.model):
+                print(i, layer.type, layer.shape)
+                print(f"l: {sl[:, layer.start:layer.end].cpu()}")
+                print(f"u: {su[:, layer.start:layer.end].cpu()}")
+        return lb, ub

@@ -127,6 +127,12 @@ def worker(program, outdir, case_names):
     src = os.path.join(REF_ROOT, "examples", "compiler_examples", f"{program}.cf")
     os.makedirs(outdir, exist_ok=True)
     cfcompile.compile(src, outdir)
+    # keep the generated program: the drop-in runtime must run it unchanged
+    keep = os.path.join(HERE, "generated", program)
+    os.makedirs(keep, exist_ok=True)
+    for f in ("main.py", "transformers.py"):
+        with open(os.path.join(outdir, f)) as fi, open(os.path.join(keep, f), "w") as fo:
+            fo.write(fi.read())
     sys.path.insert(0, outdir)
     import constraintflow.lib.flow_sparse as fs
     captured = {}
@@ -168,6 +174,13 @@ def worker(program, outdir, case_names):
 
 def main():
     sel = sys.argv[1:]
+    if sel == ["--programs-only"]:
+        for prog in ("deeppoly", "crown"):
+            with tempfile.TemporaryDirectory() as tmp:
+                code = ("import sys; sys.path.insert(0, %r); import gen_golden as g; g.worker(%r, %r, [])"
+                        % (HERE, prog, os.path.join(tmp, "out")))
+                subprocess.run([sys.executable, "-c", code], cwd=tmp, check=True)
+        return
     names = [n for n in CASES if not sel or any(n.startswith(s) for s in sel)]
     by_prog = {}
     for n in names:
