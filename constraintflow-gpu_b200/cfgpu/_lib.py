@@ -8,7 +8,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcfgpu.so")
+# CF_LIB_PATH selects another build of the library (e.g. a -lineinfo debug build).
+LIB_PATH = os.environ.get("CF_LIB_PATH") or os.path.join(_HERE, "libcfgpu.so")
 
 CF_OK, CF_ERR_SHAPE, CF_ERR_UNSUPPORTED, CF_ERR_CUDA, CF_ERR_TIMEOUT, CF_ERR_NULL, CF_ERR_WORKSPACE, \
     CF_ERR_INJECTED = range(8)

@@ -25,6 +25,8 @@
 // warp 8 allocates TMEM and streams W chunks, warp 9 issues the MMAs.
 // Every mbarrier wait is bounded (cf_tc.cuh); a timeout is recorded in the device error
 // word and all roles unwind.
+#include <type_traits>
+
 #include "cf_chain.cuh"
 #include "cf_tc.cuh"
 
@@ -34,6 +36,7 @@ using namespace tc;
 
 constexpr uint32_t kAImg = 128 * 128;  // bytes of one 128-row x 32-fp32 A plane
 constexpr int kTransformThreads = 256; // warps 0-7
+constexpr int kTransformWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 320;
@@ -91,8 +94,8 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // 16 consecutive floats p[k0 .. k0+16) with zeros at k >= K; four 16-byte loads when
-// `vec` (16-byte aligned rows and K % 4 == 0), scalar loads otherwise.
-__device__ __forceinline__ void load16(const float* __restrict__ p, int k0, int K, bool vec, float (&o)[16]) {
+// `vec` (16-byte aligned rows and K % 4 == 0), scalar loads otherwise (read-only global memory).
+__device__ __forceinline__ void load16g(const float* __restrict__ p, int k0, int K, bool vec, float (&o)[16]) {
   if (vec && k0 + 16 <= K) {
     const float4* q = reinterpret_cast<const float4*>(p + k0);
 #pragma unroll
@@ -109,26 +112,277 @@ __device__ __forceinline__ void load16(const float* __restrict__ p, int k0, int 
   }
 }
 
+// Bounded wait by every lane of a warp with a warp-uniform result, so that warp-collective
+// code after it (__syncwarp, tcgen05.ld) is reached by all lanes or by none.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
+  const bool ok = mbar_wait(bar, parity, err, site);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// 16 consecutive floats at shared-memory byte address `saddr` (16-byte aligned): four
+// ld.shared.v4.  Ordered after the mbarrier waits that publish them (asm volatile).
+__device__ __forceinline__ void lds16(uint32_t saddr, float (&o)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(o[4 * j]), "=f"(o[4 * j + 1]), "=f"(o[4 * j + 2]), "=f"(o[4 * j + 3])
+                 : "r"(saddr + 16u * j));
+}
+// Elements k0 .. k0+15 of a staged row with zeros at k >= K (bytes past K are not written).
+__device__ __forceinline__ void lds16_row(uint32_t row_saddr, int k0, int K, float (&o)[16]) {
+  if (k0 + 16 <= K) {
+    lds16(row_saddr + 4u * (uint32_t)k0, o);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float x = 0.0f;
+      if (k0 + e < K) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(row_saddr + 4u * (uint32_t)(k0 + e)));
+      o[e] = x;
+    }
+  }
+}
+
+// Shared-memory pieces the transform warps use.
+struct ChainSmem {
+  uint32_t a_region;     // A stages (shared-memory byte address)
+  uint32_t coef;         // two step buffers of relaxation vectors
+  uint32_t box;          // input-box rows
+  uint64_t* full_a;
+  uint64_t* empty_a;
+  uint64_t* coef_full;
+  uint64_t* coef_empty;
+  uint64_t* box_full;
+  uint64_t* acc_full;
+  float* red;
+};
+
+// Transform / epilogue warps (threads 0-255).  Thread -> tile row (TMEM lane) r; the two
+// halves take the two 16-column halves of every 32-column chunk.  kStaged: relaxation
+// vectors come from the shared-memory step buffers; kBox: the input box from shared memory.
+template <bool kStaged, bool kBox>
+__device__ __forceinline__ void chain_transform(const ChainParams& P, const ChainSmem& M, uint32_t tbase,
+                                                int64_t p0) {
+  const int warp = threadIdx.x >> 5;
+  int* err = P.err;
+  const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
+  const int64_t row = (int64_t)blockIdx.x * 128 + r;
+  const bool valid = row < P.rows;
+  int64_t sb_ = 0, b = 0, i = 0;
+  if (valid) {
+    sb_ = row / (P.B * P.R);
+    int64_t rem = row - sb_ * P.B * P.R;
+    b = rem / P.R;
+    i = rem - b * P.R;
+  }
+  const bool lower = sb_ == 0;
+  float cacc = (valid && P.c0 && half == 0) ? P.c0[i] : 0.0f;
+  float conc = 0.0f;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  // this thread's four 16-byte slots of a swizzled 128-byte A row (the same every chunk)
+  uint32_t soff[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) soff[q] = (uint32_t)r * 128u + ((((uint32_t)(half * 4 + q)) ^ ((uint32_t)r & 7u)) << 4);
+  const float* a0row = P.A0 + sb_ * P.a_ss + b * P.a_bs + i * P.a_rs;
+  const int slot = valid ? (int)(row / P.R - p0) : 0;
+  // input box: staged rows (l0 then u0 per slot) or global memory
+  const uint32_t box_pos = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? 0 : P.n0));
+  const uint32_t box_neg = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? P.n0 : 0));
+  const float* gpos = (lower ? P.l0 : P.u0) + b * P.n0;
+  const float* gneg = (lower ? P.u0 : P.l0) + b * P.n0;
+  uint32_t g = 0, nacc = 0;
+  bool ok = true;
+  for (int s = 0; s < P.S && ok; ++s) {
+    const ChainStep& S = P.st[s];
+    const int K = S.K;
+    const bool cvec = (K & 3) == 0;
+    if (s > 0) {
+      if (!warp_wait(M.acc_full, nacc & 1, err, 31)) { ok = false; break; }
+      ++nacc;
+      tc_fence_after();
+    }
+    // relaxation rows of this step: staged (shared-memory byte addresses) or global pointers
+    uint32_t s_pf = 0, s_nf = 0, s_mu = 0, s_bias = 0;
+    const float *g_pf = nullptr, *g_nf = nullptr, *g_mu = nullptr, *g_bias = S.bias;
+    if (kStaged) {
+      if (!warp_wait(&M.coef_full[s & 1], (s >> 1) & 1, err, 34)) { ok = false; break; }
+      const uint32_t cbuf = M.coef + 4u * (uint32_t)((s & 1) * kCoefBufFloats);
+      const uint32_t al = cbuf + 4u * (uint32_t)(slot * 3 * kCoefRow), la = al + 4u * kCoefRow;
+      s_pf = lower ? al : la;
+      s_nf = lower ? la : al;
+      s_mu = al + 8u * kCoefRow;
+      s_bias = cbuf + 4u * (uint32_t)(kCoefSlots * 3 * kCoefRow);
+    } else if (S.alpha != nullptr) {
+      g_pf = (lower ? S.alpha : S.lam) + b * K;
+      g_nf = (lower ? S.lam : S.alpha) + b * K;
+      g_mu = S.mu + b * K;
+    }
+    const uint32_t src_acc = tbase + (uint32_t)((s - 1) & 1) * 256u + lane_off;
+    const int src_cols = s > 0 ? P.st[s - 1].tile_n : 0;
+
+    // one tile of chunks, specialised on the ReLU and on the first N tile (which also
+    // accumulates the constant: mu and bias terms)
+    auto tile_chunks = [&](auto relu_c, auto first_c) -> bool {
+      constexpr bool kRelu = decltype(relu_c)::value, kFirst = decltype(first_c)::value;
+      for (int c = 0; c < S.kchunks; ++c, ++g) {
+        const uint32_t stage = g % kAStages, round = g / kAStages;
+        const int k0 = c * 32 + half * 16;
+        float pv[16], nv[16], mv[16], bv[16], v[16];
+        if (kStaged) {
+          if (kRelu) {
+            lds16_row(s_pf, k0, K, pv);
+            lds16_row(s_nf, k0, K, nv);
+            if (kFirst) lds16_row(s_mu, k0, K, mv);
+          }
+          if (kFirst) lds16_row(s_bias, k0, K, bv);
+        } else {
+          if (kRelu) {
+            load16g(g_pf, k0, K, cvec, pv);
+            load16g(g_nf, k0, K, cvec, nv);
+            if (kFirst) load16g(g_mu, k0, K, cvec, mv);
+          }
+          if (kFirst) load16g(g_bias, k0, K, cvec, bv);
+        }
+        if (s == 0) {
+          load16g(a0row, k0, valid ? K : 0, P.a0_vec, v);
+        } else if (k0 < src_cols) {
+          // columns [K, tile_n) of the previous accumulator are exact zeros (zero-padded W);
+          // a half-chunk past tile_n was never written and is skipped
+          tmem_ld16(src_acc + (uint32_t)k0, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+        }
+        float hi[16], lo[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float tr = v[e];
+          if (kRelu) {
+            const float pos = fmaxf(v[e], 0.0f), neg = fminf(v[e], 0.0f);
+            tr = fmaf(pos, pv[e], neg * nv[e]);
+            if (kFirst) cacc = fmaf(lower ? neg : pos, mv[e], cacc);
+          }
+          if (kFirst) cacc = fmaf(tr, bv[e], cacc);
+          split_tf32(tr, hi[e], lo[e]);
+        }
+        // only the stage write waits for the MMAs that read this stage kAStages chunks ago
+        if (!warp_wait(&M.empty_a[stage], (round & 1) ^ 1, err, 32)) return false;
+        const uint32_t sbase = M.a_region + stage * 2 * kAImg;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + soff[q]), "f"(hi[4 * q]),
+                       "f"(hi[4 * q + 1]), "f"(hi[4 * q + 2]), "f"(hi[4 * q + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + kAImg + soff[q]), "f"(lo[4 * q]),
+                       "f"(lo[4 * q + 1]), "f"(lo[4 * q + 2]), "f"(lo[4 * q + 3])
+                       : "memory");
+        }
+        // this thread's stores are made visible to the tensor core (async proxy)
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&M.full_a[stage]);
+      }
+      return true;
+    };
+
+    const bool relu = S.alpha != nullptr;
+    for (int t = 0; t < S.n_tiles && ok; ++t) {
+      using T = std::true_type;
+      using F = std::false_type;
+      if (relu)
+        ok = t == 0 ? tile_chunks(T{}, T{}) : tile_chunks(T{}, F{});
+      else
+        ok = t == 0 ? tile_chunks(F{}, T{}) : tile_chunks(F{}, F{});
+      if (!ok) break;
+      if (s == P.S - 1) {
+        // drain output tile t straight into the concretisation; halves take alternate
+        // 16-column groups
+        const int ng = S.tile_n / 16, nlim = valid ? S.N : 0;
+        if (kBox && !warp_wait(M.box_full, 0, err, 35)) { ok = false; break; }
+        if (!warp_wait(M.acc_full, nacc & 1, err, 33)) { ok = false; break; }
+        ++nacc;
+        tc_fence_after();
+        const uint32_t dst = tbase + (uint32_t)(s & 1) * 256u + lane_off;
+        for (int q = half; q < ng; q += 2) {
+          const int n0 = t * S.tile_n + q * 16;
+          float pb[16], nb[16], x[16];
+          if (kBox) {
+            lds16_row(box_pos, n0, nlim, pb);
+            lds16_row(box_neg, n0, nlim, nb);
+          } else {
+            load16g(gpos, n0, nlim, P.box_vec, pb);
+            load16g(gneg, n0, nlim, P.box_vec, nb);
+          }
+          tmem_ld16(dst + (uint32_t)(q * 16), x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) conc = fmaf(x[e], x[e] >= 0.0f ? pb[e] : nb[e], conc);
+        }
+        tc_fence_before();
+      }
+    }
+    // step buffer s%2 may be refilled (for step s+2)
+    if (kStaged && ok) {
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&M.coef_empty[s & 1]);
+    }
+  }
+  // combine the two halves of every row
+  if (half == 1) M.red[r] = conc + cacc;
+  asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
+  if (half == 0 && valid && ok) {
+    const float res = (conc + cacc) + M.red[r];
+    (lower ? P.out_l : P.out_u)[b * P.ld_out + i] = res;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ ChainParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const uint32_t stage_bytes = P.stage_bytes;
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kChainStages * stage_bytes);
-  uint64_t* full_w = full_a + kChainStages;
-  uint64_t* empty = full_w + kChainStages;
-  uint64_t* acc_full = empty + kChainStages;
+  // shared memory: kAStages A-operand stages (hi, lo planes), kWStages weight stages (hi, lo
+  // planes of tile_n rows), two step buffers of relaxation vectors, the input-box rows of
+  // the CTA's regions, then the mbarriers
+  const uint32_t w_stage_bytes = P.stage_bytes;
+  uint8_t* a_region = smem;
+  uint8_t* w_region = smem + kAStages * 2 * kAImg;
+  float* coef_region = reinterpret_cast<float*>(w_region + kWStages * w_stage_bytes);
+  float* box_region = coef_region + 2 * kCoefBufFloats;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(box_region) + P.box_smem_bytes);
+  uint64_t* empty_a = full_a + kAStages;
+  uint64_t* full_w = empty_a + kAStages;
+  uint64_t* empty_w = full_w + kWStages;
+  uint64_t* coef_full = empty_w + kWStages;
+  uint64_t* coef_empty = coef_full + 2;
+  uint64_t* box_full = coef_empty + 2;
+  uint64_t* acc_full = box_full + 1;
   uint64_t* mma_done = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [128] partial sums of the second half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = P.err;
+  // the (bound, region) pairs p = row / R this CTA's rows belong to: p0 .. p0+n_pairs-1.  With
+  // at most kCoefSlots of them, their relaxation vectors and box rows are staged in shared memory.
+  const int64_t row_first = (int64_t)blockIdx.x * 128;
+  const int64_t row_last = (row_first + 127 < P.rows ? row_first + 127 : P.rows - 1);
+  const int64_t p0 = row_first / P.R;
+  const int n_pairs = (int)(row_last / P.R - p0 + 1);
+  const bool staged = P.coef_ok && n_pairs <= kCoefSlots;
+  const bool box_staged = staged && P.box_smem_bytes > 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kChainStages; ++i) {
+    for (int i = 0; i < kAStages; ++i) {
       mbar_init(&full_a[i], kTransformThreads);
-      mbar_init(&full_w[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty_a[i], 1);
     }
+    for (int i = 0; i < kWStages; ++i) {
+      mbar_init(&full_w[i], 1);
+      mbar_init(&empty_w[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&coef_full[i], 1);
+      mbar_init(&coef_empty[i], kTransformWarps);
+    }
+    mbar_init(box_full, 1);
     mbar_init(acc_full, 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -146,27 +400,63 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     // ---------------------------------------------------------------- W producer
     if (lane == 0) {
       uint32_t g = 0;
+      int coef_n = 0;  // step buffers of relaxation vectors issued
+      if (box_staged) {
+        // input-box rows (l0 then u0) of every (bound, region) pair of the CTA
+        const uint32_t rb = (uint32_t)P.n0 * 4u;
+        mbar_arrive_expect_tx(box_full, 2u * rb * (uint32_t)n_pairs);
+        for (int j = 0; j < n_pairs; ++j) {
+          const int64_t b = (p0 + j) % P.B;
+          bulk_g2s(box_region + (size_t)j * 2 * P.n0, P.l0 + b * P.n0, rb, box_full);
+          bulk_g2s(box_region + (size_t)j * 2 * P.n0 + P.n0, P.u0 + b * P.n0, rb, box_full);
+        }
+      }
       for (int s = 0; s < P.S; ++s) {
         const ChainStep& S = P.st[s];
         const uint32_t plane = (uint32_t)S.tile_n * 128u;
+        if (staged) {
+          // step s's alpha / lambda / mu rows of the CTA's regions and the layer bias, into
+          // step buffer s%2 once the transform warps have finished step s-2
+          const int cb = s & 1;
+          if (!mbar_wait(&coef_empty[cb], ((s >> 1) & 1) ^ 1, err, 13)) goto done_w;
+          const uint32_t kb = (uint32_t)S.K * 4u;
+          const bool relu = S.alpha != nullptr;
+          float* dst = coef_region + cb * kCoefBufFloats;
+          mbar_arrive_expect_tx(&coef_full[cb], kb * (relu ? 3u * (uint32_t)n_pairs + 1u : 1u));
+          if (relu) {
+            for (int j = 0; j < n_pairs; ++j) {
+              const int64_t b = (p0 + j) % P.B;
+              bulk_g2s(dst + j * 3 * kCoefRow, S.alpha + b * S.K, kb, &coef_full[cb]);
+              bulk_g2s(dst + j * 3 * kCoefRow + kCoefRow, S.lam + b * S.K, kb, &coef_full[cb]);
+              bulk_g2s(dst + j * 3 * kCoefRow + 2 * kCoefRow, S.mu + b * S.K, kb, &coef_full[cb]);
+            }
+          }
+          bulk_g2s(dst + kCoefSlots * 3 * kCoefRow, S.bias, kb, &coef_full[cb]);
+          ++coef_n;
+        }
         for (int t = 0; t < S.n_tiles; ++t) {
           for (int c = 0; c < S.kchunks; ++c, ++g) {
-            const uint32_t stage = g % kChainStages, round = g / kChainStages;
-            if (!mbar_wait(&empty[stage], (round & 1) ^ 1, err, 11)) goto done_w;
-            uint8_t* sb = smem + stage * stage_bytes;
+            const uint32_t stage = g % kWStages, round = g / kWStages;
+            if (!mbar_wait(&empty_w[stage], (round & 1) ^ 1, err, 11)) goto done_w;
+            uint8_t* sb = w_region + stage * w_stage_bytes;
             const uint8_t* src = S.wimg + ((size_t)t * S.kchunks + c) * 2 * plane;
             mbar_arrive_expect_tx(&full_w[stage], 2 * plane);
-            bulk_g2s(sb + 2 * kAImg, src, plane, &full_w[stage]);
+            bulk_g2s(sb, src, plane, &full_w[stage]);
             bulk_g2s(sb + P.w_lo_off, src + plane, plane, &full_w[stage]);
           }
         }
       }
     done_w:
       // copies still in flight (error path) land before the CTA can exit
-      for (uint32_t x = 0; x < kChainStages && x < g; ++x) {
-        const uint32_t gl = g - 1 - x, stage = gl % kChainStages, round = gl / kChainStages;
+      for (uint32_t x = 0; x < kWStages && x < g; ++x) {
+        const uint32_t gl = g - 1 - x, stage = gl % kWStages, round = gl / kWStages;
         mbar_wait(&full_w[stage], round & 1, err, 12);
       }
+      for (int x = 0; x < 2 && x < coef_n; ++x) {
+        const int sl = coef_n - 1 - x;
+        mbar_wait(&coef_full[sl & 1], (sl >> 1) & 1, err, 14);
+      }
+      if (box_staged) mbar_wait(box_full, 0, err, 15);
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
@@ -178,12 +468,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         const uint32_t idesc = idesc_tf32((uint32_t)S.tile_n);
         for (int t = 0; t < S.n_tiles; ++t) {
           for (int c = 0; c < S.kchunks; ++c, ++g) {
-            const uint32_t stage = g % kChainStages, round = g / kChainStages;
-            if (!mbar_wait(&full_a[stage], round & 1, err, 21)) goto done_m;
-            if (!mbar_wait(&full_w[stage], round & 1, err, 22)) goto done_m;
+            const uint32_t as = g % kAStages, ar = g / kAStages, ws = g % kWStages, wr = g / kWStages;
+            if (!mbar_wait(&full_a[as], ar & 1, err, 21)) goto done_m;
+            if (!mbar_wait(&full_w[ws], wr & 1, err, 22)) goto done_m;
             tc_fence_after();
-            const uint32_t sb = smem_u32(smem + stage * stage_bytes);
-            const uint32_t a_hi = sb, a_lo = sb + kAImg, w_hi = sb + 2 * kAImg, w_lo = sb + P.w_lo_off;
+            const uint32_t sa = smem_u32(a_region + as * 2 * kAImg), sw = smem_u32(w_region + ws * w_stage_bytes);
+            const uint32_t a_hi = sa, a_lo = sa + kAImg, w_hi = sw, w_lo = sw + P.w_lo_off;
 #pragma unroll
             for (uint32_t ks = 0; ks < 4; ++ks) {
               const uint64_t dah = sw128_desc(a_hi + ks * 32), dal = sw128_desc(a_lo + ks * 32);
@@ -192,7 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
               mma_tf32(acc, dah, dwl, idesc, 1);
               mma_tf32(acc, dah, dwh, idesc, 1);
             }
-            mma_commit(&empty[stage]);
+            mma_commit(&empty_a[as]);
+            mma_commit(&empty_w[ws]);
           }
           mma_commit(acc_full);
         }
@@ -204,134 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     }
   } else {
     // ---------------------------------------------------------------- transform warps
-    // thread -> tile row (TMEM lane) `r`; the two halves split each 32-column chunk
-    const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
-    const int64_t row = (int64_t)blockIdx.x * 128 + r;
-    const bool valid = row < P.rows;
-    int64_t sb_ = 0, b = 0, i = 0;
-    if (valid) {
-      sb_ = row / (P.B * P.R);
-      int64_t rem = row - sb_ * P.B * P.R;
-      b = rem / P.R;
-      i = rem - b * P.R;
-    }
-    const bool lower = sb_ == 0;
-    float cacc = (valid && P.c0 && half == 0) ? P.c0[i] : 0.0f;
-    float conc = 0.0f;
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    uint32_t g = 0, nacc = 0;
-    const float* a0row = P.A0 + sb_ * P.a_ss + b * P.a_bs + i * P.a_rs;
-    const float* pos_box = (lower ? P.l0 : P.u0) + b * P.n0;
-    const float* neg_box = (lower ? P.u0 : P.l0) + b * P.n0;
-    bool ok = true;
-    for (int s = 0; s < P.S && ok; ++s) {
-      const ChainStep& S = P.st[s];
-      const int K = S.K;
-      const bool cvec = (K & 3) == 0;
-      if (s > 0) {
-        if (!mbar_wait(acc_full, nacc & 1, err, 31)) { ok = false; break; }
-        ++nacc;
-        tc_fence_after();
-      }
-      const uint32_t src_acc = tbase + (uint32_t)((s - 1) & 1) * 256u + lane_off;
-      const int src_cols = s > 0 ? P.st[s - 1].tile_n : 0;
-      const bool relu = S.alpha != nullptr;
-      const float* pf = (lower ? S.alpha : S.lam) + b * K;
-      const float* nf = (lower ? S.lam : S.alpha) + b * K;
-      const float* muv = S.mu + b * K;
-      for (int t = 0; t < S.n_tiles && ok; ++t) {
-        for (int c = 0; c < S.kchunks; ++c, ++g) {
-          const uint32_t stage = g % kChainStages, round = g / kChainStages;
-          const int k0 = c * 32 + half * 16;
-          // coefficient loads first: they depend on nothing the barriers protect
-          float pv[16], nv[16], mv[16], bv[16];
-          if (relu) {
-            load16(pf, k0, K, cvec, pv);
-            load16(nf, k0, K, cvec, nv);
-            if (t == 0) load16(muv, k0, K, cvec, mv);
-          }
-          if (t == 0) load16(S.bias, k0, K, cvec, bv);
-          float v[16];
-          if (s == 0) load16(a0row, k0, valid ? K : 0, P.a0_vec, v);
-          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, err, 32)) { ok = false; break; }
-          if (s > 0) {
-            // columns [K, tile_n) of the previous accumulator are exact zeros (zero-padded
-            // W); a half-chunk past tile_n was never written and is skipped
-            if (k0 < src_cols) {
-              tmem_ld16(src_acc + (uint32_t)k0, v);
-              tmem_ld_wait();
-            } else {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = 0.0f;
-            }
-          }
-          float hi[16], lo[16];
-          if (relu && t == 0) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float pos = fmaxf(v[e], 0.0f), neg = fminf(v[e], 0.0f);
-              const float tr = fmaf(pos, pv[e], neg * nv[e]);
-              cacc = fmaf(lower ? neg : pos, mv[e], cacc);
-              cacc = fmaf(tr, bv[e], cacc);
-              split_tf32(tr, hi[e], lo[e]);
-            }
-          } else if (relu) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float tr = fmaf(fmaxf(v[e], 0.0f), pv[e], fminf(v[e], 0.0f) * nv[e]);
-              split_tf32(tr, hi[e], lo[e]);
-            }
-          } else if (t == 0) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              cacc = fmaf(v[e], bv[e], cacc);
-              split_tf32(v[e], hi[e], lo[e]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) split_tf32(v[e], hi[e], lo[e]);
-          }
-          uint8_t* sbase = smem + stage * stage_bytes;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t qq = (uint32_t)(half * 4 + q);
-            const uint32_t off = (uint32_t)r * 128u + ((qq ^ ((uint32_t)r & 7u)) << 4);
-            *reinterpret_cast<float4*>(sbase + off) = make_float4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
-            *reinterpret_cast<float4*>(sbase + kAImg + off) =
-                make_float4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
-          }
-          fence_proxy_async_smem();
-          tc_fence_before();
-          mbar_arrive(&full_a[stage]);
-        }
-        if (!ok) break;
-        if (s == P.S - 1) {
-          // drain output tile t straight into the concretisation; halves take alternate 16-column groups
-          if (!mbar_wait(acc_full, nacc & 1, err, 33)) { ok = false; break; }
-          ++nacc;
-          tc_fence_after();
-          const uint32_t dst = tbase + (uint32_t)(s & 1) * 256u + lane_off;
-          for (int q = half; q < S.tile_n / 16; q += 2) {
-            const int n0 = t * S.tile_n + q * 16;
-            float pb[16], nb[16], x[16];
-            load16(pos_box, n0, valid ? S.N : 0, P.box_vec, pb);
-            load16(neg_box, n0, valid ? S.N : 0, P.box_vec, nb);
-            tmem_ld16(dst + (uint32_t)(q * 16), x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) conc = fmaf(x[e], x[e] >= 0.0f ? pb[e] : nb[e], conc);
-          }
-          tc_fence_before();
-        }
-      }
-    }
-    // combine the two halves of every row
-    if (half == 1) red[r] = conc + cacc;
-    asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
-    if (half == 0 && valid && ok) {
-      const float res = (conc + cacc) + red[r];
-      (lower ? P.out_l : P.out_u)[b * P.ld_out + i] = res;
-    }
+    const ChainSmem M{smem_u32(a_region), smem_u32(coef_region), smem_u32(box_region), full_a, empty_a,
+                      coef_full, coef_empty, box_full, acc_full, red};
+    if (box_staged)
+      chain_transform<true, true>(P, M, tbase, p0);
+    else if (staged)
+      chain_transform<true, false>(P, M, tbase, p0);
+    else
+      chain_transform<false, false>(P, M, tbase, p0);
   }
 
   tc_fence_before();
@@ -353,9 +524,26 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   }
   CF_REQUIRE(P.st[P.S - 1].N == P.n0, CF_ERR_SHAPE, "chain: last step does not reach the input");
   ChainParams Q = P;
-  Q.w_lo_off = 2 * kAImg + (uint32_t)tn_max * 128u;
-  Q.stage_bytes = (2 * kAImg + 2u * (uint32_t)tn_max * 128u + 1023u) & ~1023u;
-  size_t smem = 1024 + (size_t)kChainStages * Q.stage_bytes + (3 * kChainStages + 2) * 8 + 16 + 128 * 4;
+  // weight stage: hi plane then lo plane, each tn_max rows x 128 bytes (1024-aligned)
+  Q.w_lo_off = (uint32_t)tn_max * 128u;
+  Q.stage_bytes = 2u * (uint32_t)tn_max * 128u;
+  // relaxation vectors are staged through shared memory (bulk copies: 16-byte aligned rows
+  // of K <= 256 floats, K % 4 == 0); otherwise the transform warps read them from global memory
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  bool coef_ok = true;
+  for (int s = 0; s < P.S; ++s) {
+    const ChainStep& S = P.st[s];
+    coef_ok = coef_ok && S.K <= kCoefRow && S.K % 4 == 0 && S.bias != nullptr && a16(S.bias);
+    if (S.alpha) coef_ok = coef_ok && a16(S.alpha) && a16(S.lam) && a16(S.mu);
+  }
+  Q.coef_ok = coef_ok ? 1 : 0;
+  const size_t fixed = 1024 + (size_t)kAStages * 2 * kAImg + (size_t)kWStages * Q.stage_bytes +
+                       (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 128 * 4;
+  // input-box rows of up to kCoefSlots (bound, region) pairs, when they fit
+  const size_t box_bytes = (size_t)kCoefSlots * 2 * P.n0 * 4;
+  const bool box_ok = coef_ok && P.n0 % 4 == 0 && a16(P.l0) && a16(P.u0) && fixed + box_bytes <= 227 * 1024;
+  Q.box_smem_bytes = box_ok ? (uint32_t)box_bytes : 0u;
+  size_t smem = fixed + Q.box_smem_bytes;
   // at least 116 KB so that one CTA (which holds all 512 TMEM columns) runs per SM
   if (smem < 116 * 1024) smem = 116 * 1024;
   cudaError_t e = cudaFuncSetAttribute(k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);

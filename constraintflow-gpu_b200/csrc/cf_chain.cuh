@@ -4,8 +4,14 @@
 
 namespace cf {
 
-constexpr int kChainStages = 2;     // shared-memory pipeline depth
+constexpr int kAStages = 2;  // shared-memory stages of the transformed A operand (32 KB each)
+constexpr int kWStages = 2;  // shared-memory stages of weight chunks (2 x tile_n x 128 bytes each)
 constexpr int kChainMaxSteps = 24;  // substitutions per launch (affine layers below the bounded one)
+// Relaxation vectors staged in shared memory per step: alpha, lambda, mu rows (kCoefRow floats
+// each) of up to kCoefSlots (bound, region) pairs, then the layer bias; two step buffers.
+constexpr int kCoefSlots = 2;
+constexpr int kCoefRow = 256;
+constexpr int kCoefBufFloats = (kCoefSlots * 3 + 1) * kCoefRow;
 
 // One substitution: ReLU_j (if alpha != nullptr) then affine layer j, W_j [K, N].
 struct ChainStep {
@@ -33,6 +39,8 @@ struct ChainParams {
   int* err;                             // device error word (bounded-wait timeouts)
   int32_t a0_vec, box_vec;              // 16-byte loads allowed for A0 rows / the input box
   uint32_t stage_bytes, w_lo_off;       // filled by chain_launch
+  uint32_t box_smem_bytes;              // input-box staging bytes (0: read from global memory)
+  int32_t coef_ok;                      // relaxation vectors may be staged in shared memory
 };
 
 void chain_tile(int N, int& tile_n, int& n_tiles);

@@ -46,11 +46,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait.  On timeout sets *err (if not already set) and returns false.
+// Bounded wait.  On timeout sets *err (if not already set) and returns false.  The error
+// word (global memory, an L2 round trip) is read only every 16th poll so that a barrier
+// that completes mid-wait is seen at mbarrier latency.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*(volatile int*)err != 0) return false;  // another role already gave up
+    if ((i & 15u) == 15u && *(volatile int*)err != 0) return false;  // another role already gave up
   }
   atomicCAS(err, 0, site);
   return false;
@@ -119,6 +121,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 
 // ---- shared-memory matrix descriptor (K-major, 128-byte swizzle, 8-row x 128 B atoms)
 // start address >> 4 in bits [0,14), leading offset 16 B (encoded 1) in [16,30),
