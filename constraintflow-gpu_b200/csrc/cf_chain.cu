@@ -89,6 +89,13 @@ cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStr
   return check_launch("k_prep_wimg");
 }
 
+// Columns of N tile t of a step: tile_n, except the last tile, which covers the remaining
+// columns rounded up to 16.
+__device__ __forceinline__ int tile_width(const ChainStep& S, int t) {
+  const int rest = S.N - t * S.tile_n;
+  return rest >= S.tile_n ? S.tile_n : ((rest + 15) / 16) * 16;
+}
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
 }
@@ -297,7 +304,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
       if (s == P.S - 1) {
         // drain output tile t straight into the concretisation; halves take alternate
         // 16-column groups
-        const int ng = S.tile_n / 16, nlim = valid ? S.N : 0;
+        const int ng = tile_width(S, t) / 16, nlim = valid ? S.N : 0;
         if (kBox && !warp_wait(M.box_full, 0, err, 35)) { ok = false; break; }
         if (!warp_wait(M.acc_full, nacc & 1, err, 33)) { ok = false; break; }
         ++nacc;
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       }
       for (int s = 0; s < P.S; ++s) {
         const ChainStep& S = P.st[s];
-        const uint32_t plane = (uint32_t)S.tile_n * 128u;
+        const uint32_t plane = (uint32_t)S.tile_n * 128u;  // image plane stride
         if (staged) {
           // step s's alpha / lambda / mu rows of the CTA's regions and the layer bias, into
           // step buffer s%2 once the transform warps have finished step s-2
@@ -440,9 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             if (!mbar_wait(&empty_w[stage], (round & 1) ^ 1, err, 11)) goto done_w;
             uint8_t* sb = w_region + stage * w_stage_bytes;
             const uint8_t* src = S.wimg + ((size_t)t * S.kchunks + c) * 2 * plane;
-            mbar_arrive_expect_tx(&full_w[stage], 2 * plane);
-            bulk_g2s(sb, src, plane, &full_w[stage]);
-            bulk_g2s(sb + P.w_lo_off, src + plane, plane, &full_w[stage]);
+            const uint32_t bytes = (uint32_t)tile_width(S, t) * 128u;  // rows the MMAs read
+            mbar_arrive_expect_tx(&full_w[stage], 2 * bytes);
+            bulk_g2s(sb, src, bytes, &full_w[stage]);
+            bulk_g2s(sb + P.w_lo_off, src + plane, bytes, &full_w[stage]);
           }
         }
       }
@@ -465,9 +473,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       for (int s = 0; s < P.S; ++s) {
         const ChainStep& S = P.st[s];
         const uint32_t acc = tbase + (uint32_t)(s & 1) * 256u;
-        const uint32_t idesc = idesc_tf32((uint32_t)S.tile_n);
         for (int t = 0; t < S.n_tiles; ++t) {
+          // the last N tile is only as wide as the columns left (a multiple of 16)
+          const uint32_t idesc = idesc_tf32((uint32_t)tile_width(S, t));
           for (int c = 0; c < S.kchunks; ++c, ++g) {
+            // k-steps of 8 that reach below K (the rest of the chunk is zero padding)
+            const int nks = min(4, (S.K - c * 32 + 7) / 8);
             const uint32_t as = g % kAStages, ar = g / kAStages, ws = g % kWStages, wr = g / kWStages;
             if (!mbar_wait(&full_a[as], ar & 1, err, 21)) goto done_m;
             if (!mbar_wait(&full_w[ws], wr & 1, err, 22)) goto done_m;
@@ -475,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             const uint32_t sa = smem_u32(a_region + as * 2 * kAImg), sw = smem_u32(w_region + ws * w_stage_bytes);
             const uint32_t a_hi = sa, a_lo = sa + kAImg, w_hi = sw, w_lo = sw + P.w_lo_off;
 #pragma unroll
-            for (uint32_t ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks) {
+              if (ks >= nks) break;
               const uint64_t dah = sw128_desc(a_hi + ks * 32), dal = sw128_desc(a_lo + ks * 32);
               const uint64_t dwh = sw128_desc(w_hi + ks * 32), dwl = sw128_desc(w_lo + ks * 32);
               mma_tf32(acc, dal, dwh, idesc, (c | ks) != 0);
