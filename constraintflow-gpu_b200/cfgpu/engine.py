@@ -22,14 +22,22 @@ class DeepPolyEngine:
     layers: sequence of objects with ``kind`` in {'linear','conv','relu'} and, for affine
     layers, ``W`` / ``b`` arrays (Linear W [out, in]; Conv W [Cout, Cin, k, k]) plus
     ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers.
+    certifier: 'deeppoly' (deeppoly.cf, deeppoly_efficient.cf) or 'crown' (crown.cf, whose
+    ReLU branch is decided over the whole batch: a CROWN run always takes the batch in
+    one workspace chunk and checks the device status, raising NotImplementedError when
+    a layer takes the all-crossing branch).
     """
 
-    def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1):
+    def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("DeepPolyEngine runs on a CUDA device only (no CPU fallback)")
         self.input_size = int(input_size)
         self.n_spec = int(n_spec)
+        relax = {"deeppoly": _lib.CF_RELAX_DEEPPOLY, "crown": _lib.CF_RELAX_CROWN}
+        if certifier not in relax:
+            raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly and crown)")
+        self.certifier = certifier
         self._keep = []
         descs = []
         width = self.input_size
@@ -60,7 +68,7 @@ class DeepPolyEngine:
             descs.append(d)
         self.n_last = width
         self._layers = (CfLayer * len(descs))(*descs)
-        self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, _lib.CF_RELAX_DEEPPOLY)
+        self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, relax[certifier])
         self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))
         if self.N < 0:
             check(_lib.CF_ERR_SHAPE, "network description")
@@ -71,7 +79,8 @@ class DeepPolyEngine:
 
     def _workspace(self, B, budget_bytes):
         need_full = self.workspace_bytes(max(1, B))
-        need = min(need_full, max(self.workspace_bytes(1), budget_bytes))
+        # CROWN needs the whole batch in one chunk; DeepPoly regions are independent
+        need = need_full if self.certifier == "crown" else min(need_full, max(self.workspace_bytes(1), budget_bytes))
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
@@ -107,7 +116,7 @@ class DeepPolyEngine:
                                  su.data_ptr() if su is not None else None,
                                  lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         check(st, "cf_deeppoly_run")
-        if check_device:
+        if check_device or self.certifier == "crown":
             check(lib.cf_deeppoly_check(ws.data_ptr(), stream), "device status")
         if want_state:
             return lb, ub, sl, su
@@ -135,7 +144,7 @@ class DeepPolyEngine:
         return l0, u0, W
 
     def certify(self, X, y, eps, dataset, out=None):
-        """Whole pipeline on device tensors: input box, property, DeepPoly -> (lb, ub, verdict)."""
+        """Whole pipeline on device tensors: input box, property, certifier -> (lb, ub) float64."""
         l0, u0, W = self.input_spec(X, y, eps, dataset)
         lb, ub = self.run(l0, u0, W, out=out)
         return lb, ub

@@ -7,12 +7,17 @@ of the B200 network driver (cf_deeppoly_run through cfgpu.engine), which compute
 same abstract state: every neuron's l/u is written back into abs_elem.d['l'|'u'] and the
 property layer's bounds are returned as float64 (lb, ub), as Flow.flow returns them.
 
-Recognition: the compiler emits a class with Affine and Relu methods; the DeepPoly
-program (examples/compiler_examples/deeppoly.cf) is identified from the operations its
-generated Relu and Affine perform (the triangle relaxation: convert_to_poly, the
-u/(u-l) slope, the l>=0 / u<=0 cases; the backward traversal: clamp sign split,
-inner_prod, get_max_priority).  A transformer object may also declare itself with a
-``cf_certifier = "deeppoly"`` attribute.  Other programs raise NotImplementedError.
+Recognition: the compiler emits a class with Affine and Relu methods; the program is
+identified from the operations its generated code performs.  Every supported program
+has the same Affine (the backward traversal with priority2 = -layer: clamp sign split,
+inner_prod, get_max_priority over the negated layer index) and one of three Relu bodies:
+  * deeppoly.cf: per-neuron triangle relaxation over the neuron itself (convert_to_poly,
+    the u/(u-l) slope, where() on l>=0 / u<=0);
+  * deeppoly_efficient.cf: the same relaxation applied to the affine's L/U polyexps
+    (get_elem('L'/'U', prev)); it composes to exactly DeepPoly's bounds;
+  * crown.cf: whole-layer if(any(...)) branches with the -l > u lower-slope choice.
+A transformer object may also declare itself with a ``cf_certifier`` attribute
+('deeppoly' or 'crown').  Other programs raise NotImplementedError.
 """
 import inspect
 
@@ -23,13 +28,16 @@ from constraintflow.gbcsr.sparse_tensor import SparseTensor
 
 from .network import LayerType
 
+_AFFINE = ("clamp(", "inner_prod(", "get_max_priority(", "filter_trav_exp_not_stop(",
+           "get_metadata('layer'", "operator.neg")
 _DEEPPOLY_RELU = ("convert_to_poly(", "operator.truediv", "operator.le", "operator.ge", "where(")
-_DEEPPOLY_AFFINE = ("clamp(", "inner_prod(", "get_max_priority(", "filter_trav_exp_not_stop(")
-_CROWN_RELU = ("operator.gt",)
+_EFFICIENT_RELU = ("get_elem('L', prev", "get_elem('U', prev", "operator.truediv", "operator.le", "operator.ge",
+                   "where(")
+_CROWN_RELU = ("if(", "any(", "operator.gt", "convert_to_poly(", "operator.truediv", "get_elem('U', prev")
 
 
 def certifier_of(transformer):
-    """'deeppoly' for the DeepPoly program's generated transformer, else raises."""
+    """'deeppoly' or 'crown' for a recognised generated transformer, else raises."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
@@ -39,11 +47,14 @@ def certifier_of(transformer):
         affine = inspect.getsource(cls.Affine)
     except (AttributeError, OSError, TypeError) as e:
         raise NotImplementedError(f"cannot read the generated transformer: {e}")
-    if all(k in relu for k in _DEEPPOLY_RELU) and all(k in affine for k in _DEEPPOLY_AFFINE) \
-            and not any(k in relu for k in _CROWN_RELU):
-        return "deeppoly"
-    raise NotImplementedError("this runtime runs the DeepPoly certifier program; the given transformer "
-                              f"({cls.__name__}) is a different program")
+    if all(k in affine for k in _AFFINE):
+        branches = "if(" in relu or "any(" in relu or "operator.gt" in relu
+        if not branches and (all(k in relu for k in _DEEPPOLY_RELU) or all(k in relu for k in _EFFICIENT_RELU)):
+            return "deeppoly"
+        if all(k in relu for k in _CROWN_RELU):
+            return "crown"
+    raise NotImplementedError("this runtime runs the DeepPoly and CROWN certifier programs; the given "
+                              f"transformer ({cls.__name__}) is a different program")
 
 
 class _EngineLayer:
@@ -88,7 +99,7 @@ class Flow:
 
     def flow(self):
         from cfgpu.engine import DeepPolyEngine
-        certifier_of(self.transformer)
+        certifier = certifier_of(self.transformer)
         dev = torch.device("cuda", torch.cuda.current_device())
         n0 = self.input_size
         B = self.batch_size
@@ -98,7 +109,7 @@ class Flow:
         u0 = u_in.get_dense_device()[:, :n0].contiguous()
         spec = self.model[-1]
         W = torch.as_tensor(spec.weight, dtype=torch.float32).to(dev).contiguous()
-        eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]))
+        eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier)
         lb, ub, sl, su = eng.run(l0, u0, W, want_state=True)
         total = torch.tensor([B, self.model.size])
         self.abs_elem.d["l"] = SparseTensor([torch.tensor([0, 0])], [DenseBlock(sl)], 2, total,

@@ -398,10 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  // an earlier launch of this pass recorded an error (a timeout, or a CROWN layer that
+  // took the all-crossing branch): do nothing, before any copy or MMA is issued
+  if (threadIdx.x == 0) tmem_slot[1] = *(volatile int*)err != 0 ? 1u : 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  if (tmem_slot[1] != 0) {
+    if (warp == kProducerWarp) tmem_dealloc(tbase, 512);
+    return;
+  }
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- W producer
@@ -458,13 +465,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       // copies still in flight (error path) land before the CTA can exit
       for (uint32_t x = 0; x < kWStages && x < g; ++x) {
         const uint32_t gl = g - 1 - x, stage = gl % kWStages, round = gl / kWStages;
-        mbar_wait(&full_w[stage], round & 1, err, 12);
+        mbar_wait_drain(&full_w[stage], round & 1, err, 12);
       }
       for (int x = 0; x < 2 && x < coef_n; ++x) {
         const int sl = coef_n - 1 - x;
-        mbar_wait(&coef_full[sl & 1], (sl >> 1) & 1, err, 14);
+        mbar_wait_drain(&coef_full[sl & 1], (sl >> 1) & 1, err, 14);
       }
-      if (box_staged) mbar_wait(box_full, 0, err, 15);
+      if (box_staged) mbar_wait_drain(box_full, 0, err, 15);
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
@@ -503,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     done_m:
       // every MMA issued above has completed before TMEM is released
       mma_commit(mma_done);
-      mbar_wait(mma_done, 0, err, 23);
+      mbar_wait_drain(mma_done, 0, err, 23);
     }
   } else {
     // ---------------------------------------------------------------- transform warps

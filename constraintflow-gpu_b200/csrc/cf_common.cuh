@@ -10,6 +10,10 @@
 
 namespace cf {
 
+// Device error word value recorded when a CROWN ReLU layer takes the all-crossing branch
+// (bounded-wait timeouts record their small site numbers instead).
+constexpr int kCrownCrossingSite = 900;
+
 // Per-host-thread message of the last failing call (read through cf_last_error()).
 void set_error(const char* fmt, ...);
 void clear_error();

@@ -48,6 +48,71 @@ cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u
   return check_launch("k_relu_relax");
 }
 
+// ------------------------------------------------------------------ CROWN ReLU
+// The reference compiles crown.cf:25, a ternary of (l, u, L, U) tuples, into whole-layer
+// branches on any() over the layer's [B, n] bounds (generated crown Relu):
+//   any(l >= 0)            -> pass-through: l' = l, u' = u, L' = prev[L], U' = prev[U]
+//   else any(u <= 0)       -> zero:         l' = u' = 0, L' = U' = 0
+//   else (all cross zero)  -> crossing:     U' substituted one layer deeper (mixed-layer
+//                                           polyexps; not expressible as per-neuron slopes)
+// flags[0] = any(l >= 0), flags[1] = any(u <= 0); the caller zeroes them first.
+__global__ void k_crown_flags(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
+                              int64_t ld, int* __restrict__ flags) {
+  int64_t total = B * n;
+  bool any_l = false, any_u = false;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = t / n, k = t - b * n;
+    any_l |= l[b * ld + k] >= 0.0f;
+    any_u |= u[b * ld + k] <= 0.0f;
+  }
+  any_l = __any_sync(0xffffffffu, any_l);
+  any_u = __any_sync(0xffffffffu, any_u);
+  if ((threadIdx.x & 31) == 0) {
+    if (any_l) atomicOr(&flags[0], 1);
+    if (any_u) atomicOr(&flags[1], 1);
+  }
+}
+
+// Pass-through and zero branches as per-neuron slopes for the backsubstitution kernels
+// (alpha = lam = 1, mu = 0 leaves a coefficient unchanged; all 0 removes it).  The
+// crossing branch records kCrownCrossingSite in the device error word.
+__global__ void k_crown_relax(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
+                              int64_t ld_in, float* __restrict__ lo, float* __restrict__ uo, int64_t ld_out,
+                              float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu,
+                              const int* __restrict__ flags, int* __restrict__ err) {
+  const bool pass = flags[0] != 0, zero = !pass && flags[1] != 0;
+  if (!pass && !zero && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(err, 0, kCrownCrossingSite);
+  const float s = pass ? 1.0f : 0.0f;
+  int64_t total = B * n;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = t / n, k = t - b * n;
+    lo[b * ld_out + k] = pass ? l[b * ld_in + k] : 0.0f;
+    uo[b * ld_out + k] = pass ? u[b * ld_in + k] : 0.0f;
+    alpha[t] = s;
+    lam[t] = s;
+    mu[t] = 0.0f;
+  }
+}
+
+cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
+                             float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, int* flags, int* err,
+                             cudaStream_t st) {
+  int64_t total = B * n;
+  if (total == 0) return CF_OK;
+  int threads = 256;
+  int64_t blocks = ceil_div(total, threads);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (cudaMemsetAsync(flags, 0, 2 * sizeof(int), st) != cudaSuccess) {
+    set_error("crown_relax: cudaMemsetAsync failed");
+    return CF_ERR_CUDA;
+  }
+  k_crown_flags<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, flags);
+  CF_TRY(check_launch("k_crown_flags"));
+  k_crown_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu, flags,
+                                                      err);
+  return check_launch("k_crown_relax");
+}
+
 // ------------------------------------------------------------------ concretisation
 // bound(s,b,i) = c + sum_n (a>=0 ? a*box_s[n] : a*box_{1-s}[n]), box_0 = l0, box_1 = u0.
 // One warp per row; lanes stride the n0 columns (coalesced), shuffle reduction.

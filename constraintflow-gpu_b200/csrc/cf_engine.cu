@@ -98,6 +98,8 @@ static void window_sizing(const cf_network* net, Plan& p);
 static cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
   CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
+  CF_REQUIRE(net->relaxation == CF_RELAX_DEEPPOLY || net->relaxation == CF_RELAX_CROWN, CF_ERR_UNSUPPORTED,
+             "network: relaxation %d", net->relaxation);
   int64_t pos = net->n_input, prev_width = net->n_input;
   p.col.assign(net->n_layers, 0);
   p.relu_after.clear();
@@ -273,7 +275,8 @@ static bool needs_step_buffers(const cf_network* net, const Plan& p) {
 static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   WsLayout w;
   size_t off = 0;
-  w.err = off; off += 256;
+  // device error word, then two CROWN branch flags per affine layer
+  w.err = off; off += align256(64 + 8 * p.affine.size());
   w.wimg = off;
   w.wimg_off.assign(p.affine.size(), 0);
   if (use_chain() && !p.has_conv) {  // weight images for the tensor-core chain
@@ -489,8 +492,14 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
     if (p.relu_after[a] >= 0) {
       const cf_layer& Rl = net->layers[p.relu_after[a]];
       int64_t rcol = p.col[p.relu_after[a]];
-      CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a], rl[a],
-                               rm[a], st));
+      if (net->relaxation == CF_RELAX_CROWN) {
+        int* err = reinterpret_cast<int*>(ws + w.err);
+        CF_TRY(launch_crown_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a],
+                                  rl[a], rm[a], err + 16 + 2 * a, err, st));
+      } else {
+        CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a],
+                                 rl[a], rm[a], st));
+      }
     }
   }
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
@@ -572,10 +581,15 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
     else hi = mid - 1;
   }
   const int64_t Bc = lo;
+  // CROWN's ReLU branch is decided over the whole batch: one chunk only
+  CF_REQUIRE(net->relaxation != CF_RELAX_CROWN || Bc == B, CF_ERR_WORKSPACE,
+             "CROWN decides each ReLU branch over the whole batch: workspace %zu holds %lld of %lld regions "
+             "(cf_deeppoly_workspace_bytes(net, B) = %zu)", ws_bytes, (long long)Bc, (long long)B,
+             ws_layout(net, p, B).total);
   const WsLayout w = ws_layout(net, p, Bc);
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = as_stream(stream);
-  if (cudaMemsetAsync(ws + w.err, 0, 256, st) != cudaSuccess) {
+  if (cudaMemsetAsync(ws + w.err, 0, w.wimg - w.err, st) != cudaSuccess) {
     set_error("deeppoly_run: cudaMemsetAsync failed");
     return CF_ERR_CUDA;
   }
@@ -606,6 +620,11 @@ extern "C" cf_status cf_deeppoly_check(const void* workspace, void* stream) {
   if (e != cudaSuccess) {
     set_error("deeppoly_check: %s", cudaGetErrorString(e));
     return CF_ERR_CUDA;
+  }
+  if (h == kCrownCrossingSite) {
+    set_error("CROWN: every neuron of a ReLU layer crosses zero in every region (the all-crossing branch of "
+              "crown.cf's ReLU, whose U polyexps mix layers); this branch is not run on the GPU");
+    return CF_ERR_UNSUPPORTED;
   }
   if (h != 0) {
     set_error("a bounded device wait gave up (site %d)", h);

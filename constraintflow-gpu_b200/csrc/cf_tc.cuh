@@ -58,6 +58,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Bounded wait for work already in flight (bulk copies, MMAs) before the CTA releases what
+// that work writes: unlike mbar_wait it does not give up when another role has recorded
+// an error, only after kMaxPolls polls (then it records `site` if nothing was recorded).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int site) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicCAS(err, 0, site);
+  return false;
+}
+
 // Bulk copy global -> shared (TMA engine, contiguous bytes), completion on an mbarrier.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -60,8 +60,20 @@ enum {
 /* Layer kinds of a chain network (constraintflow/lib/network.py:75-87). */
 enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
 
-/* Relaxations the ReLU transformer can use. */
-enum { CF_RELAX_DEEPPOLY = 0 };
+/* Certifier programs the network driver runs (the ReLU transformer and traversal of
+ * examples/compiler_examples/<name>.cf as the reference compiler emits them).
+ *   CF_RELAX_DEEPPOLY  deeppoly.cf (and deeppoly_efficient.cf, which composes to the same
+ *                      bounds): per-neuron triangle relaxation.
+ *   CF_RELAX_CROWN     crown.cf: the reference lowers its tuple-valued ReLU ternary to
+ *                      whole-layer branches on any() over the layer's [B, n] bounds:
+ *                      any(l >= 0) -> pass-through (l' = l, u' = u, L'/U' of the affine);
+ *                      else any(u <= 0) -> zero; else every neuron crosses 0 and U' is
+ *                      substituted one layer deeper.  The branch couples the regions of
+ *                      a batch, so cf_deeppoly_run requires the whole batch in one
+ *                      workspace chunk (CF_ERR_WORKSPACE otherwise); the all-crossing
+ *                      branch is not run on the GPU and cf_deeppoly_check reports it as
+ *                      CF_ERR_UNSUPPORTED. */
+enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1 };
 
 /* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
  * Conv: W_dev [cout, cin, kh, kw], b_dev [cout]; neurons in (c, y, x) order,
@@ -83,7 +95,7 @@ typedef struct cf_network {
   const cf_layer* layers;  /* host array */
   int32_t n_input;
   int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
-  int32_t relaxation;      /* CF_RELAX_DEEPPOLY */
+  int32_t relaxation;      /* CF_RELAX_DEEPPOLY or CF_RELAX_CROWN */
 } cf_network;
 
 /* Total neuron count N of the abstract state: input + every layer + property rows
@@ -150,12 +162,15 @@ cf_status cf_deeppoly_run_static(const cf_network* net, int64_t B,
                                  double* lb_dev, double* ub_dev, void* stream);
 
 /* Synchronise `stream` and report whether a bounded device-side wait of the last
- * cf_deeppoly_run that used `workspace_dev` gave up (CF_ERR_TIMEOUT) instead of hanging. */
+ * cf_deeppoly_run that used `workspace_dev` gave up (CF_ERR_TIMEOUT) instead of hanging,
+ * or (CF_RELAX_CROWN) a ReLU layer took the all-crossing branch (CF_ERR_UNSUPPORTED; the
+ * bounds of that run are not valid). */
 cf_status cf_deeppoly_check(const void* workspace_dev, void* stream);
 
 /* ReLU transformer on pre-activation bounds l, u [B, n] (row stride ld_in):
  * l' = relu(l), u' = relu(u) (row stride ld_out), and the relaxation
- * L' = alpha*x, U' = lam*x + mu as compact [B, n] arrays. */
+ * L' = alpha*x, U' = lam*x + mu as compact [B, n] arrays.  relaxation must be
+ * CF_RELAX_DEEPPOLY (CROWN's batch-wide branches run inside cf_deeppoly_run only). */
 cf_status cf_relu_relax(int64_t B, int64_t n, const float* l_dev, const float* u_dev, int64_t ld_in,
                         float* l_out_dev, float* u_out_dev, int64_t ld_out,
                         float* alpha_dev, float* lam_dev, float* mu_dev, int32_t relaxation,

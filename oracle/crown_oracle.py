@@ -1,0 +1,180 @@
+"""CPU oracle for the reference's CROWN program (numpy, float32).
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, ``__graft_entry__.smoke()`` and bench.py's
+CPU legs may import this module, as the checker; the product path (cfgpu) never
+imports it and has no CPU fallback.
+
+What it restates: examples/compiler_examples/crown.cf as the reference compiler
+emits it (tests/golden/generated/crown/transformers.py, the reference's own
+output kept as a fixture), run by constraintflow/lib/flow_sparse.py:27-228.
+
+* Relu (crown.cf:25, generated ``Relu``): the ternary of TUPLES is lowered to
+  whole-layer ``if any(...)`` branches over the [B, n] bounds of the layer:
+    - ``any(l >= 0)``  -> pass-through: l' = l, u' = u, L' = prev[L], U' = prev[U];
+    - else ``any(u <= 0)`` -> zero: l' = u' = 0, L' = U' = 0;
+    - else (every neuron of every region crosses 0): with c = 1[-l > u],
+      l' = c*0 + (1-c)*l, u' = u, L' = (1-c)*x (the neuron itself,
+      Llist.convert_to_poly), U' = lam*(U_prev.map(replace_upper)) + (u*(0-1))*l/(u-l)
+      with lam = u/(u-l): the affine's U polyexp with every neuron it references
+      replaced by that neuron's U (coefficient >= 0) or L (< 0), i.e. one layer deeper.
+  The branch is decided over the whole batch, so a region's bounds depend on the
+  other regions of the batch (as in the reference).
+* Affine (crown.cf:24, generated ``Affine``): start from W x + b and traverse
+  backwards with priority2 = -layer (crown.cf:10): every while-iteration takes the
+  LOWEST non-input layer that has a non-zero coefficient anywhere in the batch
+  (get_max_priority, constraintflow/gbcsr/tensor_ops.py:557) and replaces its
+  neurons by L (coefficient >= 0) or U (< 0) for the lower bound, U / L for the
+  upper (replace_lower/replace_upper, crown.cf:6-7); inner_prod / clamp as in
+  tensor_ops.py:370,765.  Input neurons are never substituted (get_default_stop,
+  tensor_ops.py:497); the loop ends when only input columns are live and the
+  result is concretised against the input box (simplify_lower/upper, crown.cf:3-4).
+  With polyexps that mix layers (after a crossing branch) the substitution order
+  matters: a neuron can be substituted several times with partial coefficients.
+
+Representation: a polyexp is ({layer t: [B, r, n_t] float32}, const [B, r]);
+layer 0 is the input, then one neuron layer per network layer, in order.
+
+Pinned against: the reference's own CROWN outputs (tests/golden/crown_*.npz,
+made by tests/golden/gen_golden.py).
+"""
+import numpy as np
+
+from .deeppoly_oracle import F32, _affine_rows, layer_bias
+
+BRANCH_PASS, BRANCH_ZERO, BRANCH_CROSS = 0, 1, 2
+
+
+def _split(A):
+    return np.maximum(A, F32(0.0)), np.minimum(A, F32(0.0))
+
+
+def _add_block(blocks, t, M):
+    blocks[t] = (blocks[t] + M).astype(F32) if t in blocks else M.astype(F32)
+
+
+def _substitute(blocks, c, t, P, N_poly, lower):
+    """Replace layer t's neurons in (blocks, c): coefficient >= 0 -> P (lower) else N_poly.
+
+    P / N_poly are the (blocks, const) polyexps of layer t's neurons, [B, n_t, .] each.
+    Returns the new (blocks, const) = substituted part + the untouched blocks.
+    """
+    A = blocks.pop(t)
+    Ap, An = _split(A)
+    first, second = (P, N_poly) if lower else (N_poly, P)
+    new = {}
+    for s, M in first[0].items():
+        _add_block(new, s, np.matmul(Ap, M))
+    for s, M in second[0].items():
+        _add_block(new, s, np.matmul(An, M))
+    dc = (np.einsum('brn,bn->br', Ap, first[1], dtype=F32) +
+          np.einsum('brn,bn->br', An, second[1], dtype=F32)).astype(F32)
+    for s, M in blocks.items():   # the stopped part (other layers) is added after
+        _add_block(new, s, M)
+    return new, ((dc + F32(0.0)) + c).astype(F32)
+
+
+def _traverse(blocks, c, polys, lower, order=min):
+    """Backward traversal, lowest live layer first, until no coefficient is left.
+
+    The input layer is live from the start (constraintflow/lib/spec.py:134-135) and
+    get_default_stop (tensor_ops.py:497) stops only non-live layers, so input neurons
+    are substituted in the loop like any other layer, by their constant L/U (l0/u0):
+    whenever input columns are the lowest live layer, their current coefficients are
+    concretised there and then.  The final concretisation (generated ``l_new``) then
+    sees an empty matrix and returns the constant.
+    """
+    while True:
+        live = [t for t, M in blocks.items() if np.any(M)]
+        if not live:
+            break
+        t = order(live)
+        L, U = polys[t]
+        blocks, c = _substitute(blocks, c, t, L, U, lower)
+    return c
+
+
+def crown(layers, l0, u0, spec_W, order=min):
+    """Run the reference's CROWN program over a chain network.
+
+    layers : list of cfgpu.nets.Layer (linear / conv / relu), property layer excluded.
+    l0, u0 : [B, n0] float32 normalised input box.
+    spec_W : [B, 9, 10] per-region property matrix (bias 0).
+    order  : which live layer the traversal substitutes next (``min`` = the reference's
+             priority2 = -layer; tests plant ``max`` to show the golden vectors pin it).
+    Returns (bounds, lb, ub, branches): bounds per layer (excluding input, including
+    the property layer) of (l [B,n], u [B,n]); lb/ub float64 [B, 9]; branches the
+    BRANCH_* code of every ReLU layer.
+    """
+    l0 = np.asarray(l0, F32)
+    u0 = np.asarray(u0, F32)
+    B, n0 = l0.shape
+    zero = F32(0.0)
+    # polys[k] = (L, U) of neuron layer k; layer 0 = input: (empty, const l0 / u0)
+    polys = {0: (({}, l0), ({}, u0))}
+    bounds = []
+    branches = []
+    for idx, Lyr in enumerate(layers + ['spec']):
+        k = idx + 1
+        if Lyr != 'spec' and Lyr.kind == 'relu':
+            l, u = bounds[-1]
+            (Lb, Lc), (Ub, Uc) = polys[k - 1]
+            if np.any(l >= zero):
+                branches.append(BRANCH_PASS)
+                polys[k] = polys[k - 1]
+                bounds.append((l.copy(), u.copy()))
+            elif np.any(u <= zero):
+                branches.append(BRANCH_ZERO)
+                zc = np.zeros_like(l)
+                polys[k] = (({}, zc), ({}, zc))
+                bounds.append((np.zeros_like(l), np.zeros_like(u)))
+            else:
+                branches.append(BRANCH_CROSS)
+                cflag = ((zero - l) > u).astype(F32)
+                keep = (F32(1.0) - cflag).astype(F32)
+                l_new = ((cflag * zero) + (keep * l)).astype(F32)
+                n = l.shape[1]
+                eye = np.eye(n, dtype=F32)
+                Lpoly = ({k - 1: (keep[:, :, None] * eye[None]).astype(F32)}, np.zeros_like(l))
+                # U' = lam * (prev[U] with its neurons replaced by U (coeff >= 0) / L (< 0)) + mu
+                sub_b, sub_c = {}, None
+                for t, M in Ub.items():
+                    Mb = np.broadcast_to(M, (B,) + M.shape[-2:])
+                    Mp, Mn = _split(Mb)
+                    (tLb, tLc), (tUb, tUc) = polys[t]
+                    for s, X in tUb.items():
+                        _add_block(sub_b, s, np.matmul(Mp, X))
+                    for s, X in tLb.items():
+                        _add_block(sub_b, s, np.matmul(Mn, X))
+                    dcc = (np.einsum('bnm,bm->bn', Mp, tUc, dtype=F32) +
+                           np.einsum('bnm,bm->bn', Mn, tLc, dtype=F32)).astype(F32)
+                    sub_c = dcc if sub_c is None else (sub_c + dcc).astype(F32)
+                if sub_c is None:
+                    sub_c = np.zeros_like(l)
+                with np.errstate(divide='ignore', invalid='ignore'):
+                    den = (u - l).astype(F32)
+                    lam = (u / den).astype(F32)
+                    mu = (((u * l).astype(F32) * F32(-1.0)).astype(F32) / den).astype(F32)
+                Uconst = ((lam * (sub_c + Uc).astype(F32)).astype(F32) + mu).astype(F32)
+                Upoly = ({s: (lam[:, :, None] * X).astype(F32) for s, X in sub_b.items()}, Uconst)
+                polys[k] = (Lpoly, Upoly)
+                bounds.append((l_new, u.copy()))
+            continue
+        # affine-type layer (or the appended property layer)
+        if Lyr == 'spec':
+            A0 = np.asarray(spec_W, F32)
+            c0 = np.zeros((B, A0.shape[1]), F32)
+            W_prev = {k - 1: A0}
+        else:
+            A0 = np.ascontiguousarray(_affine_rows(Lyr, 0, Lyr.n_out, B)[0])
+            c0 = np.broadcast_to(layer_bias(Lyr), (B, Lyr.n_out)).astype(F32)
+            W_prev = {k - 1: A0[None]}
+        res = []
+        for lower in (True, False):
+            res.append(_traverse({t: np.array(np.broadcast_to(M, (B,) + M.shape[-2:]), F32)
+                                  for t, M in W_prev.items()}, c0.copy(), polys, lower, order))
+        lo, up = res
+        bounds.append((lo, up))
+        poly = (W_prev, c0)
+        polys[k] = (poly, poly)
+    lb, ub = bounds[-1]
+    return bounds, lb.astype(np.float64), ub.astype(np.float64), branches

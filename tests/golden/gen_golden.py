@@ -9,7 +9,7 @@ box never runs it.  Usage::
 
 For every case it
   1. compiles the reference's own certifier program
-     (examples/compiler_examples/deeppoly.cf or crown.cf) with the reference
+     (examples/compiler_examples/{deeppoly,crown,deeppoly2,deeppoly_efficient}.cf) with the reference
      compiler (constraintflow/compiler/compile.py:66-97) into a scratch dir;
   2. builds the seeded synthetic network in memory (cfgpu/nets.py) and hands it
      to the reference's ONNX reader through the in-memory onnx stand-in
@@ -37,6 +37,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 
+# certifier programs of examples/compiler_examples/ whose generated code is kept and run
+PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient")
+
 # name -> (program, workload id, batch, eps)
 CASES = {
     "dp_w0_b1_e1e-2": ("deeppoly", 0, 1, 0.01),
@@ -57,6 +60,16 @@ CASES = {
     "crown_w0_b4_e1e-3": ("crown", 0, 4, 0.001),
     "crown_w2_b4_e2e-3": ("crown", 2, 4, 0.002),
     "crown_w2_b4_e2e-4": ("crown", 2, 4, 0.0002),
+    # CROWN's whole-layer ReLU branches: eps 0.05 takes the zero branch at the first ReLU,
+    # eps >= 0.1 the all-crossing branch at every ReLU (mixed-layer polyexps)
+    "crown_w0_b2_e5e-2": ("crown", 0, 2, 0.05),
+    "crown_w0_b2_e1e-1": ("crown", 0, 2, 0.1),
+    "crown_w0_b2_e3e-1": ("crown", 0, 2, 0.3),
+    "crown_w1_b2_e5e-2": ("crown", 1, 2, 0.05),
+    "crown_w1_b2_e1e-1": ("crown", 1, 2, 0.1),
+    # deeppoly_efficient.cf: ReLU polyexps over the affine's inputs (prev[L] / prev[U])
+    "dpe_w0_b4_e1e-3": ("deeppoly_efficient", 0, 4, 0.001),
+    "dpe_w2_b4_e2e-4": ("deeppoly_efficient", 2, 4, 0.0002),
 }
 
 
@@ -175,7 +188,7 @@ def worker(program, outdir, case_names):
 def main():
     sel = sys.argv[1:]
     if sel == ["--programs-only"]:
-        for prog in ("deeppoly", "crown"):
+        for prog in PROGRAMS:
             with tempfile.TemporaryDirectory() as tmp:
                 code = ("import sys; sys.path.insert(0, %r); import gen_golden as g; g.worker(%r, %r, [])"
                         % (HERE, prog, os.path.join(tmp, "out")))

@@ -32,3 +32,26 @@ def test_structure_without_device():
         T.inner_prod(x, y)
     assert T.binary(2, 1, operator.sub) == 1
     assert T.clamp(-1.5, 0, True) == 0 and T.clamp(-1.5, 0, False) == -1.5
+
+
+def test_generated_programs_are_recognised():
+    """The reference compiler's own output for deeppoly.cf, deeppoly_efficient.cf and
+    crown.cf (tests/golden/generated/) is recognised by the drop-in Flow without a GPU."""
+    import importlib.util
+    import os
+    import sys
+    from constraintflow.lib.flow_sparse import certifier_of
+    here = os.path.dirname(os.path.abspath(__file__))
+    for program, expect in (("deeppoly", "deeppoly"), ("deeppoly_efficient", "deeppoly"), ("crown", "crown")):
+        path = os.path.join(here, "golden", "generated", program, "transformers.py")
+        saved = sys.modules.pop("transformers", None)
+        try:
+            spec = importlib.util.spec_from_file_location("transformers", path)
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules["transformers"] = mod
+            spec.loader.exec_module(mod)
+            assert certifier_of(mod.deeppoly()) == expect
+        finally:
+            sys.modules.pop("transformers", None)
+            if saved is not None:
+                sys.modules["transformers"] = saved

@@ -1,0 +1,115 @@
+"""GPU parity of the network driver running the reference's CROWN program
+(DeepPolyEngine(certifier='crown') -> cf_deeppoly_run with CF_RELAX_CROWN).
+
+CROWN's ReLU takes one branch per layer for the whole batch (crown.cf:25 as the
+reference compiles it): pass-through and zero run on the GPU and are compared with the
+reference (pass-through golden cases) and the CROWN oracle; the all-crossing branch is
+reported as NotImplementedError.  Tolerances: tests/parity.py.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import parity
+from golden_cases import Case, names
+from oracle import crown_oracle as C
+from oracle import deeppoly_oracle as O
+from cfgpu import nets
+
+pytestmark = pytest.mark.gpu
+
+PASS_CASES = [n for n in names("crown") if Case(n).eps < 0.1]
+CROSS_CASES = [n for n in names("crown") if Case(n).eps >= 0.1]
+
+
+def _engine(wl):
+    from cfgpu.engine import DeepPolyEngine
+    return DeepPolyEngine(wl.layers, wl.input_size, "cuda:0", certifier="crown")
+
+
+def _run(eng, l0, u0, W):
+    dev = torch.device("cuda:0")
+    lb, ub, sl, su = eng.run(torch.from_numpy(l0).to(dev), torch.from_numpy(u0).to(dev),
+                             torch.from_numpy(W).to(dev), want_state=True)
+    torch.cuda.synchronize()
+    return lb.cpu().numpy(), ub.cpu().numpy(), sl.cpu().numpy(), su.cpu().numpy()
+
+
+def _against_oracle(wl, l0, u0, W, lb, sl, su):
+    n0 = wl.input_size
+    bounds, olb, _, br = C.crown(wl.layers, l0, u0, W)
+    ol, ou = O.flatten_bounds(n0, bounds, l0.shape[0])
+    sizes = [L.n_out for L in wl.layers] + [9]
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, sizes)
+    assert worst <= 1.0, f"GPU vs CROWN oracle {worst:.3g}x tolerance at {where}"
+    np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
+    return br
+
+
+@pytest.mark.parametrize("name", PASS_CASES)
+def test_gpu_crown_matches_reference(name):
+    c = Case(name)
+    lb, ub, sl, su = _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
+    n0 = c.wl.input_size
+    assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+    assert _against_oracle(c.wl, c.l0, c.u0, c.spec_W, lb, sl, su) == [C.BRANCH_PASS] * len(c.relu_layers)
+
+
+def test_gpu_crown_zero_branch():
+    wl = nets.workload(1)
+    X = nets.centres(wl, 2)
+    y = nets.labels(wl, X)
+    l0, u0 = (t.numpy() for t in nets.input_box(X, 0.05, wl.dataset))
+    W = nets.spec_weight(y).numpy()
+    lb, ub, sl, su = _run(_engine(wl), l0, u0, W)
+    br = _against_oracle(wl, l0, u0, W, lb, sl, su)
+    assert br[0] == C.BRANCH_ZERO
+
+
+@pytest.mark.parametrize("name", CROSS_CASES)
+def test_gpu_crown_crossing_branch_is_refused(name):
+    c = Case(name)
+    with pytest.raises(NotImplementedError, match="all-crossing"):
+        _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
+
+
+def test_gpu_crown_branch_is_batch_wide():
+    """A region whose box alone makes every neuron cross zero is bounded with the
+    pass-through branch when another region of the same batch has an active neuron."""
+    wl = nets.workload(0)
+    X = nets.centres(wl, 2)
+    y = nets.labels(wl, X)
+    l_small, u_small = (t.numpy() for t in nets.input_box(X[:1], 0.001, wl.dataset))
+    l_big, u_big = (t.numpy() for t in nets.input_box(X[1:], 0.3, wl.dataset))
+    W = nets.spec_weight(y).numpy()
+    eng = _engine(wl)
+    with pytest.raises(NotImplementedError):
+        _run(eng, l_big, u_big, W[1:])
+    l0 = np.concatenate([l_small, l_big])
+    u0 = np.concatenate([u_small, u_big])
+    lb, ub, sl, su = _run(eng, l0, u0, W)
+    assert _against_oracle(wl, l0, u0, W, lb, sl, su) == [C.BRANCH_PASS] * 3
+
+
+def test_gpu_crown_needs_one_chunk():
+    """The C driver refuses a CROWN batch that does not fit one workspace chunk."""
+    from cfgpu import _lib
+    c = Case(PASS_CASES[0])
+    eng = _engine(c.wl)
+    dev = torch.device("cuda:0")
+    l0, u0 = torch.from_numpy(c.l0).to(dev), torch.from_numpy(c.u0).to(dev)
+    W = torch.from_numpy(c.spec_W).to(dev)
+    lb = torch.empty(c.B, 9, dtype=torch.float64, device=dev)
+    ub = torch.empty_like(lb)
+    one = eng.workspace_bytes(1)
+    ws = torch.empty(one, dtype=torch.uint8, device=dev)
+    st = _lib.lib.cf_deeppoly_run(ctypes.byref(eng.net), c.B, l0.data_ptr(), u0.data_ptr(), W.data_ptr(), None,
+                                  None, lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), one,
+                                  torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.CF_ERR_WORKSPACE
+    assert b"whole batch" in _lib.lib.cf_last_error()

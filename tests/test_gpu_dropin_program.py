@@ -1,6 +1,6 @@
-"""The reference compiler's own output for examples/compiler_examples/deeppoly.cf
-(tests/golden/generated/deeppoly/{main.py,transformers.py}, saved by
-tests/golden/gen_golden.py) runs UNCHANGED on this runtime's constraintflow package:
+"""The reference compiler's own output for examples/compiler_examples/{deeppoly,crown,
+deeppoly_efficient}.cf (tests/golden/generated/<program>/{main.py,transformers.py}, saved
+by tests/golden/gen_golden.py) runs UNCHANGED on this runtime's constraintflow package:
 main.run(...) -> (lb, ub) float64, matching the reference's golden bounds."""
 import importlib.util
 import os
@@ -42,14 +42,19 @@ def _load_program(program):
     return main
 
 
-@pytest.mark.parametrize("name", ["dp_w0_b4_e1e-3", "dp_w1_b16_e5e-4", "dp_w2_b8_e2e-4", "dp_w3_b4_e2e-3"])
-def test_generated_deeppoly_program_runs_unchanged(name):
+PROGRAM_CASES = [("deeppoly", n) for n in ("dp_w0_b4_e1e-3", "dp_w1_b16_e5e-4", "dp_w2_b8_e2e-4", "dp_w3_b4_e2e-3")] + \
+    [("crown", n) for n in ("crown_w0_b4_e1e-3", "crown_w2_b4_e2e-4")] + \
+    [("deeppoly_efficient", n) for n in ("dpe_w0_b4_e1e-3", "dpe_w2_b4_e2e-4")]
+
+
+@pytest.mark.parametrize("program,name", PROGRAM_CASES)
+def test_generated_program_runs_unchanged(program, name):
     import onnx
     sys.path.insert(0, os.path.join(HERE, "golden"))
     import gen_golden
     from cfgpu import nets
     c = Case(name)
-    main = _load_program("deeppoly")
+    main = _load_program(program)
     net_name = f"{name}.onnx"
     onnx.register(net_name, gen_golden._onnx_graph(nets, c.wl))
     X = torch.from_numpy(c.X)
@@ -64,8 +69,17 @@ def test_generated_deeppoly_program_runs_unchanged(name):
     assert same
 
 
-def test_other_programs_are_refused():
+def test_programs_are_recognised():
     from constraintflow.lib.flow_sparse import certifier_of
-    crown = _load_program("crown")
+    for program, expect in (("deeppoly", "deeppoly"), ("deeppoly_efficient", "deeppoly"), ("crown", "crown")):
+        assert certifier_of(_load_program(program).deeppoly()) == expect
+
+    class Other:   # some other certifier program: a ReLU without a recognised relaxation
+        def Affine(self, abs_elem, prev, curr):
+            return None
+
+        def Relu(self, abs_elem, prev, curr):
+            return None
+
     with pytest.raises(NotImplementedError):
-        certifier_of(crown.deeppoly())
+        certifier_of(Other())

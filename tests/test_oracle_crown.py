@@ -1,0 +1,82 @@
+"""The CROWN oracle (oracle/crown_oracle.py) against the reference's own CROWN outputs,
+and deeppoly_efficient.cf's reference outputs against the DeepPoly oracle.
+
+The reference cases (tests/golden/crown_*.npz, dpe_*.npz, made by gen_golden.py) cover
+CROWN's pass-through branch (eps 1e-3 .. 1e-2) and its all-crossing branch (eps >= 0.1,
+polyexps that mix layers, where the lowest-layer-first traversal order matters).  The
+reference crashes in CROWN's zero branch (abs_elem.py:929 on a PolyExpSparse built with a
+float matrix), so that branch is checked against its stated semantics instead.
+Tolerances: tests/parity.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+import parity
+from golden_cases import Case, names
+from oracle import crown_oracle as C
+from oracle import deeppoly_oracle as O
+from cfgpu import nets
+
+CROWN_CASES = names("crown")
+DPE_CASES = names("deeppoly_efficient")
+
+
+def _crown(c, **kw):
+    bounds, lb, ub, br = C.crown(c.wl.layers, c.l0, c.u0, c.spec_W, **kw)
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+    return xl, xu, lb, ub, br
+
+
+@pytest.mark.parametrize("name", CROWN_CASES)
+def test_crown_oracle_matches_reference(name):
+    c = Case(name)
+    xl, xu, lb, ub, br = _crown(c)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+    # the branch taken is visible in the reference's ReLU bounds
+    expect = C.BRANCH_CROSS if c.eps >= 0.1 else C.BRANCH_PASS
+    assert br == [expect] * len(br)
+
+
+def test_traversal_order_is_pinned():
+    """A mistake planted in the oracle (highest live layer first) breaks the crossing cases."""
+    c = Case("crown_w0_b2_e1e-1")
+    xl, xu, _, _, _ = _crown(c, order=max)
+    worst, _ = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst > 10.0
+
+
+def test_zero_branch_semantics():
+    """Workload 1 at eps 0.05: the first ReLU takes the zero branch; every later bound is
+    the plain forward pass of the biases (the remaining ReLUs pass through)."""
+    wl = nets.workload(1)
+    X = nets.centres(wl, 2)
+    y = nets.labels(wl, X)
+    l0, u0 = nets.input_box(X, 0.05, wl.dataset)
+    W = nets.spec_weight(y).numpy()
+    bounds, lb, ub, br = C.crown(wl.layers, l0.numpy(), u0.numpy(), W)
+    assert br[0] == C.BRANCH_ZERO and all(b == C.BRANCH_PASS for b in br[1:])
+    h = np.zeros((2, bounds[1][0].shape[1]), np.float32)   # the zeroed ReLU output
+    affine = [L for L in wl.layers if L.kind != "relu"]
+    k = 2
+    for L in affine[1:]:
+        h = (h @ L.W.T.astype(np.float32) + L.b.astype(np.float32)).astype(np.float32)
+        np.testing.assert_allclose(bounds[k][0], h, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(bounds[k][1], h, rtol=1e-5, atol=1e-6)
+        k += 2   # skip the pass-through ReLU (identical bounds)
+    spec = np.einsum('bij,bj->bi', W, h)
+    np.testing.assert_allclose(lb, spec, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(ub, spec, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", DPE_CASES)
+def test_deeppoly_efficient_is_deeppoly(name):
+    """deeppoly_efficient.cf's reference bounds agree with the DeepPoly oracle."""
+    c = Case(name)
+    bounds, lb, _ = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W)
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: DeepPoly oracle vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
