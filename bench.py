@@ -34,7 +34,7 @@ from cfgpu import nets  # noqa: E402
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu capture of
 # the default command (profiles/k_chain_mlp784-200x9_b256.txt); per workload id.
-NCU_TRAFFIC = {2: 10.85e6}
+NCU_TRAFFIC = {2: 10.79e6}
 
 
 def parse():
@@ -69,23 +69,80 @@ def flops_per_region(wl):
 
 
 class Clocks:
-    """nvidia-smi sampler for the timed region (one GPU)."""
+    """SM clock and clock-event-reason sampler for the timed region (one GPU).
 
-    def __init__(self, index, path):
+    NVML queries every 10 ms from a thread (read-only), so that a timed region of tens of
+    milliseconds still gets samples; nvidia-smi -lms 200 when NVML is not importable.
+    Every sample is also written to `path` (CSV) as the record of the run.
+    """
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
+
+    def __init__(self, index, path, device=None):
+        import threading
         self.path = path
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        self.samples = []
+        self.p = None
+        self.thread = None
         try:
-            self.fh = open(path, "w")
-            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}", "--format=csv,noheader",
-                                       "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            if device is not None:
+                try:
+                    uuid = str(torch.cuda.get_device_properties(device).uuid)
+                    h = nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+                except Exception:
+                    h = None
+            if h is None:
+                h = nv.nvmlDeviceGetHandleByIndex(index)
+            self.nv, self.h = nv, h
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.stop_ev = threading.Event()
+
+            def loop():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.samples.append((time.time(), float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                             int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    self.stop_ev.wait(0.01)
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
         except Exception:
-            self.p = None
+            self.thread = None
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            try:
+                self.fh = open(path, "w")
+                self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}",
+                                           "--format=csv,noheader", "-lms", "200"],
+                                          stdout=self.fh, stderr=subprocess.DEVNULL)
+            except Exception:
+                self.p = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            sm, reasons = [], set()
+            with open(self.path, "w") as fh:
+                fh.write("unix_time,sm_mhz,sm_max_mhz,clocks_event_reasons\n")
+                for t, mhz, r in self.samples:
+                    fh.write(f"{t:.3f},{mhz:.0f},{self.max_mhz:.0f},{r:#x}\n")
+                    sm.append(mhz)
+                    for name, bit in self.REASONS:
+                        if r & bit:
+                            reasons.add(name)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 10 ms"}
         if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.p.terminate()
         try:
             self.p.wait(timeout=5)
@@ -107,7 +164,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 def cpu_baseline(wl, sample, reps=3):
@@ -189,8 +246,8 @@ def run_cfgpu(args, rank, world, local):
     # ---- timed region: device events per step, L2 flushed between steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clk = Clocks(local, os.path.join(HERE, "gpurun_out", f"clocks_r{rank}.csv")) if os.path.isdir(
-        os.path.join(HERE, "gpurun_out")) else Clocks(local, f"/tmp/cf_clocks_r{rank}.csv")
+    clk = Clocks(local, os.path.join(HERE, "gpurun_out", f"clocks_r{rank}.csv") if os.path.isdir(
+        os.path.join(HERE, "gpurun_out")) else f"/tmp/cf_clocks_r{rank}.csv", device=dev)
     barrier()
     torch.cuda.synchronize()
     profile_enable(True)
