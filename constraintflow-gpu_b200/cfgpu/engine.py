@@ -24,8 +24,8 @@ class DeepPolyEngine:
     ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers.
     certifier: 'deeppoly' (deeppoly.cf, deeppoly_efficient.cf) or 'crown' (crown.cf, whose
     ReLU branch is decided over the whole batch: a CROWN run always takes the batch in
-    one workspace chunk and checks the device status, raising NotImplementedError when
-    a layer takes the all-crossing branch).
+    one workspace chunk and checks the device status; when a layer takes the all-crossing
+    branch the bounds are recomputed by the general traversal of cfgpu.crown).
     """
 
     def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
@@ -39,6 +39,7 @@ class DeepPolyEngine:
             raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly and crown)")
         self.certifier = certifier
         self._keep = []
+        self._general = []        # (kind, W, b) device tensors for cfgpu.crown
         descs = []
         width = self.input_size
         for L in layers:
@@ -46,10 +47,12 @@ class DeepPolyEngine:
             if L.kind == "relu":
                 d.kind = _lib.CF_LAYER_RELU
                 d.n_in = d.n_out = width
+                self._general.append(("relu", None, None))
             else:
                 W = torch.as_tensor(L.W, dtype=torch.float32).to(self.device).contiguous()
                 b = torch.as_tensor(L.b, dtype=torch.float32).to(self.device).contiguous()
                 self._keep += [W, b]
+                self._general.append((L.kind, W, b))
                 d.W_dev, d.b_dev = W.data_ptr(), b.data_ptr()
                 if L.kind == "linear":
                     d.kind = _lib.CF_LAYER_LINEAR
@@ -116,11 +119,31 @@ class DeepPolyEngine:
                                  su.data_ptr() if su is not None else None,
                                  lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         check(st, "cf_deeppoly_run")
-        if check_device or self.certifier == "crown":
+        if self.certifier == "crown":
+            st = lib.cf_deeppoly_check(ws.data_ptr(), stream)
+            if st == _lib.CF_ERR_UNSUPPORTED:
+                # a ReLU layer took the all-crossing branch: its polyexps mix layers
+                lb, ub, sl_g, su_g = self._crown_general(l0, u0, spec_W, lb, ub)
+                if want_state:
+                    sl.copy_(sl_g)
+                    su.copy_(su_g)
+            else:
+                check(st, "device status")
+        elif check_device:
             check(lib.cf_deeppoly_check(ws.data_ptr(), stream), "device status")
         if want_state:
             return lb, ub, sl, su
         return lb, ub
+
+    def _crown_general(self, l0, u0, spec_W, lb, ub):
+        """CROWN bounds through the general lowest-layer-first traversal (cfgpu.crown)."""
+        from . import crown
+        bounds, _ = crown.run(self._general, l0, u0, spec_W)
+        sl = torch.cat([l0] + [b[0] for b in bounds], dim=1)
+        su = torch.cat([u0] + [b[1] for b in bounds], dim=1)
+        lb.copy_(bounds[-1][0])
+        ub.copy_(bounds[-1][1])
+        return lb, ub, sl, su
 
     def input_spec(self, X, y, eps, dataset):
         """Device input box and property matrix from device centres X [B,C,H,W] and labels y [B].

@@ -1,0 +1,120 @@
+"""Tensor-level wrappers over libcfgpu's block kernels (cf_ew_binary, cf_ew_unary,
+cf_ew_where, cf_ew_clamp, cf_ew_any, cf_bmm), used by the gbcsr mirror
+(constraintflow.gbcsr) and by the general CROWN traversal (cfgpu.crown).
+
+Operands are CUDA tensors, possibly broadcast views (zero strides); results are new
+contiguous tensors.  PyTorch only allocates the memory and supplies the stream.
+"""
+import operator
+
+import torch
+
+from cfgpu import _lib
+
+_OPS = {operator.add: "add", operator.sub: "sub", operator.mul: "mul", operator.truediv: "truediv",
+        operator.ge: "ge", operator.gt: "gt", operator.le: "le", operator.lt: "lt", operator.eq: "eq",
+        operator.ne: "ne", operator.and_: "and_", operator.or_: "or_"}
+COMPARISONS = (operator.lt, operator.le, operator.eq, operator.ne, operator.gt, operator.ge, operator.and_,
+               operator.or_)
+
+
+def device():
+    if not torch.cuda.is_available():
+        raise RuntimeError("the gbcsr ops run on a CUDA device only (libcfgpu); no CPU fallback")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dt(t):
+    return _lib.CF_BOOL if t.dtype == torch.bool else _lib.CF_F32
+
+
+def _geo(t):
+    return _lib.i64_array(list(t.shape)), _lib.i64_array(list(t.stride()))
+
+
+def as_block_tensor(x, dtype=None):
+    """A block payload on the device: bool stays bool, every other dtype becomes float32."""
+    t = torch.as_tensor(x)
+    if dtype is None:
+        dtype = torch.bool if t.dtype == torch.bool else torch.float32
+    return t.to(device=device(), dtype=dtype)
+
+
+def scalar_view(value, shape, dtype):
+    """A fill value broadcast to `shape` without materialising it (all strides zero)."""
+    t = torch.tensor(value, dtype=dtype, device=device())
+    return t.expand(*shape) if len(shape) else t
+
+
+def binary(op, a, b, out_dtype):
+    assert a.shape == b.shape, (a.shape, b.shape)
+    out = torch.empty(a.shape, dtype=out_dtype, device=a.device)
+    if out.numel() == 0:
+        return out
+    shp, sa = _geo(a)
+    _, sb = _geo(b)
+    st = _lib.lib.cf_ew_binary(_lib.OPS[_OPS[op]], a.dim(), shp, a.data_ptr(), _dt(a), sa, b.data_ptr(), _dt(b), sb,
+                               out.data_ptr(), _dt(out), _stream())
+    _lib.check(st, "cf_ew_binary")
+    return out
+
+
+def unary(name, a, out_dtype):
+    out = torch.empty(a.shape, dtype=out_dtype, device=a.device)
+    if out.numel() == 0:
+        return out
+    shp, sa = _geo(a)
+    st = _lib.lib.cf_ew_unary(_lib.UOPS[name], a.dim(), shp, a.data_ptr(), _dt(a), sa, out.data_ptr(), _dt(out),
+                              _stream())
+    _lib.check(st, "cf_ew_unary")
+    return out
+
+
+def where(c, y, z):
+    out = torch.empty(c.shape, dtype=torch.float32, device=c.device)
+    if out.numel() == 0:
+        return out
+    shp, sc = _geo(c)
+    _, sy = _geo(y)
+    _, sz = _geo(z)
+    st = _lib.lib.cf_ew_where(c.dim(), shp, c.data_ptr(), sc, y.data_ptr(), sy, z.data_ptr(), sz, out.data_ptr(),
+                              _lib.CF_F32, _stream())
+    _lib.check(st, "cf_ew_where")
+    return out
+
+
+def clamp(a, const, min_true):
+    out = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    if out.numel() == 0:
+        return out
+    shp, sa = _geo(a)
+    st = _lib.lib.cf_ew_clamp(a.dim(), shp, a.data_ptr(), sa, float(const), 1 if min_true else 0, out.data_ptr(),
+                              _stream())
+    _lib.check(st, "cf_ew_clamp")
+    return out
+
+
+def any_nonzero(a):
+    if a.numel() == 0:
+        return False
+    flag = torch.zeros(1, dtype=torch.int32, device=a.device)
+    shp, sa = _geo(a)
+    st = _lib.lib.cf_ew_any(a.dim(), shp, a.data_ptr(), _dt(a), sa, flag.data_ptr(), _stream())
+    _lib.check(st, "cf_ew_any")
+    return bool(flag.item())
+
+
+def bmm(A, B, C=None, accumulate=False):
+    """C[b] (+)= A[b] @ B[b]; A [nb, M, K], B [nb, K, N] strided views."""
+    nb, M, K = A.shape
+    N = B.shape[2]
+    if C is None:
+        C = torch.empty(nb, M, N, dtype=torch.float32, device=A.device)
+    st = _lib.lib.cf_bmm(nb, M, N, K, A.data_ptr(), A.stride(0), A.stride(1), A.stride(2), B.data_ptr(),
+                         B.stride(0), B.stride(1), B.stride(2), C.data_ptr(), 1 if accumulate else 0, _stream())
+    _lib.check(st, "cf_bmm")
+    return C

@@ -145,11 +145,84 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
   }
 }
 
+// Rows shared by every region and both bounds (the first affine layer: its W rows against
+// each region's box) are two sign-split GEMMs [B, n0] x [n0, R]:
+//   out_l[b,i] = c[i] + sum_n W+[i,n] l0[b,n] + W-[i,n] u0[b,n]
+//   out_u[b,i] = c[i] + sum_n W+[i,n] u0[b,n] + W-[i,n] l0[b,n]
+// CTA tile: 64 rows x 64 regions, 32-wide k slices of W (split into W+ / W-) and of both
+// boxes in shared memory; 16x16 threads, 4 rows x 4 regions x 2 bounds each.
+constexpr int kCbT = 64, kCbK = 32;
+__global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
+                                                          int64_t a_rs, const float* __restrict__ c,
+                                                          const float* __restrict__ l0, const float* __restrict__ u0,
+                                                          float* __restrict__ out_l, float* __restrict__ out_u,
+                                                          int64_t ld_out) {
+  __shared__ __align__(16) float Wp[kCbK][kCbT + 4];
+  __shared__ __align__(16) float Wn[kCbK][kCbT + 4];
+  __shared__ __align__(16) float Ls[kCbK][kCbT + 4];
+  __shared__ __align__(16) float Us[kCbK][kCbT + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t i0 = (int64_t)blockIdx.x * kCbT, b0 = (int64_t)blockIdx.y * kCbT;
+  float lo[4][4], up[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) lo[a][q] = up[a][q] = 0.0f;
+  for (int64_t k0 = 0; k0 < n0; k0 += kCbK) {
+    for (int e = tid; e < kCbT * kCbK; e += 256) {
+      const int r = e / kCbK, kk = e - r * kCbK;
+      const int64_t k = k0 + kk, i = i0 + r, b = b0 + r;
+      const float w = (i < R && k < n0) ? A[i * a_rs + k] : 0.0f;
+      Wp[kk][r] = fmaxf(w, 0.0f);
+      Wn[kk][r] = fminf(w, 0.0f);
+      Ls[kk][r] = (b < B && k < n0) ? l0[b * n0 + k] : 0.0f;
+      Us[kk][r] = (b < B && k < n0) ? u0[b * n0 + k] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kCbK; ++kk) {
+      const float4 wp = *reinterpret_cast<const float4*>(&Wp[kk][ty * 4]);
+      const float4 wn = *reinterpret_cast<const float4*>(&Wn[kk][ty * 4]);
+      const float4 lv = *reinterpret_cast<const float4*>(&Ls[kk][tx * 4]);
+      const float4 uv = *reinterpret_cast<const float4*>(&Us[kk][tx * 4]);
+      const float wpa[4] = {wp.x, wp.y, wp.z, wp.w}, wna[4] = {wn.x, wn.y, wn.z, wn.w};
+      const float la[4] = {lv.x, lv.y, lv.z, lv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          lo[a][q] = fmaf(wpa[a], la[q], fmaf(wna[a], ua[q], lo[a][q]));
+          up[a][q] = fmaf(wpa[a], ua[q], fmaf(wna[a], la[q], up[a][q]));
+        }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int64_t i = i0 + ty * 4 + a;
+    if (i >= R) continue;
+    const float cv = c ? c[i] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int64_t b = b0 + tx * 4 + q;
+      if (b >= B) continue;
+      out_l[b * ld_out + i] = lo[a][q] + cv;
+      out_u[b * ld_out + i] = up[a][q] + cv;
+    }
+  }
+}
+
 cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
                             const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
   int64_t rows = 2 * B * R;
   if (rows == 0) return CF_OK;
+  const int64_t gx = ceil_div(R, kCbT), gy = ceil_div(B, kCbT);
+  if (a_ss == 0 && a_bs == 0 && c_ss == 0 && c_bs == 0 && gx <= 0x7fffffff && gy <= 65535) {
+    k_concretize_bcast<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(B, R, n0, A, a_rs, c, l0, u0, out_l, out_u,
+                                                                         ld_out);
+    return check_launch("k_concretize_bcast");
+  }
   int threads = 256;
   int64_t blocks = ceil_div(rows * 32, threads);
   if (blocks > 148 * 32) blocks = 148 * 32;

@@ -2,9 +2,10 @@
 (DeepPolyEngine(certifier='crown') -> cf_deeppoly_run with CF_RELAX_CROWN).
 
 CROWN's ReLU takes one branch per layer for the whole batch (crown.cf:25 as the
-reference compiles it): pass-through and zero run on the GPU and are compared with the
-reference (pass-through golden cases) and the CROWN oracle; the all-crossing branch is
-reported as NotImplementedError.  Tolerances: tests/parity.py.
+reference compiles it): pass-through and zero run in the fused driver; the all-crossing
+branch (mixed-layer polyexps) runs the general traversal of cfgpu.crown.  Every case is
+compared with the reference's golden bounds where the reference has them and with the
+CROWN oracle.  Tolerances: tests/parity.py.
 """
 import ctypes
 
@@ -72,15 +73,20 @@ def test_gpu_crown_zero_branch():
 
 
 @pytest.mark.parametrize("name", CROSS_CASES)
-def test_gpu_crown_crossing_branch_is_refused(name):
+def test_gpu_crown_crossing_branch_matches_reference(name):
     c = Case(name)
-    with pytest.raises(NotImplementedError, match="all-crossing"):
-        _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
+    lb, ub, sl, su = _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
+    n0 = c.wl.input_size
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+    assert _against_oracle(c.wl, c.l0, c.u0, c.spec_W, lb, sl, su) == [C.BRANCH_CROSS] * len(c.relu_layers)
 
 
 def test_gpu_crown_branch_is_batch_wide():
-    """A region whose box alone makes every neuron cross zero is bounded with the
-    pass-through branch when another region of the same batch has an active neuron."""
+    """A region whose box alone makes every neuron cross zero (all-crossing branch) is
+    bounded with the pass-through branch when another region of the same batch has an
+    active neuron."""
     wl = nets.workload(0)
     X = nets.centres(wl, 2)
     y = nets.labels(wl, X)
@@ -88,8 +94,8 @@ def test_gpu_crown_branch_is_batch_wide():
     l_big, u_big = (t.numpy() for t in nets.input_box(X[1:], 0.3, wl.dataset))
     W = nets.spec_weight(y).numpy()
     eng = _engine(wl)
-    with pytest.raises(NotImplementedError):
-        _run(eng, l_big, u_big, W[1:])
+    lb1, _, sl1, su1 = _run(eng, l_big, u_big, W[1:])
+    assert _against_oracle(wl, l_big, u_big, W[1:], lb1, sl1, su1) == [C.BRANCH_CROSS] * 3
     l0 = np.concatenate([l_small, l_big])
     u0 = np.concatenate([u_small, u_big])
     lb, ub, sl, su = _run(eng, l0, u0, W)
