@@ -10,10 +10,10 @@
 //   k_win_relu_bias  per row (one block): in-place sign split with the region's relaxation
 //                    at the window's absolute positions (zero outside the image), and the
 //                    constant += mu-terms + sum T(a) * bias_j[c] (deterministic tree sum);
-//   k_win_convT      the transposed convolution of every window (the adjoint of conv_j,
-//                    constraintflow/gbcsr/sparse_block.py:839-928 conv_transpose2d),
-//                    producing the window one level down; positions that fall in conv_j's
-//                    zero padding are dropped (set to 0).
+//   k_win_convT_gemm the transposed convolution of every window (the adjoint of conv_j,
+//                    constraintflow/gbcsr/sparse_block.py:839-928 conv_transpose2d) as one
+//                    implicit GEMM per stride phase, producing the window one level down;
+//                    positions that fall in conv_j's zero padding are dropped (set to 0).
 // Linear layers use the dense step GEMM on the (already transformed) rows.
 // k_win_init places a conv kernel (or a linear row) as the first window, and
 // k_win_concretize folds the input box in at level 0.  All CUDA-core float32.
@@ -131,46 +131,108 @@ __global__ void __launch_bounds__(256) k_win_relu_bias(RowGeom rg, WinGeom g, fl
 }
 
 // ------------------------------------------------------------------ transposed conv
-// out[r, ci, Y', X'] = sum_{co,ky,kx} in[r, co, Y, X] * W[co, ci, ky, kx] with
-// Y' = Y*s - p + ky (absolute image coordinates; input positions outside the input window
-// hold zero), and 0 where (Y', X') lies outside the level image (the conv's zero padding).
-// One thread per output element; W read through the L1 cache.
-__global__ void k_win_convT(RowGeom rg, WinGeom gi, WinGeom go, ConvGeom cv, const float* __restrict__ in,
-                            const float* __restrict__ W, float* __restrict__ out) {
-  const int64_t per_in = (int64_t)gi.C * gi.Ph * gi.Pw;
-  const int64_t per_out = (int64_t)go.C * go.Ph * go.Pw;
-  const int64_t total = 2 * rg.B * rg.R * per_out;
-  const int khw = cv.kh * cv.kw;
-  const int64_t a_step = (int64_t)gi.Ph * gi.Pw, w_step = (int64_t)cv.cin * khw;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / per_out, e = t - r * per_out;
-    int64_t s, b, i;
-    int oy, ox;
-    row_coords(rg, r, s, b, i, oy, ox);
-    const WinPos p = win_pos(go, e, oy, ox);
-    float acc = 0.0f;
-    if (p.in) {
-      const int y0 = oy * gi.sig_h - gi.pi_h, x0 = ox * gi.sig_w - gi.pi_w;
-      const float* a = in + r * per_in;
-      const float* wc = W + (int64_t)p.c * khw;
-      for (int ky = 0; ky < cv.kh; ++ky) {
-        const int ty = p.Y + cv.pad - ky;
-        if (ty < 0 || ty % cv.s) continue;
-        const int u = ty / cv.s - y0;
-        if (u < 0 || u >= gi.Ph) continue;
-        for (int kx = 0; kx < cv.kw; ++kx) {
-          const int tx = p.X + cv.pad - kx;
-          if (tx < 0 || tx % cv.s) continue;
-          const int v = tx / cv.s - x0;
-          if (v < 0 || v >= gi.Pw) continue;
-          const float* ain = a + (int64_t)u * gi.Pw + v;
-          const float* w = wc + ky * cv.kw + kx;
+// out[r, ci, u', v'] = sum_{co,ky,kx} in[r, co, u, v] * W[co, ci, ky, kx] over window
+// coordinates, where the conv maps input-window position (u, v) of row r and tap (ky, kx)
+// to output-window position u' = u*s + ky - D (D = pi_in*s + pad - pi_out: 0 for
+// receptive-field windows, pad for whole-image windows), and 0 where (u', v') lies outside
+// the level image (the conv's zero padding).  Since u' + D = u*s + ky, the output positions
+// split into s*s stride phases (py, px) = ((u'+D) mod s, (v'+D) mod s), and within a phase
+// only taps ky = py + ty*s, kx = px + tx*s contribute, at u = qy - ty, v = qx - tx with
+// qy = (u' + D - py)/s.  Each phase is an implicit GEMM
+//   M = rows x (phase positions), K = Cout x (phase taps), N = cin,
+// A gathered from the input windows (zero outside them), B = the phase's weight taps.
+// CTA tile 128 x BN, k slices of 32 in shared memory; 16 x 16 threads, 8 x BN/16 outputs each.
+template <int BN>
+__global__ void __launch_bounds__(256) k_win_convT_gemm(RowGeom rg, WinGeom gi, WinGeom go, ConvGeom cv,
+                                                        ConvPhase ph, const float* __restrict__ in,
+                                                        const float* __restrict__ W, float* __restrict__ out) {
+  constexpr int BM = kTcBM, BK = 32, TN = BN / 16;
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  const int tid = threadIdx.x, tm = tid >> 4, tn = tid & 15;
+  const int pos = ph.ny * ph.nx, taps = ph.tyn * ph.txn;
+  const int64_t M = 2 * rg.B * rg.R * pos;
+  const int K = gi.C * taps;
+  const int64_t m0 = (int64_t)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  const int64_t plane_in = (int64_t)gi.Ph * gi.Pw, per_in = gi.C * plane_in;
+  // the A element this thread gathers in every k slice: m = m0 + (tid % BM), k = k0 + tid/BM + 2j
+  const int a_mm = tid % BM;
+  const int64_t a_m = m0 + a_mm;
+  const float* a_row = nullptr;
+  int a_qy = 0, a_qx = 0;
+  if (a_m < M) {
+    const int64_t r = a_m / pos;
+    const int rem = (int)(a_m - r * pos);
+    const int iy = rem / ph.nx;
+    a_qy = ph.q0y + iy;
+    a_qx = ph.q0x + (rem - iy * ph.nx);
+    a_row = in + r * per_in;
+  }
+  float acc[8][TN];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += BK) {
 #pragma unroll 4
-          for (int co = 0; co < gi.C; ++co) acc = fmaf(ain[co * a_step], __ldg(w + co * w_step), acc);
-        }
+    for (int kk = tid / BM; kk < BK; kk += 256 / BM) {
+      const int k = k0 + kk;
+      float val = 0.0f;
+      if (a_row && k < K) {
+        const int co = k / taps, t = k - co * taps, ty = t / ph.txn, tx = t - ty * ph.txn;
+        const int u = a_qy - ty, v = a_qx - tx;
+        if (u >= 0 && u < gi.Ph && v >= 0 && v < gi.Pw) val = a_row[co * plane_in + u * gi.Pw + v];
       }
+      As[kk][a_mm] = val;
     }
-    out[t] = acc;
+    for (int e = tid; e < BK * BN; e += 256) {
+      const int nn = e % BN, kk = e / BN;
+      const int k = k0 + kk, ci = n0 + nn;
+      float val = 0.0f;
+      if (k < K && ci < cv.cin) {
+        const int co = k / taps, t = k - co * taps, ty = t / ph.txn, tx = t - ty * ph.txn;
+        const int ky = ph.py + ty * cv.s, kx = ph.px + tx * cv.s;
+        val = __ldg(W + (((int64_t)co * cv.cin + ci) * cv.kh + ky) * cv.kw + kx);
+      }
+      Bs[kk][nn] = val;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][tm * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][tm * 8 + 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float b[TN];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tn * TN + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  const int64_t plane_out = (int64_t)go.Ph * go.Pw, per_out = go.C * plane_out;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + tm * 8 + i;
+    if (m >= M) continue;
+    const int64_t r = m / pos;
+    const int rem = (int)(m - r * pos);
+    const int iy = rem / ph.nx, ix = rem - iy * ph.nx;
+    const int uo = ph.u0 + iy * cv.s, vo = ph.v0 + ix * cv.s;
+    int64_t sb, b, ri;
+    int oy, ox;
+    row_coords(rg, r, sb, b, ri, oy, ox);
+    const int Y = oy * go.sig_h - go.pi_h + uo, X = ox * go.sig_w - go.pi_w + vo;
+    const bool inside = Y >= 0 && Y < go.H && X >= 0 && X < go.W;
+    float* o = out + r * per_out + (int64_t)uo * go.Pw + vo;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int ci = n0 + tn * TN + j;
+      if (ci < cv.cin) o[ci * plane_out] = inside ? acc[i][j] : 0.0f;
+    }
   }
 }
 
@@ -258,10 +320,36 @@ cf_status win_relu_bias(const RowGeom& rg, const WinGeom& g, float* A, const flo
 
 cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
                     const float* W, float* out, cudaStream_t st) {
-  const int64_t total = 2 * rg.B * rg.R * (int64_t)go.C * go.Ph * go.Pw;
-  if (total == 0) return CF_OK;
-  k_win_convT<<<grid_for(total, 256, 148 * 64), 256, 0, st>>>(rg, gi, go, cv, in, W, out);
-  return check_launch("k_win_convT");
+  const int64_t rows = 2 * rg.B * rg.R;
+  if (rows * go.C * go.Ph * go.Pw == 0) return CF_OK;
+  const int s = cv.s;
+  // window-relative input index u = (u' + D - ky) / s (see k_win_convT_gemm)
+  const int Dy = gi.pi_h * s + cv.pad - go.pi_h, Dx = gi.pi_w * s + cv.pad - go.pi_w;
+  for (int py = 0; py < s; ++py) {
+    const int u0 = ((py - Dy) % s + s) % s;
+    const int ny = u0 < go.Ph ? (go.Ph - u0 + s - 1) / s : 0;
+    const int tyn = cv.kh > py ? (cv.kh - py + s - 1) / s : 0;
+    for (int px = 0; px < s; ++px) {
+      const int v0 = ((px - Dx) % s + s) % s;
+      const int nx = v0 < go.Pw ? (go.Pw - v0 + s - 1) / s : 0;
+      const int txn = cv.kw > px ? (cv.kw - px + s - 1) / s : 0;
+      if (ny == 0 || nx == 0) continue;
+      ConvPhase ph{py, px, ny, nx, tyn, txn, u0, v0, (u0 + Dy - py) / s, (v0 + Dx - px) / s};
+      const int64_t M = rows * ny * nx;
+      const int64_t gx = (M + kTcBM - 1) / kTcBM;
+      CF_REQUIRE(gx <= 0x7fffffff, CF_ERR_SHAPE, "convT: %lld output positions", (long long)M);
+      if (cv.cin > 32) {
+        k_win_convT_gemm<64><<<dim3((unsigned)gx, (unsigned)((cv.cin + 63) / 64)), 256, 0, st>>>(rg, gi, go, cv, ph,
+                                                                                                 in, W, out);
+      } else if (cv.cin > 16) {
+        k_win_convT_gemm<32><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
+      } else {
+        k_win_convT_gemm<16><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
+      }
+      CF_TRY(check_launch("k_win_convT_gemm"));
+    }
+  }
+  return CF_OK;
 }
 
 cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, const float* c, const float* l0,

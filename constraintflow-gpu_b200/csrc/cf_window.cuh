@@ -17,7 +17,7 @@ struct WinGeom {
   int32_t C, H, W, Ph, Pw, sig_h, sig_w, pi_h, pi_w;
 };
 
-// The convolution substituted by k_win_convT: weights [Cout, cin, kh, kw], stride s, pad.
+// The convolution substituted by k_win_convT_gemm: weights [Cout, cin, kh, kw], stride s, pad.
 struct ConvGeom {
   int32_t cin, kh, kw, s, pad;
 };
@@ -28,6 +28,14 @@ cf_status win_row_bias(const RowGeom& rg, const float* bias, bool conv, float* c
 cf_status win_relu_bias(const RowGeom& rg, const WinGeom& g, float* A, const float* c_in, int64_t c_ss, int64_t c_bs,
                         const float* alpha, const float* lam, const float* mu, const float* bias, float* c_out,
                         cudaStream_t st);
+// One stride phase of the transposed convolution (k_win_convT_gemm): output-window rows
+// u' = u0 + iy*s (iy < ny), columns v' = v0 + ix*s (ix < nx), taps ky = py + ty*s (ty < tyn),
+// kx = px + tx*s (tx < txn), input-window index u = q0y + iy - ty, v = q0x + ix - tx.
+struct ConvPhase {
+  int32_t py, px, ny, nx, tyn, txn, u0, v0, q0y, q0x;
+};
+constexpr int kTcBM = 128;  // output positions per CTA of k_win_convT_gemm
+
 cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
                     const float* W, float* out, cudaStream_t st);
 cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, const float* c, const float* l0,
