@@ -141,50 +141,66 @@ __global__ void __launch_bounds__(256) k_win_relu_bias(RowGeom rg, WinGeom g, fl
 // qy = (u' + D - py)/s.  Each phase is an implicit GEMM
 //   M = rows x (phase positions), K = Cout x (phase taps), N = cin,
 // A gathered from the input windows (zero outside them), B = the phase's weight taps.
-// CTA tile 128 x BN, k slices of 32 in shared memory; 16 x 16 threads, 8 x BN/16 outputs each.
-template <int BN>
+// CTA tile BM x BN, k slices of BK in shared memory; 256 threads, TM x TN outputs each.
+template <int BM, int BN, int TM, int TN, int BK>
 __global__ void __launch_bounds__(256) k_win_convT_gemm(RowGeom rg, WinGeom gi, WinGeom go, ConvGeom cv,
                                                         ConvPhase ph, const float* __restrict__ in,
                                                         const float* __restrict__ W, float* __restrict__ out) {
-  constexpr int BM = kTcBM, BK = 32, TN = BN / 16;
+  static_assert((BM / TM) * (BN / TN) == 256, "256 threads");
+  static_assert(BM % 256 == 0 || 256 % BM == 0, "A tile mapping");
+  constexpr int MPT = BM >= 256 ? BM / 256 : 1;   // A rows gathered by each thread
+  constexpr int KSTEP = BM >= 256 ? 1 : 256 / BM;  // k stride of a thread's A loads
   __shared__ __align__(16) float As[BK][BM + 4];
   __shared__ __align__(16) float Bs[BK][BN + 4];
-  const int tid = threadIdx.x, tm = tid >> 4, tn = tid & 15;
+  const int tid = threadIdx.x, tn = tid % (BN / TN), tm = tid / (BN / TN);
   const int pos = ph.ny * ph.nx, taps = ph.tyn * ph.txn;
   const int64_t M = 2 * rg.B * rg.R * pos;
   const int K = gi.C * taps;
   const int64_t m0 = (int64_t)blockIdx.x * BM;
   const int n0 = blockIdx.y * BN;
   const int64_t plane_in = (int64_t)gi.Ph * gi.Pw, per_in = gi.C * plane_in;
-  // the A element this thread gathers in every k slice: m = m0 + (tid % BM), k = k0 + tid/BM + 2j
-  const int a_mm = tid % BM;
-  const int64_t a_m = m0 + a_mm;
-  const float* a_row = nullptr;
-  int a_qy = 0, a_qx = 0;
-  if (a_m < M) {
-    const int64_t r = a_m / pos;
-    const int rem = (int)(a_m - r * pos);
-    const int iy = rem / ph.nx;
-    a_qy = ph.q0y + iy;
-    a_qx = ph.q0x + (rem - iy * ph.nx);
-    a_row = in + r * per_in;
-  }
-  float acc[8][TN];
+  // the A rows this thread gathers in every k slice: m = m0 + (tid % BM) + 256*x
+  const float* a_row[MPT];
+  int a_qy[MPT], a_qx[MPT];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int x = 0; x < MPT; ++x) {
+    const int64_t m = m0 + (tid % BM) + 256 * x;
+    a_row[x] = nullptr;
+    a_qy[x] = a_qx[x] = 0;
+    if (m < M) {
+      const int64_t r = m / pos;
+      const int rem = (int)(m - r * pos);
+      const int iy = rem / ph.nx;
+      a_qy[x] = ph.q0y + iy;
+      a_qx[x] = ph.q0x + (rem - iy * ph.nx);
+      a_row[x] = in + r * per_in;
+    }
+  }
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
   for (int k0 = 0; k0 < K; k0 += BK) {
 #pragma unroll 4
-    for (int kk = tid / BM; kk < BK; kk += 256 / BM) {
+    for (int kk = BM >= 256 ? 0 : tid / BM; kk < BK; kk += KSTEP) {
       const int k = k0 + kk;
-      float val = 0.0f;
-      if (a_row && k < K) {
-        const int co = k / taps, t = k - co * taps, ty = t / ph.txn, tx = t - ty * ph.txn;
-        const int u = a_qy - ty, v = a_qx - tx;
-        if (u >= 0 && u < gi.Ph && v >= 0 && v < gi.Pw) val = a_row[co * plane_in + u * gi.Pw + v];
+      int co = 0, u_off = 0, v_off = 0;
+      if (k < K) {
+        co = k / taps;
+        const int t = k - co * taps, ty = t / ph.txn;
+        u_off = ty;
+        v_off = t - ty * ph.txn;
       }
-      As[kk][a_mm] = val;
+#pragma unroll
+      for (int x = 0; x < MPT; ++x) {
+        float val = 0.0f;
+        if (a_row[x] && k < K) {
+          const int u = a_qy[x] - u_off, v = a_qx[x] - v_off;
+          if (u >= 0 && u < gi.Ph && v >= 0 && v < gi.Pw) val = a_row[x][co * plane_in + u * gi.Pw + v];
+        }
+        As[kk][(tid % BM) + 256 * x] = val;
+      }
     }
     for (int e = tid; e < BK * BN; e += 256) {
       const int nn = e % BN, kk = e / BN;
@@ -200,14 +216,19 @@ __global__ void __launch_bounds__(256) k_win_convT_gemm(RowGeom rg, WinGeom gi, 
     __syncthreads();
 #pragma unroll 8
     for (int kk = 0; kk < BK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][tm * 8]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][tm * 8 + 4]);
-      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      float b[TN];
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; i += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(&As[kk][tm * TM + i]);
+        a[i] = q.x;
+        a[i + 1] = q.y;
+        a[i + 2] = q.z;
+        a[i + 3] = q.w;
+      }
 #pragma unroll
       for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tn * TN + j];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < TM; ++i)
 #pragma unroll
         for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
@@ -215,8 +236,8 @@ __global__ void __launch_bounds__(256) k_win_convT_gemm(RowGeom rg, WinGeom gi, 
   }
   const int64_t plane_out = (int64_t)go.Ph * go.Pw, per_out = go.C * plane_out;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int64_t m = m0 + tm * 8 + i;
+  for (int i = 0; i < TM; ++i) {
+    const int64_t m = m0 + tm * TM + i;
     if (m >= M) continue;
     const int64_t r = m / pos;
     const int rem = (int)(m - r * pos);
@@ -336,15 +357,20 @@ cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, con
       if (ny == 0 || nx == 0) continue;
       ConvPhase ph{py, px, ny, nx, tyn, txn, u0, v0, (u0 + Dy - py) / s, (v0 + Dx - px) / s};
       const int64_t M = rows * ny * nx;
-      const int64_t gx = (M + kTcBM - 1) / kTcBM;
+      const int bm = cv.cin > 4 ? 128 : 1024;
+      const int64_t gx = (M + bm - 1) / bm;
       CF_REQUIRE(gx <= 0x7fffffff, CF_ERR_SHAPE, "convT: %lld output positions", (long long)M);
+      // tile by input-channel count: 128 positions x 64/32/16 channels, or 1024 x 4 for the
+      // first layer of an image network (cin <= 4)
       if (cv.cin > 32) {
-        k_win_convT_gemm<64><<<dim3((unsigned)gx, (unsigned)((cv.cin + 63) / 64)), 256, 0, st>>>(rg, gi, go, cv, ph,
-                                                                                                 in, W, out);
+        k_win_convT_gemm<128, 64, 8, 4, 32><<<dim3((unsigned)gx, (unsigned)((cv.cin + 63) / 64)), 256, 0, st>>>(
+            rg, gi, go, cv, ph, in, W, out);
       } else if (cv.cin > 16) {
-        k_win_convT_gemm<32><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
+        k_win_convT_gemm<128, 32, 8, 2, 32><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
+      } else if (cv.cin > 4) {
+        k_win_convT_gemm<128, 16, 8, 1, 32><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
       } else {
-        k_win_convT_gemm<16><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
+        k_win_convT_gemm<1024, 4, 4, 4, 8><<<dim3((unsigned)gx, 1), 256, 0, st>>>(rg, gi, go, cv, ph, in, W, out);
       }
       CF_TRY(check_launch("k_win_convT_gemm"));
     }

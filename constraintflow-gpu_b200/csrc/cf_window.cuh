@@ -34,7 +34,6 @@ cf_status win_relu_bias(const RowGeom& rg, const WinGeom& g, float* A, const flo
 struct ConvPhase {
   int32_t py, px, ny, nx, tyn, txn, u0, v0, q0y, q0x;
 };
-constexpr int kTcBM = 128;  // output positions per CTA of k_win_convT_gemm
 
 cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
                     const float* W, float* out, cudaStream_t st);
