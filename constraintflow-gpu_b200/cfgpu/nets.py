@@ -28,10 +28,13 @@ CIFAR_STD = (0.2023, 0.1994, 0.2010)
 
 @dataclass
 class Layer:
-    """One network layer.  ``kind`` is 'linear', 'conv' or 'relu'.
+    """One network layer.  ``kind`` is 'linear', 'conv', 'relu', 'add' or 'concat'.
 
     Linear: W [out, in], b [out].  Conv: W [Cout, Cin, kh, kw], b [Cout], square
     ``stride``/``pad``; ``in_shape``/``out_shape`` are (C, H, W).
+    ``parents``: indices of the input layers in the layer list (-1 = the network input);
+    None means the previous layer.  'add' sums its two parents elementwise, 'concat'
+    stacks them (constraintflow/lib/parse.py:165-200, flow_sparse.py:67-178).
     """
     kind: str
     W: np.ndarray = None
@@ -40,6 +43,7 @@ class Layer:
     pad: int = 0
     in_shape: tuple = None
     out_shape: tuple = None
+    parents: tuple = None
 
     @property
     def n_in(self):
@@ -113,8 +117,63 @@ def _convnet(in_shape, convs, fcs, seed):
     return layers
 
 
+def _residual(seed):
+    """784 -> 100, then two residual blocks [fc, relu, fc] + skip, relu; -> 10."""
+    g = torch.Generator().manual_seed(seed)
+
+    def fc(n_in, n_out, parents=None):
+        return Layer('linear', _kaiming((n_out, n_in), g).numpy(), (torch.randn(n_out, generator=g) * 0.01).numpy(),
+                     in_shape=(n_in, 1, 1), out_shape=(n_out, 1, 1), parents=parents)
+
+    def relu(n, parents=None):
+        return Layer('relu', in_shape=(n, 1, 1), out_shape=(n, 1, 1), parents=parents)
+
+    L = [fc(784, 100), relu(100)]                         # 0, 1
+    for _ in range(2):
+        skip = len(L) - 1
+        L += [fc(100, 100), relu(100), fc(100, 100)]
+        L.append(Layer('add', in_shape=(100, 1, 1), out_shape=(100, 1, 1), parents=(len(L) - 1, skip)))
+        L.append(relu(100))
+    L.append(fc(100, 10))
+    return L
+
+
+def _branches(seed):
+    """784 -> 60 -> relu, two branches 60 -> 40 -> relu, concatenated (80) -> 10.
+
+    Listed in the reference reader's breadth-first layer order (parse.py:250-300), which
+    also numbers the layers: both branch Gemms, then both ReLUs."""
+    g = torch.Generator().manual_seed(seed)
+
+    def fc(n_in, n_out, parents=None):
+        return Layer('linear', _kaiming((n_out, n_in), g).numpy(), (torch.randn(n_out, generator=g) * 0.01).numpy(),
+                     in_shape=(n_in, 1, 1), out_shape=(n_out, 1, 1), parents=parents)
+
+    def relu(n, parents=None):
+        return Layer('relu', in_shape=(n, 1, 1), out_shape=(n, 1, 1), parents=parents)
+
+    L = [fc(784, 60), relu(60)]                            # 0, 1
+    L += [fc(60, 40, (1,)), fc(60, 40, (1,))]              # 2, 3: the two branches
+    L += [relu(40, (2,)), relu(40, (3,))]                  # 4, 5
+    L.append(Layer('concat', in_shape=(80, 1, 1), out_shape=(80, 1, 1), parents=(4, 5)))   # 6
+    L.append(fc(80, 10))                                   # 7
+    return L
+
+
+def parents_of(layers, i):
+    """Parent indices of layer i (-1 = the network input)."""
+    p = layers[i].parents
+    return tuple(p) if p is not None else (i - 1,)
+
+
+def is_chain(layers):
+    return all(L.kind in ('linear', 'conv', 'relu') and parents_of(layers, i) == (i - 1,)
+               for i, L in enumerate(layers))
+
+
 def workload(wid):
-    """The five certification workloads: id -> Workload (full batch size)."""
+    """The certification workloads: id -> Workload (full batch size).  0-4 are chains;
+    5 (residual blocks) and 6 (concatenated branches) are DAGs."""
     if wid == 0:
         return Workload(0, "mlp_784-50x3-10", (1, 28, 28), _mlp([784, 50, 50, 50, 10], 0, None),
                         1, 0.01, 'mnist', 0, "DeepPoly, ReLU MLP 784-50-50-50-10, 1 region, eps 0.01")
@@ -133,6 +192,12 @@ def workload(wid):
                         _convnet((3, 32, 32), [(32, 3, 1, 1), (32, 4, 2, 1), (64, 3, 1, 1), (64, 4, 2, 1)],
                                  [512, 512, 10], 4),
                         1024, 2.0 / 255.0, 'cifar', 4, "DeepPoly, conv net 3x32x32, 1024 regions, eps 2/255")
+    if wid == 5:
+        return Workload(5, "resmlp_784-100-2x(100,100,add)-10", (1, 28, 28), _residual(5),
+                        32, 0.002, 'mnist', 5, "DeepPoly, residual MLP (two skip blocks), 32 regions")
+    if wid == 6:
+        return Workload(6, "branch_784-60-(40|40)-concat-10", (1, 28, 28), _branches(6),
+                        32, 0.002, 'mnist', 6, "DeepPoly, two branches concatenated, 32 regions")
     raise ValueError(f"unknown workload {wid}")
 
 
@@ -170,16 +235,24 @@ def input_box(X, eps, dataset):
 
 def forward(layers, x):
     """float32 forward pass of the layer list on [B, C, H, W] inputs -> logits [B, 10]."""
-    h = torch.as_tensor(x, dtype=torch.float32)
-    for L in layers:
+    x = torch.as_tensor(x, dtype=torch.float32)
+    outs = []
+    for i, L in enumerate(layers):
+        ps = parents_of(layers, i)
+        h = x if ps[0] < 0 else outs[ps[0]]
         if L.kind == 'conv':
             h = torch.nn.functional.conv2d(h, torch.from_numpy(L.W), torch.from_numpy(L.b),
                                            stride=L.stride, padding=L.pad)
         elif L.kind == 'linear':
             h = h.reshape(h.shape[0], -1) @ torch.from_numpy(L.W).T + torch.from_numpy(L.b)
-        else:
+        elif L.kind == 'relu':
             h = torch.relu(h)
-    return h
+        elif L.kind == 'add':
+            h = h + outs[ps[1]]
+        elif L.kind == 'concat':
+            h = torch.cat([h.reshape(h.shape[0], -1), outs[ps[1]].reshape(h.shape[0], -1)], dim=1)
+        outs.append(h)
+    return outs[-1]
 
 
 def labels(wl, X):

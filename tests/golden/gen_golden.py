@@ -70,6 +70,13 @@ CASES = {
     # deeppoly_efficient.cf: ReLU polyexps over the affine's inputs (prev[L] / prev[U])
     "dpe_w0_b4_e1e-3": ("deeppoly_efficient", 0, 4, 0.001),
     "dpe_w2_b4_e2e-4": ("deeppoly_efficient", 2, 4, 0.0002),
+    # DAG networks: residual blocks (Add) and concatenated branches (Concat)
+    "dp_w5_b4_e2e-3": ("deeppoly", 5, 4, 0.002),
+    "dp_w5_b4_e2e-4": ("deeppoly", 5, 4, 0.0002),
+    "dp_w6_b4_e2e-3": ("deeppoly", 6, 4, 0.002),
+    "dp_w6_b4_e2e-4": ("deeppoly", 6, 4, 0.0002),
+    "crown_w5_b2_e2e-3": ("crown", 5, 2, 0.002),
+    "crown_w6_b2_e2e-3": ("crown", 6, 2, 0.002),
 }
 
 
@@ -81,43 +88,45 @@ def _load_nets():
 
 
 def _onnx_graph(nets, wl):
-    """In-memory graph with the fields constraintflow/lib/parse.py:60-143 reads.
+    """In-memory graph with the fields constraintflow/lib/parse.py:60-200 reads.
 
     Conv attributes are positional in torch-export order
     (dilations, group, kernel_shape, pads, strides): parse.py:110-112.  A leading
     Flatten (skipped by the reader as identity, parse.py:240-247) keeps the
-    4-D input shape for the first Gemm (parse.py:137).
+    4-D input shape for the first Gemm (parse.py:137).  Add / Concat nodes name their two
+    parents' outputs (parse.py:165-200).
     """
     import types
     NS = types.SimpleNamespace
     inits, nodes = [], []
-    prev = "input"
-    conv_i = fc_i = relu_i = 0
+    out_name = {-1: "input"}
     flattened = False
-    for L in wl.layers:
+    for i, L in enumerate(wl.layers):
+        ps = nets.parents_of(wl.layers, i)
+        src = out_name[ps[0]]
+        name = f"n{i}"
         if L.kind == "conv":
             k = L.W.shape[2]
-            inits += [NS(name=f"c{conv_i}.weight", array=L.W), NS(name=f"c{conv_i}.bias", array=L.b)]
-            nodes.append(NS(op_type="Conv", input=[prev, f"c{conv_i}.weight", f"c{conv_i}.bias"],
-                            output=[f"cv{conv_i}"],
+            inits += [NS(name=f"c{i}.weight", array=L.W), NS(name=f"c{i}.bias", array=L.b)]
+            nodes.append(NS(op_type="Conv", input=[src, f"c{i}.weight", f"c{i}.bias"], output=[name],
                             attribute=[NS(ints=[1, 1]), NS(ints=[1]), NS(ints=[k, k]),
                                        NS(ints=[L.pad] * 4), NS(ints=[L.stride] * 2)]))
-            prev = f"cv{conv_i}"
-            conv_i += 1
         elif L.kind == "linear":
             if not flattened:
-                nodes.append(NS(op_type="Flatten", input=[prev], output=["flat"], attribute=[]))
-                prev = "flat"
+                nodes.append(NS(op_type="Flatten", input=[src], output=["flat"], attribute=[]))
+                out_name[ps[0]] = src = "flat"
                 flattened = True
-            inits += [NS(name=f"fc{fc_i}.weight", array=L.W), NS(name=f"fc{fc_i}.bias", array=L.b)]
-            nodes.append(NS(op_type="Gemm", input=[prev, f"fc{fc_i}.weight", f"fc{fc_i}.bias"],
-                            output=[f"g{fc_i}"], attribute=[]))
-            prev = f"g{fc_i}"
-            fc_i += 1
+            inits += [NS(name=f"fc{i}.weight", array=L.W), NS(name=f"fc{i}.bias", array=L.b)]
+            nodes.append(NS(op_type="Gemm", input=[src, f"fc{i}.weight", f"fc{i}.bias"], output=[name],
+                            attribute=[]))
+        elif L.kind == "relu":
+            nodes.append(NS(op_type="Relu", input=[src], output=[name], attribute=[]))
+        elif L.kind in ("add", "concat"):
+            nodes.append(NS(op_type="Add" if L.kind == "add" else "Concat", input=[src, out_name[ps[1]]],
+                            output=[name], attribute=[]))
         else:
-            nodes.append(NS(op_type="Relu", input=[prev], output=[f"r{relu_i}"], attribute=[]))
-            prev = f"r{relu_i}"
-            relu_i += 1
+            raise ValueError(L.kind)
+        out_name[i] = name
     C, H, W = wl.input_shape
     dims = [NS(dim_value=v) for v in (1, C, H, W)]
     return NS(input=[NS(name="input", type=NS(tensor_type=NS(shape=NS(dim=dims))))],
