@@ -1,10 +1,11 @@
 """Host side of the DeepPoly network driver: network upload + one call into libcfgpu.
 
 ``DeepPolyEngine`` mirrors what ``Flow(abs_elem, deeppoly(), network).flow()``
-(constraintflow/lib/flow_sparse.py:27-228) computes for a chain network, but runs the
+(constraintflow/lib/flow_sparse.py:27-228) computes.  For a chain network it runs the
 whole layer loop inside ``cf_deeppoly_run``: one C-ABI call per batch of regions, all
-work stream-ordered on the current torch stream.  Torch only provides device memory
-and the stream handle.
+work stream-ordered on the current torch stream.  Networks with Add / Concat layers (and
+CROWN's all-crossing branch) run the general traversal of cfgpu.general over libcfgpu's
+block kernels.  Torch only provides device memory and the stream handle.
 """
 import ctypes
 
@@ -17,15 +18,17 @@ N_CLASSES = 10
 
 
 class DeepPolyEngine:
-    """A chain network resident on one GPU, ready to certify batches of input regions.
+    """A network resident on one GPU, ready to certify batches of input regions.
 
-    layers: sequence of objects with ``kind`` in {'linear','conv','relu'} and, for affine
-    layers, ``W`` / ``b`` arrays (Linear W [out, in]; Conv W [Cout, Cin, k, k]) plus
-    ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers.
+    layers: sequence of objects with ``kind`` in {'linear','conv','relu','add','concat'}
+    and, for affine layers, ``W`` / ``b`` arrays (Linear W [out, in]; Conv W [Cout, Cin,
+    k, k]) plus ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers;
+    optional ``parents`` (layer-list indices, -1 = the network input; default the previous
+    layer), listed in the reference reader's order (every parent before its children).
     certifier: 'deeppoly' (deeppoly.cf, deeppoly_efficient.cf) or 'crown' (crown.cf, whose
     ReLU branch is decided over the whole batch: a CROWN run always takes the batch in
     one workspace chunk and checks the device status; when a layer takes the all-crossing
-    branch the bounds are recomputed by the general traversal of cfgpu.crown).
+    branch the bounds are recomputed by the general traversal of cfgpu.general).
     """
 
     def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
@@ -39,20 +42,32 @@ class DeepPolyEngine:
             raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly and crown)")
         self.certifier = certifier
         self._keep = []
-        self._general = []        # (kind, W, b) device tensors for cfgpu.crown
+        self._general = []        # (kind, W, b, parents) device tensors for cfgpu.general
+        widths = []
         descs = []
-        width = self.input_size
-        for L in layers:
+        self.chain = True
+        for i, L in enumerate(layers):
+            parents = tuple(int(p) for p in getattr(L, "parents", None) or (i - 1,))
+            if any(not -1 <= p < i for p in parents):
+                raise ValueError(f"layer {i}: parents {parents} must precede it in the list")
+            pw = [self.input_size if p < 0 else widths[p] for p in parents]
+            self.chain &= parents == (i - 1,)
             d = CfLayer()
-            if L.kind == "relu":
+            if L.kind in ("relu", "add", "concat"):
+                if L.kind != "relu":
+                    self.chain = False
+                    if len(parents) != 2:
+                        raise ValueError(f"layer {i}: {L.kind} takes two parents, got {parents}")
+                    if L.kind == "add" and pw[0] != pw[1]:
+                        raise ValueError(f"layer {i}: add of widths {pw}")
                 d.kind = _lib.CF_LAYER_RELU
-                d.n_in = d.n_out = width
-                self._general.append(("relu", None, None))
+                d.n_in = d.n_out = sum(pw) if L.kind == "concat" else pw[0]
+                self._general.append((L.kind, None, None, parents))
             else:
                 W = torch.as_tensor(L.W, dtype=torch.float32).to(self.device).contiguous()
                 b = torch.as_tensor(L.b, dtype=torch.float32).to(self.device).contiguous()
                 self._keep += [W, b]
-                self._general.append((L.kind, W, b))
+                self._general.append((L.kind, W, b, parents))
                 d.W_dev, d.b_dev = W.data_ptr(), b.data_ptr()
                 if L.kind == "linear":
                     d.kind = _lib.CF_LAYER_LINEAR
@@ -67,17 +82,29 @@ class DeepPolyEngine:
                     d.n_out = d.cout * d.oh * d.ow
                 else:
                     raise NotImplementedError(f"layer kind {L.kind}")
-            width = d.n_out
+                if d.n_in != pw[0]:
+                    raise ValueError(f"layer {i}: {L.kind} reads {d.n_in} neurons, its parent has {pw[0]}")
+            widths.append(int(d.n_out))
             descs.append(d)
-        self.n_last = width
-        self._layers = (CfLayer * len(descs))(*descs)
-        self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, relax[certifier])
-        self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))
-        if self.N < 0:
-            check(_lib.CF_ERR_SHAPE, "network description")
+        self.n_last = widths[-1] if widths else self.input_size
+        if self.chain:
+            self._layers = (CfLayer * len(descs))(*descs)
+            self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, relax[certifier])
+            self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))
+            if self.N < 0:
+                check(_lib.CF_ERR_SHAPE, "network description")
+        else:
+            # Add / Concat: polyexps mix layers; the general traversal runs the whole network
+            if any(g[0] == "conv" for g in self._general):
+                raise NotImplementedError("conv layers in a network with Add / Concat layers (the general "
+                                          "traversal runs linear, relu, add and concat layers)")
+            self.net = None
+            self.N = self.input_size + sum(widths) + self.n_spec
         self._ws = None
 
     def workspace_bytes(self, chunk):
+        if self.net is None:
+            raise ValueError("the fused driver's workspace applies to chain networks only")
         return int(lib.cf_deeppoly_workspace_bytes(ctypes.byref(self.net), int(chunk)))
 
     def _workspace(self, B, budget_bytes):
@@ -112,6 +139,13 @@ class DeepPolyEngine:
         if want_state:
             sl = torch.empty(B, self.N, dtype=torch.float32, device=self.device)
             su = torch.empty_like(sl)
+        if self.net is None:
+            lb, ub, sl_g, su_g = self._general_run(l0, u0, spec_W, lb, ub)
+            if want_state:
+                sl.copy_(sl_g)
+                su.copy_(su_g)
+                return lb, ub, sl, su
+            return lb, ub
         ws = self._workspace(B, workspace_budget)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         st = lib.cf_deeppoly_run(ctypes.byref(self.net), B, l0.data_ptr(), u0.data_ptr(), spec_W.data_ptr(),
@@ -123,7 +157,7 @@ class DeepPolyEngine:
             st = lib.cf_deeppoly_check(ws.data_ptr(), stream)
             if st == _lib.CF_ERR_UNSUPPORTED:
                 # a ReLU layer took the all-crossing branch: its polyexps mix layers
-                lb, ub, sl_g, su_g = self._crown_general(l0, u0, spec_W, lb, ub)
+                lb, ub, sl_g, su_g = self._general_run(l0, u0, spec_W, lb, ub)
                 if want_state:
                     sl.copy_(sl_g)
                     su.copy_(su_g)
@@ -135,12 +169,11 @@ class DeepPolyEngine:
             return lb, ub, sl, su
         return lb, ub
 
-    def _crown_general(self, l0, u0, spec_W, lb, ub):
-        """CROWN bounds through the general lowest-layer-first traversal (cfgpu.crown)."""
-        from . import crown
-        bounds, _ = crown.run(self._general, l0, u0, spec_W)
-        sl = torch.cat([l0] + [b[0] for b in bounds], dim=1)
-        su = torch.cat([u0] + [b[1] for b in bounds], dim=1)
+    def _general_run(self, l0, u0, spec_W, lb, ub):
+        """Bounds through the general lowest-layer-first traversal (cfgpu.general)."""
+        from . import general
+        bounds, _ = general.run(self._general, l0, u0, spec_W, self.certifier)
+        sl, su = general.state(l0, u0, bounds)
         lb.copy_(bounds[-1][0])
         ub.copy_(bounds[-1][1])
         return lb, ub, sl, su

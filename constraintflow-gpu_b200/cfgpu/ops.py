@@ -1,6 +1,6 @@
 """Tensor-level wrappers over libcfgpu's block kernels (cf_ew_binary, cf_ew_unary,
 cf_ew_where, cf_ew_clamp, cf_ew_any, cf_bmm), used by the gbcsr mirror
-(constraintflow.gbcsr) and by the general CROWN traversal (cfgpu.crown).
+(constraintflow.gbcsr) and by the general traversal (cfgpu.general).
 
 Operands are CUDA tensors, possibly broadcast views (zero strides); results are new
 contiguous tensors.  PyTorch only allocates the memory and supplies the stream.

@@ -58,32 +58,43 @@ def certifier_of(transformer):
 
 
 class _EngineLayer:
-    def __init__(self, kind, W=None, b=None, in_shape=None, out_shape=None, stride=1, pad=0):
+    def __init__(self, kind, W=None, b=None, in_shape=None, out_shape=None, stride=1, pad=0, parents=None):
         self.kind, self.W, self.b = kind, W, b
         self.in_shape, self.out_shape, self.stride, self.pad = in_shape, out_shape, stride, pad
+        self.parents = parents
 
 
 def engine_layers(model):
-    """The network as the driver's chain of linear / conv / relu layers (property layer excluded)."""
+    """The network as the driver's layer list (property layer excluded): linear / conv /
+    relu / add / concat, each with its parents as indices into that list (-1 = input)."""
     out = []
+    last = len(model) - 1
+    if list(model[last].parents) != [last - 1]:
+        raise NotImplementedError("the property layer must read the last layer of the network")
     for i, layer in enumerate(model):
-        if layer.type == LayerType.Input or i == len(model) - 1:
+        if layer.type == LayerType.Input or i == last:
             continue
+        parents = tuple(int(p) - 1 for p in layer.parents)
         if layer.type == LayerType.Linear:
-            out.append(_EngineLayer("linear", layer.weight.float(), layer.bias.float()))
+            bias = layer.bias if layer.bias is not None else torch.zeros(layer.weight.shape[0])
+            out.append(_EngineLayer("linear", layer.weight.float(), bias.float(), parents=parents))
         elif layer.type == LayerType.Conv2D:
             parent = model[layer.parents[0]]
             bias = getattr(layer, "bias_channel", None)
             if bias is None:
                 bias = layer.bias.reshape(layer.weight.shape[0], -1)[:, 0]
             out.append(_EngineLayer("conv", layer.weight.float(), bias.float(), in_shape=tuple(parent.shape[1:]),
-                                    out_shape=tuple(layer.shape[1:]), stride=layer.stride[0], pad=layer.padding[0]))
+                                    out_shape=tuple(layer.shape[1:]), stride=layer.stride[0], pad=layer.padding[0],
+                                    parents=parents))
         elif layer.type == LayerType.ReLU:
-            out.append(_EngineLayer("relu"))
+            out.append(_EngineLayer("relu", parents=parents))
+        elif layer.type == LayerType.Add:
+            out.append(_EngineLayer("add", parents=parents))
+        elif layer.type == LayerType.Concat:
+            out.append(_EngineLayer("concat", parents=parents))
         else:
-            raise NotImplementedError(f"layer type {layer.type} (the driver runs chains of Linear/Conv2D/ReLU)")
-        if len(layer.parents) != 1:
-            raise NotImplementedError("non-chain networks (Add / Concat)")
+            raise NotImplementedError(f"layer type {layer.type} (the driver runs Linear, Conv2D, ReLU, Add and "
+                                      "Concat layers)")
     return out
 
 

@@ -2,13 +2,19 @@
 constraintflow/lib/parse.py:29-301.
 
 Reads Conv (attributes positional as torch exports them: [2] kernel_shape, [3] pads,
-[4] strides, parse.py:110-112), Gemm (weight input 1, bias input 2), Relu, Sigmoid, and
-a constant Add folded into the previous layer's bias; other nodes (Flatten, ...) are
-identity.  The robustness property is always appended as a final Linear layer with the
-per-region weight (parse.py:230-238).  Works with the `onnx` package, or with any module
-of that name whose ``load(name)`` returns an object with the same ``graph`` fields.
+[4] strides, parse.py:110-112), Gemm (weight input 1, bias input 2), MatMul (weight
+input 0, data input 1), Relu, Sigmoid, Add (of two layers: an Add layer; with a constant:
+folded into the previous layer's bias) and Concat of two layers; other nodes (Flatten,
+...) are identity.  The robustness property is always appended as a Linear layer with the
+per-region weight reading the last layer read (parse.py:230-238).  The list is then put
+in breadth-first order from the input, a layer entering the queue once all its parents
+have been placed (parse.py:250-300), and the neuron ranges renumbered in that order.
+Works with the `onnx` package, or with any module of that name whose ``load(name)``
+returns an object with the same ``graph`` fields.
 """
+import copy
 import math
+from collections import deque
 
 import numpy as np
 import torch
@@ -94,10 +100,28 @@ def parse_onnx_layers(net, spec_weight, spec_bias, no_sparsity=False):
             layer = Layer(type=LayerType.ReLU if op == "Relu" else LayerType.Sigmoid, identifier=index,
                           parents=[ids[src]])
             layer.shape = list(layers[ids[src]].shape)
+        elif op == "MatMul":
+            index += 1
+            w = vals[node.input[0]]
+            layer = Layer(weight=w, bias=None, type=LayerType.Linear, identifier=index,
+                          parents=[ids[str(node.input[1])]])
+            layer.shape = [1, int(w.shape[0]), 1, 1]
         elif op == "Add" and len(node.input) > 1 and node.input[1] in vals:
             ids[str(node.output[0])] = index
             layers[-1].bias = vals[node.input[1]]
             continue
+        elif op == "Add":
+            index += 1
+            pa = [ids[str(node.input[0])], ids[str(node.input[1])]]
+            layer = Layer(type=LayerType.Add, identifier=index, parents=pa)
+            layer.shape = copy.deepcopy(list(layers[pa[0]].shape))
+        elif op == "Concat":
+            if not all(str(i) in ids for i in node.input[:2]):
+                raise NotImplementedError("Concat of a tensor that is not a layer output")
+            index += 1
+            pa = [ids[str(node.input[0])], ids[str(node.input[1])]]
+            layer = Layer(type=LayerType.Concat, identifier=index, parents=pa)
+            layer.shape = [1, int(layers[pa[0]].shape[1]) + int(layers[pa[1]].shape[1]), 1, 1]
         else:
             if src is not None and src in ids:
                 ids[str(node.output[0])] = ids[src]
@@ -118,7 +142,42 @@ def parse_onnx_layers(net, spec_weight, spec_bias, no_sparsity=False):
     layers.size += spec.size
     spec.end = layers.size
     layers.append(spec)
+    return _breadth_first(layers)
+
+
+def _breadth_first(layers):
+    """The layers in breadth-first order from the input: a layer is queued when the last
+    of its parents is placed (children visited in identifier order); identifiers, parents,
+    children and neuron ranges are renumbered in the new order (parse.py:250-300)."""
+    by_id = {lay.identifier: lay for lay in layers}
+    for lay in layers:
+        lay.children = []
     for lay in layers:
         for p in lay.parents:
-            layers[p].children.append(lay.identifier)
-    return layers
+            by_id[p].children.append(lay.identifier)
+    placed = {}
+    order = []
+    queue = deque([by_id[0]])
+    while queue:
+        lay = queue.popleft()
+        if lay.identifier in placed:
+            continue
+        placed[lay.identifier] = len(order)
+        order.append(lay)
+        for c in lay.children:
+            if c not in placed and all(p in placed for p in by_id[c].parents):
+                queue.append(by_id[c])
+    if len(order) != len(layers):
+        raise ValueError("network graph: some layers are not reachable from the input")
+    out = layers.similar()
+    start = 0
+    for lay in order:
+        lay.identifier = placed[lay.identifier]
+        lay.parents = [placed[p] for p in lay.parents]
+        lay.children = [placed[c] for c in lay.children]
+        if lay.type != LayerType.Input:
+            lay.start, lay.end = start, start + lay.size
+        start += lay.size
+        out.append(lay)
+    out.size = start
+    return out

@@ -77,6 +77,7 @@ CASES = {
     "dp_w6_b4_e2e-4": ("deeppoly", 6, 4, 0.0002),
     "crown_w5_b2_e2e-3": ("crown", 5, 2, 0.002),
     "crown_w6_b2_e2e-3": ("crown", 6, 2, 0.002),
+    "crown_w6_b2_e1e-1": ("crown", 6, 2, 0.1),
 }
 
 

@@ -2,6 +2,8 @@
 (structure, shape/type checks) works without launching anything."""
 import operator
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -55,3 +57,66 @@ def test_generated_programs_are_recognised():
             sys.modules.pop("transformers", None)
             if saved is not None:
                 sys.modules["transformers"] = saved
+
+
+@pytest.mark.parametrize("wid", [0, 3, 5, 6])
+def test_onnx_reader_layer_list(wid):
+    """The ONNX reader mirror on the synthetic networks: the layer list, parents and
+    neuron ranges the driver receives are those of the network (workload 6 lists its
+    layers breadth first, as the reference's reader orders them)."""
+    import os
+    import sys
+    from cfgpu import nets
+    from constraintflow.lib.parse import parse_onnx_layers
+    from constraintflow.lib.network import LayerType
+    from constraintflow.lib.flow_sparse import engine_layers
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(here, "golden"))
+    import gen_golden
+    wl = nets.workload(wid)
+    spec = torch.zeros(1, 9, wl.layers[-1].n_out)
+    import types
+    graph = types.SimpleNamespace(graph=gen_golden._onnx_graph(nets, wl))
+    model = parse_onnx_layers(graph, spec, torch.zeros(1, 9))
+    assert model[0].type == LayerType.Input and model[-1].last_layer
+    start = 0
+    for i, lay in enumerate(model):
+        assert lay.identifier == i and lay.start == start
+        assert all(p < i for p in lay.parents)
+        start = lay.end
+    assert model.size == start == wl.input_size + sum(L.n_out for L in wl.layers) + 9
+    eng = engine_layers(model)
+    assert [L.kind for L in eng] == [L.kind for L in wl.layers]
+    assert [L.parents for L in eng] == [nets.parents_of(wl.layers, i) for i in range(len(wl.layers))]
+    for a, b in zip(eng, wl.layers):
+        if b.W is not None:
+            np.testing.assert_array_equal(a.W.numpy(), b.W)
+
+
+def test_onnx_reader_orders_breadth_first():
+    """Branches written depth first in the ONNX graph (Linear, ReLU of one branch, then
+    the other's) come out breadth first, as the reference's reader lists them."""
+    import os
+    import sys
+    import types
+    from cfgpu import nets
+    from constraintflow.lib.parse import parse_onnx_layers
+    from constraintflow.lib.flow_sparse import engine_layers
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import gen_golden
+    wl = nets.workload(6)
+    bfs = wl.layers
+    dfs_order = [0, 1, 2, 4, 3, 5, 6, 7]           # new position -> index in the breadth-first list
+    pos = {old: new for new, old in enumerate(dfs_order)}
+    dfs = [nets.Layer(**{**bfs[o].__dict__, "parents": tuple(pos[p] if p >= 0 else -1
+                                                              for p in nets.parents_of(bfs, o))})
+           for o in dfs_order]
+    graph = types.SimpleNamespace(graph=gen_golden._onnx_graph(nets, types.SimpleNamespace(**{**wl.__dict__,
+                                                                                             "layers": dfs})))
+    model = parse_onnx_layers(graph, torch.zeros(1, 9, 10), torch.zeros(1, 9))
+    eng = engine_layers(model)
+    assert [L.kind for L in eng] == [L.kind for L in bfs]
+    assert [L.parents for L in eng] == [nets.parents_of(bfs, i) for i in range(len(bfs))]
+    for a, b in zip(eng, bfs):
+        if b.W is not None:
+            np.testing.assert_array_equal(a.W.numpy(), b.W)

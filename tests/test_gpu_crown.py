@@ -3,7 +3,7 @@
 
 CROWN's ReLU takes one branch per layer for the whole batch (crown.cf:25 as the
 reference compiles it): pass-through and zero run in the fused driver; the all-crossing
-branch (mixed-layer polyexps) runs the general traversal of cfgpu.crown.  Every case is
+branch (mixed-layer polyexps) runs the general traversal of cfgpu.general.  Every case is
 compared with the reference's golden bounds where the reference has them and with the
 CROWN oracle.  Tolerances: tests/parity.py.
 """

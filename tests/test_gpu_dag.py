@@ -1,0 +1,98 @@
+"""GPU parity on networks with residual Add and Concat layers (DeepPolyEngine on a
+non-chain layer list -> the general traversal of cfgpu.general over libcfgpu kernels),
+against the reference's own DeepPoly and CROWN outputs (tests/golden/dp_w5_*, dp_w6_*,
+crown_w5_*, crown_w6_*) and the general oracle; and the general traversal on chain
+networks against the fused driver.  Tolerances: tests/parity.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+import parity
+from golden_cases import Case, names
+from oracle import crown_oracle as C
+from oracle import deeppoly_oracle as O
+from cfgpu import nets
+
+pytestmark = pytest.mark.gpu
+
+DAG_CASES = [n for p in ("deeppoly", "crown") for n in names(p, max_wid=9) if Case(n).wid >= 5]
+
+
+def _run(wl, certifier, l0, u0, W):
+    from cfgpu.engine import DeepPolyEngine
+    eng = DeepPolyEngine(wl.layers, wl.input_size, "cuda:0", certifier=certifier)
+    dev = torch.device("cuda:0")
+    lb, ub, sl, su = eng.run(torch.from_numpy(l0).to(dev), torch.from_numpy(u0).to(dev),
+                             torch.from_numpy(W).to(dev), want_state=True)
+    torch.cuda.synchronize()
+    return eng, lb.cpu().numpy(), ub.cpu().numpy(), sl.cpu().numpy(), su.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", DAG_CASES)
+def test_gpu_dag_matches_reference(name):
+    c = Case(name)
+    rel = "crown" if c.program == "crown" else "deeppoly"
+    eng, lb, ub, sl, su = _run(c.wl, rel, c.l0, c.u0, c.spec_W)
+    assert not eng.chain and eng.net is None
+    n0 = c.wl.input_size
+    assert sl.shape[1] == n0 + sum(c.sizes)
+    assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+    np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
+    np.testing.assert_array_equal(ub, su[:, -9:].astype(np.float64))
+    bounds, _, _, _ = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, rel)
+    ol, ou = O.flatten_bounds(n0, bounds, c.B)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
+
+
+@pytest.mark.parametrize("wid,eps", [(5, 0.1), (6, 0.3)])
+def test_gpu_dag_crown_crossing(wid, eps):
+    """Wide boxes: every CROWN ReLU layer of the residual / concat network takes the
+    all-crossing branch (the reference itself raises there on the residual network,
+    abs_elem.py:459; its concat-network output at eps 0.1 is a golden case); the GPU
+    traversal matches the general oracle."""
+    wl = nets.workload(wid)
+    X = nets.centres(wl, 2)
+    y = nets.labels(wl, X)
+    l0, u0 = (t.numpy() for t in nets.input_box(X, eps, wl.dataset))
+    W = nets.spec_weight(y).numpy()
+    _, lb, ub, sl, su = _run(wl, "crown", l0, u0, W)
+    bounds, olb, _, br = C.certify(wl.layers, l0, u0, W, "crown")
+    assert br == [C.BRANCH_CROSS] * len(br)
+    ol, ou = O.flatten_bounds(wl.input_size, bounds, 2)
+    sizes = [L.n_out for L in wl.layers] + [9]
+    n0 = wl.input_size
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, sizes)
+    assert worst <= 1.0, f"GPU vs oracle {worst:.3g}x tolerance at {where}"
+
+
+@pytest.mark.parametrize("name", ["dp_w0_b4_e1e-3", "dp_w2_b8_e2e-4"])
+def test_gpu_general_on_chain_matches_fused_driver(name):
+    """The general traversal over a chain network gives the fused driver's bounds."""
+    from cfgpu import general
+    from cfgpu.engine import DeepPolyEngine
+    c = Case(name)
+    eng, lb, ub, sl, su = _run(c.wl, "deeppoly", c.l0, c.u0, c.spec_W)
+    assert eng.chain
+    dev = torch.device("cuda:0")
+    l0, u0 = torch.from_numpy(c.l0).to(dev), torch.from_numpy(c.u0).to(dev)
+    bounds, _ = general.run(eng._general, l0, u0, torch.from_numpy(c.spec_W).to(dev), "deeppoly")
+    gl, gu = (t.cpu().numpy() for t in general.state(l0, u0, bounds))
+    n0 = c.wl.input_size
+    worst, where = parity.continuous_errors(gl[:, n0:], gu[:, n0:], sl[:, n0:], su[:, n0:], c.sizes)
+    assert worst <= 1.0, f"{name}: general vs fused {worst:.3g}x tolerance at {where}"
+    del DeepPolyEngine
+
+
+def test_gpu_dag_rejects_bad_layers():
+    from cfgpu.engine import DeepPolyEngine
+    wl = nets.workload(5)
+    layers = list(wl.layers)
+    i = next(k for k, L in enumerate(layers) if L.kind == "add")
+    bad = nets.Layer(**{**layers[i].__dict__, "parents": (i + 1, 0)})
+    with pytest.raises(ValueError):
+        DeepPolyEngine(layers[:i] + [bad] + layers[i + 1:], wl.input_size, "cuda:0")

@@ -1,7 +1,8 @@
 """The reference compiler's own output for examples/compiler_examples/{deeppoly,crown,
 deeppoly_efficient}.cf (tests/golden/generated/<program>/{main.py,transformers.py}, saved
 by tests/golden/gen_golden.py) runs UNCHANGED on this runtime's constraintflow package:
-main.run(...) -> (lb, ub) float64, matching the reference's golden bounds."""
+main.run(...) -> (lb, ub) float64, matching the reference's golden bounds (chain, residual
+Add and Concat networks)."""
 import importlib.util
 import os
 import sys
@@ -44,7 +45,9 @@ def _load_program(program):
 
 PROGRAM_CASES = [("deeppoly", n) for n in ("dp_w0_b4_e1e-3", "dp_w1_b16_e5e-4", "dp_w2_b8_e2e-4", "dp_w3_b4_e2e-3")] + \
     [("crown", n) for n in ("crown_w0_b4_e1e-3", "crown_w2_b4_e2e-4")] + \
-    [("deeppoly_efficient", n) for n in ("dpe_w0_b4_e1e-3", "dpe_w2_b4_e2e-4")]
+    [("deeppoly_efficient", n) for n in ("dpe_w0_b4_e1e-3", "dpe_w2_b4_e2e-4")] + \
+    [("deeppoly", n) for n in ("dp_w5_b4_e2e-3", "dp_w6_b4_e2e-3")] + \
+    [("crown", n) for n in ("crown_w5_b2_e2e-3", "crown_w6_b2_e1e-1")]
 
 
 @pytest.mark.parametrize("program,name", PROGRAM_CASES)
