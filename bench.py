@@ -155,19 +155,33 @@ class Clocks:
                 "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
+# regions per CPU sample of the oracle port, per workload id (about 0.5-1 s each)
+CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
+
+
+def _oracle_fn(wl):
+    """The oracle for the workload: the chain DeepPoly oracle, or the general one for a
+    network with Add / Concat layers."""
+    if nets.is_chain(wl.layers):
+        from oracle import deeppoly_oracle as O
+        return lambda l0, u0, W: O.deeppoly(wl.layers, l0, u0, W)
+    from oracle import crown_oracle as C
+    return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "deeppoly")
+
+
 def cpu_baseline(wl, sample, reps=3):
     """Oracle (numpy float32, all host threads) on `sample` regions of the workload: regions/s."""
-    from oracle import deeppoly_oracle as O
+    fn = _oracle_fn(wl)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
     W = nets.spec_weight(y).numpy()
     l0, u0 = l0.numpy(), u0.numpy()
-    O.deeppoly(wl.layers, l0[:1], u0[:1], W[:1])  # warm
+    fn(l0[:1], u0[:1], W[:1])  # warm
     ts = []
     for _ in range(reps):
         t = time.perf_counter()
-        O.deeppoly(wl.layers, l0, u0, W)
+        fn(l0, u0, W)
         ts.append(time.perf_counter() - t)
     return sample / statistics.median(ts), statistics.median(ts)
 
@@ -180,19 +194,19 @@ def run_reference(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": "the oracle port needs ~385 s per region of this "
                           "net (dense conv rows), beyond a bounded per-step sample"}))
         return
-    sample = {0: 1, 1: 16, 2: 8, 3: 4}[args.workload]
-    from oracle import deeppoly_oracle as O
+    sample = CPU_SAMPLE[args.workload]
+    fn = _oracle_fn(wl)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
     W = nets.spec_weight(y).numpy()
     l0, u0 = l0.numpy(), u0.numpy()
     for _ in range(args.warmup):
-        O.deeppoly(wl.layers, l0, u0, W)
+        fn(l0, u0, W)
     ts = []
     for _ in range(args.steps):
         t = time.perf_counter()
-        O.deeppoly(wl.layers, l0, u0, W)
+        fn(l0, u0, W)
         ts.append(time.perf_counter() - t)
     ms = 1000 * statistics.mean(ts)
     val = sample / (ms / 1000)
@@ -302,8 +316,9 @@ def run_cfgpu(args, rank, world, local):
     bf16, hbm, src = peaks()
     achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
     conv = any(L.kind == "conv" for L in wl.layers)
-    if conv:
-        # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe);
+    if conv or not eng.chain:
+        # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
+        # with Add / Concat layers: the general traversal's k_bmm GEMMs, also on the FP32 pipe.
         # MEASURED_PEAKS holds no FP32-pipe figure, so the nominal one: SMs x 128 lanes x 2 x max clock
         props = torch.cuda.get_device_properties(dev)
         mhz = clocks.get("sm_max_mhz") or 1965.0
@@ -328,7 +343,8 @@ def run_cfgpu(args, rank, world, local):
                      "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
                                         "CTAs) from one ncu --set full capture of this command")
                      if args.workload in NCU_TRAFFIC else None,
-                     "kernel": "backsubstitution step", "peak_source": peak_src,
+                     "kernel": "backsubstitution step" if eng.chain else "k_bmm (general traversal)",
+                     "peak_source": peak_src,
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
                      "step_launches": prof["step_launches"]},
         "clocks": clocks,
@@ -340,7 +356,7 @@ def run_cfgpu(args, rank, world, local):
         out["cpu_baseline"] = {"value": None, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
                                "sample": "not timed: the oracle port needs ~385 s per region of this net"}
     elif world == 1:
-        sample = {0: 1, 1: 16, 2: 8, 3: 4}[args.workload]
+        sample = CPU_SAMPLE[args.workload]
         v, t1 = cpu_baseline(wl, sample)
         out["cpu_baseline"] = {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
                                "sample": f"oracle numpy float32, {sample} regions of {wl.name}, median of 3 "

@@ -266,10 +266,21 @@ extern "C" cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K, const f
   CF_REQUIRE(nb >= 0 && M >= 0 && N >= 0 && K >= 0, CF_ERR_SHAPE, "bmm: negative size");
   if (nb * M * N == 0) return CF_OK;
   CF_REQUIRE(C && (K == 0 || (A && B)), CF_ERR_NULL, "bmm: NULL argument");
+  const double flops = 2.0 * nb * M * N * K;
+  const double bytes = 4.0 * ((double)nb * M * K + (double)(b_bs ? nb : 1) * K * N + (double)nb * M * N);
+  // one matrix B shared by every batch (stride 0) and batch-contiguous A rows: a single
+  // GEMM over nb*M rows (C is compact [nb, M, N], so its rows line up)
+  if (nb > 1 && b_bs == 0 && a_bs == M * a_ms && ceil_div(nb * M, BM_M) <= 65535) {
+    M *= nb;
+    nb = 1;
+    a_bs = 0;
+  }
   const int64_t gx = ceil_div(N, BM_N), gy = ceil_div(M, BM_M);
   CF_REQUIRE(gx <= 0x7fffffff && gy <= 65535, CF_ERR_SHAPE, "bmm: %lld x %lld too large", (long long)M,
              (long long)N);
   dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(nb < 65535 ? nb : 65535));
+  prof_step_begin(as_stream(stream));
   k_bmm<<<grid, 256, 0, as_stream(stream)>>>(nb, M, N, K, A, a_bs, a_ms, a_ks, B, b_bs, b_ks, b_ns, C, accumulate);
+  prof_step_end(as_stream(stream), flops, bytes);
   return check_launch("k_bmm");
 }
