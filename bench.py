@@ -2,11 +2,14 @@
 """Benchmark: certified input regions/sec (DeepPoly, whole input box) on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cfgpu|reference] [--workload 2]
+                    [--certifier deeppoly|crown|zono|ibp] [--batch B]
 
 One step = one whole DeepPoly pass (input box, property matrix, every layer's
 backsubstitution down to the input, final bounds) over one batch of regions of the
 workload (default: ReLU MLP 784-(200x9)-10, 256 regions per GPU, eps 0.002; seeded
 synthetic network and centres, since no dataset or trained model is available offline).
+--certifier runs another of the reference's programs on the same workload (a zono / ibp
+step is one forward pass).
 Multi-GPU: one process per GPU (torchrun), each certifying its own 256 regions (weak
 scaling; regions are independent, no collective on the data path).  Rank 0 prints one
 JSON line.
@@ -34,7 +37,7 @@ from cfgpu import nets  # noqa: E402
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu capture of
 # the default command (profiles/k_chain_mlp784-200x9_b256.txt); per workload id.
-NCU_TRAFFIC = {2: 10.79e6}
+NCU_TRAFFIC = {(2, "deeppoly"): 10.79e6}
 
 
 def parse():
@@ -45,6 +48,8 @@ def parse():
     ap.add_argument("--impl", default="cfgpu", choices=["cfgpu", "reference"])
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
+    ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp"],
+                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf)")
     return ap.parse_args()
 
 
@@ -159,9 +164,24 @@ class Clocks:
 CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
 
 
-def _oracle_fn(wl):
-    """The oracle for the workload: the chain DeepPoly oracle, or the general one for a
-    network with Add / Concat layers."""
+METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)"}
+
+
+def _metric(certifier):
+    return f"certified input regions/sec ({METRIC[certifier]}, whole box)"
+
+
+def _oracle_fn(wl, certifier="deeppoly"):
+    """The oracle for the workload and program: the chain DeepPoly oracle, the general one
+    (CROWN, or a network with Add / Concat layers), or the zonotope / interval one."""
+    if certifier in ("zono", "ibp"):
+        from oracle import zono_oracle as Z
+        if certifier == "zono":
+            return lambda l0, u0, W: Z.zono(wl.layers, l0, u0, W)
+        return lambda l0, u0, W: Z.ibp(wl.layers, l0, u0, W)
+    if certifier == "crown":
+        from oracle import crown_oracle as C
+        return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "crown")
     if nets.is_chain(wl.layers):
         from oracle import deeppoly_oracle as O
         return lambda l0, u0, W: O.deeppoly(wl.layers, l0, u0, W)
@@ -169,9 +189,9 @@ def _oracle_fn(wl):
     return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "deeppoly")
 
 
-def cpu_baseline(wl, sample, reps=3):
+def cpu_baseline(wl, sample, reps=3, certifier="deeppoly"):
     """Oracle (numpy float32, all host threads) on `sample` regions of the workload: regions/s."""
-    fn = _oracle_fn(wl)
+    fn = _oracle_fn(wl, certifier)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
@@ -195,7 +215,7 @@ def run_reference(args, rank, world):
                           "net (dense conv rows), beyond a bounded per-step sample"}))
         return
     sample = CPU_SAMPLE[args.workload]
-    fn = _oracle_fn(wl)
+    fn = _oracle_fn(wl, args.certifier)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
@@ -213,10 +233,10 @@ def run_reference(args, rank, world):
     cores = os.cpu_count()
     desc = f"oracle port (numpy float32 BLAS, {cores} threads), {sample} regions of {wl.name} per step"
     print(json.dumps({
-        "impl": "reference", "metric": "certified input regions/sec (DeepPoly, whole box)", "value": val,
+        "impl": "reference", "metric": _metric(args.certifier), "value": val,
         "unit": "regions/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "regions_per_step": sample, "eps": wl.eps},
+        "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_step": sample, "eps": wl.eps},
         "cpu_baseline": {"value": val, "unit": "regions/s", "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": val, "unit": "regions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
@@ -233,7 +253,7 @@ def run_cfgpu(args, rank, world, local):
     lo, hi = cdist.shard_range(B * world, rank, world)
     X = Xall[lo:hi].contiguous()
     y = nets.labels(wl, X)
-    eng = DeepPolyEngine(wl.layers, wl.input_size, dev)
+    eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=args.certifier)
     Xd, yd = X.to(dev), y.to(dev)
     lb = torch.empty(B, 9, dtype=torch.float64, device=dev)
     ub = torch.empty_like(lb)
@@ -316,9 +336,10 @@ def run_cfgpu(args, rank, world, local):
     bf16, hbm, src = peaks()
     achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
     conv = any(L.kind == "conv" for L in wl.layers)
-    if conv or not eng.chain:
+    if conv or not eng.chain or args.certifier in ("zono", "ibp"):
         # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
-        # with Add / Concat layers: the general traversal's k_bmm GEMMs, also on the FP32 pipe.
+        # with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass: k_zono_gemm
+        # over the noise-symbol rows -- all on the FP32 pipe.
         # MEASURED_PEAKS holds no FP32-pipe figure, so the nominal one: SMs x 128 lanes x 2 x max clock
         props = torch.cuda.get_device_properties(dev)
         mhz = clocks.get("sm_max_mhz") or 1965.0
@@ -327,10 +348,11 @@ def run_cfgpu(args, rank, world, local):
     else:
         peak, bound, peak_src = bf16 / 2.0 / 3.0, "tensor", f"3xTF32 = bf16/2/3 of {src} MEASURED_PEAKS"
     out = {
-        "metric": "certified input regions/sec (DeepPoly, whole box)", "value": value, "unit": "regions/s",
+        "metric": _metric(args.certifier), "value": value, "unit": "regions/s",
         "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "regions_per_gpu": B, "global_regions": B * world, "eps": wl.eps,
+        "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_gpu": B,
+                   "global_regions": B * world, "eps": wl.eps,
                    "parallelism": f"regions sharded over {world} GPU(s)", "l2": "flushed between timed steps",
                    "certified": int(certified.item())},
         "e2e": {"value": e2e_val, "unit": "regions/s",
@@ -339,11 +361,12 @@ def run_cfgpu(args, rank, world, local):
         "gpu_launches": int(prof["kernel_launches"]),
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None,
-                     "traffic": NCU_TRAFFIC.get(args.workload),
+                     "traffic": NCU_TRAFFIC.get((args.workload, args.certifier)),
                      "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
                                         "CTAs) from one ncu --set full capture of this command")
-                     if args.workload in NCU_TRAFFIC else None,
-                     "kernel": "backsubstitution step" if eng.chain else "k_bmm (general traversal)",
+                     if (args.workload, args.certifier) in NCU_TRAFFIC else None,
+                     "kernel": {"zono": "k_zono_gemm", "ibp": None}.get(
+                         args.certifier, "backsubstitution step" if eng.chain else "k_bmm (general traversal)"),
                      "peak_source": peak_src,
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
                      "step_launches": prof["step_launches"]},
@@ -357,7 +380,7 @@ def run_cfgpu(args, rank, world, local):
                                "sample": "not timed: the oracle port needs ~385 s per region of this net"}
     elif world == 1:
         sample = CPU_SAMPLE[args.workload]
-        v, t1 = cpu_baseline(wl, sample)
+        v, t1 = cpu_baseline(wl, sample, certifier=args.certifier)
         out["cpu_baseline"] = {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
                                "sample": f"oracle numpy float32, {sample} regions of {wl.name}, median of 3 "
                                          f"({t1:.2f} s each)"}

@@ -25,10 +25,12 @@ class DeepPolyEngine:
     k, k]) plus ``in_shape`` / ``out_shape`` / ``stride`` / ``pad`` for conv layers;
     optional ``parents`` (layer-list indices, -1 = the network input; default the previous
     layer), listed in the reference reader's order (every parent before its children).
-    certifier: 'deeppoly' (deeppoly.cf, deeppoly_efficient.cf) or 'crown' (crown.cf, whose
+    certifier: 'deeppoly' (deeppoly.cf, deeppoly_efficient.cf), 'crown' (crown.cf, whose
     ReLU branch is decided over the whole batch: a CROWN run always takes the batch in
     one workspace chunk and checks the device status; when a layer takes the all-crossing
-    branch the bounds are recomputed by the general traversal of cfgpu.general).
+    branch the bounds are recomputed by the general traversal of cfgpu.general), 'zono'
+    (zono.cf, DeepZ: forward zonotope pass, linear chains) or 'ibp' (ibp.cf: interval
+    bounds).
     """
 
     def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
@@ -37,9 +39,10 @@ class DeepPolyEngine:
             raise ValueError("DeepPolyEngine runs on a CUDA device only (no CPU fallback)")
         self.input_size = int(input_size)
         self.n_spec = int(n_spec)
-        relax = {"deeppoly": _lib.CF_RELAX_DEEPPOLY, "crown": _lib.CF_RELAX_CROWN}
+        relax = {"deeppoly": _lib.CF_RELAX_DEEPPOLY, "crown": _lib.CF_RELAX_CROWN, "zono": _lib.CF_RELAX_ZONO,
+                 "ibp": _lib.CF_RELAX_IBP}
         if certifier not in relax:
-            raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly and crown)")
+            raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly, crown, zono and ibp)")
         self.certifier = certifier
         self._keep = []
         self._general = []        # (kind, W, b, parents) device tensors for cfgpu.general
@@ -95,6 +98,9 @@ class DeepPolyEngine:
                 check(_lib.CF_ERR_SHAPE, "network description")
         else:
             # Add / Concat: polyexps mix layers; the general traversal runs the whole network
+            if certifier not in ("deeppoly", "crown"):
+                raise NotImplementedError(f"{certifier} on a network with Add / Concat layers (the forward "
+                                          "drivers run chain networks)")
             if any(g[0] == "conv" for g in self._general):
                 raise NotImplementedError("conv layers in a network with Add / Concat layers (the general "
                                           "traversal runs linear, relu, add and concat layers)")

@@ -16,8 +16,14 @@ inner_prod, get_max_priority over the negated layer index) and one of three Relu
   * deeppoly_efficient.cf: the same relaxation applied to the affine's L/U polyexps
     (get_elem('L'/'U', prev)); it composes to exactly DeepPoly's bounds;
   * crown.cf: whole-layer if(any(...)) branches with the -l > u lower-slope choice.
+Two forward programs are recognised by their own Affine / Relu:
+  * zono.cf (DeepZ): the Affine maps the previous layer's symbolic expression Z and
+    concretises sum |coefficient|; the Relu opens fresh noise symbols (get_new_eps);
+  * ibp.cf: interval arithmetic on the previous layer's l / u (clamp sign split, no
+    traversal); the Relu clamps l and u.
 A transformer object may also declare itself with a ``cf_certifier`` attribute
-('deeppoly' or 'crown').  Other programs raise NotImplementedError.
+('deeppoly', 'crown', 'zono' or 'ibp').  Other programs (zono2.cf's whole-layer branches
+among them) raise NotImplementedError.
 """
 import inspect
 
@@ -34,10 +40,16 @@ _DEEPPOLY_RELU = ("convert_to_poly(", "operator.truediv", "operator.le", "operat
 _EFFICIENT_RELU = ("get_elem('L', prev", "get_elem('U', prev", "operator.truediv", "operator.le", "operator.ge",
                    "where(")
 _CROWN_RELU = ("if(", "any(", "operator.gt", "convert_to_poly(", "operator.truediv", "get_elem('U', prev")
+# zono.cf: forward symbol algebra (Affine concretises sum |coefficient|, Relu opens fresh symbols)
+_ZONO_AFFINE = ("get_elem('Z', prev", "get_mat(SymExpSparse.count", "inner_prod(", "clamp(", ".sum(2")
+_ZONO_RELU = ("get_new_eps(", "get_elem('Z', prev", "operator.truediv", "operator.le", "operator.ge", "where(")
+# ibp.cf: interval arithmetic over the previous layer's l / u
+_IBP_AFFINE = ("inner_prod(", "clamp(", "get_elem('l'", "get_elem('u'")
+_IBP_RELU = ("convert_to_float(", "operator.ge", "get_elem('l', prev", "get_elem('u', prev")
 
 
 def certifier_of(transformer):
-    """'deeppoly' or 'crown' for a recognised generated transformer, else raises."""
+    """'deeppoly', 'crown', 'zono' or 'ibp' for a recognised generated transformer, else raises."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
@@ -53,7 +65,14 @@ def certifier_of(transformer):
             return "deeppoly"
         if all(k in relu for k in _CROWN_RELU):
             return "crown"
-    raise NotImplementedError("this runtime runs the DeepPoly and CROWN certifier programs; the given "
+    branches = "if(" in relu or "any(" in relu
+    if all(k in affine for k in _ZONO_AFFINE) and all(k in relu for k in _ZONO_RELU) and not branches:
+        return "zono"
+    if (all(k in affine for k in _IBP_AFFINE) and all(k in relu for k in _IBP_RELU) and "get_max_priority(" not in affine
+            and "get_new_eps(" not in relu and "convert_to_poly(" not in relu and not branches):
+        return "ibp"
+    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf) and interval (ibp.cf) "
+                              "certifier programs; the given "
                               f"transformer ({cls.__name__}) is a different program")
 
 

@@ -75,7 +75,9 @@ def create_U(u, network, batch_size, no_sparsity=False):
 
 
 def create_Z(l, u, network, no_sparsity=False):
-    """Zonotope start state; used only by DeepZ-style programs, which this runtime does not run."""
+    """Zonotope start state of zono.cf-style programs (reference spec.py:106-132).  The
+    network driver builds it on the device from the input box (c0 = (l+u)/2, one symbol
+    per input neuron with coefficient (u-l)/2); this object only carries the network."""
     return SymExpSparse(network, None, None)
 
 

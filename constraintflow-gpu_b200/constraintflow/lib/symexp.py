@@ -1,11 +1,14 @@
 """Zonotope symbolic expressions (reference: constraintflow/lib/symexp.py:14-273).
 
-Kept importable for generated programs (`from constraintflow.lib.symexp import *`); the
-DeepZ family of certifiers that computes with them is not run by this runtime."""
+Kept importable for generated programs (`from constraintflow.lib.symexp import *`).  The
+zonotope state of zono.cf is held by the network driver on the device (cf_deeppoly_run with
+CF_RELAX_ZONO: symbol coefficients one row per noise symbol); Flow.flow runs the whole
+program there, so these objects are never computed with on the host."""
 
 
 def get_new_eps(*args, **kwargs):
-    raise NotImplementedError("zonotope (DeepZ) certifiers are not run by this runtime")
+    raise NotImplementedError("zonotope programs run as a whole in the network driver (Flow.flow); the "
+                              "op-by-op symbol algebra is not provided")
 
 
 class SymExpSparse:

@@ -15,6 +15,7 @@
 #include "cf_chain.cuh"
 #include "cf_common.cuh"
 #include "cf_kernels.cuh"
+#include "cf_plan.cuh"
 #include "cf_step.cuh"
 #include "cf_window.cuh"
 
@@ -75,30 +76,12 @@ cf_status launch_copy_rows(int64_t B, int64_t n, const float* src, int64_t ld_sr
 }
 
 // ------------------------------------------------------------------ network plan
-struct Img {
-  int32_t C, H, W;
-};
-
-struct Plan {
-  std::vector<int> affine;      // layer indices of affine layers, in order
-  std::vector<Img> in_img, out_img;  // per affine index: input / output image (linear: (n,1,1) out)
-  bool has_conv = false;
-  int64_t win_floats = 0;       // window path: per region, max rows*window floats of one buffer
-  std::vector<int> relu_after;  // per affine index: layer index of the ReLU that follows, or -1
-  std::vector<int64_t> col;     // per layer: first state column (input = 0)
-  int64_t n_out_last = 0;       // width of the last affine layer (property matrix columns)
-  int64_t N = 0;                // total neurons incl. input and property rows
-  int64_t spec_col = 0;
-  int64_t r_max = 0, k_max = 0, n_max = 0, relu_total = 0;
-  int64_t r_max_all = 0;        // rows of the widest bounded layer, first layer and property included
-};
-
 static void window_sizing(const cf_network* net, Plan& p);
 
-static cf_status make_plan(const cf_network* net, Plan& p) {
+cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
   CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
-  CF_REQUIRE(net->relaxation == CF_RELAX_DEEPPOLY || net->relaxation == CF_RELAX_CROWN, CF_ERR_UNSUPPORTED,
+  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_IBP, CF_ERR_UNSUPPORTED,
              "network: relaxation %d", net->relaxation);
   int64_t pos = net->n_input, prev_width = net->n_input;
   p.col.assign(net->n_layers, 0);
@@ -558,6 +541,7 @@ extern "C" int64_t cf_network_neurons(const cf_network* net) {
 extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk) {
   Plan p;
   if (make_plan(net, p) != CF_OK || chunk < 1) return 0;
+  if (is_forward(net)) return forward_workspace_bytes(net, p, chunk);
   return ws_layout(net, p, chunk).total;
 }
 
@@ -571,6 +555,8 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
   CF_REQUIRE(B >= 0, CF_ERR_SHAPE, "B < 0");
   if (B == 0) return CF_OK;
   CF_REQUIRE(l0 && u0 && specW && lb && ub && workspace, CF_ERR_NULL, "deeppoly_run: NULL argument");
+  if (is_forward(net))
+    return forward_run(net, p, B, l0, u0, specW, state_l, state_u, lb, ub, workspace, ws_bytes, as_stream(stream));
   // largest chunk that fits the workspace
   size_t base = ws_layout(net, p, 1).total;
   CF_REQUIRE(ws_bytes >= base, CF_ERR_WORKSPACE, "workspace %zu < %zu bytes needed for one region", ws_bytes, base);

@@ -26,7 +26,9 @@
  *   cf_concretize        the input-layer substitution + final bound (generated Affine tail;
  *                        DenseBlock.matmul_unequal_dims sparse_block.py:964)
  *   cf_deeppoly_run      Flow.flow over a chain network (constraintflow/lib/flow_sparse.py:27-228)
- *                        with the generated deeppoly transformer
+ *                        with the generated deeppoly / crown transformer, or the forward flow
+ *                        of zono.cf (SymExpSparse, constraintflow/lib/symexp.py:14-273;
+ *                        create_Z, spec.py:106-132) and ibp.cf
  *   cf_ew_binary / cf_ew_unary / cf_ew_where / cf_ew_clamp / cf_ew_any
  *                        block kernels of the gbcsr elementwise ops: SparseBlock.binary
  *                        (sparse_block.py:181), unary_operation (:60), where_block (:104),
@@ -72,8 +74,18 @@ enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
  *                      a batch, so cf_deeppoly_run requires the whole batch in one
  *                      workspace chunk (CF_ERR_WORKSPACE otherwise); the all-crossing
  *                      branch is not run on the GPU and cf_deeppoly_check reports it as
- *                      CF_ERR_UNSUPPORTED. */
-enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1 };
+ *                      CF_ERR_UNSUPPORTED.
+ *   CF_RELAX_ZONO      zono.cf (DeepZ): forward zonotope propagation.  The input box is one
+ *                      noise symbol per input neuron (constraintflow/lib/spec.py:106-132);
+ *                      an affine layer maps the symbol coefficients and concretises
+ *                      l/u = c -/+ sum |coefficient|; a ReLU opens one fresh symbol per
+ *                      neuron (constraintflow/lib/symexp.py:14) and its own l, u are 0.
+ *                      Linear layers only (CF_ERR_UNSUPPORTED for conv).
+ *   CF_RELAX_IBP       ibp.cf: interval bounds layer by layer (W+ l + W- u + b; ReLU
+ *                      clamps), linear and conv layers.
+ * CF_RELAX_ZONO and CF_RELAX_IBP run forward through cf_deeppoly_run as well; their
+ * regions are independent (any chunk size). */
+enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1, CF_RELAX_ZONO = 2, CF_RELAX_IBP = 3 };
 
 /* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
  * Conv: W_dev [cout, cin, kh, kw], b_dev [cout]; neurons in (c, y, x) order,
@@ -95,7 +107,7 @@ typedef struct cf_network {
   const cf_layer* layers;  /* host array */
   int32_t n_input;
   int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
-  int32_t relaxation;      /* CF_RELAX_DEEPPOLY or CF_RELAX_CROWN */
+  int32_t relaxation;      /* CF_RELAX_DEEPPOLY, CF_RELAX_CROWN, CF_RELAX_ZONO or CF_RELAX_IBP */
 } cf_network;
 
 /* Total neuron count N of the abstract state: input + every layer + property rows
@@ -106,7 +118,8 @@ int64_t cf_network_neurons(const cf_network* net);
  * in further chunks inside one cf_deeppoly_run call). */
 size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk);
 
-/* Whole DeepPoly pass over B regions.
+/* Whole certifier pass over B regions (the program net->relaxation names: DeepPoly /
+ * CROWN backsubstitution, or the zono / ibp forward passes).
  *   l0_dev, u0_dev   [B, n_input]   normalised input box
  *   spec_W_dev       [B, n_spec, n_out(last layer)]  per-region property matrix (bias 0)
  *   state_l_dev, state_u_dev  [B, N] or NULL: every neuron's bounds in the reference's

@@ -38,7 +38,7 @@ REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 
 # certifier programs of examples/compiler_examples/ whose generated code is kept and run
-PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient")
+PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient", "zono", "zono2", "ibp")
 
 # name -> (program, workload id, batch, eps)
 CASES = {
@@ -78,6 +78,20 @@ CASES = {
     "crown_w5_b2_e2e-3": ("crown", 5, 2, 0.002),
     "crown_w6_b2_e2e-3": ("crown", 6, 2, 0.002),
     "crown_w6_b2_e1e-1": ("crown", 6, 2, 0.1),
+    # zonotope (DeepZ) and interval programs: forward flow
+    "zono_w0_b4_e1e-3": ("zono", 0, 4, 0.001),
+    "zono_w0_b4_e1e-2": ("zono", 0, 4, 0.01),
+    "zono_w1_b8_e5e-4": ("zono", 1, 8, 0.0005),
+    "zono_w2_b4_e2e-3": ("zono", 2, 4, 0.002),
+    "zono_w2_b4_e2e-4": ("zono", 2, 4, 0.0002),
+    "zono_w3_b2_e2e-3": ("zono", 3, 2, 0.002),
+    "zono2_w0_b4_e1e-3": ("zono2", 0, 4, 0.001),
+    "zono2_w0_b2_e5e-2": ("zono2", 0, 2, 0.05),
+    "zono_w5_b4_e2e-3": ("zono", 5, 4, 0.002),
+    "ibp_w0_b4_e1e-3": ("ibp", 0, 4, 0.001),
+    "ibp_w2_b4_e2e-4": ("ibp", 2, 4, 0.0002),
+    "ibp_w3_b2_e2e-3": ("ibp", 3, 2, 0.002),
+    "ibp_w5_b4_e2e-4": ("ibp", 5, 4, 0.0002),
 }
 
 

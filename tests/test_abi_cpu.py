@@ -118,3 +118,27 @@ def test_argument_validation_without_launch():
     assert _lib.lib.cf_ew_binary(0, 9, shape, 8, 0, None, 8, 0, None, 8, 0, None) == _lib.CF_ERR_SHAPE
     # empty problems are no-ops that touch nothing
     assert _lib.lib.cf_relu_relax(0, 4, None, None, 4, None, None, 4, None, None, None, 0, None) == _lib.CF_OK
+
+
+@pytest.mark.parametrize("relax", [2, 3])
+def test_forward_programs_plan_without_device(relax):
+    """zono.cf / ibp.cf networks: same neuron layout, a workspace linear in the chunk, and
+    the zonotope driver's refusal of conv layers happens before any launch."""
+    assert (_lib.CF_RELAX_ZONO, _lib.CF_RELAX_IBP) == (2, 3)
+    wl = nets.workload(2)
+    net, keep = _net(wl)
+    net.relaxation = relax
+    assert _lib.lib.cf_network_neurons(ctypes.byref(net)) == 4403
+    w1 = _lib.lib.cf_deeppoly_workspace_bytes(ctypes.byref(net), 1)
+    w8 = _lib.lib.cf_deeppoly_workspace_bytes(ctypes.byref(net), 8)
+    w15 = _lib.lib.cf_deeppoly_workspace_bytes(ctypes.byref(net), 15)
+    assert 0 < w1 < w8 < w15 and abs((w15 - w8) / 7 - (w8 - w1) / 7) < 4096
+    st = _lib.lib.cf_deeppoly_run(ctypes.byref(net), 4, 8, 8, 8, None, None, 8, 8, 8, w1 - 1, None)
+    assert st == _lib.CF_ERR_WORKSPACE
+    conv, keep2 = _net(nets.workload(3))
+    conv.relaxation = relax
+    st = _lib.lib.cf_deeppoly_run(ctypes.byref(conv), 1, 8, 8, 8, None, None, 8, 8, 8, 1 << 30, None)
+    if relax == 2:
+        assert st == _lib.CF_ERR_UNSUPPORTED and b"conv" in _lib.lib.cf_last_error()
+    net.relaxation = 7
+    assert _lib.lib.cf_network_neurons(ctypes.byref(net)) == -1
