@@ -336,7 +336,8 @@ def run_cfgpu(args, rank, world, local):
     bf16, hbm, src = peaks()
     achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
     conv = any(L.kind == "conv" for L in wl.layers)
-    if conv or not eng.chain or args.certifier in ("zono", "ibp"):
+    zono_tc = args.certifier == "zono" and os.environ.get("CF_STEP_IMPL") != "simt"
+    if conv or not eng.chain or (args.certifier in ("zono", "ibp") and not zono_tc):
         # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
         # with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass: k_zono_gemm
         # over the noise-symbol rows -- all on the FP32 pipe.
@@ -365,7 +366,7 @@ def run_cfgpu(args, rank, world, local):
                      "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
                                         "CTAs) from one ncu --set full capture of this command")
                      if (args.workload, args.certifier) in NCU_TRAFFIC else None,
-                     "kernel": {"zono": "k_zono_gemm", "ibp": None}.get(
+                     "kernel": {"zono": "k_chain (zonotope mode)" if zono_tc else "k_zono_gemm", "ibp": None}.get(
                          args.certifier, "backsubstitution step" if eng.chain else "k_bmm (general traversal)"),
                      "peak_source": peak_src,
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,

@@ -149,6 +149,61 @@ __device__ __forceinline__ void lds16_row(uint32_t row_saddr, int k0, int K, flo
   }
 }
 
+// Column sums over the 32 lanes of a warp of the 16 values every lane holds (lane <->
+// row): four halving exchange rounds and a last pair exchange; afterwards v[0] of lanes
+// 2c and 2c+1 is the sum of column c.
+__device__ __forceinline__ void warp_colsum16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int o = 16 >> r, m = 8 >> r;
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < m; ++j) {
+      const float send = hi ? v[j] : v[j + m];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, o);
+      v[j] = (hi ? v[j + m] : v[j]) + recv;
+    }
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// Zonotope drain of 16 columns n0 .. n0+15 of this thread's row: store the row's values
+// (columns below N) and the warp's per-slot column sums of the positive / negative parts.
+__device__ __forceinline__ void zono_drain(const ChainParams& P, int N, int n0, const float (&x)[16], bool valid,
+                                           int64_t b, int64_t i, int slot, bool two_slots) {
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3;
+  if (valid) {
+    float* o = P.zout + b * P.zo_bs + i * N + n0;
+    if (P.zo_vec && n0 + 16 <= N) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        reinterpret_cast<float4*>(o)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (n0 + e < N) o[e] = x[e];
+    }
+  }
+  for (int sl = 0; sl < (two_slots ? 2 : 1); ++sl) {
+    float p[16], q[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float v = (valid && (!two_slots || slot == sl)) ? x[e] : 0.0f;
+      p[e] = fmaxf(v, 0.0f);
+      q[e] = fminf(v, 0.0f);
+    }
+    warp_colsum16(p);
+    warp_colsum16(q);
+    const int c = n0 + (lane >> 1);
+    if ((lane & 1) == 0 && c < N) {
+      const size_t idx = (((size_t)blockIdx.x * 4 + w) * 2 + sl) * (size_t)N + c;
+      P.zpos[idx] = p[0];
+      P.zneg[idx] = q[0];
+    }
+  }
+}
+
 // Shared-memory pieces the transform warps use.
 struct ChainSmem {
   uint32_t a_region;     // A stages (shared-memory byte address)
@@ -166,7 +221,7 @@ struct ChainSmem {
 // Transform / epilogue warps (threads 0-255).  Thread -> tile row (TMEM lane) r; the two
 // halves take the two 16-column halves of every 32-column chunk.  kStaged: relaxation
 // vectors come from the shared-memory step buffers; kBox: the input box from shared memory.
-template <bool kStaged, bool kBox>
+template <bool kStaged, bool kBox, bool kZono>
 __device__ __forceinline__ void chain_transform(const ChainParams& P, const ChainSmem& M, uint32_t tbase,
                                                 int64_t p0) {
   const int warp = threadIdx.x >> 5;
@@ -182,6 +237,10 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
     i = rem - b * P.R;
   }
   const bool lower = sb_ == 0;
+  // zonotope mode: does the CTA's row range reach into a second region
+  const bool two_slots = kZono && ((P.rows - 1 < (int64_t)blockIdx.x * 128 + 127 ? P.rows - 1
+                                                                                   : (int64_t)blockIdx.x * 128 + 127) /
+                                       P.R) != p0;
   float cacc = (valid && P.c0 && half == 0) ? P.c0[i] : 0.0f;
   float conc = 0.0f;
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -312,6 +371,13 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
         const uint32_t dst = tbase + (uint32_t)(s & 1) * 256u + lane_off;
         for (int q = half; q < ng; q += 2) {
           const int n0 = t * S.tile_n + q * 16;
+          if constexpr (kZono) {
+            float x[16];
+            tmem_ld16(dst + (uint32_t)(q * 16), x);
+            tmem_ld_wait();
+            zono_drain(P, S.N, n0, x, valid, b, i, slot, two_slots);
+            continue;
+          }
           float pb[16], nb[16], x[16];
           if (kBox) {
             lds16_row(box_pos, n0, nlim, pb);
@@ -334,6 +400,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
       if ((threadIdx.x & 31) == 0) mbar_arrive(&M.coef_empty[s & 1]);
     }
   }
+  if constexpr (kZono) return;   // rows and column sums were written by the drain
   // combine the two halves of every row
   if (half == 1) M.red[r] = conc + cacc;
   asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
@@ -343,6 +410,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   }
 }
 
+template <bool kZono>
 __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ ChainParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -516,12 +584,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     // ---------------------------------------------------------------- transform warps
     const ChainSmem M{smem_u32(a_region), smem_u32(coef_region), smem_u32(box_region), full_a, empty_a,
                       coef_full, coef_empty, box_full, acc_full, red};
-    if (box_staged)
-      chain_transform<true, true>(P, M, tbase, p0);
-    else if (staged)
-      chain_transform<true, false>(P, M, tbase, p0);
-    else
-      chain_transform<false, false>(P, M, tbase, p0);
+    if constexpr (kZono) {
+      if (staged)
+        chain_transform<true, false, true>(P, M, tbase, p0);
+      else
+        chain_transform<false, false, true>(P, M, tbase, p0);
+    } else {
+      if (box_staged)
+        chain_transform<true, true, false>(P, M, tbase, p0);
+      else if (staged)
+        chain_transform<true, false, false>(P, M, tbase, p0);
+      else
+        chain_transform<false, false, false>(P, M, tbase, p0);
+    }
   }
 
   tc_fence_before();
@@ -560,12 +635,19 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
                        (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 128 * 4;
   // input-box rows of up to kCoefSlots (bound, region) pairs, when they fit
   const size_t box_bytes = (size_t)kCoefSlots * 2 * P.n0 * 4;
-  const bool box_ok = coef_ok && P.n0 % 4 == 0 && a16(P.l0) && a16(P.u0) && fixed + box_bytes <= 227 * 1024;
+  const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && a16(P.l0) && a16(P.u0) &&
+                      fixed + box_bytes <= 227 * 1024;
   Q.box_smem_bytes = box_ok ? (uint32_t)box_bytes : 0u;
   size_t smem = fixed + Q.box_smem_bytes;
   // at least 116 KB so that one CTA (which holds all 512 TMEM columns) runs per SM
   if (smem < 116 * 1024) smem = 116 * 1024;
-  cudaError_t e = cudaFuncSetAttribute(k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (P.zono) {
+    CF_REQUIRE(P.S == 1 && P.R >= 128 && P.rows % P.R == 0 && P.zout && P.zpos && P.zneg, CF_ERR_UNSUPPORTED,
+               "chain: zonotope mode needs one step, >= 128 rows per region and its outputs");
+    Q.zo_vec = (P.st[0].N % 4 == 0 && a16(P.zout) && (P.zo_bs % 4) == 0) ? 1 : 0;
+  }
+  auto kern = P.zono ? k_chain<true> : k_chain<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) {
     set_error("chain: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     return CF_ERR_CUDA;
@@ -573,8 +655,8 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "chain: %zu bytes of shared memory", smem);
   const int64_t tiles = ceil_div(P.rows, 128);
   CF_REQUIRE(tiles <= 0x7fffffff, CF_ERR_SHAPE, "chain: too many rows");
-  k_chain<<<(unsigned)tiles, kThreads, smem, st>>>(Q);
-  return check_launch("k_chain");
+  kern<<<(unsigned)tiles, kThreads, smem, st>>>(Q);
+  return check_launch(P.zono ? "k_chain (zonotope)" : "k_chain");
 }
 
 }  // namespace cf

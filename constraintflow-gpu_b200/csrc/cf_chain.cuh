@@ -41,6 +41,17 @@ struct ChainParams {
   uint32_t stage_bytes, w_lo_off;       // filled by chain_launch
   uint32_t box_smem_bytes;              // input-box staging bytes (0: read from global memory)
   int32_t coef_ok;                      // relaxation vectors may be staged in shared memory
+  // Forward zonotope mode (zono != 0, one step, R >= 128, rows = B*R symbol rows of the
+  // lower half only): the step's ReLU relaxation is the column scaling alpha = lam, and the
+  // drain writes every row of the result to zout[b*zo_bs + i*N + n] and, per warp w = warp%4
+  // and region slot (region - first region of the CTA), the column sums of the positive /
+  // negative coefficients to zpos / zneg[((cta*4 + w)*2 + slot)*N + n].  No input box.
+  int32_t zono;
+  int32_t zo_vec;                       // 16-byte stores allowed for zout rows
+  float* zout;
+  int64_t zo_bs;
+  float* zpos;
+  float* zneg;
 };
 
 void chain_tile(int N, int& tile_n, int& n_tiles);

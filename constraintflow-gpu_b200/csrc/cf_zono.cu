@@ -18,6 +18,10 @@
 //     tiles of a region in a fixed order.
 // The ReLU's column scaling multiplies by lam = u/(u-l) where the reference divides
 // (u*M)/(u-l): the two differ by at most an ulp per coefficient.
+#include <stdlib.h>
+#include <string.h>
+
+#include "cf_chain.cuh"
 #include "cf_common.cuh"
 #include "cf_kernels.cuh"
 #include "cf_plan.cuh"
@@ -109,11 +113,10 @@ __global__ void __launch_bounds__(256) k_zono_gemm(int64_t E, int64_t K, int64_t
 
 // Rows of the symbols of a diagonal block d [B, K] (the input box, or the symbols the
 // previous ReLU opened): out[b, row0 + k, n] = d[b, k] W(b, k, n), with their column sums
-// in partial slot `slot`.  Grid (ceil(N/128), B), one thread per column.
+// in dpos/dneg[b, n].  Grid (ceil(N/128), B), one thread per column.
 __global__ void k_zono_diag(int64_t K, int64_t N, const float* __restrict__ d, const float* __restrict__ W,
                             int64_t w_bs, int64_t w_ks, int64_t w_ns, float* __restrict__ out, int64_t o_bs,
-                            int64_t row0, float* __restrict__ ppos, float* __restrict__ pneg, int64_t p_bs,
-                            int64_t slot) {
+                            int64_t row0, float* __restrict__ dpos, float* __restrict__ dneg) {
   const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.y;
   if (n >= N) return;
@@ -127,8 +130,8 @@ __global__ void k_zono_diag(int64_t K, int64_t N, const float* __restrict__ d, c
     sp += fmaxf(v, 0.0f);
     sn += fminf(v, 0.0f);
   }
-  ppos[b * p_bs + slot * N + n] = sp;
-  pneg[b * p_bs + slot * N + n] = sn;
+  dpos[b * N + n] = sp;
+  dneg[b * N + n] = sn;
 }
 
 // Affine constant: c'[b, n] = (sum_k W(b, k, n) c[b, k]) + bias[n].  Grid (ceil(N/128), B).
@@ -145,11 +148,25 @@ __global__ void k_zono_const(int64_t K, int64_t N, const float* __restrict__ c, 
   c_out[b * N + n] = s + (bias ? bias[n] : 0.0f);
 }
 
+// Where the column sums of one affine layer's symbol rows are: the GEMM tiles of
+// k_zono_gemm ([b][tile][n], `tiles` per region), or the per-warp sums of the tensor-core
+// chain (E rows per region in 128-row CTAs: [((cta*4 + w)*2 + slot)*N + n]); then the
+// diagonal block's sums ([b][n]) if one entered the layer.
+struct ZonoSums {
+  const float* gpos;
+  const float* gneg;
+  int64_t tiles;
+  const float* cpos;
+  const float* cneg;
+  int64_t E;
+  const float* dpos;
+  const float* dneg;
+};
+
 // Concretisation: l = ((-P) + Nn) + c, u = (P + (-Nn)) + c with P / Nn the positive /
-// negative coefficient sums over the `slots` partials.  Writes the compact l/u [B, N],
-// the state columns (ld_state) and, for the property layer, the float64 bounds.
-__global__ void k_zono_bounds(int64_t B, int64_t N, int64_t slots, const float* __restrict__ ppos,
-                              const float* __restrict__ pneg, int64_t p_bs, const float* __restrict__ c,
+// negative coefficient sums, added in a fixed order.  Writes the compact l/u [B, N], the
+// state columns (ld_state) and, for the property layer, the float64 bounds.
+__global__ void k_zono_bounds(int64_t B, int64_t N, ZonoSums S, const float* __restrict__ c,
                               float* __restrict__ lo, float* __restrict__ uo, float* __restrict__ sl,
                               float* __restrict__ su, int64_t ld_state, double* __restrict__ lb,
                               double* __restrict__ ub) {
@@ -157,9 +174,25 @@ __global__ void k_zono_bounds(int64_t B, int64_t N, int64_t slots, const float* 
   if (t >= B * N) return;
   const int64_t b = t / N, n = t - b * N;
   float P = 0.0f, Q = 0.0f;
-  for (int64_t s = 0; s < slots; ++s) {
-    P += ppos[b * p_bs + s * N + n];
-    Q += pneg[b * p_bs + s * N + n];
+  if (S.gpos) {
+    for (int64_t s = 0; s < S.tiles; ++s) {
+      P += S.gpos[(b * S.tiles + s) * N + n];
+      Q += S.gneg[(b * S.tiles + s) * N + n];
+    }
+  } else if (S.cpos && S.E > 0) {
+    const int64_t c_lo = b * S.E / 128, c_hi = ((b + 1) * S.E - 1) / 128;
+    for (int64_t cta = c_lo; cta <= c_hi; ++cta) {
+      const int64_t slot = b - cta * 128 / S.E;
+      for (int w = 0; w < 4; ++w) {
+        const int64_t idx = ((cta * 4 + w) * 2 + slot) * N + n;
+        P += S.cpos[idx];
+        Q += S.cneg[idx];
+      }
+    }
+  }
+  if (S.dpos) {
+    P += S.dpos[b * N + n];
+    Q += S.dneg[b * N + n];
   }
   const float cc = c[t];
   const float l = (-P + Q) + cc;
@@ -329,12 +362,19 @@ __global__ void k_ibp_relu(int64_t B, int64_t n, const float* __restrict__ l, co
 
 static inline size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Tensor-core chain (k_chain in zonotope mode) for the symbol-row GEMMs unless
+// CF_STEP_IMPL=simt selects the CUDA-core kernel; the chain needs >= 128 rows per region.
+static bool zono_use_chain(int64_t E) {
+  const char* e = getenv("CF_STEP_IMPL");
+  return E >= 128 && !(e && strcmp(e, "simt") == 0);
+}
+
 // Symbol bookkeeping of the zonotope pass, per affine index a (a == affine.size(): the
 // property layer): rows stored before the layer (E_in) and the width of the diagonal
 // block entering it (D_in, 0 if none).
 struct ZonoShape {
   std::vector<int64_t> K, N, E_in, D_in;
-  int64_t max_rows_n = 0, max_parts_n = 0, n_max = 0;
+  int64_t max_rows_n = 0, max_tiles_n = 0, max_cta_rows_n = 0, n_max = 0;
 };
 
 static ZonoShape zono_shape(const cf_network* net, const Plan& p) {
@@ -350,8 +390,8 @@ static ZonoShape zono_shape(const cf_network* net, const Plan& p) {
     z.E_in.push_back(E);
     z.D_in.push_back(D);
     if (a < na && (E + D) * N > z.max_rows_n) z.max_rows_n = (E + D) * N;
-    const int64_t slots = ceil_div(E, kZT) + 1;
-    if (slots * N > z.max_parts_n) z.max_parts_n = slots * N;
+    if (ceil_div(E, kZT) * N > z.max_tiles_n) z.max_tiles_n = ceil_div(E, kZT) * N;
+    if (a < na && E * N > z.max_cta_rows_n) z.max_cta_rows_n = E * N;
     if (N > z.n_max) z.n_max = N;
     if (K > z.n_max) z.n_max = K;
     E += D;
@@ -361,23 +401,28 @@ static ZonoShape zono_shape(const cf_network* net, const Plan& p) {
 }
 
 struct FwdLayout {
-  size_t err, wt, A[2], P[2], C[2], lam, nu, lu[2], state, total;
-  std::vector<size_t> wt_off;
+  size_t err, wt, A[2], G[2], Z[2], Dg[2], C[2], lam, nu, zeros, lu[2], state, total;
+  std::vector<size_t> wt_off, wimg_off;
 };
 
 static FwdLayout fwd_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   FwdLayout w;
   size_t off = 0;
+  const bool zono = net->relaxation == CF_RELAX_ZONO;
   w.err = off; off += 256;
   w.wt = off;
   w.wt_off.assign(p.affine.size(), 0);
+  w.wimg_off.assign(p.affine.size(), 0);
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     if (L.kind != CF_LAYER_LINEAR) continue;
     w.wt_off[a] = off;
     off += al256((size_t)L.n_in * L.n_out * sizeof(float));
+    if (zono) {  // tensor-core image of W^T [n_in, n_out]
+      w.wimg_off[a] = off;
+      off += al256(chain_wimg_bytes(L.n_in, L.n_out));
+    }
   }
-  const bool zono = net->relaxation == CF_RELAX_ZONO;
   const ZonoShape z = zono ? zono_shape(net, p) : ZonoShape{};
   int64_t n_max = z.n_max;
   if (!zono) {
@@ -386,16 +431,23 @@ static FwdLayout fwd_layout(const cf_network* net, const Plan& p, int64_t Bc) {
       if (net->layers[li].n_out > n_max) n_max = net->layers[li].n_out;
   }
   const size_t a_bytes = zono ? al256((size_t)Bc * z.max_rows_n * sizeof(float)) : 0;
-  const size_t p_bytes = zono ? al256((size_t)Bc * z.max_parts_n * sizeof(float)) : 0;
+  const size_t g_bytes = zono ? al256((size_t)Bc * z.max_tiles_n * sizeof(float)) : 0;
+  // chain column sums: 8 (warp, slot) rows of N per 128-row CTA, ceil(Bc*E/128) CTAs
+  const size_t z_bytes = zono ? al256((size_t)8 * (Bc * z.max_cta_rows_n / 128 + (z.n_max + 1)) * sizeof(float)) : 0;
   const size_t v_bytes = al256((size_t)Bc * n_max * sizeof(float));
   w.A[0] = off; off += a_bytes;
   w.A[1] = off; off += a_bytes;
-  w.P[0] = off; off += p_bytes;
-  w.P[1] = off; off += p_bytes;
+  w.G[0] = off; off += g_bytes;
+  w.G[1] = off; off += g_bytes;
+  w.Z[0] = off; off += z_bytes;
+  w.Z[1] = off; off += z_bytes;
+  w.Dg[0] = off; off += zono ? v_bytes : 0;
+  w.Dg[1] = off; off += zono ? v_bytes : 0;
   w.C[0] = off; off += zono ? v_bytes : 0;
   w.C[1] = off; off += zono ? v_bytes : 0;
   w.lam = off; off += zono ? v_bytes : 0;
   w.nu = off; off += zono ? v_bytes : 0;
+  w.zeros = off; off += zono ? v_bytes : 0;
   w.lu[0] = off; off += 2 * v_bytes;
   w.lu[1] = off; off += 2 * v_bytes;
   w.state = off; off += al256((size_t)2 * Bc * p.N * sizeof(float));
@@ -413,11 +465,16 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
   const ZonoShape z = zono_shape(net, p);
   const int64_t n0 = net->n_input, Ntot = p.N;
   float* A[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
-  float* Pp = reinterpret_cast<float*>(ws + w.P[0]);
-  float* Pn = reinterpret_cast<float*>(ws + w.P[1]);
+  float* Gp = reinterpret_cast<float*>(ws + w.G[0]);
+  float* Gn = reinterpret_cast<float*>(ws + w.G[1]);
+  float* Zp = reinterpret_cast<float*>(ws + w.Z[0]);
+  float* Zn = reinterpret_cast<float*>(ws + w.Z[1]);
+  float* Dp = reinterpret_cast<float*>(ws + w.Dg[0]);
+  float* Dn = reinterpret_cast<float*>(ws + w.Dg[1]);
   float* C[2] = {reinterpret_cast<float*>(ws + w.C[0]), reinterpret_cast<float*>(ws + w.C[1])};
   float* lam = reinterpret_cast<float*>(ws + w.lam);
   float* nu = reinterpret_cast<float*>(ws + w.nu);
+  float* zeros = reinterpret_cast<float*>(ws + w.zeros);
   const int64_t vstride = (int64_t)((w.lu[1] - w.lu[0]) / 2 / sizeof(float));
   float* lo = reinterpret_cast<float*>(ws + w.lu[0]);
   float* uo = lo + vstride;
@@ -447,19 +504,49 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
     }
     float* out = spec ? nullptr : A[cur ^ 1];
     const int64_t o_bs = (E + (diag ? K : 0)) * N;
-    const int64_t T = ceil_div(E, kZT);
-    const int64_t p_bs = (T + 1) * N;
+    ZonoSums S{nullptr, nullptr, 0, nullptr, nullptr, 0, diag ? Dp : nullptr, diag ? Dn : nullptr};
     if (E > 0) {
-      dim3 grid((unsigned)ceil_div(N, kZT), (unsigned)T, (unsigned)Bc);
-      prof_step_begin(st);
-      k_zono_gemm<<<grid, 256, 0, st>>>(E, K, N, A[cur], E * K, lam_in, W, w_bs, w_ks, w_ns, out, o_bs, Pp, Pn,
-                                         p_bs);
-      prof_step_end(st, 2.0 * Bc * E * K * N, 4.0 * Bc * (E * K + E * N));
-      CF_TRY(check_launch("k_zono_gemm"));
+      if (!spec && zono_use_chain(E)) {
+        // symbol rows on the tensor cores: one chain step (ReLU column scaling, then W^T)
+        ChainParams P{};
+        P.S = 1;
+        ChainStep& CS = P.st[0];
+        CS.wimg = reinterpret_cast<const uint8_t*>(ws + w.wimg_off[a]);
+        CS.alpha = lam_in;
+        CS.lam = lam_in;
+        CS.mu = zeros;       // constant terms of the chain are not used in this mode
+        CS.bias = zeros;
+        CS.K = (int32_t)K;
+        CS.N = (int32_t)N;
+        chain_tile((int)N, CS.tile_n, CS.n_tiles);
+        CS.kchunks = (int32_t)ceil_div(K, 32);
+        P.B = Bc; P.R = E; P.rows = Bc * E;
+        P.A0 = A[cur]; P.a_ss = 0; P.a_bs = E * K; P.a_rs = K;
+        P.n0 = N;
+        P.err = reinterpret_cast<int*>(ws + w.err);
+        P.a0_vec = (K % 4 == 0) ? 1 : 0;
+        P.zono = 1;
+        P.zout = out; P.zo_bs = o_bs;
+        P.zpos = Zp; P.zneg = Zn;
+        prof_step_begin(st);
+        cf_status cs = chain_launch(P, st);
+        prof_step_end(st, 2.0 * Bc * E * K * N, 4.0 * Bc * (E * K + E * N));
+        CF_TRY(cs);
+        S.cpos = Zp; S.cneg = Zn; S.E = E;
+      } else {
+        const int64_t T = ceil_div(E, kZT);
+        dim3 grid((unsigned)ceil_div(N, kZT), (unsigned)T, (unsigned)Bc);
+        prof_step_begin(st);
+        k_zono_gemm<<<grid, 256, 0, st>>>(E, K, N, A[cur], E * K, lam_in, W, w_bs, w_ks, w_ns, out, o_bs, Gp,
+                                           Gn, T * N);
+        prof_step_end(st, 2.0 * Bc * E * K * N, 4.0 * Bc * (E * K + E * N));
+        CF_TRY(check_launch("k_zono_gemm"));
+        S.gpos = Gp; S.gneg = Gn; S.tiles = T;
+      }
     }
     if (diag) {
       dim3 grid((unsigned)ceil_div(N, 128), (unsigned)Bc);
-      k_zono_diag<<<grid, 128, 0, st>>>(K, N, nu, W, w_bs, w_ks, w_ns, out, o_bs, E, Pp, Pn, p_bs, T);
+      k_zono_diag<<<grid, 128, 0, st>>>(K, N, nu, W, w_bs, w_ks, w_ns, out, o_bs, E, Dp, Dn);
       CF_TRY(check_launch("k_zono_diag"));
     }
     {
@@ -468,14 +555,9 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
       CF_TRY(check_launch("k_zono_const"));
       cc ^= 1;
     }
-    {
-      // partial slots: the T GEMM tiles, then (at index T) the diagonal block's sums
-      const int64_t slots = diag ? T + 1 : T;
-      k_zono_bounds<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, slots, Pp, Pn, p_bs, C[cc], lo, uo,
-                                                                     sl + col, su + col, Ntot, spec ? lb : nullptr,
-                                                                     spec ? ub : nullptr);
-      CF_TRY(check_launch("k_zono_bounds"));
-    }
+    k_zono_bounds<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, S, C[cc], lo, uo, sl + col, su + col, Ntot,
+                                                                   spec ? lb : nullptr, spec ? ub : nullptr);
+    CF_TRY(check_launch("k_zono_bounds"));
     if (spec) break;
     cur ^= 1;
     lam_in = nullptr;
@@ -566,12 +648,18 @@ cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const flo
     set_error("forward run: cudaMemsetAsync failed");
     return CF_ERR_CUDA;
   }
+  if (zono && cudaMemsetAsync(ws + w.zeros, 0, w.lu[0] - w.zeros, st) != cudaSuccess) {
+    set_error("forward run: cudaMemsetAsync failed");
+    return CF_ERR_CUDA;
+  }
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     if (L.kind != CF_LAYER_LINEAR) continue;
+    float* Wt = reinterpret_cast<float*>(ws + w.wt_off[a]);
     dim3 grid((unsigned)ceil_div(L.n_in, 32), (unsigned)ceil_div(L.n_out, 32));
-    k_transpose<<<grid, dim3(32, 8), 0, st>>>(L.n_out, L.n_in, L.W_dev, reinterpret_cast<float*>(ws + w.wt_off[a]));
+    k_transpose<<<grid, dim3(32, 8), 0, st>>>(L.n_out, L.n_in, L.W_dev, Wt);
     CF_TRY(check_launch("k_transpose"));
+    if (zono) CF_TRY(chain_prep_weights(Wt, L.n_in, L.n_out, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
   }
   const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
   for (int64_t b0 = 0; b0 < B; b0 += Bc) {
