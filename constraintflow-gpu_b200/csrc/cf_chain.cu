@@ -289,6 +289,10 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
     // accumulates the constant: mu and bias terms)
     auto tile_chunks = [&](auto relu_c, auto first_c) -> bool {
       constexpr bool kRelu = decltype(relu_c)::value, kFirst = decltype(first_c)::value;
+      // zonotope mode: every chunk's rows come from global memory; the next chunk's values
+      // are loaded one chunk ahead so that their latency overlaps this chunk's transform
+      float vnext[16];
+      if constexpr (kZono) load16g(a0row, half * 16, valid ? K : 0, P.a0_vec, vnext);
       for (int c = 0; c < S.kchunks; ++c, ++g) {
         const uint32_t stage = g % kAStages, round = g / kAStages;
         const int k0 = c * 32 + half * 16;
@@ -308,7 +312,11 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
           }
           if (kFirst) load16g(g_bias, k0, K, cvec, bv);
         }
-        if (s == 0) {
+        if (kZono) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = vnext[e];
+          if (c + 1 < S.kchunks) load16g(a0row, k0 + 32, valid ? K : 0, P.a0_vec, vnext);
+        } else if (s == 0) {
           load16g(a0row, k0, valid ? K : 0, P.a0_vec, v);
         } else if (k0 < src_cols) {
           // columns [K, tile_n) of the previous accumulator are exact zeros (zero-padded W);

@@ -361,10 +361,12 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
   return s;
 }
 
-// One chunk of Bc regions.  All pointers already offset to the chunk.
-static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
-                           const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
-                           const WsLayout& w, cudaStream_t st) {
+// Network layers li_begin .. li_end-1 (li == n_layers: the property layer) of one chunk of
+// Bc regions.  All pointers already offset to the chunk.  Layer 0 also writes the input
+// columns of the state.
+static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
+                            const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
+                            const WsLayout& w, cudaStream_t st, int li_begin, int li_end) {
   (void)w.wimg;
   const int64_t N = p.N, n0 = net->n_input;
   float* Abuf[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
@@ -383,8 +385,10 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
       rm[a] = q; q += Bc * n;
     }
   }
-  CF_TRY(launch_copy_rows(Bc, n0, l0, n0, st_l, N, st));
-  CF_TRY(launch_copy_rows(Bc, n0, u0, n0, st_u, N, st));
+  if (li_begin == 0) {
+    CF_TRY(launch_copy_rows(Bc, n0, l0, n0, st_l, N, st));
+    CF_TRY(launch_copy_rows(Bc, n0, u0, n0, st_u, N, st));
+  }
 
   // bound one affine-type layer: rows R, coefficient source (A0 strides), bias c0
   auto bound_layer = [&](size_t ma, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs, const float* c0,
@@ -465,14 +469,16 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
-    if (p.has_conv)
-      CF_TRY(bound_window(a, col));
-    else if (chain_applicable(net, p, a))
-      CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
-                                st_u + col, ra, rl, rm, st));
-    else
-      CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
-    if (p.relu_after[a] >= 0) {
+    if (p.affine[a] >= li_begin && p.affine[a] < li_end) {
+      if (p.has_conv)
+        CF_TRY(bound_window(a, col));
+      else if (chain_applicable(net, p, a))
+        CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
+                                  st_u + col, ra, rl, rm, st));
+      else
+        CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
+    }
+    if (p.relu_after[a] >= li_begin && p.relu_after[a] < li_end) {
       const cf_layer& Rl = net->layers[p.relu_after[a]];
       int64_t rcol = p.col[p.relu_after[a]];
       if (net->relaxation == CF_RELAX_CROWN) {
@@ -485,6 +491,7 @@ static cf_status run_chunk(const cf_network* net, const Plan& p, int64_t Bc, con
       }
     }
   }
+  if (net->n_layers < li_begin || net->n_layers >= li_end) return CF_OK;
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
   if (p.has_conv) {
     const int64_t R = net->n_spec;
@@ -590,10 +597,45 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
     int64_t nb = (B - b0 < Bc) ? (B - b0) : Bc;
     float* sl = state_l ? state_l + b0 * N : reinterpret_cast<float*>(ws + w.state);
     float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
-    CF_TRY(run_chunk(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su, lb + b0 * ns,
-                     ub + b0 * ns, ws, w, st));
+    CF_TRY(run_layers(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su,
+                      lb + b0 * ns, ub + b0 * ns, ws, w, st, 0, net->n_layers + 1));
   }
   return CF_OK;
+}
+
+extern "C" cf_status cf_deeppoly_layer(const cf_network* net, int32_t layer, int64_t B, const float* l0,
+                                       const float* u0, const float* specW, float* state_l, float* state_u,
+                                       double* lb, double* ub, void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  CF_INJECT("deeppoly_layer");
+  Plan p;
+  CF_TRY(make_plan(net, p));
+  CF_REQUIRE(layer >= 0 && layer <= net->n_layers, CF_ERR_SHAPE, "layer %d of a %d-layer network", layer,
+             net->n_layers);
+  CF_REQUIRE(B >= 0, CF_ERR_SHAPE, "B < 0");
+  if (B == 0) return CF_OK;
+  CF_REQUIRE(l0 && u0 && specW && state_l && state_u && lb && ub && workspace, CF_ERR_NULL,
+             "deeppoly_layer: NULL argument");
+  cudaStream_t st = as_stream(stream);
+  if (is_forward(net))
+    return forward_layer(net, p, layer, B, l0, u0, specW, state_l, state_u, lb, ub, workspace, ws_bytes, st);
+  const WsLayout w = ws_layout(net, p, B);
+  CF_REQUIRE(ws_bytes >= w.total, CF_ERR_WORKSPACE,
+             "per-layer runs keep the whole batch: workspace %zu < %zu bytes (cf_deeppoly_workspace_bytes(net, B))",
+             ws_bytes, w.total);
+  char* ws = static_cast<char*>(workspace);
+  if (layer == 0 && cudaMemsetAsync(ws + w.err, 0, w.wimg - w.err, st) != cudaSuccess) {
+    set_error("deeppoly_layer: cudaMemsetAsync failed");
+    return CF_ERR_CUDA;
+  }
+  if (use_chain() && !p.has_conv) {
+    for (size_t a = 0; a < p.affine.size(); ++a) {
+      const cf_layer& L = net->layers[p.affine[a]];
+      if (p.affine[a] == layer)
+        CF_TRY(chain_prep_weights(L.W_dev, L.n_out, L.n_in, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
+    }
+  }
+  return run_layers(net, p, B, l0, u0, specW, state_l, state_u, lb, ub, ws, w, st, layer, layer + 1);
 }
 
 extern "C" cf_status cf_deeppoly_check(const void* workspace, void* stream) {

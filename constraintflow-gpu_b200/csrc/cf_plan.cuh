@@ -38,5 +38,10 @@ size_t forward_workspace_bytes(const cf_network* net, const Plan& p, int64_t chu
 cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const float* l0, const float* u0,
                       const float* specW, float* state_l, float* state_u, double* lb, double* ub, void* ws,
                       size_t ws_bytes, cudaStream_t st);
+// One layer of a forward pass (layer == n_layers: the property layer); the workspace holds
+// the whole batch and the layers before it ran on it.
+cf_status forward_layer(const cf_network* net, const Plan& p, int layer, int64_t B, const float* l0,
+                        const float* u0, const float* specW, float* state_l, float* state_u, double* lb, double* ub,
+                        void* ws, size_t ws_bytes, cudaStream_t st);
 
 }  // namespace cf

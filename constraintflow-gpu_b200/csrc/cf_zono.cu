@@ -113,39 +113,63 @@ __global__ void __launch_bounds__(256) k_zono_gemm(int64_t E, int64_t K, int64_t
 
 // Rows of the symbols of a diagonal block d [B, K] (the input box, or the symbols the
 // previous ReLU opened): out[b, row0 + k, n] = d[b, k] W(b, k, n), with their column sums
-// in dpos/dneg[b, n].  Grid (ceil(N/128), B), one thread per column.
-__global__ void k_zono_diag(int64_t K, int64_t N, const float* __restrict__ d, const float* __restrict__ W,
-                            int64_t w_bs, int64_t w_ks, int64_t w_ns, float* __restrict__ out, int64_t o_bs,
-                            int64_t row0, float* __restrict__ dpos, float* __restrict__ dneg) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// in dpos/dneg[b, n].  Block (32, 8): 32 columns x 8 interleaved row groups, the groups'
+// sums added in a fixed order; grid (ceil(N/32), B).
+__global__ void __launch_bounds__(256) k_zono_diag(int64_t K, int64_t N, const float* __restrict__ d,
+                                                   const float* __restrict__ W, int64_t w_bs, int64_t w_ks,
+                                                   int64_t w_ns, float* __restrict__ out, int64_t o_bs, int64_t row0,
+                                                   float* __restrict__ dpos, float* __restrict__ dneg) {
+  __shared__ float red[2][8][32];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t n = (int64_t)blockIdx.x * 32 + tx;
   const int64_t b = blockIdx.y;
-  if (n >= N) return;
-  const float* db = d + b * K;
-  const float* Wb = W + b * w_bs + n * w_ns;
-  float* ob = out ? out + b * o_bs + row0 * N + n : nullptr;
   float sp = 0.0f, sn = 0.0f;
-  for (int64_t k = 0; k < K; ++k) {
-    const float v = db[k] * Wb[k * w_ks];
-    if (ob) ob[k * N] = v;
-    sp += fmaxf(v, 0.0f);
-    sn += fminf(v, 0.0f);
+  if (n < N) {
+    const float* db = d + b * K;
+    const float* Wb = W + b * w_bs + n * w_ns;
+    float* ob = out ? out + b * o_bs + row0 * N + n : nullptr;
+    for (int64_t k = ty; k < K; k += 8) {
+      const float v = db[k] * Wb[k * w_ks];
+      if (ob) ob[k * N] = v;
+      sp += fmaxf(v, 0.0f);
+      sn += fminf(v, 0.0f);
+    }
   }
-  dpos[b * N + n] = sp;
-  dneg[b * N + n] = sn;
+  red[0][ty][tx] = sp;
+  red[1][ty][tx] = sn;
+  __syncthreads();
+  if (ty < 2 && n < N) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += red[ty][j][tx];
+    (ty == 0 ? dpos : dneg)[b * N + n] = s;
+  }
 }
 
-// Affine constant: c'[b, n] = (sum_k W(b, k, n) c[b, k]) + bias[n].  Grid (ceil(N/128), B).
-__global__ void k_zono_const(int64_t K, int64_t N, const float* __restrict__ c, const float* __restrict__ W,
-                             int64_t w_bs, int64_t w_ks, int64_t w_ns, const float* __restrict__ bias,
-                             float* __restrict__ c_out) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Affine constant: c'[b, n] = (sum_k W(b, k, n) c[b, k]) + bias[n].  Block (32, 8) as in
+// k_zono_diag; grid (ceil(N/32), B).
+__global__ void __launch_bounds__(256) k_zono_const(int64_t K, int64_t N, const float* __restrict__ c,
+                                                    const float* __restrict__ W, int64_t w_bs, int64_t w_ks,
+                                                    int64_t w_ns, const float* __restrict__ bias,
+                                                    float* __restrict__ c_out) {
+  __shared__ float red[8][32];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t n = (int64_t)blockIdx.x * 32 + tx;
   const int64_t b = blockIdx.y;
-  if (n >= N) return;
-  const float* cb = c + b * K;
-  const float* Wb = W + b * w_bs + n * w_ns;
   float s = 0.0f;
-  for (int64_t k = 0; k < K; ++k) s = fmaf(Wb[k * w_ks], cb[k], s);
-  c_out[b * N + n] = s + (bias ? bias[n] : 0.0f);
+  if (n < N) {
+    const float* cb = c + b * K;
+    const float* Wb = W + b * w_bs + n * w_ns;
+    for (int64_t k = ty; k < K; k += 8) s = fmaf(Wb[k * w_ks], cb[k], s);
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && n < N) {
+    float t = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][tx];
+    c_out[b * N + n] = t + (bias ? bias[n] : 0.0f);
+  }
 }
 
 // Where the column sums of one affine layer's symbol rows are: the GEMM tiles of
@@ -459,9 +483,12 @@ size_t forward_workspace_bytes(const cf_network* net, const Plan& p, int64_t chu
   return fwd_layout(net, p, chunk).total;
 }
 
-static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
-                            const float* specW, float* sl, float* su, double* lb, double* ub, char* ws,
-                            const FwdLayout& w, cudaStream_t st) {
+// Network layers li_begin .. li_end-1 (li == n_layers: the property layer) of the zonotope
+// pass over one chunk.  Which buffers hold a layer's inputs follows from its position, so a
+// range can start at any layer of a pass that ran the layers before it on this workspace.
+static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
+                             const float* specW, float* sl, float* su, double* lb, double* ub, char* ws,
+                             const FwdLayout& w, cudaStream_t st, int li_begin, int li_end) {
   const ZonoShape z = zono_shape(net, p);
   const int64_t n0 = net->n_input, Ntot = p.N;
   float* A[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
@@ -478,16 +505,41 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
   const int64_t vstride = (int64_t)((w.lu[1] - w.lu[0]) / 2 / sizeof(float));
   float* lo = reinterpret_cast<float*>(ws + w.lu[0]);
   float* uo = lo + vstride;
-  CF_TRY(launch_copy_rows(Bc, n0, l0, n0, sl, Ntot, st));
-  CF_TRY(launch_copy_rows(Bc, n0, u0, n0, su, Ntot, st));
-  k_zono_init<<<(unsigned)ceil_div(Bc * n0, 256), 256, 0, st>>>(Bc * n0, l0, u0, C[0], nu);
-  CF_TRY(check_launch("k_zono_init"));
+  if (li_begin == 0) {
+    CF_TRY(launch_copy_rows(Bc, n0, l0, n0, sl, Ntot, st));
+    CF_TRY(launch_copy_rows(Bc, n0, u0, n0, su, Ntot, st));
+    k_zono_init<<<(unsigned)ceil_div(Bc * n0, 256), 256, 0, st>>>(Bc * n0, l0, u0, C[0], nu);
+    CF_TRY(check_launch("k_zono_init"));
+  }
   int cur = 0, cc = 0;
   const float* lam_in = nullptr;        // column scaling of the ReLU before the next affine
   bool diag = true;                     // a diagonal block (nu) enters the next affine
   const size_t na = p.affine.size();
   for (size_t a = 0; a <= na; ++a) {
     const bool spec = a == na;
+    const int li_aff = spec ? net->n_layers : p.affine[a];
+    const int li_relu = spec ? -1 : p.relu_after[a];
+    if (li_aff >= li_end) break;
+    if (li_aff < li_begin) {
+      // layers already run: advance the buffer positions as they did
+      cur ^= 1;
+      cc ^= 1;
+      lam_in = nullptr;
+      diag = false;
+      if (li_relu >= 0) {
+        if (li_relu >= li_begin && li_relu < li_end) {
+          const int64_t N = z.N[a];
+          const int64_t rcol = p.col[li_relu];
+          k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, lo, uo, C[cc], lam, nu, C[cc ^ 1],
+                                                                       sl + rcol, su + rcol, Ntot);
+          CF_TRY(check_launch("k_zono_relu"));
+        }
+        cc ^= 1;
+        lam_in = lam;
+        diag = true;
+      }
+      continue;
+    }
     const int64_t K = z.K[a], N = z.N[a], E = z.E_in[a];
     const float* W;
     int64_t w_bs, w_ks, w_ns;
@@ -545,13 +597,13 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
       }
     }
     if (diag) {
-      dim3 grid((unsigned)ceil_div(N, 128), (unsigned)Bc);
-      k_zono_diag<<<grid, 128, 0, st>>>(K, N, nu, W, w_bs, w_ks, w_ns, out, o_bs, E, Dp, Dn);
+      dim3 grid((unsigned)ceil_div(N, 32), (unsigned)Bc);
+      k_zono_diag<<<grid, dim3(32, 8), 0, st>>>(K, N, nu, W, w_bs, w_ks, w_ns, out, o_bs, E, Dp, Dn);
       CF_TRY(check_launch("k_zono_diag"));
     }
     {
-      dim3 grid((unsigned)ceil_div(N, 128), (unsigned)Bc);
-      k_zono_const<<<grid, 128, 0, st>>>(K, N, C[cc], W, w_bs, w_ks, w_ns, bias, C[cc ^ 1]);
+      dim3 grid((unsigned)ceil_div(N, 32), (unsigned)Bc);
+      k_zono_const<<<grid, dim3(32, 8), 0, st>>>(K, N, C[cc], W, w_bs, w_ks, w_ns, bias, C[cc ^ 1]);
       CF_TRY(check_launch("k_zono_const"));
       cc ^= 1;
     }
@@ -562,8 +614,8 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
     cur ^= 1;
     lam_in = nullptr;
     diag = false;
-    if (p.relu_after[a] >= 0) {
-      const int64_t rcol = p.col[p.relu_after[a]];
+    if (li_relu >= 0 && li_relu < li_end) {
+      const int64_t rcol = p.col[li_relu];
       k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, lo, uo, C[cc], lam, nu, C[cc ^ 1],
                                                                    sl + rcol, su + rcol, Ntot);
       CF_TRY(check_launch("k_zono_relu"));
@@ -575,57 +627,76 @@ static cf_status zono_chunk(const cf_network* net, const Plan& p, int64_t Bc, co
   return CF_OK;
 }
 
-static cf_status ibp_chunk(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
-                           const float* specW, float* sl, float* su, double* lb, double* ub, char* ws,
-                           const FwdLayout& w, cudaStream_t st) {
+// Network layers li_begin .. li_end-1 of the interval pass over one chunk (layer li writes
+// compact buffer li % 2 and reads li-1's).
+static cf_status ibp_layers(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
+                            const float* specW, float* sl, float* su, double* lb, double* ub, char* ws,
+                            const FwdLayout& w, cudaStream_t st, int li_begin, int li_end) {
   const int64_t n0 = net->n_input, Ntot = p.N;
   const int64_t vstride = (int64_t)((w.lu[1] - w.lu[0]) / 2 / sizeof(float));
   float* Lb[2] = {reinterpret_cast<float*>(ws + w.lu[0]), reinterpret_cast<float*>(ws + w.lu[1])};
   float* Ub[2] = {Lb[0] + vstride, Lb[1] + vstride};
-  CF_TRY(launch_copy_rows(Bc, n0, l0, n0, sl, Ntot, st));
-  CF_TRY(launch_copy_rows(Bc, n0, u0, n0, su, Ntot, st));
-  const float* lc = l0;
-  const float* uc = u0;
-  int nx = 0;
-  size_t a = 0;
-  for (int li = 0; li < net->n_layers; ++li) {
-    const cf_layer& L = net->layers[li];
-    const int64_t col = p.col[li];
-    float *lo = Lb[nx], *uo = Ub[nx];
-    if (L.kind == CF_LAYER_RELU) {
-      k_ibp_relu<<<(unsigned)ceil_div(Bc * L.n_out, 256), 256, 0, st>>>(Bc, L.n_out, lc, uc, lo, uo, sl + col,
-                                                                        su + col, Ntot);
-      CF_TRY(check_launch("k_ibp_relu"));
-    } else if (L.kind == CF_LAYER_LINEAR) {
-      const float* Wt = reinterpret_cast<const float*>(ws + w.wt_off[a]);
-      dim3 grid((unsigned)ceil_div(L.n_out, 128), (unsigned)Bc);
-      k_ibp_linear<<<grid, 128, 0, st>>>(L.n_in, L.n_out, lc, uc, Wt, 0, L.n_out, 1, L.b_dev, lo, uo, sl + col,
-                                          su + col, Ntot, nullptr, nullptr);
-      CF_TRY(check_launch("k_ibp_linear"));
-      ++a;
-    } else {
-      ConvGeo g{L.cin, L.ih, L.iw, L.cout, L.oh, L.ow, L.kh, L.kw, L.stride, L.pad};
-      k_ibp_conv<<<(unsigned)ceil_div(Bc * L.n_out, 128), 128, 0, st>>>(Bc, g, lc, uc, L.W_dev, L.b_dev, lo, uo,
-                                                                        sl + col, su + col, Ntot);
-      CF_TRY(check_launch("k_ibp_conv"));
-      ++a;
-    }
-    lc = lo;
-    uc = uo;
-    nx ^= 1;
+  if (li_begin == 0) {
+    CF_TRY(launch_copy_rows(Bc, n0, l0, n0, sl, Ntot, st));
+    CF_TRY(launch_copy_rows(Bc, n0, u0, n0, su, Ntot, st));
   }
-  const int64_t K = p.n_out_last, N = net->n_spec;
-  dim3 grid((unsigned)ceil_div(N, 128), (unsigned)Bc);
-  k_ibp_linear<<<grid, 128, 0, st>>>(K, N, lc, uc, specW, N * K, 1, K, nullptr, Lb[nx], Ub[nx], sl + p.spec_col,
-                                      su + p.spec_col, Ntot, lb, ub);
-  return check_launch("k_ibp_linear");
+  size_t a = 0;  // affine index of layer li
+  for (int li = 0; li <= net->n_layers && li < li_end; ++li) {
+    const bool spec = li == net->n_layers;
+    const bool affine = spec || net->layers[li].kind != CF_LAYER_RELU;
+    if (li >= li_begin) {
+      const float* lc = li == 0 ? l0 : Lb[(li - 1) & 1];
+      const float* uc = li == 0 ? u0 : Ub[(li - 1) & 1];
+      float *lo = Lb[li & 1], *uo = Ub[li & 1];
+      if (spec) {
+        const int64_t K = p.n_out_last, N = net->n_spec;
+        dim3 grid((unsigned)ceil_div(N, 128), (unsigned)Bc);
+        k_ibp_linear<<<grid, 128, 0, st>>>(K, N, lc, uc, specW, N * K, 1, K, nullptr, lo, uo, sl + p.spec_col,
+                                            su + p.spec_col, Ntot, lb, ub);
+        CF_TRY(check_launch("k_ibp_linear"));
+        break;
+      }
+      const cf_layer& L = net->layers[li];
+      const int64_t col = p.col[li];
+      if (L.kind == CF_LAYER_RELU) {
+        k_ibp_relu<<<(unsigned)ceil_div(Bc * L.n_out, 256), 256, 0, st>>>(Bc, L.n_out, lc, uc, lo, uo, sl + col,
+                                                                          su + col, Ntot);
+        CF_TRY(check_launch("k_ibp_relu"));
+      } else if (L.kind == CF_LAYER_LINEAR) {
+        const float* Wt = reinterpret_cast<const float*>(ws + w.wt_off[a]);
+        dim3 grid((unsigned)ceil_div(L.n_out, 128), (unsigned)Bc);
+        k_ibp_linear<<<grid, 128, 0, st>>>(L.n_in, L.n_out, lc, uc, Wt, 0, L.n_out, 1, L.b_dev, lo, uo, sl + col,
+                                            su + col, Ntot, nullptr, nullptr);
+        CF_TRY(check_launch("k_ibp_linear"));
+      } else {
+        ConvGeo g{L.cin, L.ih, L.iw, L.cout, L.oh, L.ow, L.kh, L.kw, L.stride, L.pad};
+        k_ibp_conv<<<(unsigned)ceil_div(Bc * L.n_out, 128), 128, 0, st>>>(Bc, g, lc, uc, L.W_dev, L.b_dev, lo, uo,
+                                                                          sl + col, su + col, Ntot);
+        CF_TRY(check_launch("k_ibp_conv"));
+      }
+    }
+    if (affine) ++a;
+  }
+  return CF_OK;
 }
 
-cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const float* l0, const float* u0,
-                      const float* specW, float* state_l, float* state_u, double* lb, double* ub, void* workspace,
-                      size_t ws_bytes, cudaStream_t st) {
-  const bool zono = net->relaxation == CF_RELAX_ZONO;
-  if (zono) {
+// Per-call preparation of the weights of affine index a (transposed copy; tensor-core image
+// for the zonotope chain).
+static cf_status fwd_prep_weights(const cf_network* net, const Plan& p, size_t a, char* ws, const FwdLayout& w,
+                                  cudaStream_t st) {
+  const cf_layer& L = net->layers[p.affine[a]];
+  if (L.kind != CF_LAYER_LINEAR) return CF_OK;
+  float* Wt = reinterpret_cast<float*>(ws + w.wt_off[a]);
+  dim3 grid((unsigned)ceil_div(L.n_in, 32), (unsigned)ceil_div(L.n_out, 32));
+  k_transpose<<<grid, dim3(32, 8), 0, st>>>(L.n_out, L.n_in, L.W_dev, Wt);
+  CF_TRY(check_launch("k_transpose"));
+  if (net->relaxation == CF_RELAX_ZONO)
+    CF_TRY(chain_prep_weights(Wt, L.n_in, L.n_out, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
+  return CF_OK;
+}
+
+static cf_status fwd_check(const cf_network* net, const Plan& p) {
+  if (net->relaxation == CF_RELAX_ZONO) {
     CF_REQUIRE(!p.has_conv, CF_ERR_UNSUPPORTED,
                "zono: conv layers are not supported by the zonotope driver (linear and ReLU layers)");
     const ZonoShape z = zono_shape(net, p);
@@ -633,6 +704,40 @@ cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const flo
       CF_REQUIRE(ceil_div(z.E_in[a], kZT) <= 65535, CF_ERR_SHAPE, "zono: %lld noise symbols",
                  (long long)z.E_in[a]);
   }
+  return CF_OK;
+}
+
+static cf_status fwd_begin(char* ws, const FwdLayout& w, bool zono, cudaStream_t st) {
+  if (cudaMemsetAsync(ws + w.err, 0, 256, st) != cudaSuccess ||
+      (zono && cudaMemsetAsync(ws + w.zeros, 0, w.lu[0] - w.zeros, st) != cudaSuccess)) {
+    set_error("forward run: cudaMemsetAsync failed");
+    return CF_ERR_CUDA;
+  }
+  return CF_OK;
+}
+
+cf_status forward_layer(const cf_network* net, const Plan& p, int layer, int64_t B, const float* l0,
+                        const float* u0, const float* specW, float* state_l, float* state_u, double* lb, double* ub,
+                        void* workspace, size_t ws_bytes, cudaStream_t st) {
+  CF_TRY(fwd_check(net, p));
+  CF_REQUIRE(B <= 65535, CF_ERR_SHAPE, "per-layer runs: at most 65535 regions per call");
+  const FwdLayout w = fwd_layout(net, p, B);
+  CF_REQUIRE(ws_bytes >= w.total, CF_ERR_WORKSPACE,
+             "per-layer runs keep the whole batch: workspace %zu < %zu bytes", ws_bytes, w.total);
+  char* ws = static_cast<char*>(workspace);
+  if (layer == 0) CF_TRY(fwd_begin(ws, w, net->relaxation == CF_RELAX_ZONO, st));
+  for (size_t a = 0; a < p.affine.size(); ++a)
+    if (p.affine[a] == layer) CF_TRY(fwd_prep_weights(net, p, a, ws, w, st));
+  if (net->relaxation == CF_RELAX_ZONO)
+    return zono_layers(net, p, B, l0, u0, specW, state_l, state_u, lb, ub, ws, w, st, layer, layer + 1);
+  return ibp_layers(net, p, B, l0, u0, specW, state_l, state_u, lb, ub, ws, w, st, layer, layer + 1);
+}
+
+cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const float* l0, const float* u0,
+                      const float* specW, float* state_l, float* state_u, double* lb, double* ub, void* workspace,
+                      size_t ws_bytes, cudaStream_t st) {
+  const bool zono = net->relaxation == CF_RELAX_ZONO;
+  CF_TRY(fwd_check(net, p));
   const size_t base = fwd_layout(net, p, 1).total;
   CF_REQUIRE(ws_bytes >= base, CF_ERR_WORKSPACE, "workspace %zu < %zu bytes needed for one region", ws_bytes, base);
   int64_t lo = 1, hi = B < 65535 ? B : 65535;
@@ -644,23 +749,8 @@ cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const flo
   const int64_t Bc = lo;
   const FwdLayout w = fwd_layout(net, p, Bc);
   char* ws = static_cast<char*>(workspace);
-  if (cudaMemsetAsync(ws + w.err, 0, 256, st) != cudaSuccess) {
-    set_error("forward run: cudaMemsetAsync failed");
-    return CF_ERR_CUDA;
-  }
-  if (zono && cudaMemsetAsync(ws + w.zeros, 0, w.lu[0] - w.zeros, st) != cudaSuccess) {
-    set_error("forward run: cudaMemsetAsync failed");
-    return CF_ERR_CUDA;
-  }
-  for (size_t a = 0; a < p.affine.size(); ++a) {
-    const cf_layer& L = net->layers[p.affine[a]];
-    if (L.kind != CF_LAYER_LINEAR) continue;
-    float* Wt = reinterpret_cast<float*>(ws + w.wt_off[a]);
-    dim3 grid((unsigned)ceil_div(L.n_in, 32), (unsigned)ceil_div(L.n_out, 32));
-    k_transpose<<<grid, dim3(32, 8), 0, st>>>(L.n_out, L.n_in, L.W_dev, Wt);
-    CF_TRY(check_launch("k_transpose"));
-    if (zono) CF_TRY(chain_prep_weights(Wt, L.n_in, L.n_out, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
-  }
+  CF_TRY(fwd_begin(ws, w, zono, st));
+  for (size_t a = 0; a < p.affine.size(); ++a) CF_TRY(fwd_prep_weights(net, p, a, ws, w, st));
   const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
   for (int64_t b0 = 0; b0 < B; b0 += Bc) {
     const int64_t nb = (B - b0 < Bc) ? (B - b0) : Bc;
@@ -668,9 +758,11 @@ cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const flo
     float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
     const float* sw = specW + b0 * ns * p.n_out_last;
     if (zono)
-      CF_TRY(zono_chunk(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, sw, sl, su, lb + b0 * ns, ub + b0 * ns, ws, w, st));
+      CF_TRY(zono_layers(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, sw, sl, su, lb + b0 * ns, ub + b0 * ns, ws, w, st, 0,
+                         net->n_layers + 1));
     else
-      CF_TRY(ibp_chunk(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, sw, sl, su, lb + b0 * ns, ub + b0 * ns, ws, w, st));
+      CF_TRY(ibp_layers(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, sw, sl, su, lb + b0 * ns, ub + b0 * ns, ws, w, st, 0,
+                        net->n_layers + 1));
   }
   return CF_OK;
 }

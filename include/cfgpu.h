@@ -133,6 +133,19 @@ cf_status cf_deeppoly_run(const cf_network* net, int64_t B,
                           double* lb_dev, double* ub_dev,
                           void* workspace_dev, size_t workspace_bytes, void* stream);
 
+/* One layer of the pass, for callers that drive the layer loop themselves as Flow.flow does
+ * (constraintflow/lib/flow_sparse.py:27-228 calls the transformer once per layer; code
+ * emitted by cfgpu.codegen calls this once per layer).  layer = 0 .. n_layers-1 runs that
+ * network layer (an affine layer: its bounds by backsubstitution, or its zonotope / interval
+ * step; a ReLU: its relaxation), layer = n_layers the property layer (lb/ub).  Layers run in
+ * order 0, 1, .. on one workspace that holds the whole batch
+ * (>= cf_deeppoly_workspace_bytes(net, B)); state_l / state_u are required.  The bounds
+ * equal those of cf_deeppoly_run. */
+cf_status cf_deeppoly_layer(const cf_network* net, int32_t layer, int64_t B,
+                            const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
+                            float* state_l_dev, float* state_u_dev, double* lb_dev, double* ub_dev,
+                            void* workspace_dev, size_t workspace_bytes, void* stream);
+
 /* Input boundary (constraintflow/lib/spec.py:21-47, 61-72).
  * cf_input_box: l0 = (clip(X - eps, 0, 1) - mean[c]) / std[c], u0 likewise with +eps, for
  * X [B, C, HW] float32 (C mean/std values given on the host, C <= 4).
