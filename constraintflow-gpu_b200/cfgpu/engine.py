@@ -90,6 +90,7 @@ class DeepPolyEngine:
             widths.append(int(d.n_out))
             descs.append(d)
         self.n_last = widths[-1] if widths else self.input_size
+        self.kinds = [g[0] for g in self._general]
         if self.chain:
             self._layers = (CfLayer * len(descs))(*descs)
             self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, relax[certifier])

@@ -59,3 +59,22 @@ class LayerRun:
         stream = torch.cuda.current_stream(self.engine.device).cuda_stream
         _lib.check(_lib.lib.cf_deeppoly_check(self.ws.data_ptr(), stream), "device status")
         return self.lb, self.ub
+
+
+_OP_OF_KIND = {"linear": "Affine", "conv": "Affine", "relu": "Relu"}
+
+
+def run_operation(abs_elem, op, layer_index):
+    """The fused call behind one operation of an emitted transformer: runs model layer
+    `layer_index` (1 = the first network layer; the property layer last) on the pass that
+    Flow.flow attached to the abstract element, after checking that the layer is of the
+    operation's kind."""
+    run = getattr(abs_elem, "cf_run", None)
+    if run is None:
+        raise RuntimeError("no per-layer pass is attached to this abstract element (Flow.flow attaches it)")
+    li = int(layer_index) - 1
+    kinds = run.engine.kinds
+    kind = "linear" if li == run.n_layers else kinds[li]
+    if _OP_OF_KIND.get(kind) != op:
+        raise ValueError(f"layer {layer_index} is a {kind} layer; the transformer called {op}")
+    run.layer(li)

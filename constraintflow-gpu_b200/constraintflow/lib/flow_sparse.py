@@ -140,7 +140,10 @@ class Flow:
         spec = self.model[-1]
         W = torch.as_tensor(spec.weight, dtype=torch.float32).to(dev).contiguous()
         eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier)
-        lb, ub, sl, su = eng.run(l0, u0, W, want_state=True)
+        if getattr(self.transformer, "cf_layerwise", False) and eng.net is not None:
+            lb, ub, sl, su = self._layer_by_layer(eng, l0, u0, W)
+        else:
+            lb, ub, sl, su = eng.run(l0, u0, W, want_state=True)
         total = torch.tensor([B, self.model.size])
         self.abs_elem.d["l"] = SparseTensor([torch.tensor([0, 0])], [DenseBlock(sl)], 2, total,
                                             dense_const=float("-inf"))
@@ -154,3 +157,28 @@ class Flow:
                 print(f"l: {sl[:, layer.start:layer.end].cpu()}")
                 print(f"u: {su[:, layer.start:layer.end].cpu()}")
         return lb, ub
+
+    def _layer_by_layer(self, eng, l0, u0, W):
+        """Programs emitted by cfgpu.codegen: the transformer's operation is called for every
+        layer in order (as flow_sparse.py:27-228 does), each one fused libcfgpu call."""
+        from cfgpu.layerwise import LayerRun
+        run = LayerRun(eng, l0, u0, W)
+        self.abs_elem.cf_run = run
+        B = self.batch_size
+        try:
+            for tmp, layer in enumerate(self.model):
+                if layer.type == LayerType.Input:
+                    continue
+                op = "Relu" if layer.type == LayerType.ReLU else "Affine"
+                getattr(self.transformer, op)(self.abs_elem, None, None, self.model.size, layer.size, None,
+                                              self.input_size, B, layer_index=tmp)
+            lb, ub = run.finish()
+        except NotImplementedError:
+            if eng.certifier != "crown":
+                raise
+            # a CROWN layer took the all-crossing branch: the whole-network driver runs the
+            # general traversal for it
+            return eng.run(l0, u0, W, want_state=True)
+        finally:
+            self.abs_elem.cf_run = None
+        return lb, ub, run.state_l, run.state_u

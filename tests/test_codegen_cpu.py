@@ -1,0 +1,94 @@
+"""The compiler backend (cfgpu.codegen) on the reference's example programs, without a GPU:
+its analysis of the ASTs the reference front end built (tests/golden/ast/, made by
+tests/golden/gen_codegen.py), the code it emits, its refusals, and planted mistakes in a
+program that it must refuse."""
+import copy
+import importlib.util
+import json
+import os
+import sys
+
+import pytest
+
+from cfgpu import codegen
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLDEN = os.path.join(HERE, "golden")
+sys.path.insert(0, GOLDEN)
+import ast_json  # noqa: E402
+
+RUNS = {"deeppoly": "deeppoly", "deeppoly_efficient": "deeppoly", "crown": "crown", "zono": "zono", "ibp": "ibp"}
+REFUSED = ("deeppoly_priority", "deeppolyh", "zono2", "ibp2", "polyzono")
+
+
+def _ast(prog):
+    with open(os.path.join(GOLDEN, "ast", f"{prog}.json")) as f:
+        return ast_json.from_json(json.load(f))
+
+
+@pytest.mark.parametrize("prog", sorted(RUNS))
+def test_backend_recognises_program(prog):
+    a = codegen.analyse(_ast(prog))
+    assert a.certifier == RUNS[prog]
+    assert a.ops["Affine"] in ("backsub", "zonotope", "interval") and a.ops["Relu"] is not None
+
+
+@pytest.mark.parametrize("prog", sorted(RUNS))
+def test_emitted_code_is_committed(prog):
+    files = codegen.generate(_ast(prog), f"{prog}.cf")
+    for name, text in files.items():
+        with open(os.path.join(GOLDEN, "generated_cfgpu", prog, name)) as f:
+            assert f.read() == text
+
+
+@pytest.mark.parametrize("prog", REFUSED)
+def test_backend_refuses_other_programs(prog):
+    with pytest.raises(codegen.CodegenError):
+        codegen.analyse(_ast(prog))
+    refused = json.load(open(os.path.join(GOLDEN, "generated_cfgpu", "refused.json")))
+    assert prog in refused and "deeppoly2" in refused and "hybrid_zono" in refused
+
+
+def _funcs(ast):
+    out = {}
+
+    def walk(s):
+        if type(s).__name__ == "SeqNode":
+            walk(s.stmt1)
+            walk(s.stmt2)
+        elif type(s).__name__ == "FuncNode":
+            out[s.decl.name.name] = s
+    walk(ast.stmt)
+    return out
+
+
+@pytest.mark.parametrize("mistake", ["replace_sign", "priority_order", "relu_slope", "simplify_choice"])
+def test_planted_mistakes_are_refused(mistake):
+    """Mistakes planted in deeppoly.cf's AST (each changes the certifier's meaning) make the
+    backend refuse the program instead of running the DeepPoly kernels."""
+    ast = copy.deepcopy(_ast("deeppoly"))
+    f = _funcs(ast)
+    if mistake == "replace_sign":          # coefficient >= 0 substitutes U instead of L
+        f["replace_lower"].expr.texpr.right.elem.name = "U"
+    elif mistake == "priority_order":      # highest layer first
+        f["priority2"].expr = f["priority2"].expr.expr
+    elif mistake == "relu_slope":          # lower relaxation on l >= 0 instead of l + u >= 0
+        f["relu_n"].expr.cond.left = f["relu_n"].expr.cond.left.left
+    elif mistake == "simplify_choice":     # concretise a negative coefficient with l
+        f["simplify_lower"].expr.fexpr.right.elem.name = "l"
+    assert codegen.analyse(copy.deepcopy(_ast("deeppoly"))).certifier == "deeppoly"
+    with pytest.raises(codegen.CodegenError) as e:
+        codegen.analyse(ast)
+    assert ("Relu (unrecognised)" if mistake == "relu_slope" else "Affine (unrecognised)") in str(e.value)
+
+
+@pytest.mark.parametrize("prog", sorted(RUNS))
+def test_emitted_transformer_declares_its_family(prog):
+    from constraintflow.lib.flow_sparse import certifier_of
+    path = os.path.join(GOLDEN, "generated_cfgpu", prog, "transformers.py")
+    spec = importlib.util.spec_from_file_location(f"cfgpu_emitted_{prog}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    a = codegen.analyse(_ast(prog))
+    obj = getattr(mod, a.name)()
+    assert obj.cf_layerwise and certifier_of(obj) == RUNS[prog]
