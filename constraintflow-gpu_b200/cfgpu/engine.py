@@ -108,6 +108,9 @@ class DeepPolyEngine:
             self.net = None
             self.N = self.input_size + sum(widths) + self.n_spec
         self._ws = None
+        self.graphs = True           # CUDA-graph replay of the general traversal (DeepPoly)
+        self._graph_cache = {}
+        self.replayed_launches = 0   # libcfgpu kernels replayed by those graphs
 
     def workspace_bytes(self, chunk):
         if self.net is None:
@@ -177,13 +180,54 @@ class DeepPolyEngine:
         return lb, ub
 
     def _general_run(self, l0, u0, spec_W, lb, ub):
-        """Bounds through the general lowest-layer-first traversal (cfgpu.general)."""
+        """Bounds through the general lowest-layer-first traversal (cfgpu.general).
+
+        DeepPoly's traversal takes no data-dependent decision on the host, so for a given
+        batch size its launches are captured once in a CUDA graph and replayed (the inputs
+        are copied into the graph's buffers); CROWN decides its ReLU branches on the host and
+        runs eagerly."""
         from . import general
+        if self.certifier == "deeppoly" and self.graphs:
+            g = self._graph_cache.get(int(l0.shape[0]))
+            if g is None:
+                g = self._capture(l0, u0, spec_W)
+            if g is not None:
+                g["l0"].copy_(l0)
+                g["u0"].copy_(u0)
+                g["W"].copy_(spec_W)
+                g["graph"].replay()
+                self.replayed_launches += g["launches"]
+                lb.copy_(g["sl"][:, -self.n_spec:])
+                ub.copy_(g["su"][:, -self.n_spec:])
+                return lb, ub, g["sl"], g["su"]
         bounds, _ = general.run(self._general, l0, u0, spec_W, self.certifier)
         sl, su = general.state(l0, u0, bounds)
         lb.copy_(bounds[-1][0])
         ub.copy_(bounds[-1][1])
         return lb, ub, sl, su
+
+    def _capture(self, l0, u0, spec_W):
+        from . import general
+        static = {"l0": l0.clone(), "u0": u0.clone(), "W": spec_W.clone()}
+        try:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):      # warm-up outside the capture
+                general.run(self._general, static["l0"], static["u0"], static["W"], "deeppoly")
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            from . import ops
+            n0 = ops.LAUNCHES[0]
+            with torch.cuda.graph(graph):
+                bounds, _ = general.run(self._general, static["l0"], static["u0"], static["W"], "deeppoly")
+                static["sl"], static["su"] = general.state(static["l0"], static["u0"], bounds)
+        except RuntimeError:
+            self.graphs = False                  # capture refused: run eagerly from now on
+            return None
+        static["graph"] = graph
+        static["launches"] = ops.LAUNCHES[0] - n0
+        self._graph_cache[int(l0.shape[0])] = static
+        return static
 
     def input_spec(self, X, y, eps, dataset):
         """Device input box and property matrix from device centres X [B,C,H,W] and labels y [B].

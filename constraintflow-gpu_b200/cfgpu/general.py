@@ -95,14 +95,19 @@ def _substitute(B, blocks, c, t, P, Q):
 
 
 def _traverse(B, blocks, c, polys, lower):
-    """Backward traversal, lowest live layer first, until no coefficient is left."""
-    while True:
-        live = [t for t, M in blocks.items() if ops.any_nonzero(M)]
-        if not live:
-            return c
-        t = min(live)
+    """Backward traversal, lowest layer first, until no coefficient block is left.
+
+    The reference substitutes only live layers (a block with a non-zero coefficient
+    somewhere in the batch) and leaves all-zero blocks stopped, where they concretise to 0.
+    Substituting an all-zero block instead adds exact zeros to the constant and to the
+    blocks of the layers below it, and does not change which other layer comes next, so
+    the bounds are the same while the traversal needs no device-to-host liveness test:
+    the whole pass is stream-ordered (and can be captured in a CUDA graph)."""
+    while blocks:
+        t = min(blocks)
         L, U = polys[t]
         blocks, c = _substitute(B, blocks, c, t, L, U) if lower else _substitute(B, blocks, c, t, U, L)
+    return c
 
 
 def _scal(v, like):
@@ -114,6 +119,7 @@ def _deeppoly_relu(B, k_in, l, u):
     n = l.shape[1]
     l_new, u_new, alpha, lam, mu = (torch.empty(B, n, dtype=F32, device=l.device) for _ in range(5))
     lc, uc = l.contiguous(), u.contiguous()
+    ops.LAUNCHES[0] += 1
     st = _lib.lib.cf_relu_relax(B, n, lc.data_ptr(), uc.data_ptr(), n, l_new.data_ptr(), u_new.data_ptr(), n,
                                 alpha.data_ptr(), lam.data_ptr(), mu.data_ptr(), _lib.CF_RELAX_DEEPPOLY,
                                 torch.cuda.current_stream().cuda_stream)

@@ -18,6 +18,11 @@ COMPARISONS = (operator.lt, operator.le, operator.eq, operator.ne, operator.gt, 
                operator.or_)
 
 
+# libcfgpu launches made through these wrappers (each wrapper launches one kernel); the
+# engine uses it to count the launches a captured CUDA graph replays
+LAUNCHES = [0]
+
+
 def device():
     if not torch.cuda.is_available():
         raise RuntimeError("the gbcsr ops run on a CUDA device only (libcfgpu); no CPU fallback")
@@ -46,7 +51,7 @@ def as_block_tensor(x, dtype=None):
 
 def scalar_view(value, shape, dtype):
     """A fill value broadcast to `shape` without materialising it (all strides zero)."""
-    t = torch.tensor(value, dtype=dtype, device=device())
+    t = torch.full((), value, dtype=dtype, device=device())   # a fill kernel: no host copy
     return t.expand(*shape) if len(shape) else t
 
 
@@ -57,6 +62,7 @@ def binary(op, a, b, out_dtype):
         return out
     shp, sa = _geo(a)
     _, sb = _geo(b)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_ew_binary(_lib.OPS[_OPS[op]], a.dim(), shp, a.data_ptr(), _dt(a), sa, b.data_ptr(), _dt(b), sb,
                                out.data_ptr(), _dt(out), _stream())
     _lib.check(st, "cf_ew_binary")
@@ -68,6 +74,7 @@ def unary(name, a, out_dtype):
     if out.numel() == 0:
         return out
     shp, sa = _geo(a)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_ew_unary(_lib.UOPS[name], a.dim(), shp, a.data_ptr(), _dt(a), sa, out.data_ptr(), _dt(out),
                               _stream())
     _lib.check(st, "cf_ew_unary")
@@ -81,6 +88,7 @@ def where(c, y, z):
     shp, sc = _geo(c)
     _, sy = _geo(y)
     _, sz = _geo(z)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_ew_where(c.dim(), shp, c.data_ptr(), sc, y.data_ptr(), sy, z.data_ptr(), sz, out.data_ptr(),
                               _lib.CF_F32, _stream())
     _lib.check(st, "cf_ew_where")
@@ -92,6 +100,7 @@ def clamp(a, const, min_true):
     if out.numel() == 0:
         return out
     shp, sa = _geo(a)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_ew_clamp(a.dim(), shp, a.data_ptr(), sa, float(const), 1 if min_true else 0, out.data_ptr(),
                               _stream())
     _lib.check(st, "cf_ew_clamp")
@@ -103,6 +112,7 @@ def any_nonzero(a):
         return False
     flag = torch.zeros(1, dtype=torch.int32, device=a.device)
     shp, sa = _geo(a)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_ew_any(a.dim(), shp, a.data_ptr(), _dt(a), sa, flag.data_ptr(), _stream())
     _lib.check(st, "cf_ew_any")
     return bool(flag.item())
@@ -114,6 +124,7 @@ def bmm(A, B, C=None, accumulate=False):
     N = B.shape[2]
     if C is None:
         C = torch.empty(nb, M, N, dtype=torch.float32, device=A.device)
+    LAUNCHES[0] += 1
     st = _lib.lib.cf_bmm(nb, M, N, K, A.data_ptr(), A.stride(0), A.stride(1), A.stride(2), B.data_ptr(),
                          B.stride(0), B.stride(1), B.stride(2), C.data_ptr(), 1 if accumulate else 0, _stream())
     _lib.check(st, "cf_bmm")

@@ -96,3 +96,25 @@ def test_gpu_dag_rejects_bad_layers():
     bad = nets.Layer(**{**layers[i].__dict__, "parents": (i + 1, 0)})
     with pytest.raises(ValueError):
         DeepPolyEngine(layers[:i] + [bad] + layers[i + 1:], wl.input_size, "cuda:0")
+
+
+@pytest.mark.parametrize("wid", [5, 6])
+def test_gpu_dag_graph_replay_equals_eager(wid):
+    """DeepPoly's general traversal is captured in a CUDA graph per batch size and
+    replayed with new inputs: bitwise the eager traversal, for two different batches."""
+    from cfgpu.engine import DeepPolyEngine
+    wl = nets.workload(wid)
+    dev = torch.device("cuda:0")
+    eng = DeepPolyEngine(wl.layers, wl.input_size, dev)
+    ref = DeepPolyEngine(wl.layers, wl.input_size, dev)
+    ref.graphs = False
+    for eps, seed_off in ((0.002, 0), (0.004, 8)):
+        X = nets.centres(wl, 16)[seed_off // 8:seed_off // 8 + 8]
+        y = nets.labels(wl, X)
+        l0, u0 = (t.to(dev) for t in nets.input_box(X, eps, wl.dataset))
+        W = nets.spec_weight(y).to(dev)
+        lb, ub, sl, su = eng.run(l0, u0, W, want_state=True)
+        lb2, ub2, sl2, su2 = ref.run(l0, u0, W, want_state=True)
+        torch.cuda.synchronize()
+        assert torch.equal(lb, lb2) and torch.equal(sl, sl2) and torch.equal(su, su2)
+    assert eng.graphs and len(eng._graph_cache) == 1
