@@ -172,6 +172,128 @@ __global__ void __launch_bounds__(256) k_zono_const(int64_t K, int64_t N, const 
   }
 }
 
+struct ConvGeo {
+  int32_t cin, ih, iw, cout, oh, ow, kh, kw, stride, pad;
+};
+
+// ---- conv layers of the zonotope pass (CUDA cores): the convolution applied to every
+// symbol row as an image (C, H, W); neuron n = (co, oy, ox), input k = (ci, iy, ix).
+
+// A' rows [0, E): out[b, e, n] = sum_{ci,ky,kx} A[b, e, k] lam[b, k] W[co, ci, ky, kx] with
+// (iy, ix) = (oy*s - pad + ky, ox*s - pad + kx) inside the input; tile column sums as
+// k_zono_gemm ([b][row tile of 64][n]).  Block (64, 4): 64 neurons x 4 row groups of 16
+// rows; grid (ceil(N/64), ceil(E/64), B).
+__global__ void __launch_bounds__(256) k_zono_conv_rows(int64_t E, ConvGeo g, const float* __restrict__ A,
+                                                        int64_t a_bs, const float* __restrict__ lam,
+                                                        const float* __restrict__ W, float* __restrict__ out,
+                                                        int64_t o_bs, float* __restrict__ ppos,
+                                                        float* __restrict__ pneg, int64_t p_bs) {
+  __shared__ float red[2][4][64];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t N = (int64_t)g.cout * g.oh * g.ow, K = (int64_t)g.cin * g.ih * g.iw;
+  const int64_t n = (int64_t)blockIdx.x * 64 + tx, b = blockIdx.z, e0 = (int64_t)blockIdx.y * 64;
+  float sp = 0.0f, sn = 0.0f;
+  if (n < N) {
+    const int co = (int)(n / ((int64_t)g.oh * g.ow)), rem = (int)(n % ((int64_t)g.oh * g.ow));
+    const int oy = rem / g.ow, ox = rem % g.ow;
+    const float* lb = lam ? lam + b * K : nullptr;
+    for (int j = 0; j < 16; ++j) {
+      const int64_t e = e0 + ty + 4 * j;
+      if (e >= E) break;
+      const float* ar = A + b * a_bs + e * K;
+      float acc = 0.0f;
+      for (int ci = 0; ci < g.cin; ++ci)
+        for (int ky = 0; ky < g.kh; ++ky) {
+          const int iy = oy * g.stride - g.pad + ky;
+          if (iy < 0 || iy >= g.ih) continue;
+          for (int kx = 0; kx < g.kw; ++kx) {
+            const int ix = ox * g.stride - g.pad + kx;
+            if (ix < 0 || ix >= g.iw) continue;
+            const int64_t k = ((int64_t)ci * g.ih + iy) * g.iw + ix;
+            const float v = lb ? ar[k] * lb[k] : ar[k];
+            acc = fmaf(v, W[(((int64_t)co * g.cin + ci) * g.kh + ky) * g.kw + kx], acc);
+          }
+        }
+      out[b * o_bs + e * N + n] = acc;
+      sp += fmaxf(acc, 0.0f);
+      sn += fminf(acc, 0.0f);
+    }
+  }
+  red[0][ty][tx] = sp;
+  red[1][ty][tx] = sn;
+  __syncthreads();
+  if (ty < 2 && n < N) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += red[ty][j][tx];
+    (ty == 0 ? ppos : pneg)[b * p_bs + (int64_t)blockIdx.y * N + n] = s;
+  }
+}
+
+// Rows of a diagonal block d [B, K] over the conv input neurons: out[b, row0 + k, n] =
+// d[b, k] W[co, ci, iy - oy*s + pad, ix - ox*s + pad] (0 where the kernel does not cover
+// input k), with their column sums in dpos/dneg[b, n].  Block (32, 8), grid (ceil(N/32), B).
+__global__ void __launch_bounds__(256) k_zono_diag_conv(ConvGeo g, const float* __restrict__ d,
+                                                        const float* __restrict__ W, float* __restrict__ out,
+                                                        int64_t o_bs, int64_t row0, float* __restrict__ dpos,
+                                                        float* __restrict__ dneg) {
+  __shared__ float red[2][8][32];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t N = (int64_t)g.cout * g.oh * g.ow, K = (int64_t)g.cin * g.ih * g.iw;
+  const int64_t n = (int64_t)blockIdx.x * 32 + tx, b = blockIdx.y;
+  float sp = 0.0f, sn = 0.0f;
+  if (n < N) {
+    const int co = (int)(n / ((int64_t)g.oh * g.ow)), rem = (int)(n % ((int64_t)g.oh * g.ow));
+    const int y0 = (rem / g.ow) * g.stride - g.pad, x0 = (rem % g.ow) * g.stride - g.pad;
+    const float* db = d + b * K;
+    float* ob = out + b * o_bs + row0 * N + n;
+    for (int64_t k = ty; k < K; k += 8) {
+      const int ci = (int)(k / ((int64_t)g.ih * g.iw)), r2 = (int)(k % ((int64_t)g.ih * g.iw));
+      const int ky = r2 / g.iw - y0, kx = r2 % g.iw - x0;
+      float v = 0.0f;
+      if (ky >= 0 && ky < g.kh && kx >= 0 && kx < g.kw)
+        v = db[k] * W[(((int64_t)co * g.cin + ci) * g.kh + ky) * g.kw + kx];
+      ob[k * N] = v;
+      sp += fmaxf(v, 0.0f);
+      sn += fminf(v, 0.0f);
+    }
+  }
+  red[0][ty][tx] = sp;
+  red[1][ty][tx] = sn;
+  __syncthreads();
+  if (ty < 2 && n < N) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += red[ty][j][tx];
+    (ty == 0 ? dpos : dneg)[b * N + n] = s;
+  }
+}
+
+// Conv constant: c'[b, n] = sum W[co, ci, ky, kx] c[b, (ci, iy, ix)] + bias[co].
+__global__ void k_zono_const_conv(int64_t B, ConvGeo g, const float* __restrict__ c, const float* __restrict__ W,
+                                  const float* __restrict__ bias, float* __restrict__ c_out) {
+  const int64_t N = (int64_t)g.cout * g.oh * g.ow, K = (int64_t)g.cin * g.ih * g.iw;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= B * N) return;
+  const int64_t b = t / N, n = t - b * N;
+  const int co = (int)(n / ((int64_t)g.oh * g.ow)), rem = (int)(n % ((int64_t)g.oh * g.ow));
+  const int oy = rem / g.ow, ox = rem % g.ow;
+  const float* cb = c + b * K;
+  float acc = 0.0f;
+  for (int ci = 0; ci < g.cin; ++ci)
+    for (int ky = 0; ky < g.kh; ++ky) {
+      const int iy = oy * g.stride - g.pad + ky;
+      if (iy < 0 || iy >= g.ih) continue;
+      for (int kx = 0; kx < g.kw; ++kx) {
+        const int ix = ox * g.stride - g.pad + kx;
+        if (ix < 0 || ix >= g.iw) continue;
+        acc = fmaf(W[(((int64_t)co * g.cin + ci) * g.kh + ky) * g.kw + kx], cb[((int64_t)ci * g.ih + iy) * g.iw + ix],
+                   acc);
+      }
+    }
+  c_out[t] = acc + bias[co];
+}
+
 // Where the column sums of one affine layer's symbol rows are: the GEMM tiles of
 // k_zono_gemm ([b][tile][n], `tiles` per region), or the per-warp sums of the tensor-core
 // chain (E rows per region in 128-row CTAs: [((cta*4 + w)*2 + slot)*N + n]); then the
@@ -323,10 +445,6 @@ __global__ void k_ibp_linear(int64_t K, int64_t N, const float* __restrict__ l, 
     ub[b * N + n] = (double)uv;
   }
 }
-
-struct ConvGeo {
-  int32_t cin, ih, iw, cout, oh, ow, kh, kw, stride, pad;
-};
 
 // ibp.Affine for a conv layer: one thread per output neuron (co, oy, ox) of region b.
 __global__ void k_ibp_conv(int64_t B, ConvGeo g, const float* __restrict__ l, const float* __restrict__ u,
@@ -557,7 +675,29 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
     float* out = spec ? nullptr : A[cur ^ 1];
     const int64_t o_bs = (E + (diag ? K : 0)) * N;
     ZonoSums S{nullptr, nullptr, 0, nullptr, nullptr, 0, diag ? Dp : nullptr, diag ? Dn : nullptr};
-    if (E > 0) {
+    const bool conv = !spec && net->layers[p.affine[a]].kind == CF_LAYER_CONV;
+    if (conv) {
+      // the convolution of every symbol row, of the diagonal block and of the constant
+      const cf_layer& L = net->layers[p.affine[a]];
+      const ConvGeo g{L.cin, L.ih, L.iw, L.cout, L.oh, L.ow, L.kh, L.kw, L.stride, L.pad};
+      const int64_t T = ceil_div(E, kZT);
+      if (E > 0) {
+        dim3 grid((unsigned)ceil_div(N, 64), (unsigned)T, (unsigned)Bc);
+        prof_step_begin(st);
+        k_zono_conv_rows<<<grid, dim3(64, 4), 0, st>>>(E, g, A[cur], E * K, lam_in, L.W_dev, out, o_bs, Gp, Gn, T * N);
+        prof_step_end(st, 2.0 * Bc * E * N * L.cin * L.kh * L.kw, 4.0 * Bc * (E * K + E * N));
+        CF_TRY(check_launch("k_zono_conv_rows"));
+        S.gpos = Gp; S.gneg = Gn; S.tiles = T;
+      }
+      if (diag) {
+        dim3 grid((unsigned)ceil_div(N, 32), (unsigned)Bc);
+        k_zono_diag_conv<<<grid, dim3(32, 8), 0, st>>>(g, nu, L.W_dev, out, o_bs, E, Dp, Dn);
+        CF_TRY(check_launch("k_zono_diag_conv"));
+      }
+      k_zono_const_conv<<<(unsigned)ceil_div(Bc * N, 128), 128, 0, st>>>(Bc, g, C[cc], L.W_dev, L.b_dev, C[cc ^ 1]);
+      CF_TRY(check_launch("k_zono_const_conv"));
+      cc ^= 1;
+    } else if (E > 0) {
       if (!spec && zono_use_chain(E)) {
         // symbol rows on the tensor cores: one chain step (ReLU column scaling, then W^T)
         ChainParams P{};
@@ -596,12 +736,12 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
         S.gpos = Gp; S.gneg = Gn; S.tiles = T;
       }
     }
-    if (diag) {
+    if (diag && !conv) {
       dim3 grid((unsigned)ceil_div(N, 32), (unsigned)Bc);
       k_zono_diag<<<grid, dim3(32, 8), 0, st>>>(K, N, nu, W, w_bs, w_ks, w_ns, out, o_bs, E, Dp, Dn);
       CF_TRY(check_launch("k_zono_diag"));
     }
-    {
+    if (!conv) {
       dim3 grid((unsigned)ceil_div(N, 32), (unsigned)Bc);
       k_zono_const<<<grid, dim3(32, 8), 0, st>>>(K, N, C[cc], W, w_bs, w_ks, w_ns, bias, C[cc ^ 1]);
       CF_TRY(check_launch("k_zono_const"));
@@ -697,8 +837,6 @@ static cf_status fwd_prep_weights(const cf_network* net, const Plan& p, size_t a
 
 static cf_status fwd_check(const cf_network* net, const Plan& p) {
   if (net->relaxation == CF_RELAX_ZONO) {
-    CF_REQUIRE(!p.has_conv, CF_ERR_UNSUPPORTED,
-               "zono: conv layers are not supported by the zonotope driver (linear and ReLU layers)");
     const ZonoShape z = zono_shape(net, p);
     for (size_t a = 0; a < z.E_in.size(); ++a)
       CF_REQUIRE(ceil_div(z.E_in[a], kZT) <= 65535, CF_ERR_SHAPE, "zono: %lld noise symbols",

@@ -80,7 +80,7 @@ enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
  *                      an affine layer maps the symbol coefficients and concretises
  *                      l/u = c -/+ sum |coefficient|; a ReLU opens one fresh symbol per
  *                      neuron (constraintflow/lib/symexp.py:14) and its own l, u are 0.
- *                      Linear layers only (CF_ERR_UNSUPPORTED for conv).
+ *                      Linear and conv layers.
  *   CF_RELAX_IBP       ibp.cf: interval bounds layer by layer (W+ l + W- u + b; ReLU
  *                      clamps), linear and conv layers.
  * CF_RELAX_ZONO and CF_RELAX_IBP run forward through cf_deeppoly_run as well; their
