@@ -170,12 +170,13 @@ __device__ __forceinline__ void warp_colsum16(float (&v)[16]) {
 
 // Zonotope drain of 16 columns n0 .. n0+15 of this thread's row: store the row's values
 // (columns below N) and the warp's per-slot column sums of the positive / negative parts.
-__device__ __forceinline__ void zono_drain(const ChainParams& P, int N, int n0, const float (&x)[16], bool valid,
+__device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_vec, float* zpos, float* zneg,
+                                           int64_t cta, int N, int n0, const float (&x)[16], bool valid,
                                            int64_t b, int64_t i, int slot, bool two_slots) {
   const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3;
   if (valid) {
-    float* o = P.zout + b * P.zo_bs + i * N + n0;
-    if (P.zo_vec && n0 + 16 <= N) {
+    float* o = zout + b * zo_bs + i * N + n0;
+    if (zo_vec && n0 + 16 <= N) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         reinterpret_cast<float4*>(o)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
@@ -197,9 +198,9 @@ __device__ __forceinline__ void zono_drain(const ChainParams& P, int N, int n0, 
     warp_colsum16(q);
     const int c = n0 + (lane >> 1);
     if ((lane & 1) == 0 && c < N) {
-      const size_t idx = (((size_t)blockIdx.x * 4 + w) * 2 + sl) * (size_t)N + c;
-      P.zpos[idx] = p[0];
-      P.zneg[idx] = q[0];
+      const size_t idx = (((size_t)cta * 4 + w) * 2 + sl) * (size_t)N + c;
+      zpos[idx] = p[0];
+      zneg[idx] = q[0];
     }
   }
 }
@@ -383,7 +384,8 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
             float x[16];
             tmem_ld16(dst + (uint32_t)(q * 16), x);
             tmem_ld_wait();
-            zono_drain(P, S.N, n0, x, valid, b, i, slot, two_slots);
+            zono_drain(P.zout, P.zo_bs, P.zo_vec, P.zpos, P.zneg, blockIdx.x, S.N, n0, x, valid, b, i, slot,
+                       two_slots);
             continue;
           }
           float pb[16], nb[16], x[16];
@@ -665,6 +667,255 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   CF_REQUIRE(tiles <= 0x7fffffff, CF_ERR_SHAPE, "chain: too many rows");
   kern<<<(unsigned)tiles, kThreads, smem, st>>>(Q);
   return check_launch(P.zono ? "k_chain (zonotope)" : "k_chain");
+}
+
+// ------------------------------------------------------------------ persistent zonotope GEMM
+// 448 threads: warps 0-7 stage the A operand (thread <-> tile row r = t % 128, 16-column
+// half t / 128 of every 32-column chunk: rows and lam loaded from global memory one chunk
+// ahead, scaled, split into tf32 hi + lo, written as the SW128 image), warp 8 allocates TMEM
+// and streams the W^T chunks (bulk copies), warp 9 issues the 3xTF32 MMAs, warps 10-13
+// drain (thread <-> TMEM lane).  A CTA loops over the row tiles blockIdx.x, +gridDim.x,
+// ...; tile i accumulates in TMEM buffer i % 2, so the drain of tile i overlaps the MMAs
+// of tile i+1.  Every wait is bounded.  (Staging the 128 rows of a chunk through per-row
+// bulk copies instead was 2.8x slower: the copy engine handles 128-byte copies slowly.)
+constexpr int kZtThreads = 448;
+
+__global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_constant__ ZonoTcParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* a_region = smem;                               // 2 stages x (hi, lo) planes
+  uint8_t* w_region = smem + 2 * 2 * kAImg;               // 2 stages x stage_bytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_region + 2 * P.stage_bytes);
+  uint64_t* full_a = bars;
+  uint64_t* empty_a = bars + 2;
+  uint64_t* full_w = bars + 4;
+  uint64_t* empty_w = bars + 6;
+  uint64_t* acc_full = bars + 8;
+  uint64_t* acc_empty = bars + 10;
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = P.err;
+  const int64_t n_tiles = (P.rows + 127) / 128;
+  const int64_t my_tiles = (int64_t)blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full_a[i], kTransformThreads);
+      mbar_init(&empty_a[i], 1);
+      mbar_init(&full_w[i], 1);
+      mbar_init(&empty_w[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == kProducerWarp) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) tmem_slot[1] = *(volatile int*)err != 0 ? 1u : 0u;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  if (tmem_slot[1] != 0) {
+    if (warp == kProducerWarp) tmem_dealloc(tbase, 512);
+    return;
+  }
+  const uint32_t plane = (uint32_t)P.tile_n * 128u;
+
+  if (warp == kProducerWarp) {
+    // ---------------------------------------------------------------- W^T chunks
+    if (lane == 0) {
+      uint32_t g = 0;
+      for (int64_t i = 0; i < my_tiles; ++i) {
+        for (int c = 0; c < P.kchunks; ++c, ++g) {
+          const uint32_t stage = g & 1u, round = g >> 1;
+          if (!mbar_wait(&empty_w[stage], (round & 1u) ^ 1u, err, 51)) goto done_w;
+          uint8_t* sb = w_region + stage * P.stage_bytes;
+          const uint8_t* src = P.wimg + (size_t)c * 2 * plane;
+          mbar_arrive_expect_tx(&full_w[stage], 2 * plane);
+          bulk_g2s(sb, src, plane, &full_w[stage]);
+          bulk_g2s(sb + P.w_lo_off, src + plane, plane, &full_w[stage]);
+        }
+      }
+    done_w:
+      for (uint32_t x = 0; x < 2 && x < g; ++x) {
+        const uint32_t gl = g - 1 - x;
+        mbar_wait_drain(&full_w[gl & 1u], (gl >> 1) & 1u, err, 52);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32((uint32_t)P.tile_n);
+      uint32_t g = 0;
+      for (int64_t i = 0; i < my_tiles; ++i) {
+        const uint32_t buf = (uint32_t)(i & 1);
+        if (i >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)((i >> 1) & 1) ^ 1u, err, 53)) goto done_m;
+        tc_fence_after();
+        const uint32_t acc = tbase + buf * 256u;
+        for (int c = 0; c < P.kchunks; ++c, ++g) {
+          const int nks = min(4, (P.K - c * 32 + 7) / 8);
+          const uint32_t stage = g & 1u, round = g >> 1;
+          if (!mbar_wait(&full_a[stage], round & 1u, err, 54)) goto done_m;
+          if (!mbar_wait(&full_w[stage], round & 1u, err, 55)) goto done_m;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(a_region + stage * 2 * kAImg), sw = smem_u32(w_region + stage * P.stage_bytes);
+          const uint32_t a_hi = sa, a_lo = sa + kAImg, w_hi = sw, w_lo = sw + P.w_lo_off;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            if (ks >= nks) break;
+            const uint64_t dah = sw128_desc(a_hi + ks * 32), dal = sw128_desc(a_lo + ks * 32);
+            const uint64_t dwh = sw128_desc(w_hi + ks * 32), dwl = sw128_desc(w_lo + ks * 32);
+            mma_tf32(acc, dal, dwh, idesc, (c | ks) != 0);
+            mma_tf32(acc, dah, dwl, idesc, 1);
+            mma_tf32(acc, dah, dwh, idesc, 1);
+          }
+          mma_commit(&empty_a[stage]);
+          mma_commit(&empty_w[stage]);
+        }
+        mma_commit(&acc_full[buf]);
+      }
+    done_m:
+      mma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, err, 56);
+    }
+  } else if (warp < kTransformWarps) {
+    // ---------------------------------------------------------------- A operand
+    const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
+    uint32_t soff[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) soff[q] = (uint32_t)r * 128u + ((((uint32_t)(half * 4 + q)) ^ ((uint32_t)r & 7u)) << 4);
+    uint32_t g = 0;
+    bool ok = true;
+    // this thread's row of tile i: A row, lam row, columns (0 for rows past the end)
+    const float* arow = nullptr;
+    const float* lrow = nullptr;
+    int klim = 0;
+    auto tile_row = [&](int64_t i) {
+      const int64_t row = ((int64_t)blockIdx.x + i * gridDim.x) * 128 + r;
+      const bool valid = row < P.rows;
+      const int64_t b = valid ? row / P.E : 0, e = valid ? row - b * P.E : 0;
+      arow = P.A + b * P.a_bs + e * P.K;
+      lrow = P.lam ? P.lam + b * P.K : nullptr;
+      klim = valid ? P.K : 0;
+    };
+    // the values of the next chunk (of this tile, or the first of the next tile) are
+    // loaded one chunk ahead, so that their latency overlaps this chunk's work
+    float vnext[16], lnext[16];
+    if (my_tiles > 0) {
+      tile_row(0);
+      load16g(arow, half * 16, klim, P.a_vec, vnext);
+      if (lrow) load16g(lrow, half * 16, klim, P.lam_vec, lnext);
+    }
+    for (int64_t i = 0; i < my_tiles && ok; ++i) {
+      for (int c = 0; c < P.kchunks; ++c, ++g) {
+        const int k0 = c * 32 + half * 16;
+        const uint32_t stage = g & 1u, round = g >> 1;
+        float v[16], hi[16], lo[16];
+        const bool scale = lrow != nullptr;
+#pragma unroll
+        for (int x = 0; x < 16; ++x) v[x] = scale ? vnext[x] * lnext[x] : vnext[x];
+        if (c + 1 < P.kchunks) {
+          load16g(arow, k0 + 32, klim, P.a_vec, vnext);
+          if (lrow) load16g(lrow, k0 + 32, klim, P.lam_vec, lnext);
+        } else if (i + 1 < my_tiles) {
+          tile_row(i + 1);
+          load16g(arow, half * 16, klim, P.a_vec, vnext);
+          if (lrow) load16g(lrow, half * 16, klim, P.lam_vec, lnext);
+        }
+#pragma unroll
+        for (int x = 0; x < 16; ++x) split_tf32(v[x], hi[x], lo[x]);
+        if (!warp_wait(&empty_a[stage], (round & 1u) ^ 1u, err, 57)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sbase = smem_u32(a_region) + stage * 2 * kAImg;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + soff[q]), "f"(hi[4 * q]),
+                       "f"(hi[4 * q + 1]), "f"(hi[4 * q + 2]), "f"(hi[4 * q + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + kAImg + soff[q]), "f"(lo[4 * q]),
+                       "f"(lo[4 * q + 1]), "f"(lo[4 * q + 2]), "f"(lo[4 * q + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full_a[stage]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- drain (warps 10-13)
+    const int q4 = warp & 3;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    for (int64_t i = 0; i < my_tiles; ++i) {
+      const uint32_t buf = (uint32_t)(i & 1);
+      const int64_t tile = (int64_t)blockIdx.x + i * gridDim.x;
+      const int64_t first = tile * 128, last = first + 127 < P.rows ? first + 127 : P.rows - 1;
+      const int64_t p0 = first / P.E;
+      const bool two_slots = last / P.E != p0;
+      const int64_t row = first + q4 * 32 + lane;
+      const bool valid = row < P.rows;
+      const int64_t b = valid ? row / P.E : 0, e = valid ? row - b * P.E : 0;
+      const int slot = valid ? (int)(b - p0) : 0;
+      if (!warp_wait(&acc_full[buf], (uint32_t)((i >> 1) & 1), err, 58)) break;
+      tc_fence_after();
+      const uint32_t src = tbase + buf * 256u + lane_off;
+      for (int q = 0; q < P.tile_n / 16; ++q) {
+        float x[16];
+        tmem_ld16(src + (uint32_t)(q * 16), x);
+        tmem_ld_wait();
+        zono_drain(P.out, P.o_bs, P.o_vec, P.zpos, P.zneg, tile, P.N, q * 16, x, valid, b, e, slot, two_slots);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kProducerWarp) tmem_dealloc(tbase, 512);
+}
+
+cf_status zono_tc_launch(const ZonoTcParams& P, cudaStream_t st) {
+  int tile_n, nt;
+  chain_tile(P.N, tile_n, nt);
+  CF_REQUIRE(nt == 1 && P.N >= 1 && P.K >= 1 && P.E >= 128 && P.rows == P.B * P.E && P.out && P.zpos && P.zneg &&
+                 P.wimg && P.A && P.err,
+             CF_ERR_UNSUPPORTED, "zono_tc: N %d, K %d, E %lld", P.N, P.K, (long long)P.E);
+  ZonoTcParams Q = P;
+  Q.tile_n = tile_n;
+  Q.kchunks = (P.K + 31) / 32;
+  Q.w_lo_off = (uint32_t)tile_n * 128u;
+  Q.stage_bytes = 2u * (uint32_t)tile_n * 128u;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  Q.a_vec = (P.K % 4 == 0 && P.a_bs % 4 == 0 && a16(P.A)) ? 1 : 0;
+  Q.lam_vec = (P.lam && P.K % 4 == 0 && a16(P.lam)) ? 1 : 0;
+  Q.o_vec = (P.N % 4 == 0 && P.o_bs % 4 == 0 && a16(P.out)) ? 1 : 0;
+  size_t smem = 1024 + (size_t)4 * kAImg + (size_t)2 * Q.stage_bytes + 13 * 8 + 16;
+  if (smem < 116 * 1024) smem = 116 * 1024;  // one CTA per SM: it holds all 512 TMEM columns
+  CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "zono_tc: %zu bytes of shared memory", smem);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  cudaError_t e = cudaFuncSetAttribute(k_zono_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) {
+    set_error("zono_tc: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return CF_ERR_CUDA;
+  }
+  const int64_t tiles = (P.rows + 127) / 128;
+  const int64_t grid = tiles < sms ? tiles : sms;
+  k_zono_persist<<<(unsigned)grid, kZtThreads, smem, st>>>(Q);
+  return check_launch("k_zono_persist");
 }
 
 }  // namespace cf

@@ -54,6 +54,30 @@ struct ChainParams {
   float* zneg;
 };
 
+// Persistent zonotope symbol-row GEMM (k_zono_persist): rows = B*E rows (b, e) of A (row
+// at A + b*a_bs + e*K, K contiguous floats) times diag(lam[b]) times W^T (image of
+// chain_prep_weights(W^T [K, N])), N <= 256, E >= 128.  Every 128-row tile writes its rows
+// to out[b*o_bs + e*N + n] and, per TMEM lane quarter w and region slot, the column sums of
+// the positive / negative coefficients to zpos / zneg[((tile*4 + w)*2 + slot)*N + n] (the
+// layout of the zonotope mode of k_chain).
+struct ZonoTcParams {
+  const uint8_t* wimg;
+  const float* lam;
+  const float* A;
+  int64_t a_bs;
+  int32_t K, N, tile_n, kchunks;
+  int64_t B, E, rows;
+  float* out;
+  int64_t o_bs;
+  float* zpos;
+  float* zneg;
+  int* err;
+  int32_t a_vec, lam_vec, o_vec;
+  uint32_t stage_bytes, w_lo_off;  // filled by zono_tc_launch
+};
+
+cf_status zono_tc_launch(const ZonoTcParams& P, cudaStream_t st);
+
 void chain_tile(int N, int& tile_n, int& n_tiles);
 size_t chain_wimg_bytes(int K, int N);
 cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStream_t st);

@@ -698,8 +698,30 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
       CF_TRY(check_launch("k_zono_const_conv"));
       cc ^= 1;
     } else if (E > 0) {
-      if (!spec && zono_use_chain(E)) {
-        // symbol rows on the tensor cores: one chain step (ReLU column scaling, then W^T)
+      if (!spec && zono_use_chain(E) && N <= 256 && K % 4 == 0) {
+        // symbol rows on the tensor cores: persistent 3xTF32 GEMM (ReLU column scaling, W^T)
+        ZonoTcParams Zt{};
+        Zt.wimg = reinterpret_cast<const uint8_t*>(ws + w.wimg_off[a]);
+        Zt.lam = lam_in;
+        Zt.A = A[cur];
+        Zt.a_bs = E * K;
+        Zt.K = (int32_t)K;
+        Zt.N = (int32_t)N;
+        Zt.B = Bc;
+        Zt.E = E;
+        Zt.rows = Bc * E;
+        Zt.out = out;
+        Zt.o_bs = o_bs;
+        Zt.zpos = Zp;
+        Zt.zneg = Zn;
+        Zt.err = reinterpret_cast<int*>(ws + w.err);
+        prof_step_begin(st);
+        cf_status cs = zono_tc_launch(Zt, st);
+        prof_step_end(st, 2.0 * Bc * E * K * N, 4.0 * Bc * (E * K + E * N));
+        CF_TRY(cs);
+        S.cpos = Zp; S.cneg = Zn; S.E = E;
+      } else if (!spec && zono_use_chain(E)) {
+        // N > 256 or K % 4 != 0: one k_chain step per 128-row tile (ReLU column scaling, W^T)
         ChainParams P{};
         P.S = 1;
         ChainStep& CS = P.st[0];
