@@ -168,24 +168,11 @@ __device__ __forceinline__ void warp_colsum16(float (&v)[16]) {
   v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
-// Zonotope drain of 16 columns n0 .. n0+15 of this thread's row: store the row's values
-// (columns below N) and the warp's per-slot column sums of the positive / negative parts.
-__device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_vec, float* zpos, float* zneg,
-                                           int64_t cta, int N, int n0, const float (&x)[16], bool valid,
-                                           int64_t b, int64_t i, int slot, bool two_slots) {
+// The warp's per-slot column sums of the positive / negative parts of 16 columns n0 ..
+// n0+15 (lane <-> row) into zpos / zneg[((cta*4 + w)*2 + slot)*N + n], w = warp % 4.
+__device__ __forceinline__ void zono_colsums(float* zpos, float* zneg, int64_t cta, int N, int n0,
+                                             const float (&x)[16], bool valid, int slot, bool two_slots) {
   const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3;
-  if (valid) {
-    float* o = zout + b * zo_bs + i * N + n0;
-    if (zo_vec && n0 + 16 <= N) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        reinterpret_cast<float4*>(o)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (n0 + e < N) o[e] = x[e];
-    }
-  }
   for (int sl = 0; sl < (two_slots ? 2 : 1); ++sl) {
     float p[16], q[16];
 #pragma unroll
@@ -203,6 +190,26 @@ __device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_ve
       zneg[idx] = q[0];
     }
   }
+}
+
+// Zonotope drain of 16 columns n0 .. n0+15 of this thread's row: store the row's values
+// (columns below N) and the warp's per-slot column sums.
+__device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_vec, float* zpos, float* zneg,
+                                           int64_t cta, int N, int n0, const float (&x)[16], bool valid,
+                                           int64_t b, int64_t i, int slot, bool two_slots) {
+  if (valid) {
+    float* o = zout + b * zo_bs + i * N + n0;
+    if (zo_vec && n0 + 16 <= N) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        reinterpret_cast<float4*>(o)[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (n0 + e < N) o[e] = x[e];
+    }
+  }
+  zono_colsums(zpos, zneg, cta, N, n0, x, valid, slot, two_slots);
 }
 
 // Shared-memory pieces the transform warps use.
@@ -670,9 +677,9 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ persistent zonotope GEMM
-// 448 threads: warps 0-7 stage the A operand (thread <-> tile row r = t % 128, 16-column
-// half t / 128 of every 32-column chunk: rows and lam loaded from global memory one chunk
-// ahead, scaled, split into tf32 hi + lo, written as the SW128 image), warp 8 allocates TMEM
+// 448 threads: warps 0-7 stage the A operand (coalesced 16-byte pieces of the chunk's rows
+// and of lam loaded from global memory one chunk ahead, scaled, split into tf32 hi + lo,
+// written at their SW128 positions), warp 8 allocates TMEM
 // and streams the W^T chunks (bulk copies), warp 9 issues the 3xTF32 MMAs, warps 10-13
 // drain (thread <-> TMEM lane).  A CTA loops over the row tiles blockIdx.x, +gridDim.x,
 // ...; tile i accumulates in TMEM buffer i % 2, so the drain of tile i overlaps the MMAs
@@ -785,50 +792,60 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
     }
   } else if (warp < kTransformWarps) {
     // ---------------------------------------------------------------- A operand
-    const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
-    uint32_t soff[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) soff[q] = (uint32_t)r * 128u + ((((uint32_t)(half * 4 + q)) ^ ((uint32_t)r & 7u)) << 4);
+    // Thread t handles the 16-byte pieces f = t + 256*q (q < 4) of the 128-row x 128-byte
+    // chunk: row f / 8, piece f % 8 -- eight consecutive threads read one row's 128 bytes
+    // (coalesced), scale by the row's region's lam, split, and write the piece to its SW128
+    // position (row*128 + ((piece ^ row%8) << 4)) in the hi and lo planes.  Requires K % 4 == 0.
+    const int t = threadIdx.x;
     uint32_t g = 0;
     bool ok = true;
-    // this thread's row of tile i: A row, lam row, columns (0 for rows past the end)
-    const float* arow = nullptr;
-    const float* lrow = nullptr;
-    int klim = 0;
-    auto tile_row = [&](int64_t i) {
-      const int64_t row = ((int64_t)blockIdx.x + i * gridDim.x) * 128 + r;
-      const bool valid = row < P.rows;
-      const int64_t b = valid ? row / P.E : 0, e = valid ? row - b * P.E : 0;
-      arow = P.A + b * P.a_bs + e * P.K;
-      lrow = P.lam ? P.lam + b * P.K : nullptr;
-      klim = valid ? P.K : 0;
+    const float* prow[4];
+    const float* plam[4];
+    bool pval[4];
+    auto tile_rows = [&](int64_t i) {
+      const int64_t first = ((int64_t)blockIdx.x + i * gridDim.x) * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int64_t row = first + ((t + 256 * q) >> 3);
+        pval[q] = row < P.rows;
+        const int64_t b = pval[q] ? row / P.E : 0, e = pval[q] ? row - b * P.E : 0;
+        prow[q] = P.A + b * P.a_bs + e * P.K;
+        plam[q] = P.lam ? P.lam + b * P.K : nullptr;
+      }
     };
-    // the values of the next chunk (of this tile, or the first of the next tile) are
-    // loaded one chunk ahead, so that their latency overlaps this chunk's work
-    float vnext[16], lnext[16];
+    // chunk c's pieces (and lam) of the current rows; zeros past the rows or columns
+    auto load_chunk = [&](int c, float4 (&v)[4], float4 (&l)[4]) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k = c * 32 + ((t + 256 * q) & 7) * 4;
+        const bool in = pval[q] && k < P.K;
+        v[q] = in ? __ldg(reinterpret_cast<const float4*>(prow[q] + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        l[q] = (in && plam[q]) ? __ldg(reinterpret_cast<const float4*>(plam[q] + k)) : make_float4(1.f, 1.f, 1.f, 1.f);
+      }
+    };
+    float4 vnext[4], lnext[4];
     if (my_tiles > 0) {
-      tile_row(0);
-      load16g(arow, half * 16, klim, P.a_vec, vnext);
-      if (lrow) load16g(lrow, half * 16, klim, P.lam_vec, lnext);
+      tile_rows(0);
+      load_chunk(0, vnext, lnext);
     }
     for (int64_t i = 0; i < my_tiles && ok; ++i) {
       for (int c = 0; c < P.kchunks; ++c, ++g) {
-        const int k0 = c * 32 + half * 16;
         const uint32_t stage = g & 1u, round = g >> 1;
-        float v[16], hi[16], lo[16];
-        const bool scale = lrow != nullptr;
+        float4 hi[4], lo[4];
 #pragma unroll
-        for (int x = 0; x < 16; ++x) v[x] = scale ? vnext[x] * lnext[x] : vnext[x];
-        if (c + 1 < P.kchunks) {
-          load16g(arow, k0 + 32, klim, P.a_vec, vnext);
-          if (lrow) load16g(lrow, k0 + 32, klim, P.lam_vec, lnext);
-        } else if (i + 1 < my_tiles) {
-          tile_row(i + 1);
-          load16g(arow, half * 16, klim, P.a_vec, vnext);
-          if (lrow) load16g(lrow, half * 16, klim, P.lam_vec, lnext);
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = vnext[q], l = lnext[q];
+          split_tf32(v.x * l.x, hi[q].x, lo[q].x);
+          split_tf32(v.y * l.y, hi[q].y, lo[q].y);
+          split_tf32(v.z * l.z, hi[q].z, lo[q].z);
+          split_tf32(v.w * l.w, hi[q].w, lo[q].w);
         }
-#pragma unroll
-        for (int x = 0; x < 16; ++x) split_tf32(v[x], hi[x], lo[x]);
+        if (c + 1 < P.kchunks) {
+          load_chunk(c + 1, vnext, lnext);
+        } else if (i + 1 < my_tiles) {
+          tile_rows(i + 1);
+          load_chunk(0, vnext, lnext);
+        }
         if (!warp_wait(&empty_a[stage], (round & 1u) ^ 1u, err, 57)) {
           ok = false;
           break;
@@ -836,11 +853,13 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
         const uint32_t sbase = smem_u32(a_region) + stage * 2 * kAImg;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + soff[q]), "f"(hi[4 * q]),
-                       "f"(hi[4 * q + 1]), "f"(hi[4 * q + 2]), "f"(hi[4 * q + 3])
+          const uint32_t f = (uint32_t)(t + 256 * q), row = f >> 3, piece = f & 7u;
+          const uint32_t off = row * 128u + ((piece ^ (row & 7u)) << 4);
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + off), "f"(hi[q].x), "f"(hi[q].y),
+                       "f"(hi[q].z), "f"(hi[q].w)
                        : "memory");
-          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + kAImg + soff[q]), "f"(lo[4 * q]),
-                       "f"(lo[4 * q + 1]), "f"(lo[4 * q + 2]), "f"(lo[4 * q + 3])
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + kAImg + off), "f"(lo[q].x),
+                       "f"(lo[q].y), "f"(lo[q].z), "f"(lo[q].w)
                        : "memory");
         }
         fence_proxy_async_smem();
@@ -885,8 +904,8 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
 cf_status zono_tc_launch(const ZonoTcParams& P, cudaStream_t st) {
   int tile_n, nt;
   chain_tile(P.N, tile_n, nt);
-  CF_REQUIRE(nt == 1 && P.N >= 1 && P.K >= 1 && P.E >= 128 && P.rows == P.B * P.E && P.out && P.zpos && P.zneg &&
-                 P.wimg && P.A && P.err,
+  CF_REQUIRE(nt == 1 && P.N >= 1 && P.K >= 1 && P.K % 4 == 0 && P.E >= 128 && P.rows == P.B * P.E && P.out &&
+                 P.zpos && P.zneg && P.wimg && P.A && P.err,
              CF_ERR_UNSUPPORTED, "zono_tc: N %d, K %d, E %lld", P.N, P.K, (long long)P.E);
   ZonoTcParams Q = P;
   Q.tile_n = tile_n;
