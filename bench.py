@@ -272,8 +272,8 @@ def run_cfgpu(args, rank, world, local):
     # ---- timed region: device events per step, L2 flushed between steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clk = Clocks(local, os.path.join(HERE, "gpurun_out", f"clocks_r{rank}.csv") if os.path.isdir(
-        os.path.join(HERE, "gpurun_out")) else f"/tmp/cf_clocks_r{rank}.csv", device=dev)
+    clk_dir = os.environ.get("CF_CLOCKS_DIR", "/tmp")   # where the per-rank clock samples are written
+    clk = Clocks(local, os.path.join(clk_dir, f"cf_clocks_r{rank}.csv"), device=dev)
     barrier()
     torch.cuda.synchronize()
     profile_enable(True)

@@ -61,6 +61,7 @@ def _load():
         "cf_deeppoly_workspace_bytes": (_sz, [P(CfNetwork), _i64]),
         "cf_deeppoly_run": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
         "cf_deeppoly_layer": (_i32, [P(CfNetwork), _i32, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+        "cf_signscale": (_i32, [_i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
         "cf_deeppoly_check": (_i32, [_vp, _vp]),
         "cf_deeppoly_run_static": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
         "cf_relu_relax": (_i32, [_i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp]),
@@ -93,7 +94,7 @@ lib = _load()
 
 # Every symbol the C header declares (checked by the CPU test suite).
 EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_deeppoly_check",
-            "cf_deeppoly_layer",
+            "cf_deeppoly_layer", "cf_signscale",
             "cf_deeppoly_run_static",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",

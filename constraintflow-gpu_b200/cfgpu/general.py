@@ -24,9 +24,9 @@ the input, then one neuron layer per network layer, in list order.  A block is e
 dense, [1 or B, r, n_t] float32 (a batch-shared layer weight has batch 1), or diagonal,
 [B, n_t] (a ReLU's per-neuron relaxation over its own input layer, r = n_t), so a ReLU
 substitution is a column scaling instead of a product with an n x n matrix.  Every
-arithmetic operation is a libcfgpu kernel (cfgpu.ops: cf_bmm, cf_ew_binary, cf_ew_clamp,
-cf_ew_any; cf_relu_relax for DeepPoly's relaxation); torch provides memory, views and
-copies.
+arithmetic operation is a libcfgpu kernel (cfgpu.ops: cf_bmm, cf_signscale, cf_ew_binary,
+cf_ew_clamp, cf_ew_any; cf_relu_relax for DeepPoly's relaxation); torch provides memory,
+views and copies.
 """
 import operator
 
@@ -72,22 +72,43 @@ def _apply(B, A, M):
     return ops.binary(operator.mul, A, M.unsqueeze(1).expand(A.shape), F32)
 
 
+def _vec(B, v):
+    """[1 or B, n] -> [B, n] (materialised when shared)."""
+    return v.expand(B, v.shape[1]).contiguous() if v.shape[0] != B else v
+
+
 def _rowdot(A, c):
     """A [B, r, n] . c [B, n] -> [B, r]."""
     return ops.bmm(A, c.unsqueeze(2))[:, :, 0]
 
 
 def _substitute(B, blocks, c, t, P, Q):
-    """Replace layer t's neurons: coefficient >= 0 -> P, < 0 -> Q (each (blocks, const))."""
+    """Replace layer t's neurons: coefficient >= 0 -> P, < 0 -> Q (each (blocks, const)).
+
+    When P and Q are the same polyexp (an affine layer, whose L and U are both W x + b, or
+    an Add / Concat of such layers) the sign split A+ P + A- Q is A P: one product instead
+    of two (as the tensor-core chain substitutes affine layers)."""
     A = _full(B, blocks.pop(t))
-    Ap = ops.clamp(A, 0.0, True)
-    An = ops.clamp(A, 0.0, False)
     new = {}
-    for s, M in P[0].items():
-        _add_block(B, new, s, _apply(B, Ap, M))
-    for s, M in Q[0].items():
-        _add_block(B, new, s, _apply(B, An, M))
-    dc = _add(_rowdot(Ap, P[1]), _rowdot(An, Q[1]))
+    (ps, pm), = P[0].items() if len(P[0]) == 1 else ((None, None),)
+    (qs, qm), = Q[0].items() if len(Q[0]) == 1 else ((None, None),)
+    if P is not Q and ps is not None and ps == qs and pm.dim() == 2 and qm.dim() == 2:
+        # a ReLU layer's per-neuron relaxations (diagonal blocks over one layer): one fused
+        # sign-selected column scaling, the constant terms in the same pass
+        out, dc = ops.signscale(A, _vec(B, pm), _vec(B, qm), _vec(B, P[1]), _vec(B, Q[1]))
+        new[ps] = out
+    elif P is Q:
+        for s, M in P[0].items():
+            _add_block(B, new, s, _apply(B, A, M))
+        dc = _rowdot(A, P[1])
+    else:
+        Ap = ops.clamp(A, 0.0, True)
+        An = ops.clamp(A, 0.0, False)
+        for s, M in P[0].items():
+            _add_block(B, new, s, _apply(B, Ap, M))
+        for s, M in Q[0].items():
+            _add_block(B, new, s, _apply(B, An, M))
+        dc = _add(_rowdot(Ap, P[1]), _rowdot(An, Q[1]))
     for s, M in blocks.items():     # the stopped part (the other layers) is added after
         _add_block(B, new, s, _full(B, M))
     zero = ops.scalar_view(0.0, tuple(dc.shape), F32)
@@ -228,14 +249,17 @@ def run(layers, l0, u0, spec_W, relaxation="deeppoly"):
                 raise ValueError(f"layer {idx}: {kind} takes two parents, got {parents}")
             (l1, u1), (l2, u2) = bnd[ks[0]], bnd[ks[1]]
             (L1, U1), (L2, U2) = polys[ks[0]], polys[ks[1]]
+            same = L1 is U1 and L2 is U2    # parents whose L and U are one polyexp
             if kind == "add":
                 if l1.shape != l2.shape:
                     raise ValueError(f"layer {idx}: add of {tuple(l1.shape)} and {tuple(l2.shape)}")
                 bnd[k] = (_add(l1, l2), _add(u1, u2))
-                polys[k] = (_sum_poly(B, L1, L2), _sum_poly(B, U1, U2))
+                lo = _sum_poly(B, L1, L2)
+                polys[k] = (lo, lo if same else _sum_poly(B, U1, U2))
             else:
                 bnd[k] = (torch.cat([l1, l2], dim=1), torch.cat([u1, u2], dim=1))
-                polys[k] = (_stack_poly(B, L1, L2), _stack_poly(B, U1, U2))
+                lo = _stack_poly(B, L1, L2)
+                polys[k] = (lo, lo if same else _stack_poly(B, U1, U2))
             continue
         if kind == "spec":
             A0 = W

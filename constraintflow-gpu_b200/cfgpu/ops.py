@@ -118,6 +118,26 @@ def any_nonzero(a):
     return bool(flag.item())
 
 
+def signscale(A, p, q, pc, qc):
+    """out = A * (A >= 0 ? p : q) column-wise per batch, dc = sum_n A * (A >= 0 ? pc : qc).
+
+    A [nb, M, N] with unit column stride; p, q, pc, qc [nb, N] contiguous (pc / qc may be
+    None: 0).  Returns (out [nb, M, N], dc [nb, M])."""
+    nb, M, N = A.shape
+    if A.stride(2) != 1:
+        A = A.contiguous()
+    out = torch.empty(nb, M, N, dtype=torch.float32, device=A.device)
+    dc = torch.empty(nb, M, dtype=torch.float32, device=A.device)
+    vs = [v.contiguous() if v is not None else None for v in (p, q, pc, qc)]
+    LAUNCHES[0] += 1
+    st = _lib.lib.cf_signscale(nb, M, N, A.data_ptr(), A.stride(0), A.stride(1), vs[0].data_ptr(), vs[1].data_ptr(),
+                               vs[2].data_ptr() if vs[2] is not None else None,
+                               vs[3].data_ptr() if vs[3] is not None else None, N, out.data_ptr(), dc.data_ptr(),
+                               _stream())
+    _lib.check(st, "cf_signscale")
+    return out, dc
+
+
 def bmm(A, B, C=None, accumulate=False):
     """C[b] (+)= A[b] @ B[b]; A [nb, M, K], B [nb, K, N] strided views."""
     nb, M, K = A.shape

@@ -258,6 +258,50 @@ extern "C" cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x
   return check_launch("k_ew_any");
 }
 
+// Sign-selected column scaling of rows (the substitution of a ReLU layer's per-neuron
+// relaxation into a coefficient matrix): out[b,m,n] = A[b,m,n] * (A >= 0 ? p[b,n] : q[b,n]),
+// dc[b,m] = sum_n A[b,m,n] * (A >= 0 ? pc[b,n] : qc[b,n]).  One warp per row.
+__global__ void k_signscale(int64_t nb, int64_t M, int64_t N, const float* __restrict__ A, int64_t a_bs,
+                            int64_t a_ms, const float* __restrict__ p, const float* __restrict__ q,
+                            const float* __restrict__ pc, const float* __restrict__ qc, int64_t v_bs,
+                            float* __restrict__ out, float* __restrict__ dc) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= nb * M) return;
+  const int64_t b = w / M, m = w - b * M;
+  const float* a = A + b * a_bs + m * a_ms;
+  const float *pb = p + b * v_bs, *qb = q + b * v_bs;
+  const float* pcb = pc ? pc + b * v_bs : nullptr;
+  const float* qcb = qc ? qc + b * v_bs : nullptr;
+  float* o = out + w * N;
+  float acc = 0.0f;
+  for (int64_t n = lane; n < N; n += 32) {
+    const float x = a[n];
+    const bool pos = x >= 0.0f;
+    o[n] = x * (pos ? pb[n] : qb[n]);
+    const float* cv = pos ? pcb : qcb;
+    if (cv) acc = fmaf(x, cv[n], acc);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (dc && lane == 0) dc[w] = acc;
+}
+
+extern "C" cf_status cf_signscale(int64_t nb, int64_t M, int64_t N, const float* A, int64_t a_bs, int64_t a_ms,
+                                  const float* p, const float* q, const float* pc, const float* qc, int64_t v_bs,
+                                  float* out, float* dc, void* stream) {
+  clear_error();
+  CF_INJECT("signscale");
+  CF_REQUIRE(nb >= 0 && M >= 0 && N >= 0, CF_ERR_SHAPE, "signscale: negative size");
+  if (nb * M == 0) return CF_OK;
+  CF_REQUIRE(A && p && q && out, CF_ERR_NULL, "signscale: NULL argument");
+  const int64_t warps = nb * M;
+  const int64_t blocks = ceil_div(warps * 32, 256);
+  CF_REQUIRE(blocks <= 0x7fffffff, CF_ERR_SHAPE, "signscale: too many rows");
+  k_signscale<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(nb, M, N, A, a_bs, a_ms, p, q, pc, qc, v_bs, out, dc);
+  return check_launch("k_signscale");
+}
+
 extern "C" cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K, const float* A, int64_t a_bs, int64_t a_ms,
                             int64_t a_ks, const float* B, int64_t b_bs, int64_t b_ks, int64_t b_ns, float* C,
                             int32_t accumulate, void* stream) {

@@ -264,6 +264,16 @@ cf_status cf_ew_clamp(int32_t ndim, const int64_t* shape, const float* x_dev, co
  * with (b_bs, b_ks, b_ns) (zero strides broadcast), C contiguous [nb, M, N]; float32.
  * The block-pair product of SparseTensor.matmul (constraintflow/gbcsr/sparse_tensor.py:1671-2060,
  * DenseBlock.matmul_equal_dims sparse_block.py:748, matmul_unequal_dims :964). */
+/* Substitution of a per-neuron (diagonal) relaxation into coefficient rows, sign-selected:
+ * out[b,m,n] = A[b,m,n] * (A >= 0 ? p[b,n] : q[b,n]) (out compact [nb, M, N]) and, if dc is
+ * not NULL, dc[b,m] = sum_n A[b,m,n] * (A >= 0 ? pc[b,n] : qc[b,n]) (pc or qc NULL: 0).
+ * A row (b,m) at A + b*a_bs + m*a_ms, n contiguous; p, q, pc, qc rows at b*v_bs.  The fused
+ * form of clamp (tensor_ops.py:765) + inner_prod with a DiagonalBlock
+ * (sparse_block.py:790) + binary add for the two signs. */
+cf_status cf_signscale(int64_t nb, int64_t M, int64_t N, const float* A, int64_t a_bs, int64_t a_ms,
+                       const float* p, const float* q, const float* pc, const float* qc, int64_t v_bs,
+                       float* out, float* dc, void* stream);
+
 cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K,
                  const float* A_dev, int64_t a_bs, int64_t a_ms, int64_t a_ks,
                  const float* B_dev, int64_t b_bs, int64_t b_ks, int64_t b_ns,

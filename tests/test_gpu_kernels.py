@@ -211,3 +211,25 @@ def test_ew_unary_where_clamp_any():
     assert int(flag.item()) == 0
     L.check(L.lib.cf_ew_any(2, shp, xt.data_ptr(), 0, cs, flag.data_ptr(), s))
     assert int(flag.item()) == 1
+
+
+def test_signscale_matches_torch():
+    """cf_signscale: sign-selected column scaling and the constant row sums, against a
+    float64 torch restatement."""
+    import torch
+    from cfgpu import ops
+    g = torch.Generator().manual_seed(7)
+    dev = torch.device("cuda:0")
+    nb, M, N = 3, 37, 203
+    A = torch.randn(nb, M, N, generator=g)
+    A[0, 0, :5] = 0.0
+    p, q, pc, qc = (torch.randn(nb, N, generator=g) for _ in range(4))
+    out, dc = ops.signscale(A.to(dev), p.to(dev), q.to(dev), pc.to(dev), qc.to(dev))
+    pos = A >= 0
+    ref = torch.where(pos, A * p[:, None, :], A * q[:, None, :])
+    rdc = torch.where(pos, A.double() * pc[:, None, :].double(), A.double() * qc[:, None, :].double()).sum(-1)
+    assert torch.equal(out.cpu(), ref)
+    assert torch.allclose(dc.cpu().double(), rdc, rtol=1e-5, atol=1e-5)
+    out2, dc2 = ops.signscale(A.to(dev), p.to(dev), q.to(dev), None, qc.to(dev))
+    rdc2 = torch.where(pos, torch.zeros_like(A).double(), A.double() * qc[:, None, :].double()).sum(-1)
+    assert torch.equal(out2.cpu(), ref) and torch.allclose(dc2.cpu().double(), rdc2, rtol=1e-5, atol=1e-5)
