@@ -2,7 +2,7 @@
 """Benchmark: certified input regions/sec (DeepPoly, whole input box) on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cfgpu|reference] [--workload 2]
-                    [--certifier deeppoly|crown|zono|ibp] [--batch B]
+                    [--certifier deeppoly|crown|zono|ibp|polyzono] [--batch B]
 
 One step = one whole DeepPoly pass (input box, property matrix, every layer's
 backsubstitution down to the input, final bounds) over one batch of regions of the
@@ -48,8 +48,8 @@ def parse():
     ap.add_argument("--impl", default="cfgpu", choices=["cfgpu", "reference"])
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
-    ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp"],
-                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf)")
+    ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp", "polyzono"],
+                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf)")
     return ap.parse_args()
 
 
@@ -164,7 +164,8 @@ class Clocks:
 CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
 
 
-METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)"}
+METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)",
+          "polyzono": "polyzono (DeepPoly met with the zonotope)"}
 
 
 def _metric(certifier):
@@ -174,8 +175,10 @@ def _metric(certifier):
 def _oracle_fn(wl, certifier="deeppoly"):
     """The oracle for the workload and program: the chain DeepPoly oracle, the general one
     (CROWN, or a network with Add / Concat layers), or the zonotope / interval one."""
-    if certifier in ("zono", "ibp"):
+    if certifier in ("zono", "ibp", "polyzono"):
         from oracle import zono_oracle as Z
+        if certifier == "polyzono":
+            return lambda l0, u0, W: Z.polyzono(wl.layers, l0, u0, W)
         if certifier == "zono":
             return lambda l0, u0, W: Z.zono(wl.layers, l0, u0, W)
         return lambda l0, u0, W: Z.ibp(wl.layers, l0, u0, W)
@@ -253,7 +256,11 @@ def run_cfgpu(args, rank, world, local):
     lo, hi = cdist.shard_range(B * world, rank, world)
     X = Xall[lo:hi].contiguous()
     y = nets.labels(wl, X)
-    eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=args.certifier)
+    if args.certifier == "polyzono":
+        from cfgpu.polyzono import PolyZonoEngine
+        eng = PolyZonoEngine(wl.layers, wl.input_size, dev)
+    else:
+        eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=args.certifier)
     Xd, yd = X.to(dev), y.to(dev)
     lb = torch.empty(B, 9, dtype=torch.float64, device=dev)
     ub = torch.empty_like(lb)
@@ -340,7 +347,7 @@ def run_cfgpu(args, rank, world, local):
     bf16, hbm, src = peaks()
     achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
     conv = any(L.kind == "conv" for L in wl.layers)
-    zono_tc = args.certifier == "zono" and os.environ.get("CF_STEP_IMPL") != "simt"
+    zono_tc = args.certifier in ("zono", "polyzono") and os.environ.get("CF_STEP_IMPL") != "simt"
     if conv or not eng.chain or (args.certifier in ("zono", "ibp") and not zono_tc):
         # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
         # with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass: k_zono_gemm
@@ -370,7 +377,8 @@ def run_cfgpu(args, rank, world, local):
                      "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
                                         "CTAs) from one ncu --set full capture of this command")
                      if (args.workload, args.certifier) in NCU_TRAFFIC else None,
-                     "kernel": {"zono": "k_chain (zonotope mode)" if zono_tc else "k_zono_gemm", "ibp": None}.get(
+                     "kernel": {"zono": "k_zono_persist" if zono_tc else "k_zono_gemm", "ibp": None,
+                                "polyzono": "k_chain (backsubstitution) + k_zono_persist"}.get(
                          args.certifier, "backsubstitution step" if eng.chain else "k_bmm (general traversal)"),
                      "peak_source": peak_src,
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,

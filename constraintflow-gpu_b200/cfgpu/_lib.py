@@ -74,6 +74,7 @@ def _load():
         "cf_ew_where": (_i32, [_i32, _p64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _i32, _vp]),
         "cf_ew_clamp": (_i32, [_i32, _p64, _vp, _p64, _f32, _i32, _vp, _vp]),
         "cf_ew_any": (_i32, [_i32, _p64, _vp, _i32, _p64, _vp, _vp]),
+        "cf_bounds_meet": (_i32, [_i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
         "cf_bmm": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _vp]),
         "cf_input_box": (_i32, [_i64, _i32, _i64, _vp, _f32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp, _vp,
                                 _vp]),
@@ -94,7 +95,7 @@ lib = _load()
 
 # Every symbol the C header declares (checked by the CPU test suite).
 EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_deeppoly_check",
-            "cf_deeppoly_layer", "cf_signscale",
+            "cf_deeppoly_layer", "cf_signscale", "cf_bounds_meet",
             "cf_deeppoly_run_static",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",

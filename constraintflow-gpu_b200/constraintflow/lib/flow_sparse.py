@@ -21,8 +21,11 @@ Two forward programs are recognised by their own Affine / Relu:
     concretises sum |coefficient|; the Relu opens fresh noise symbols (get_new_eps);
   * ibp.cf: interval arithmetic on the previous layer's l / u (clamp sign split, no
     traversal); the Relu clamps l and u.
+polyzono.cf carries both states: its Affine is DeepPoly's traversal met (cf_max / cf_min)
+with the zonotope's concretisation, its Relu both relaxations (convert_to_poly and
+get_new_eps); it runs as cfgpu.polyzono's coupled DeepPoly and zonotope passes.
 A transformer object may also declare itself with a ``cf_certifier`` attribute
-('deeppoly', 'crown', 'zono' or 'ibp').  Other programs (zono2.cf's whole-layer branches
+('deeppoly', 'crown', 'zono', 'ibp' or 'polyzono').  Other programs (zono2.cf's whole-layer branches
 among them) raise NotImplementedError.
 """
 import inspect
@@ -46,10 +49,14 @@ _ZONO_RELU = ("get_new_eps(", "get_elem('Z', prev", "operator.truediv", "operato
 # ibp.cf: interval arithmetic over the previous layer's l / u
 _IBP_AFFINE = ("inner_prod(", "clamp(", "get_elem('l'", "get_elem('u'")
 _IBP_RELU = ("convert_to_float(", "operator.ge", "get_elem('l', prev", "get_elem('u', prev")
+# polyzono.cf: DeepPoly's traversal met with the zonotope bound; both relaxations in the Relu
+_POLYZONO_AFFINE = _AFFINE + ("get_elem('Z', prev", "cf_max(", "cf_min(")
+_POLYZONO_RELU = ("convert_to_poly(", "get_new_eps(", "get_elem('Z', prev", "operator.truediv", "where(")
 
 
 def certifier_of(transformer):
-    """'deeppoly', 'crown', 'zono' or 'ibp' for a recognised generated transformer, else raises."""
+    """'deeppoly', 'crown', 'zono', 'ibp' or 'polyzono' for a recognised generated transformer,
+    else raises."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
@@ -59,6 +66,10 @@ def certifier_of(transformer):
         affine = inspect.getsource(cls.Affine)
     except (AttributeError, OSError, TypeError) as e:
         raise NotImplementedError(f"cannot read the generated transformer: {e}")
+    if all(k in affine for k in _POLYZONO_AFFINE) and all(k in relu for k in _POLYZONO_RELU):
+        if "if(" in relu or "any(" in relu:
+            raise NotImplementedError("a polyzono-style program with whole-layer branches")
+        return "polyzono"
     if all(k in affine for k in _AFFINE):
         branches = "if(" in relu or "any(" in relu or "operator.gt" in relu
         if not branches and (all(k in relu for k in _DEEPPOLY_RELU) or all(k in relu for k in _EFFICIENT_RELU)):
@@ -71,8 +82,8 @@ def certifier_of(transformer):
     if (all(k in affine for k in _IBP_AFFINE) and all(k in relu for k in _IBP_RELU) and "get_max_priority(" not in affine
             and "get_new_eps(" not in relu and "convert_to_poly(" not in relu and not branches):
         return "ibp"
-    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf) and interval (ibp.cf) "
-                              "certifier programs; the given "
+    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf), interval (ibp.cf) "
+                              "and polyzono.cf certifier programs; the given "
                               f"transformer ({cls.__name__}) is a different program")
 
 
@@ -139,7 +150,11 @@ class Flow:
         u0 = u_in.get_dense_device()[:, :n0].contiguous()
         spec = self.model[-1]
         W = torch.as_tensor(spec.weight, dtype=torch.float32).to(dev).contiguous()
-        eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier)
+        if certifier == "polyzono":
+            from cfgpu.polyzono import PolyZonoEngine
+            eng = PolyZonoEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]))
+        else:
+            eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier)
         if getattr(self.transformer, "cf_layerwise", False) and eng.net is not None:
             lb, ub, sl, su = self._layer_by_layer(eng, l0, u0, W)
         else:
@@ -162,7 +177,8 @@ class Flow:
         """Programs emitted by cfgpu.codegen: the transformer's operation is called for every
         layer in order (as flow_sparse.py:27-228 does), each one fused libcfgpu call."""
         from cfgpu.layerwise import LayerRun
-        run = LayerRun(eng, l0, u0, W)
+        from cfgpu.polyzono import PolyZonoRun
+        run = PolyZonoRun(eng, l0, u0, W) if eng.certifier == "polyzono" else LayerRun(eng, l0, u0, W)
         self.abs_elem.cf_run = run
         B = self.batch_size
         try:

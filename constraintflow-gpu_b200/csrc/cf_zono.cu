@@ -310,11 +310,11 @@ struct ZonoSums {
 };
 
 // Concretisation: l = ((-P) + Nn) + c, u = (P + (-Nn)) + c with P / Nn the positive /
-// negative coefficient sums, added in a fixed order.  Writes the compact l/u [B, N], the
-// state columns (ld_state) and, for the property layer, the float64 bounds.
+// negative coefficient sums, added in a fixed order.  Writes the state columns (ld_state)
+// and, for the property layer, the float64 bounds.
 __global__ void k_zono_bounds(int64_t B, int64_t N, ZonoSums S, const float* __restrict__ c,
-                              float* __restrict__ lo, float* __restrict__ uo, float* __restrict__ sl,
-                              float* __restrict__ su, int64_t ld_state, double* __restrict__ lb,
+                              float* __restrict__ sl, float* __restrict__ su, int64_t ld_state,
+                              double* __restrict__ lb,
                               double* __restrict__ ub) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= B * N) return;
@@ -343,8 +343,6 @@ __global__ void k_zono_bounds(int64_t B, int64_t N, ZonoSums S, const float* __r
   const float cc = c[t];
   const float l = (-P + Q) + cc;
   const float u = (P + (-Q)) + cc;
-  lo[t] = l;
-  uo[t] = u;
   sl[b * ld_state + n] = l;
   su[b * ld_state + n] = u;
   if (lb) {
@@ -353,16 +351,18 @@ __global__ void k_zono_bounds(int64_t B, int64_t N, ZonoSums S, const float* __r
   }
 }
 
-// Generated zono.Relu on the affine's l, u, c [B, n]: column scaling lam, fresh-symbol
-// coefficients nu, new constant; the ReLU layer's own l, u are 0.
+// Generated zono.Relu on the affine's l, u (its state columns, row stride ld_in) and c
+// [B, n]: column scaling lam, fresh-symbol coefficients nu, new constant; the ReLU layer's
+// own l, u are 0.  Reading the bounds from the state lets a caller that tightened them
+// there (polyzono.cf: the max / min with the DeepPoly bounds) relax with the tighter ones.
 __global__ void k_zono_relu(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
-                            const float* __restrict__ c, float* __restrict__ lam, float* __restrict__ nu,
-                            float* __restrict__ c_out, float* __restrict__ sl, float* __restrict__ su,
-                            int64_t ld_state) {
+                            int64_t ld_in, const float* __restrict__ c, float* __restrict__ lam,
+                            float* __restrict__ nu, float* __restrict__ c_out, float* __restrict__ sl,
+                            float* __restrict__ su, int64_t ld_state) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= B * n) return;
   const int64_t b = t / n, k = t - b * n;
-  const float lv = l[t], uv = u[t], cv = c[t];
+  const float lv = l[b * ld_in + k], uv = u[b * ld_in + k], cv = c[t];
   const bool pos = lv >= 0.0f;
   const bool dead = !pos && uv <= 0.0f;
   float lm, nv, co;
@@ -620,9 +620,6 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
   float* lam = reinterpret_cast<float*>(ws + w.lam);
   float* nu = reinterpret_cast<float*>(ws + w.nu);
   float* zeros = reinterpret_cast<float*>(ws + w.zeros);
-  const int64_t vstride = (int64_t)((w.lu[1] - w.lu[0]) / 2 / sizeof(float));
-  float* lo = reinterpret_cast<float*>(ws + w.lu[0]);
-  float* uo = lo + vstride;
   if (li_begin == 0) {
     CF_TRY(launch_copy_rows(Bc, n0, l0, n0, sl, Ntot, st));
     CF_TRY(launch_copy_rows(Bc, n0, u0, n0, su, Ntot, st));
@@ -648,7 +645,9 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
         if (li_relu >= li_begin && li_relu < li_end) {
           const int64_t N = z.N[a];
           const int64_t rcol = p.col[li_relu];
-          k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, lo, uo, C[cc], lam, nu, C[cc ^ 1],
+          const int64_t acol = p.col[p.affine[a]];
+          k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, sl + acol, su + acol, Ntot, C[cc], lam,
+                                                                       nu, C[cc ^ 1],
                                                                        sl + rcol, su + rcol, Ntot);
           CF_TRY(check_launch("k_zono_relu"));
         }
@@ -769,7 +768,7 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
       CF_TRY(check_launch("k_zono_const"));
       cc ^= 1;
     }
-    k_zono_bounds<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, S, C[cc], lo, uo, sl + col, su + col, Ntot,
+    k_zono_bounds<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, S, C[cc], sl + col, su + col, Ntot,
                                                                    spec ? lb : nullptr, spec ? ub : nullptr);
     CF_TRY(check_launch("k_zono_bounds"));
     if (spec) break;
@@ -778,7 +777,8 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
     diag = false;
     if (li_relu >= 0 && li_relu < li_end) {
       const int64_t rcol = p.col[li_relu];
-      k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, lo, uo, C[cc], lam, nu, C[cc ^ 1],
+      k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, sl + col, su + col, Ntot, C[cc], lam, nu,
+                                                                   C[cc ^ 1],
                                                                    sl + rcol, su + rcol, Ntot);
       CF_TRY(check_launch("k_zono_relu"));
       cc ^= 1;
@@ -927,4 +927,42 @@ cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const flo
   return CF_OK;
 }
 
+// l = max(l_a, l_b), u = min(u_a, u_b) over [B, n], written back to both states (rows at
+// ld_a / ld_b) and, if lb is not NULL, to the float64 bounds [B, n].  NaN in either operand
+// gives NaN, as torch.maximum / torch.minimum do.
+__global__ void k_bounds_meet(int64_t B, int64_t n, float* __restrict__ la, float* __restrict__ ua, int64_t ld_a,
+                              float* __restrict__ lb_, float* __restrict__ ub_, int64_t ld_b,
+                              double* __restrict__ lo, double* __restrict__ hi) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= B * n) return;
+  const int64_t b = t / n, k = t - b * n;
+  const int64_t ia = b * ld_a + k, ib = b * ld_b + k;
+  const float l1 = la[ia], l2 = lb_[ib], u1 = ua[ia], u2 = ub_[ib];
+  const float l = (l1 != l1 || l2 != l2) ? __int_as_float(0x7fc00000) : fmaxf(l1, l2);
+  const float u = (u1 != u1 || u2 != u2) ? __int_as_float(0x7fc00000) : fminf(u1, u2);
+  la[ia] = l;
+  lb_[ib] = l;
+  ua[ia] = u;
+  ub_[ib] = u;
+  if (lo) {
+    lo[t] = (double)l;
+    hi[t] = (double)u;
+  }
+}
+
 }  // namespace cf
+
+using namespace cf;
+
+extern "C" cf_status cf_bounds_meet(int64_t B, int64_t n, float* l_a, float* u_a, int64_t ld_a, float* l_b,
+                                    float* u_b, int64_t ld_b, double* lb, double* ub, void* stream) {
+  clear_error();
+  CF_INJECT("bounds_meet");
+  CF_REQUIRE(B >= 0 && n >= 0 && ld_a >= n && ld_b >= n, CF_ERR_SHAPE, "bounds_meet: bad sizes");
+  if (B * n == 0) return CF_OK;
+  CF_REQUIRE(l_a && u_a && l_b && u_b, CF_ERR_NULL, "bounds_meet: NULL argument");
+  CF_REQUIRE((lb == nullptr) == (ub == nullptr), CF_ERR_NULL, "bounds_meet: lb and ub both or neither");
+  k_bounds_meet<<<(unsigned)ceil_div(B * n, 256), 256, 0, as_stream(stream)>>>(B, n, l_a, u_a, ld_a, l_b, u_b, ld_b,
+                                                                              lb, ub);
+  return check_launch("k_bounds_meet");
+}

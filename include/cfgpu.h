@@ -278,6 +278,13 @@ cf_status cf_bmm(int64_t nb, int64_t M, int64_t N, int64_t K,
                  const float* A_dev, int64_t a_bs, int64_t a_ms, int64_t a_ks,
                  const float* B_dev, int64_t b_bs, int64_t b_ks, int64_t b_ns,
                  float* C_dev, int32_t accumulate, void* stream);
+/* Bound combination of a certifier that carries two abstract states (polyzono.cf: the
+ * DeepPoly polyexps and the zonotope): l = max(l_a, l_b), u = min(u_a, u_b) over [B, n],
+ * written back into both states (rows at ld_a / ld_b floats) and, when lb / ub are not
+ * NULL, to float64 [B, n].  Replaces the cf_max / cf_min calls of the generated
+ * polyzono.Affine (constraintflow/gbcsr/tensor_ops.py:226, :245) on dense bound blocks. */
+cf_status cf_bounds_meet(int64_t B, int64_t n, float* l_a, float* u_a, int64_t ld_a,
+                         float* l_b, float* u_b, int64_t ld_b, double* lb, double* ub, void* stream);
 /* *flag_dev |= 1 if any element of x is nonzero (flag is a device uint32). */
 cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x_dev, int32_t x_dtype,
                     const int64_t* x_strides, uint32_t* flag_dev, void* stream);

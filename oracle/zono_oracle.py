@@ -1,11 +1,12 @@
-"""CPU oracle for the reference's zonotope (DeepZ) and interval programs (numpy, float32).
+"""CPU oracle for the reference's zonotope (DeepZ), interval and polyzono programs (numpy,
+float32).
 
 TEST INFRASTRUCTURE ONLY.  Only tests/, ``__graft_entry__.smoke()`` and bench.py's
 CPU legs may import this module, as the checker; the product path (cfgpu) never
 imports it and has no CPU fallback.
 
 What it restates: the reference compiler's output for
-examples/compiler_examples/zono.cf, zono2.cf and ibp.cf (kept as fixtures in
+examples/compiler_examples/zono.cf, zono2.cf, ibp.cf and polyzono.cf (kept as fixtures in
 tests/golden/generated/<program>/transformers.py), run forward by
 constraintflow/lib/flow_sparse.py:27-228.
 
@@ -30,9 +31,13 @@ constraintflow/lib/flow_sparse.py:27-228.
   else l' = (u*l)/(u-l), u' = u, Z' = (u*Z)/(u-l) - ((u*l)/(2*(u-l))) * (1 + eps).
 * ibp (ibp.cf): Affine l' = (W+ l + W- u) + b, u' = (W+ u + W- l) + b;
   Relu l' = 1[l>=0] l + (1 - 1[l>=0]) 0 (same for u).
+* polyzono (polyzono.cf:30-46): DeepPoly's state and the zonotope side by side; an
+  affine layer's bounds are max / min of the two (cf_max / cf_min,
+  constraintflow/gbcsr/tensor_ops.py:226, :245), and both ReLU relaxations use the met
+  bounds (``polyzono`` below).
 
 Pinned against: the reference's own outputs (tests/golden/zono_*.npz, zono2_*.npz,
-ibp_*.npz, made by tests/golden/gen_golden.py).
+ibp_*.npz, pz_*.npz, made by tests/golden/gen_golden.py).
 """
 import numpy as np
 
@@ -223,5 +228,55 @@ def ibp(layers, l0, u0, spec_W):
             u = (pu @ Wp.T + pl @ Wn.T).astype(F32)
         state[k] = ((l + b).astype(F32), (u + b).astype(F32))
     bounds = [state[k] for k in range(1, len(layers) + 2)]
+    lb, ub = bounds[-1]
+    return bounds, lb.astype(np.float64), ub.astype(np.float64)
+
+
+def polyzono(layers, l0, u0, spec_W):
+    """Run polyzono.cf over a chain network: the DeepPoly state (L, U polyexps, backward
+    traversal lowest layer first) and the zonotope Z carried side by side.
+
+    Affine (generated polyzono.Affine): l = max(Z's concretisation, the DeepPoly backward
+    bound), u = min(...); L = U = W x + b; Z' = W Z + b.  Relu: l' = relu(l), u' = relu(u) and
+    DeepPoly's L', U' from the combined bounds (its strict comparisons in relu and
+    compute_upper give the same values as deeppoly.cf's at l = 0 or u = 0); Z' as in zono.cf,
+    also from the combined bounds.  Returns (bounds, lb, ub).
+    """
+    from .crown_oracle import _deeppoly_relu, _traverse
+    from .deeppoly_oracle import _affine_rows
+    l0 = np.asarray(l0, F32)
+    u0 = np.asarray(u0, F32)
+    B = l0.shape[0]
+    polys = {0: (({}, l0), ({}, u0))}
+    bnd = {0: (l0, u0)}
+    M, c = create_z(l0, u0)
+    E = M.shape[2]
+    for idx, L in enumerate(list(layers) + ['spec']):
+        k = idx + 1
+        kind = 'spec' if L == 'spec' else L.kind
+        pl, pu = bnd[k - 1]
+        M = _widen(M, E)
+        if kind == 'relu':
+            polys[k], bnd[k] = _deeppoly_relu(pl, pu, k - 1, B)
+            M, c = zono_relu(pl, pu, M, c)
+            E = M.shape[2]
+            continue
+        if kind == 'spec':
+            A0 = np.asarray(spec_W, F32)
+            c0 = np.zeros((B, A0.shape[1]), F32)
+            W_prev = {k - 1: A0}
+            Wm, b = A0, np.zeros(A0.shape[1], F32)
+        else:
+            A0 = np.ascontiguousarray(_affine_rows(L, 0, L.n_out, B)[0])
+            c0 = np.broadcast_to(layer_bias(L), (B, L.n_out)).astype(F32)
+            W_prev = {k - 1: A0[None]}
+            Wm, b = weight_matrix(L), _bias(L)
+        res = [_traverse({t: np.array(np.broadcast_to(X, (B,) + X.shape[-2:]), F32) for t, X in W_prev.items()},
+                         c0.copy(), polys, lower) for lower in (True, False)]
+        lz, uz, M, c = zono_affine(M, c, Wm, b)
+        bnd[k] = (np.maximum(lz, res[0]).astype(F32), np.minimum(uz, res[1]).astype(F32))
+        poly = (W_prev, c0)
+        polys[k] = (poly, poly)
+    bounds = [bnd[k] for k in range(1, len(layers) + 2)]
     lb, ub = bounds[-1]
     return bounds, lb.astype(np.float64), ub.astype(np.float64)

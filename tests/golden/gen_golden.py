@@ -38,7 +38,7 @@ REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 
 # certifier programs of examples/compiler_examples/ whose generated code is kept and run
-PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient", "zono", "zono2", "ibp")
+PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient", "zono", "zono2", "ibp", "polyzono")
 
 # name -> (program, workload id, batch, eps)
 CASES = {
@@ -92,6 +92,11 @@ CASES = {
     "ibp_w2_b4_e2e-4": ("ibp", 2, 4, 0.0002),
     "ibp_w3_b2_e2e-3": ("ibp", 3, 2, 0.002),
     "ibp_w5_b4_e2e-4": ("ibp", 5, 4, 0.0002),
+    # polyzono.cf: DeepPoly backsubstitution and the zonotope in one state
+    "pz_w0_b4_e1e-2": ("polyzono", 0, 4, 0.01),
+    "pz_w1_b8_e5e-4": ("polyzono", 1, 8, 0.0005),
+    "pz_w2_b4_e2e-3": ("polyzono", 2, 4, 0.002),
+    "pz_w2_b4_e2e-4": ("polyzono", 2, 4, 0.0002),
 }
 
 

@@ -38,7 +38,7 @@ def test_structure_without_device():
 
 def test_generated_programs_are_recognised():
     """The reference compiler's own output for deeppoly.cf, deeppoly_efficient.cf,
-    crown.cf, zono.cf and ibp.cf (tests/golden/generated/) is recognised by the drop-in
+    crown.cf, zono.cf, ibp.cf and polyzono.cf (tests/golden/generated/) is recognised by the drop-in
     Flow without a GPU; zono2.cf (whole-layer branches, not run) is refused."""
     import importlib.util
     import os
@@ -46,7 +46,7 @@ def test_generated_programs_are_recognised():
     from constraintflow.lib.flow_sparse import certifier_of
     here = os.path.dirname(os.path.abspath(__file__))
     for program, expect in (("deeppoly", "deeppoly"), ("deeppoly_efficient", "deeppoly"), ("crown", "crown"),
-                            ("zono", "zono"), ("ibp", "ibp"), ("zono2", None)):
+                            ("zono", "zono"), ("ibp", "ibp"), ("polyzono", "polyzono"), ("zono2", None)):
         path = os.path.join(here, "golden", "generated", program, "transformers.py")
         saved = sys.modules.pop("transformers", None)
         try:
@@ -54,7 +54,8 @@ def test_generated_programs_are_recognised():
             mod = importlib.util.module_from_spec(spec)
             sys.modules["transformers"] = mod
             spec.loader.exec_module(mod)
-            cls = getattr(mod, "ibp" if program == "ibp" else "zono" if program.startswith("zono") else "deeppoly")
+            cls = getattr(mod, program if program in ("ibp", "polyzono") else
+                          "zono" if program.startswith("zono") else "deeppoly")
             if expect is None:
                 with pytest.raises(NotImplementedError):
                     certifier_of(cls())

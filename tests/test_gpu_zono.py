@@ -1,7 +1,8 @@
 """GPU parity of the forward programs: zono.cf (DeepZ) and ibp.cf through
 DeepPolyEngine(certifier='zono' | 'ibp') -> cf_deeppoly_run with CF_RELAX_ZONO /
-CF_RELAX_IBP, against the reference's own outputs (tests/golden/zono_*, ibp_*) and the
-oracle; full-size soundness by sampling; the driver's refusals.
+CF_RELAX_IBP, and polyzono.cf through cfgpu.polyzono (DeepPoly and zonotope layer runs met
+by cf_bounds_meet), against the reference's own outputs (tests/golden/zono_*, ibp_*,
+pz_*) and the oracle; full-size soundness by sampling; the driver's refusals.
 Tolerances: tests/parity.py.
 """
 import numpy as np
@@ -18,10 +19,14 @@ pytestmark = pytest.mark.gpu
 
 CHAIN_ZONO = [n for n in names("zono", max_wid=9) if nets.is_chain(Case(n).wl.layers)]
 CHAIN_IBP = [n for n in names("ibp", max_wid=9) if nets.is_chain(Case(n).wl.layers)]
+PZ = names("polyzono", max_wid=9)
 
 
 def _engine(wl, certifier):
     from cfgpu.engine import DeepPolyEngine
+    if certifier == "polyzono":
+        from cfgpu.polyzono import PolyZonoEngine
+        return PolyZonoEngine(wl.layers, wl.input_size, "cuda:0")
     return DeepPolyEngine(wl.layers, wl.input_size, "cuda:0", certifier=certifier)
 
 
@@ -33,7 +38,15 @@ def _run(eng, l0, u0, W):
     return lb.cpu().numpy(), ub.cpu().numpy(), sl.cpu().numpy(), su.cpu().numpy()
 
 
-@pytest.mark.parametrize("name", CHAIN_ZONO + CHAIN_IBP)
+def _oracle(program, layers, l0, u0, W):
+    if program == "ibp":
+        return Z.ibp(layers, l0, u0, W)[0]
+    if program == "polyzono":
+        return Z.polyzono(layers, l0, u0, W)[0]
+    return Z.zono(layers, l0, u0, W)[0]
+
+
+@pytest.mark.parametrize("name", CHAIN_ZONO + CHAIN_IBP + PZ)
 def test_gpu_forward_matches_reference(name):
     c = Case(name)
     lb, ub, sl, su = _run(_engine(c.wl, c.program), c.l0, c.u0, c.spec_W)
@@ -44,17 +57,15 @@ def test_gpu_forward_matches_reference(name):
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
     np.testing.assert_array_equal(ub, su[:, -9:].astype(np.float64))
-    if c.program == "ibp":
-        bounds, _, _ = Z.ibp(c.wl.layers, c.l0, c.u0, c.spec_W)
-    else:
-        bounds, _, _, _ = Z.zono(c.wl.layers, c.l0, c.u0, c.spec_W)
+    bounds = _oracle(c.program, c.wl.layers, c.l0, c.u0, c.spec_W)
     ol, ou = O.flatten_bounds(n0, bounds, c.B)
     worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
     assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
 
 
 @pytest.mark.parametrize("certifier,wid,B,eps", [("zono", 2, 256, 0.002), ("zono", 1, 64, 0.005),
-                                                 ("ibp", 4, 8, 2.0 / 255.0), ("zono", 3, 128, 0.02)])
+                                                 ("ibp", 4, 8, 2.0 / 255.0), ("zono", 3, 128, 0.02),
+                                                 ("polyzono", 1, 64, 0.005), ("polyzono", 3, 32, 0.02)])
 def test_gpu_forward_full_size_sound(certifier, wid, B, eps):
     """The workload's full batch: concrete points of every box (its corners included) stay
     inside the bounds of every affine layer and of the property rows; the first regions
@@ -86,10 +97,7 @@ def test_gpu_forward_full_size_sound(certifier, wid, B, eps):
                 (certifier, int(b), k, kind)
     if wid != 4:
         nb = 2
-        if certifier == "ibp":
-            bounds, _, _ = Z.ibp(wl.layers, l0[:nb], u0[:nb], W[:nb])
-        else:
-            bounds, _, _, _ = Z.zono(wl.layers, l0[:nb], u0[:nb], W[:nb])
+        bounds = _oracle(certifier, wl.layers, l0[:nb], u0[:nb], W[:nb])
         ol, ou = O.flatten_bounds(n0, bounds, nb)
         sizes = [L.n_out for L in wl.layers] + [9]
         worst, where = parity.continuous_errors(sl[:nb, n0:], su[:nb, n0:], ol, ou, sizes)
@@ -127,6 +135,20 @@ def test_gpu_zono_refusals():
     reference's exception type."""
     with pytest.raises(NotImplementedError):
         _engine(nets.workload(5), "zono")
+    with pytest.raises(NotImplementedError):
+        _engine(nets.workload(5), "polyzono")
+
+
+def test_gpu_polyzono_tighter_than_either_half():
+    """The met property bounds are at least as tight as DeepPoly's and the zonotope's alone
+    on the same regions."""
+    c = Case("pz_w0_b4_e1e-2")
+    lbp, ubp, _, _ = _run(_engine(c.wl, "polyzono"), c.l0, c.u0, c.spec_W)
+    lbz, ubz, _, _ = _run(_engine(c.wl, "zono"), c.l0, c.u0, c.spec_W)
+    lbd, ubd, _, _ = _run(_engine(c.wl, "deeppoly"), c.l0, c.u0, c.spec_W)
+    tol = 1e-5 * np.abs(lbp).max()
+    assert (lbp >= np.maximum(lbz, lbd) - tol).all() and (ubp <= np.minimum(ubz, ubd) + tol).all()
+    assert (lbp > np.maximum(lbz, lbd) + tol).any()     # the meet inside the network tightens further
 
 
 def test_gpu_forward_chunks_match_one_pass():

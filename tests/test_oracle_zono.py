@@ -1,6 +1,7 @@
-"""The zonotope (zono.cf, zono2.cf) and interval (ibp.cf) oracle against the reference's
-own outputs (tests/golden/zono_*.npz, zono2_*.npz, ibp_*.npz), a planted mistake, and
-soundness: concrete points of the input box stay inside every affine layer's bounds.
+"""The zonotope (zono.cf, zono2.cf), interval (ibp.cf) and polyzono.cf oracles against the
+reference's own outputs (tests/golden/zono_*.npz, zono2_*.npz, ibp_*.npz, pz_*.npz), planted
+mistakes, and soundness: concrete points of the input box stay inside every affine layer's
+bounds.
 Tolerances: tests/parity.py.
 """
 import numpy as np
@@ -14,12 +15,16 @@ from cfgpu import nets
 
 ZONO_CASES = names("zono", max_wid=9) + names("zono2", max_wid=9)
 IBP_CASES = names("ibp", max_wid=9)
+PZ_CASES = names("polyzono", max_wid=9)
 
 
 def _run(c, program=None, relu=None):
     program = program or c.program
     if program == "ibp":
         bounds, lb, ub = Z.ibp(c.wl.layers, c.l0, c.u0, c.spec_W)
+        br = None
+    elif program == "polyzono":
+        bounds, lb, ub = Z.polyzono(c.wl.layers, c.l0, c.u0, c.spec_W)
         br = None
     else:
         saved = Z.zono_relu
@@ -36,9 +41,10 @@ def _run(c, program=None, relu=None):
 def test_cases_present():
     assert len(names("zono", max_wid=9)) >= 7 and len(names("zono2", max_wid=9)) >= 2 and len(IBP_CASES) >= 4
     assert {Case(n).wid for n in ZONO_CASES + IBP_CASES} >= {0, 1, 2, 3, 5}
+    assert len(PZ_CASES) >= 4 and {Case(n).wid for n in PZ_CASES} >= {0, 1, 2}
 
 
-@pytest.mark.parametrize("name", ZONO_CASES + IBP_CASES)
+@pytest.mark.parametrize("name", ZONO_CASES + IBP_CASES + PZ_CASES)
 def test_oracle_matches_reference(name):
     c = Case(name)
     xl, xu, lb, ub, br = _run(c)
@@ -60,6 +66,39 @@ def test_planted_missing_symbol_fails():
         return Mn, cn
     c = Case("zono_w2_b4_e2e-3")
     xl, xu, _, _, _ = _run(c, relu=no_symbol)
+    worst, _ = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst > 10.0
+
+
+def test_polyzono_meets_both_certifiers():
+    """polyzono's bounds are the tightest of its two halves: at the first affine layer (the
+    same input box for both) they are exactly max / min of DeepPoly's and the zonotope's,
+    and the property bounds are at least as tight as either program's alone."""
+    from oracle import crown_oracle as C
+    c = Case("pz_w2_b4_e2e-3")
+    bp, lbp, ubp = Z.polyzono(c.wl.layers, c.l0, c.u0, c.spec_W)
+    bz, lbz, _, _ = Z.zono(c.wl.layers, c.l0, c.u0, c.spec_W, "zono")
+    bd, lbd, _, _ = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, "deeppoly")
+    np.testing.assert_array_equal(bp[0][0], np.maximum(bz[0][0], bd[0][0]))
+    np.testing.assert_array_equal(bp[0][1], np.minimum(bz[0][1], bd[0][1]))
+    assert (lbp >= np.maximum(lbz, lbd) - 1e-5 * np.abs(lbp).max()).all()
+
+
+def test_planted_unmet_bounds_fail():
+    """A mistake planted in the oracle (the zonotope ReLU relaxed with a lower bound 5% of
+    the interval below the met one) breaks a polyzono case where the zonotope is the
+    tighter half (the larger box)."""
+    c = Case("pz_w0_b4_e1e-2")
+    saved = Z.zono_relu
+
+    def looser(l, u, M, c_):
+        return saved(l - np.float32(0.05) * (u - l), u, M, c_)
+    Z.zono_relu = looser
+    try:
+        bounds, _, _ = Z.polyzono(c.wl.layers, c.l0, c.u0, c.spec_W)
+    finally:
+        Z.zono_relu = saved
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
     worst, _ = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
     assert worst > 10.0
 
