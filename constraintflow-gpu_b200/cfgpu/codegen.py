@@ -14,6 +14,8 @@ own definitions, which fused kernel family implements each transformer operation
           zonotope          map(Ez, g_low), map(Ez, g_up), Ez with Ez = prev[Z] . weight +
                             bias and g_low(c) = -|c|, g_up(c) = |c|
           interval          map(E, G_low), map(E, G_up) without a traversal
+          backsubstitution  max(zonotope low, backsubstitution low), min(... up), E, E, Ez
+          + zonotope        over the shape (l, u, L, U, Z) (polyzono.cf), either order
   Relu    DeepPoly          (relu(l), relu(u), 1[l+u>=0] x, l>=0 ? x : u<=0 ? 0 :
                             lam (x - l)), lam = u/(u-l), x the neuron (prev, prev[L] and
                             prev[U] all denote the affine input of the ReLU)
@@ -21,6 +23,8 @@ own definitions, which fused kernel family implements each transformer operation
                             tuple (whole-layer branches, crown.cf:25)
           zonotope          (0, 0, l>=0 ? Z : u<=0 ? 0 : lam Z + (u l / (2 (u-l))) (eps-1))
           interval          (relu(l), relu(u))
+          DeepPoly          DeepPoly's four members followed by the zonotope's Z member
+          + zonotope        over the shape (l, u, L, U, Z)
 
 Each candidate is checked on sample bounds (l, u) with exact arithmetic on affine forms
 over the symbols x, L, U, Z, eps; a program whose operations match no family is refused
@@ -439,21 +443,41 @@ def _abs_map(prog, fname, sign):
     return True
 
 
+def _zono_bound(prog, n, lower):
+    """n is map(prev[Z] . weight + bias, g) with g(c) = -|c| (lower) or |c| (upper)."""
+    m = _inline_call(prog, n)
+    return (_kind(m) == "MapNode" and _affine_expr_ok(prog, m.expr, "Z")
+            and _abs_map(prog, _name(m.func), -1.0 if lower else 1.0))
+
+
+def _met_bound(prog, n, lower):
+    """n is max (lower) / min (upper) of the zonotope bound and the backsubstitution bound."""
+    n = _inline_call(prog, n)
+    if _kind(n) != "MaxOpNode" or getattr(n, "op", None) != ("max" if lower else "min"):
+        return False
+    a, b = n.expr1, n.expr2
+    return any(_zono_bound(prog, x, lower) and _check_backsub_member(prog, y, lower) for x, y in ((a, b), (b, a)))
+
+
 def _classify_affine(prog, ret):
     exprs = _ret_tuple(ret)
     if exprs is None or len(exprs) != len(prog.shape):
         return None
     names = [m for _, m in prog.shape]
+    if names == ["l", "u", "L", "U", "Z"]:
+        if (_met_bound(prog, exprs[0], True) and _met_bound(prog, exprs[1], False)
+                and _affine_expr_ok(prog, exprs[2], "") and _affine_expr_ok(prog, exprs[3], "")
+                and _affine_expr_ok(prog, exprs[4], "Z")):
+            return "backsub+zonotope"
+        return None
     if names == ["l", "u", "L", "U"]:
         if (_check_backsub_member(prog, exprs[0], True) and _check_backsub_member(prog, exprs[1], False)
                 and _affine_expr_ok(prog, exprs[2], "") and _affine_expr_ok(prog, exprs[3], "")):
             return "backsub"
         return None
     if names == ["l", "u", "Z"]:
-        m0, m1 = _inline_call(prog, exprs[0]), _inline_call(prog, exprs[1])
-        if (_kind(m0) == "MapNode" and _kind(m1) == "MapNode" and _affine_expr_ok(prog, m0.expr, "Z")
-                and _affine_expr_ok(prog, m1.expr, "Z") and _affine_expr_ok(prog, exprs[2], "Z")
-                and _abs_map(prog, _name(m0.func), -1.0) and _abs_map(prog, _name(m1.func), 1.0)):
+        if (_zono_bound(prog, exprs[0], True) and _zono_bound(prog, exprs[1], False)
+                and _affine_expr_ok(prog, exprs[2], "Z")):
             return "zonotope"
         return None
     if names == ["l", "u"]:
@@ -474,6 +498,9 @@ def _classify_relu(prog, ret):
             return "deeppoly" if _check_relu_basic(prog, ret, _deeppoly_relu, merge=True) else None
         if names == ["l", "u", "Z"]:
             return "zonotope" if _check_relu_basic(prog, ret, _zono_relu, merge=False) else None
+        if names == ["l", "u", "L", "U", "Z"]:
+            both = _check_relu_basic(prog, ret, lambda l, u: _deeppoly_relu(l, u) + _zono_relu(l, u)[2:], merge=True)
+            return "deeppoly+zonotope" if both else None
         if names == ["l", "u"]:
             return "interval" if _check_relu_basic(prog, ret, _ibp_relu, merge=False) else None
     except (CodegenError, ZeroDivisionError):
@@ -483,7 +510,8 @@ def _classify_relu(prog, ret):
 
 # certifier = (Affine family, Relu family)
 _CERTIFIERS = {("backsub", "deeppoly"): "deeppoly", ("backsub", "crown"): "crown",
-               ("zonotope", "zonotope"): "zono", ("interval", "interval"): "ibp"}
+               ("zonotope", "zonotope"): "zono", ("interval", "interval"): "ibp",
+               ("backsub+zonotope", "deeppoly+zonotope"): "polyzono"}
 
 
 class Analysis:
@@ -527,6 +555,8 @@ _DOC = {"backsub": "backsubstitution of the layer's coefficient rows down to the
         "zonotope": "zonotope step: symbol coefficients times the weights, concretised",
         "interval": "interval step: sign-split weights against the previous bounds",
         "deeppoly": "DeepPoly triangle relaxation", "crown": "CROWN whole-layer branches",
+        "backsub+zonotope": "backsubstitution and zonotope step, bounds met (max / min)",
+        "deeppoly+zonotope": "DeepPoly and zonotope relaxations from the met bounds",
         None: "no fused kernel"}
 
 

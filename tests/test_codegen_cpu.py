@@ -17,8 +17,9 @@ GOLDEN = os.path.join(HERE, "golden")
 sys.path.insert(0, GOLDEN)
 import ast_json  # noqa: E402
 
-RUNS = {"deeppoly": "deeppoly", "deeppoly_efficient": "deeppoly", "crown": "crown", "zono": "zono", "ibp": "ibp"}
-REFUSED = ("deeppoly_priority", "deeppolyh", "zono2", "ibp2", "polyzono")
+RUNS = {"deeppoly": "deeppoly", "deeppoly_efficient": "deeppoly", "crown": "crown", "zono": "zono", "ibp": "ibp",
+        "polyzono": "polyzono"}
+REFUSED = ("deeppoly_priority", "deeppolyh", "zono2", "ibp2")
 
 
 def _ast(prog):
@@ -30,7 +31,7 @@ def _ast(prog):
 def test_backend_recognises_program(prog):
     a = codegen.analyse(_ast(prog))
     assert a.certifier == RUNS[prog]
-    assert a.ops["Affine"] in ("backsub", "zonotope", "interval") and a.ops["Relu"] is not None
+    assert a.ops["Affine"] in ("backsub", "zonotope", "interval", "backsub+zonotope") and a.ops["Relu"] is not None
 
 
 @pytest.mark.parametrize("prog", sorted(RUNS))
@@ -92,3 +93,39 @@ def test_emitted_transformer_declares_its_family(prog):
     a = codegen.analyse(_ast(prog))
     obj = getattr(mod, a.name)()
     assert obj.cf_layerwise and certifier_of(obj) == RUNS[prog]
+
+
+def _nodes(n, kind, out=None):
+    """Every node of class `kind` under n (depth first)."""
+    out = [] if out is None else out
+    if type(n).__name__ == kind:
+        out.append(n)
+    if isinstance(n, (list, tuple)):
+        for x in n:
+            _nodes(x, kind, out)
+    elif hasattr(n, "__dict__"):
+        for k, v in vars(n).items():
+            if k not in ("left", "right") or not hasattr(n, "texpr"):
+                _nodes(v, kind, out)
+    return out
+
+
+@pytest.mark.parametrize("mistake", ["meet_direction", "zono_sign", "zono_relu_scale"])
+def test_planted_polyzono_mistakes_are_refused(mistake):
+    """Mistakes planted in polyzono.cf's AST make the backend refuse it: the lower bound
+    met with min instead of max; the zonotope's lower concretisation with +|c|; the
+    fresh-symbol coefficient of the zonotope ReLU halved once more."""
+    ast = copy.deepcopy(_ast("polyzono"))
+    f = _funcs(ast)
+    if mistake == "meet_direction":
+        meets = [m for m in _nodes(ast.stmt, "MaxOpNode") if m.op == "max"]
+        assert meets
+        meets[0].op = "min"
+    elif mistake == "zono_sign":           # deepz_lower(c) = c > 0 ? c * 1 : c * 1
+        f["deepz_lower"].expr.texpr = f["deepz_lower"].expr.fexpr
+    elif mistake == "zono_relu_scale":     # x(l, u, z): (u l (eps - 1)) / (4 (u - l))
+        f["x"].expr.right.right.left.value = 4
+    assert codegen.analyse(copy.deepcopy(_ast("polyzono"))).certifier == "polyzono"
+    with pytest.raises(codegen.CodegenError) as e:
+        codegen.analyse(ast)
+    assert ("Relu (unrecognised)" if mistake == "zono_relu_scale" else "Affine (unrecognised)") in str(e.value)
