@@ -9,7 +9,10 @@ backsubstitution down to the input, final bounds) over one batch of regions of t
 workload (default: ReLU MLP 784-(200x9)-10, 256 regions per GPU, eps 0.002; seeded
 synthetic network and centres, since no dataset or trained model is available offline).
 --certifier runs another of the reference's programs on the same workload (a zono / ibp
-step is one forward pass).
+step is one forward pass; polyzono.cf runs a DeepPoly and a zonotope pass layer by layer).
+`roofline` covers the dominant (tensor-core) kernels; `memory_bound` the HBM-bound kernels
+of the pass (relaxations, concretisation, conversions): their algorithmic bytes, device
+time and GB/s against the measured HBM copy bandwidth.
 Multi-GPU: one process per GPU (torchrun), each certifying its own 256 regions (weak
 scaling; regions are independent, no collective on the data path).  Rank 0 prints one
 JSON line.
@@ -383,6 +386,18 @@ def run_cfgpu(args, rank, world, local):
                      "peak_source": peak_src,
                      "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
                      "step_launches": prof["step_launches"]},
+        "memory_bound": {
+            "kernels": {"zono": "k_zono_bounds, k_zono_relu", "polyzono": "k_relu_relax, k_zono_bounds, "
+                        "k_zono_relu, k_to_f64, k_prep_wimg", "ibp": None}.get(
+                            args.certifier, "k_relu_relax / k_crown_relax, k_concretize, k_to_f64, k_prep_wimg"),
+            "launches": int(prof["mem_launches"]),
+            "bytes_per_pass": prof["mem_bytes"] / args.steps,
+            "ms_per_pass": prof["mem_ms"] / args.steps,
+            "achieved": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 if prof["mem_ms"] > 0 else None,
+            "peak": hbm, "unit": "GB/s",
+            "frac": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 / hbm if prof["mem_ms"] > 0 else None,
+            "peak_source": f"{src} MEASURED_PEAKS hbm_gbs",
+            "share_of_pass": prof["mem_ms"] / ms if ms > 0 else None},
         "clocks": clocks,
         "wall_s_timed": wall,
     }

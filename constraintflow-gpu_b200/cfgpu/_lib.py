@@ -42,7 +42,8 @@ class CfLayer(ctypes.Structure):
 
 class CfProfileStats(ctypes.Structure):
     _fields_ = [("kernel_launches", _i64), ("step_launches", _i64), ("step_ms", ctypes.c_double),
-                ("step_flops", ctypes.c_double), ("step_bytes", ctypes.c_double)]
+                ("step_flops", ctypes.c_double), ("step_bytes", ctypes.c_double),
+                ("mem_launches", _i64), ("mem_ms", ctypes.c_double), ("mem_bytes", ctypes.c_double)]
 
 
 class CfNetwork(ctypes.Structure):

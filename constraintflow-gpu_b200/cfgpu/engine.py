@@ -265,4 +265,5 @@ def profile_collect():
     st = _lib.CfProfileStats()
     check(lib.cf_profile_collect(ctypes.byref(st)), "cf_profile_collect")
     return dict(kernel_launches=st.kernel_launches, step_launches=st.step_launches, step_ms=st.step_ms,
-                step_flops=st.step_flops, step_bytes=st.step_bytes)
+                step_flops=st.step_flops, step_bytes=st.step_bytes, mem_launches=st.mem_launches,
+                mem_ms=st.mem_ms, mem_bytes=st.mem_bytes)

@@ -85,7 +85,9 @@ cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStr
   int64_t total = (int64_t)n_tiles * kchunks * tile_n * 32;
   int64_t blocks = ceil_div(total, 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
+  prof_mem_begin(st);
   k_prep_wimg<<<(unsigned)blocks, 256, 0, st>>>(W, K, N, tile_n, n_tiles, kchunks, img);
+  prof_mem_end(st, 4.0 * K * N + (double)chain_wimg_bytes(K, N));   // W in, the hi / lo image out
   return check_launch("k_prep_wimg");
 }
 

@@ -31,6 +31,9 @@ void prof_count_launch();
 bool prof_enabled();
 void prof_step_begin(cudaStream_t st);
 void prof_step_end(cudaStream_t st, double flops, double bytes);
+// the same around a launch of a memory-bound kernel (relaxation, concretisation, conversions)
+void prof_mem_begin(cudaStream_t st);
+void prof_mem_end(cudaStream_t st, double bytes);
 
 inline cf_status check_launch(const char* what) {
   prof_count_launch();

@@ -44,7 +44,9 @@ cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u
   int threads = 256;
   int64_t blocks = ceil_div(total, threads);
   if (blocks > 148 * 16) blocks = 148 * 16;
+  prof_mem_begin(st);
   k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu);
+  prof_mem_end(st, 28.0 * total);   // l, u in; l', u', alpha, lambda, mu out
   return check_launch("k_relu_relax");
 }
 
@@ -218,16 +220,24 @@ cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, in
   int64_t rows = 2 * B * R;
   if (rows == 0) return CF_OK;
   const int64_t gx = ceil_div(R, kCbT), gy = ceil_div(B, kCbT);
-  if (a_ss == 0 && a_bs == 0 && c_ss == 0 && c_bs == 0 && gx <= 0x7fffffff && gy <= 65535) {
+  // coefficient rows (once if shared by every region), the input box, the constants, the bounds
+  const bool bcast = a_ss == 0 && a_bs == 0 && c_ss == 0 && c_bs == 0;
+  const double bytes = 4.0 * ((bcast ? (double)R : (double)rows) * n0 + 2.0 * B * n0 + (c ? (bcast ? R : rows) : 0) +
+                              2.0 * B * R);
+  if (bcast && gx <= 0x7fffffff && gy <= 65535) {
+    prof_mem_begin(st);
     k_concretize_bcast<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(B, R, n0, A, a_rs, c, l0, u0, out_l, out_u,
                                                                          ld_out);
+    prof_mem_end(st, bytes);
     return check_launch("k_concretize_bcast");
   }
   int threads = 256;
   int64_t blocks = ceil_div(rows * 32, threads);
   if (blocks > 148 * 32) blocks = 148 * 32;
+  prof_mem_begin(st);
   k_concretize<<<(unsigned)blocks, threads, 0, st>>>(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, out_l,
                                                       out_u, ld_out);
+  prof_mem_end(st, bytes);
   return check_launch("k_concretize");
 }
 

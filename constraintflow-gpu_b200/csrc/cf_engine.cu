@@ -59,7 +59,9 @@ cf_status launch_to_f64(int64_t B, int64_t n, const float* src, int64_t ld_src, 
   if (B * n == 0) return CF_OK;
   int64_t blocks = ceil_div(B * n, 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
+  prof_mem_begin(st);
   k_to_f64<<<(unsigned)blocks, 256, 0, st>>>(B, n, src, ld_src, dst);
+  prof_mem_end(st, 12.0 * B * n);
   return check_launch("k_to_f64");
 }
 

@@ -42,6 +42,7 @@ __global__ void k_spec_matrix(int64_t B, int32_t nc, const int64_t* __restrict__
 struct ProfRec {
   cudaEvent_t a, b;
   double flops, bytes;
+  bool mem;
 };
 struct ProfState {
   bool on = false;
@@ -66,15 +67,19 @@ void prof_count_launch() {
   if (g_prof.on) ++g_prof.launches;
 }
 bool prof_enabled() { return g_prof.on; }
-void prof_step_begin(cudaStream_t st) {
+static void prof_begin(cudaStream_t st, bool mem) {
   if (!g_prof.on) return;
   ProfRec r;
   r.a = take_event();
   r.b = take_event();
   r.flops = r.bytes = 0;
+  r.mem = mem;
   cudaEventRecord(r.a, st);
   g_prof.open.push_back(r);
 }
+void prof_step_begin(cudaStream_t st) { prof_begin(st, false); }
+void prof_mem_begin(cudaStream_t st) { prof_begin(st, true); }
+void prof_mem_end(cudaStream_t st, double bytes) { prof_step_end(st, 0.0, bytes); }
 void prof_step_end(cudaStream_t st, double flops, double bytes) {
   if (!g_prof.on || g_prof.open.empty()) return;
   ProfRec& r = g_prof.open.back();
@@ -139,10 +144,16 @@ extern "C" cf_status cf_profile_collect(cf_profile_stats* out) {
       set_error("profile_collect: %s", cudaGetErrorString(e));
       status = CF_ERR_CUDA;
     }
-    out->step_launches += 1;
-    out->step_ms += ms;
-    out->step_flops += r.flops;
-    out->step_bytes += r.bytes;
+    if (r.mem) {
+      out->mem_launches += 1;
+      out->mem_ms += ms;
+      out->mem_bytes += r.bytes;
+    } else {
+      out->step_launches += 1;
+      out->step_ms += ms;
+      out->step_flops += r.flops;
+      out->step_bytes += r.bytes;
+    }
     g_prof.pool.push_back(r.a);
     g_prof.pool.push_back(r.b);
   }

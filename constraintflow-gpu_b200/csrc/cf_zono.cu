@@ -768,8 +768,12 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
       CF_TRY(check_launch("k_zono_const"));
       cc ^= 1;
     }
+    // tile column sums in, the constant in, l / u out (and the float64 property bounds)
+    const double zb_in = S.gpos ? 8.0 * Bc * S.tiles * N : S.cpos ? 8.0 * 8.0 * ceil_div(Bc * S.E, 128) * N : 0.0;
+    prof_mem_begin(st);
     k_zono_bounds<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, S, C[cc], sl + col, su + col, Ntot,
                                                                    spec ? lb : nullptr, spec ? ub : nullptr);
+    prof_mem_end(st, zb_in + (S.dpos ? 8.0 * Bc * N : 0.0) + 4.0 * Bc * N + (spec ? 24.0 : 8.0) * Bc * N);
     CF_TRY(check_launch("k_zono_bounds"));
     if (spec) break;
     cur ^= 1;
@@ -777,9 +781,11 @@ static cf_status zono_layers(const cf_network* net, const Plan& p, int64_t Bc, c
     diag = false;
     if (li_relu >= 0 && li_relu < li_end) {
       const int64_t rcol = p.col[li_relu];
+      prof_mem_begin(st);
       k_zono_relu<<<(unsigned)ceil_div(Bc * N, 256), 256, 0, st>>>(Bc, N, sl + col, su + col, Ntot, C[cc], lam, nu,
                                                                    C[cc ^ 1],
                                                                    sl + rcol, su + rcol, Ntot);
+      prof_mem_end(st, 32.0 * Bc * N);   // l, u, c in; lambda, nu, c', l', u' out
       CF_TRY(check_launch("k_zono_relu"));
       cc ^= 1;
       lam_in = lam;

@@ -158,15 +158,20 @@ cf_status cf_spec_matrix(int64_t B, int32_t n_classes, const int64_t* labels_dev
                          void* stream);
 
 /* Profiling: while enabled (per host thread), cf_deeppoly_run records CUDA events around
- * every backsubstitution-step launch on the caller's stream and counts every kernel it
- * launches; cf_profile_collect waits for those events and returns the totals since the
- * last collect. */
+ * every backsubstitution-step launch and every launch of a memory-bound kernel (ReLU
+ * relaxation, concretisation, float64 conversion, weight-image preparation, zonotope
+ * concretisation and ReLU) on the caller's stream and counts every kernel it launches;
+ * cf_profile_collect waits for those events and returns the totals since the last
+ * collect. */
 typedef struct cf_profile_stats {
   int64_t kernel_launches;   /* all kernels launched by cf_deeppoly_run */
   int64_t step_launches;     /* backsubstitution steps (the dominant kernel) */
   double step_ms;            /* summed device time of the steps */
   double step_flops;         /* algorithmic FLOPs of those steps: 2*rows*K*N each */
   double step_bytes;         /* algorithmic bytes: A in + A out + W + relaxation vectors */
+  int64_t mem_launches;      /* memory-bound kernel launches */
+  double mem_ms;             /* their summed device time */
+  double mem_bytes;          /* their algorithmic bytes (each input and output once) */
 } cf_profile_stats;
 cf_status cf_profile_enable(int32_t on);
 cf_status cf_profile_collect(cf_profile_stats* out);
