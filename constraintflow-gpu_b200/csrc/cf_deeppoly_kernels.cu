@@ -151,9 +151,10 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
 // each region's box) are two sign-split GEMMs [B, n0] x [n0, R]:
 //   out_l[b,i] = c[i] + sum_n W+[i,n] l0[b,n] + W-[i,n] u0[b,n]
 //   out_u[b,i] = c[i] + sum_n W+[i,n] u0[b,n] + W-[i,n] l0[b,n]
-// CTA tile: 64 rows x 64 regions, 32-wide k slices of W (split into W+ / W-) and of both
-// boxes in shared memory; 16x16 threads, 4 rows x 4 regions x 2 bounds each.
-constexpr int kCbT = 64, kCbK = 32;
+// CTA tile: 32 rows x 32 regions (a 200-row layer and 256 regions give 56 CTAs), 32-wide
+// k slices of W (split into W+ / W-) and of both boxes in shared memory; 16x16 threads,
+// 2 rows x 2 regions x 2 bounds each.
+constexpr int kCbT = 32, kCbK = 32, kCbM = kCbT / 16;
 __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
                                                           int64_t a_rs, const float* __restrict__ c,
                                                           const float* __restrict__ l0, const float* __restrict__ u0,
@@ -165,11 +166,11 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
   __shared__ __align__(16) float Us[kCbK][kCbT + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t i0 = (int64_t)blockIdx.x * kCbT, b0 = (int64_t)blockIdx.y * kCbT;
-  float lo[4][4], up[4][4];
+  float lo[kCbM][kCbM], up[kCbM][kCbM];
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < kCbM; ++a)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) lo[a][q] = up[a][q] = 0.0f;
+    for (int q = 0; q < kCbM; ++q) lo[a][q] = up[a][q] = 0.0f;
   for (int64_t k0 = 0; k0 < n0; k0 += kCbK) {
     for (int e = tid; e < kCbT * kCbK; e += 256) {
       const int r = e / kCbK, kk = e - r * kCbK;
@@ -183,16 +184,18 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
     __syncthreads();
 #pragma unroll 8
     for (int kk = 0; kk < kCbK; ++kk) {
-      const float4 wp = *reinterpret_cast<const float4*>(&Wp[kk][ty * 4]);
-      const float4 wn = *reinterpret_cast<const float4*>(&Wn[kk][ty * 4]);
-      const float4 lv = *reinterpret_cast<const float4*>(&Ls[kk][tx * 4]);
-      const float4 uv = *reinterpret_cast<const float4*>(&Us[kk][tx * 4]);
-      const float wpa[4] = {wp.x, wp.y, wp.z, wp.w}, wna[4] = {wn.x, wn.y, wn.z, wn.w};
-      const float la[4] = {lv.x, lv.y, lv.z, lv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+      float wpa[kCbM], wna[kCbM], la[kCbM], ua[kCbM];
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int a = 0; a < kCbM; ++a) {
+        wpa[a] = Wp[kk][ty * kCbM + a];
+        wna[a] = Wn[kk][ty * kCbM + a];
+        la[a] = Ls[kk][tx * kCbM + a];
+        ua[a] = Us[kk][tx * kCbM + a];
+      }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+      for (int a = 0; a < kCbM; ++a)
+#pragma unroll
+        for (int q = 0; q < kCbM; ++q) {
           lo[a][q] = fmaf(wpa[a], la[q], fmaf(wna[a], ua[q], lo[a][q]));
           up[a][q] = fmaf(wpa[a], ua[q], fmaf(wna[a], la[q], up[a][q]));
         }
@@ -200,13 +203,13 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
     __syncthreads();
   }
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    const int64_t i = i0 + ty * 4 + a;
+  for (int a = 0; a < kCbM; ++a) {
+    const int64_t i = i0 + ty * kCbM + a;
     if (i >= R) continue;
     const float cv = c ? c[i] : 0.0f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int64_t b = b0 + tx * 4 + q;
+    for (int q = 0; q < kCbM; ++q) {
+      const int64_t b = b0 + tx * kCbM + q;
       if (b >= B) continue;
       out_l[b * ld_out + i] = lo[a][q] + cv;
       out_u[b * ld_out + i] = up[a][q] + cv;
