@@ -2,7 +2,7 @@
 """Benchmark: certified input regions/sec (DeepPoly, whole input box) on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cfgpu|reference] [--workload 2]
-                    [--certifier deeppoly|crown|zono|ibp|polyzono] [--batch B]
+                    [--certifier deeppoly|crown|zono|ibp|polyzono|crownibp] [--batch B]
 
 One step = one whole DeepPoly pass (input box, property matrix, every layer's
 backsubstitution down to the input, final bounds) over one batch of regions of the
@@ -51,8 +51,9 @@ def parse():
     ap.add_argument("--impl", default="cfgpu", choices=["cfgpu", "reference"])
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
-    ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp", "polyzono"],
-                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf)")
+    ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp", "polyzono",
+                                                                  "crownibp"],
+                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf, crownibp.cf)")
     return ap.parse_args()
 
 
@@ -168,7 +169,7 @@ CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
 
 
 METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)",
-          "polyzono": "polyzono (DeepPoly met with the zonotope)"}
+          "polyzono": "polyzono (DeepPoly met with the zonotope)", "crownibp": "CROWN-IBP (crownibp.cf)"}
 
 
 def _metric(certifier):
@@ -188,6 +189,9 @@ def _oracle_fn(wl, certifier="deeppoly"):
     if certifier == "crown":
         from oracle import crown_oracle as C
         return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "crown")
+    if certifier == "crownibp":
+        from oracle import crown_oracle as C
+        return lambda l0, u0, W: C.crownibp(wl.layers, l0, u0, W)
     if nets.is_chain(wl.layers):
         from oracle import deeppoly_oracle as O
         return lambda l0, u0, W: O.deeppoly(wl.layers, l0, u0, W)

@@ -29,8 +29,9 @@ class DeepPolyEngine:
     ReLU branch is decided over the whole batch: a CROWN run always takes the batch in
     one workspace chunk and checks the device status; when a layer takes the all-crossing
     branch the bounds are recomputed by the general traversal of cfgpu.general), 'zono'
-    (zono.cf, DeepZ: forward zonotope pass, linear chains) or 'ibp' (ibp.cf: interval
-    bounds).
+    (zono.cf, DeepZ: forward zonotope pass, linear chains), 'ibp' (ibp.cf: interval
+    bounds) or 'crownibp' (crownibp.cf: interval bounds below the property, DeepPoly's
+    ReLU relaxation from them, one backsubstitution of the property rows; chains).
     """
 
     def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
@@ -40,9 +41,10 @@ class DeepPolyEngine:
         self.input_size = int(input_size)
         self.n_spec = int(n_spec)
         relax = {"deeppoly": _lib.CF_RELAX_DEEPPOLY, "crown": _lib.CF_RELAX_CROWN, "zono": _lib.CF_RELAX_ZONO,
-                 "ibp": _lib.CF_RELAX_IBP}
+                 "ibp": _lib.CF_RELAX_IBP, "crownibp": _lib.CF_RELAX_CROWNIBP}
         if certifier not in relax:
-            raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly, crown, zono and ibp)")
+            raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly, crown, zono, ibp and "
+                                      "crownibp)")
         self.certifier = certifier
         self._keep = []
         self._general = []        # (kind, W, b, parents) device tensors for cfgpu.general

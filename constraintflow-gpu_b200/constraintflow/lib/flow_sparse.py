@@ -24,8 +24,11 @@ Two forward programs are recognised by their own Affine / Relu:
 polyzono.cf carries both states: its Affine is DeepPoly's traversal met (cf_max / cf_min)
 with the zonotope's concretisation, its Relu both relaxations (convert_to_poly and
 get_new_eps); it runs as cfgpu.polyzono's coupled DeepPoly and zonotope passes.
+crownibp.cf branches its Affine on the last_layer metadata: interval bounds below the
+property (map(simplify_lower) over the previous layer's l / u), the traversal for the
+property rows; its Relu is DeepPoly's.
 A transformer object may also declare itself with a ``cf_certifier`` attribute
-('deeppoly', 'crown', 'zono', 'ibp' or 'polyzono').  Other programs (zono2.cf's whole-layer branches
+('deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp').  Other programs (zono2.cf's whole-layer branches
 among them) raise NotImplementedError.
 """
 import inspect
@@ -49,14 +52,18 @@ _ZONO_RELU = ("get_new_eps(", "get_elem('Z', prev", "operator.truediv", "operato
 # ibp.cf: interval arithmetic over the previous layer's l / u
 _IBP_AFFINE = ("inner_prod(", "clamp(", "get_elem('l'", "get_elem('u'")
 _IBP_RELU = ("convert_to_float(", "operator.ge", "get_elem('l', prev", "get_elem('u', prev")
+# crownibp.cf: interval bounds below the property (a branch on the last_layer metadata), the
+# traversal only for the property rows; DeepPoly's Relu
+_CROWNIBP_AFFINE = ("get_metadata('last_layer'", "if(", "clamp(", "inner_prod(", "get_max_priority(",
+                    "get_metadata('layer'", "get_elem('l'", "get_elem('u'")
 # polyzono.cf: DeepPoly's traversal met with the zonotope bound; both relaxations in the Relu
 _POLYZONO_AFFINE = _AFFINE + ("get_elem('Z', prev", "cf_max(", "cf_min(")
 _POLYZONO_RELU = ("convert_to_poly(", "get_new_eps(", "get_elem('Z', prev", "operator.truediv", "where(")
 
 
 def certifier_of(transformer):
-    """'deeppoly', 'crown', 'zono', 'ibp' or 'polyzono' for a recognised generated transformer,
-    else raises."""
+    """'deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp' for a recognised generated
+    transformer, else raises."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
@@ -70,6 +77,9 @@ def certifier_of(transformer):
         if "if(" in relu or "any(" in relu:
             raise NotImplementedError("a polyzono-style program with whole-layer branches")
         return "polyzono"
+    if all(k in affine for k in _CROWNIBP_AFFINE) and "if(" not in relu and "any(" not in relu and (
+            all(k in relu for k in _DEEPPOLY_RELU)):
+        return "crownibp"
     if all(k in affine for k in _AFFINE):
         branches = "if(" in relu or "any(" in relu or "operator.gt" in relu
         if not branches and (all(k in relu for k in _DEEPPOLY_RELU) or all(k in relu for k in _EFFICIENT_RELU)):
@@ -82,8 +92,8 @@ def certifier_of(transformer):
     if (all(k in affine for k in _IBP_AFFINE) and all(k in relu for k in _IBP_RELU) and "get_max_priority(" not in affine
             and "get_new_eps(" not in relu and "convert_to_poly(" not in relu and not branches):
         return "ibp"
-    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf), interval (ibp.cf) "
-                              "and polyzono.cf certifier programs; the given "
+    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf), interval (ibp.cf), "
+                              "polyzono.cf and crownibp.cf certifier programs; the given "
                               f"transformer ({cls.__name__}) is a different program")
 
 

@@ -120,8 +120,8 @@ cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* 
 // One warp per row; lanes stride the n0 columns (coalesced), shuffle reduction.
 __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A, int64_t a_ss,
                              int64_t a_bs, int64_t a_rs, const float* __restrict__ c, int64_t c_ss, int64_t c_bs,
-                             const float* __restrict__ l0, const float* __restrict__ u0, float* __restrict__ out_l,
-                             float* __restrict__ out_u, int64_t ld_out) {
+                             const float* __restrict__ l0, const float* __restrict__ u0, int64_t ld_box,
+                             float* __restrict__ out_l, float* __restrict__ out_u, int64_t ld_out) {
   int lane = threadIdx.x & 31;
   int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -129,8 +129,8 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
   for (int64_t r = warp; r < rows; r += nwarps) {
     int64_t s = r / (B * R), rem = r - s * B * R, b = rem / R, i = rem - b * R;
     const float* a = A + s * a_ss + b * a_bs + i * a_rs;
-    const float* pos_box = (s == 0 ? l0 : u0) + b * n0;
-    const float* neg_box = (s == 0 ? u0 : l0) + b * n0;
+    const float* pos_box = (s == 0 ? l0 : u0) + b * ld_box;
+    const float* neg_box = (s == 0 ? u0 : l0) + b * ld_box;
     float acc = 0.0f;
     for (int64_t k = lane; k < n0; k += 32) {
       float v = a[k];
@@ -158,8 +158,8 @@ constexpr int kCbT = 32, kCbK = 32, kCbM = kCbT / 16;
 __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
                                                           int64_t a_rs, const float* __restrict__ c,
                                                           const float* __restrict__ l0, const float* __restrict__ u0,
-                                                          float* __restrict__ out_l, float* __restrict__ out_u,
-                                                          int64_t ld_out) {
+                                                          int64_t ld_box, float* __restrict__ out_l,
+                                                          float* __restrict__ out_u, int64_t ld_out) {
   __shared__ __align__(16) float Wp[kCbK][kCbT + 4];
   __shared__ __align__(16) float Wn[kCbK][kCbT + 4];
   __shared__ __align__(16) float Ls[kCbK][kCbT + 4];
@@ -178,8 +178,8 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
       const float w = (i < R && k < n0) ? A[i * a_rs + k] : 0.0f;
       Wp[kk][r] = fmaxf(w, 0.0f);
       Wn[kk][r] = fminf(w, 0.0f);
-      Ls[kk][r] = (b < B && k < n0) ? l0[b * n0 + k] : 0.0f;
-      Us[kk][r] = (b < B && k < n0) ? u0[b * n0 + k] : 0.0f;
+      Ls[kk][r] = (b < B && k < n0) ? l0[b * ld_box + k] : 0.0f;
+      Us[kk][r] = (b < B && k < n0) ? u0[b * ld_box + k] : 0.0f;
     }
     __syncthreads();
 #pragma unroll 8
@@ -220,6 +220,13 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
 cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
                             const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
+  return launch_concretize_box(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, n0, out_l, out_u, ld_out, st);
+}
+
+cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
+                                int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
+                                const float* u0, int64_t ld_box, float* out_l, float* out_u, int64_t ld_out,
+                                cudaStream_t st) {
   int64_t rows = 2 * B * R;
   if (rows == 0) return CF_OK;
   const int64_t gx = ceil_div(R, kCbT), gy = ceil_div(B, kCbT);
@@ -229,8 +236,8 @@ cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, in
                               2.0 * B * R);
   if (bcast && gx <= 0x7fffffff && gy <= 65535) {
     prof_mem_begin(st);
-    k_concretize_bcast<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(B, R, n0, A, a_rs, c, l0, u0, out_l, out_u,
-                                                                         ld_out);
+    k_concretize_bcast<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(B, R, n0, A, a_rs, c, l0, u0, ld_box, out_l,
+                                                                         out_u, ld_out);
     prof_mem_end(st, bytes);
     return check_launch("k_concretize_bcast");
   }
@@ -238,8 +245,8 @@ cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, in
   int64_t blocks = ceil_div(rows * 32, threads);
   if (blocks > 148 * 32) blocks = 148 * 32;
   prof_mem_begin(st);
-  k_concretize<<<(unsigned)blocks, threads, 0, st>>>(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, out_l,
-                                                      out_u, ld_out);
+  k_concretize<<<(unsigned)blocks, threads, 0, st>>>(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, ld_box,
+                                                      out_l, out_u, ld_out);
   prof_mem_end(st, bytes);
   return check_launch("k_concretize");
 }

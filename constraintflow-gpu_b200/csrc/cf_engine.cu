@@ -83,7 +83,7 @@ static void window_sizing(const cf_network* net, Plan& p);
 cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
   CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
-  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_IBP, CF_ERR_UNSUPPORTED,
+  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_CROWNIBP, CF_ERR_UNSUPPORTED,
              "network: relaxation %d", net->relaxation);
   int64_t pos = net->n_input, prev_width = net->n_input;
   p.col.assign(net->n_layers, 0);
@@ -472,7 +472,16 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
     if (p.affine[a] >= li_begin && p.affine[a] < li_end) {
-      if (p.has_conv)
+      if (net->relaxation == CF_RELAX_CROWNIBP) {
+        // crownibp.cf: the interval bound over the previous layer's state columns (the
+        // input's columns start at 0)
+        const int64_t in_col = p.affine[a] == 0 ? 0 : p.col[p.affine[a] - 1];
+        if (L.kind == CF_LAYER_CONV)
+          CF_TRY(launch_ibp_conv_state(Bc, L, st_l + in_col, st_u + in_col, N, st_l + col, st_u + col, N, st));
+        else
+          CF_TRY(launch_concretize_box(Bc, L.n_out, L.n_in, L.W_dev, 0, 0, L.n_in, L.b_dev, 0, 0, st_l + in_col,
+                                       st_u + in_col, N, st_l + col, st_u + col, N, st));
+      } else if (p.has_conv)
         CF_TRY(bound_window(a, col));
       else if (chain_applicable(net, p, a))
         CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,

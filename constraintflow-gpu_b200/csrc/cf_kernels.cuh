@@ -15,6 +15,15 @@ cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* 
 cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
                             const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
+// the same with the box rows of region b at l0 + b*ld_box (e.g. a layer's state columns)
+cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
+                                int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
+                                const float* u0, int64_t ld_box, float* out_l, float* out_u, int64_t ld_out,
+                                cudaStream_t st);
+// interval bound of a conv layer (ibp.Affine) from the previous layer's bounds (rows at
+// l + b*ld_in) into the state columns (rows at sl + b*ld_state)
+cf_status launch_ibp_conv_state(int64_t B, const cf_layer& L, const float* l, const float* u, int64_t ld_in,
+                                float* sl, float* su, int64_t ld_state, cudaStream_t st);
 
 cf_status launch_step_const(int64_t B, int64_t R, int64_t K, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c_in, int64_t c_ss, int64_t c_bs, const float* alpha,

@@ -446,19 +446,20 @@ __global__ void k_ibp_linear(int64_t K, int64_t N, const float* __restrict__ l, 
   }
 }
 
-// ibp.Affine for a conv layer: one thread per output neuron (co, oy, ox) of region b.
+// ibp.Affine for a conv layer: one thread per output neuron (co, oy, ox) of region b; the
+// input bounds of region b at l + b*ld_in; lo / uo (compact [B, n_out]) may be NULL.
 __global__ void k_ibp_conv(int64_t B, ConvGeo g, const float* __restrict__ l, const float* __restrict__ u,
-                           const float* __restrict__ W, const float* __restrict__ bias, float* __restrict__ lo,
-                           float* __restrict__ uo, float* __restrict__ sl, float* __restrict__ su,
-                           int64_t ld_state) {
+                           int64_t ld_in, const float* __restrict__ W, const float* __restrict__ bias,
+                           float* __restrict__ lo, float* __restrict__ uo, float* __restrict__ sl,
+                           float* __restrict__ su, int64_t ld_state) {
   const int64_t nout = (int64_t)g.cout * g.oh * g.ow, nin = (int64_t)g.cin * g.ih * g.iw;
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= B * nout) return;
   const int64_t b = t / nout, o = t - b * nout;
   const int co = (int)(o / (g.oh * g.ow)), rem = (int)(o % (g.oh * g.ow));
   const int oy = rem / g.ow, ox = rem % g.ow;
-  const float* lb_ = l + b * nin;
-  const float* ub_ = u + b * nin;
+  const float* lb_ = l + b * ld_in;
+  const float* ub_ = u + b * ld_in;
   float pl = 0.0f, nu = 0.0f, pu = 0.0f, nl = 0.0f;
   for (int ci = 0; ci < g.cin; ++ci)
     for (int ky = 0; ky < g.kh; ++ky) {
@@ -478,8 +479,10 @@ __global__ void k_ibp_conv(int64_t B, ConvGeo g, const float* __restrict__ l, co
     }
   const float bv = bias[co];
   const float lv = (pl + nu) + bv, uv = (pu + nl) + bv;
-  lo[t] = lv;
-  uo[t] = uv;
+  if (lo) {
+    lo[t] = lv;
+    uo[t] = uv;
+  }
   sl[b * ld_state + o] = lv;
   su[b * ld_state + o] = uv;
 }
@@ -838,8 +841,8 @@ static cf_status ibp_layers(const cf_network* net, const Plan& p, int64_t Bc, co
         CF_TRY(check_launch("k_ibp_linear"));
       } else {
         ConvGeo g{L.cin, L.ih, L.iw, L.cout, L.oh, L.ow, L.kh, L.kw, L.stride, L.pad};
-        k_ibp_conv<<<(unsigned)ceil_div(Bc * L.n_out, 128), 128, 0, st>>>(Bc, g, lc, uc, L.W_dev, L.b_dev, lo, uo,
-                                                                          sl + col, su + col, Ntot);
+        k_ibp_conv<<<(unsigned)ceil_div(Bc * L.n_out, 128), 128, 0, st>>>(Bc, g, lc, uc, L.n_in, L.W_dev, L.b_dev,
+                                                                          lo, uo, sl + col, su + col, Ntot);
         CF_TRY(check_launch("k_ibp_conv"));
       }
     }
@@ -954,6 +957,17 @@ __global__ void k_bounds_meet(int64_t B, int64_t n, float* __restrict__ la, floa
     lo[t] = (double)l;
     hi[t] = (double)u;
   }
+}
+
+cf_status launch_ibp_conv_state(int64_t B, const cf_layer& L, const float* l, const float* u, int64_t ld_in,
+                                float* sl, float* su, int64_t ld_state, cudaStream_t st) {
+  if (B * L.n_out == 0) return CF_OK;
+  const ConvGeo g{L.cin, L.ih, L.iw, L.cout, L.oh, L.ow, L.kh, L.kw, L.stride, L.pad};
+  prof_mem_begin(st);
+  k_ibp_conv<<<(unsigned)ceil_div(B * L.n_out, 128), 128, 0, st>>>(B, g, l, u, ld_in, L.W_dev, L.b_dev, nullptr,
+                                                                    nullptr, sl, su, ld_state);
+  prof_mem_end(st, 4.0 * (2.0 * B * L.n_in + (double)L.cout * L.cin * L.kh * L.kw + L.cout + 2.0 * B * L.n_out));
+  return check_launch("k_ibp_conv");
 }
 
 }  // namespace cf

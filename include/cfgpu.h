@@ -83,9 +83,13 @@ enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
  *                      Linear and conv layers.
  *   CF_RELAX_IBP       ibp.cf: interval bounds layer by layer (W+ l + W- u + b; ReLU
  *                      clamps), linear and conv layers.
+ *   CF_RELAX_CROWNIBP  crownibp.cf: every affine layer below the property gets the
+ *                      interval bound of its expression over the previous layer's l / u
+ *                      (no traversal); the ReLU relaxation is DeepPoly's, from those
+ *                      bounds; only the property rows are backsubstituted to the input.
  * CF_RELAX_ZONO and CF_RELAX_IBP run forward through cf_deeppoly_run as well; their
  * regions are independent (any chunk size). */
-enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1, CF_RELAX_ZONO = 2, CF_RELAX_IBP = 3 };
+enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1, CF_RELAX_ZONO = 2, CF_RELAX_IBP = 3, CF_RELAX_CROWNIBP = 4 };
 
 /* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
  * Conv: W_dev [cout, cin, kh, kw], b_dev [cout]; neurons in (c, y, x) order,
@@ -107,7 +111,7 @@ typedef struct cf_network {
   const cf_layer* layers;  /* host array */
   int32_t n_input;
   int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
-  int32_t relaxation;      /* CF_RELAX_DEEPPOLY, CF_RELAX_CROWN, CF_RELAX_ZONO or CF_RELAX_IBP */
+  int32_t relaxation;      /* CF_RELAX_DEEPPOLY, _CROWN, _ZONO, _IBP or _CROWNIBP */
 } cf_network;
 
 /* Total neuron count N of the abstract state: input + every layer + property rows

@@ -180,7 +180,7 @@ def _stack_poly(P, Q, B):
     return blocks, np.concatenate([P[1], Q[1]], axis=1).astype(F32)
 
 
-def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min):
+def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=False):
     """Run the reference's DeepPoly or CROWN program over a network of linear / conv / relu /
     add / concat layers listed in the reference reader's breadth-first order.
 
@@ -190,6 +190,9 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min):
     relaxation : 'deeppoly' (deeppoly.cf) or 'crown' (crown.cf).
     order  : which live layer the traversal substitutes next (``min`` = the reference's
              priority2 = -layer; tests plant ``max`` to show the golden vectors pin it).
+    interval : crownibp.cf -- every affine layer below the property gets the interval
+             bound of its polyexp over the previous layer's l / u (``map(simplify_lower)``
+             without a traversal); only the property layer is backsubstituted.
     Returns (bounds, lb, ub, branches): bounds per layer (excluding input, including
     the property layer) of (l [B,n], u [B,n]); lb/ub float64 [B, 9]; branches the
     BRANCH_* code of every ReLU layer (CROWN).
@@ -235,16 +238,29 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min):
             A0 = np.ascontiguousarray(_affine_rows(Lyr, 0, Lyr.n_out, B)[0])
             c0 = np.broadcast_to(layer_bias(Lyr), (B, Lyr.n_out)).astype(F32)
             W_prev = {ks[0]: A0[None]}
-        res = []
-        for lower in (True, False):
-            res.append(_traverse({t: np.array(np.broadcast_to(M, (B,) + M.shape[-2:]), F32)
-                                  for t, M in W_prev.items()}, c0.copy(), polys, lower, order))
-        bnd[k] = (res[0], res[1])
+        if interval and kind != 'spec':
+            pl, pu = bnd[ks[0]]
+            Wp, Wn = np.maximum(A0, F32(0)), np.minimum(A0, F32(0))
+            bnd[k] = ((pl @ Wp.T + pu @ Wn.T + c0).astype(F32), (pu @ Wp.T + pl @ Wn.T + c0).astype(F32))
+        else:
+            res = []
+            for lower in (True, False):
+                res.append(_traverse({t: np.array(np.broadcast_to(M, (B,) + M.shape[-2:]), F32)
+                                      for t, M in W_prev.items()}, c0.copy(), polys, lower, order))
+            bnd[k] = (res[0], res[1])
         poly = (W_prev, c0)
         polys[k] = (poly, poly)
     bounds = [bnd[k] for k in range(1, len(layers) + 2)]
     lb, ub = bounds[-1]
     return bounds, lb.astype(np.float64), ub.astype(np.float64), branches
+
+
+def crownibp(layers, l0, u0, spec_W, order=max):
+    """The reference's crownibp.cf: interval bounds for every layer below the property,
+    DeepPoly's ReLU relaxation from them (relu_n, compute_upper: crownibp.cf:19-21), and
+    one backward traversal of the property rows (priority2 = +layer: the highest live layer
+    first, crownibp.cf:10,24)."""
+    return certify(layers, l0, u0, spec_W, "deeppoly", order, interval=True)
 
 
 def crown(layers, l0, u0, spec_W, order=min):

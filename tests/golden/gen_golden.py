@@ -38,7 +38,7 @@ REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 
 # certifier programs of examples/compiler_examples/ whose generated code is kept and run
-PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient", "zono", "zono2", "ibp", "polyzono")
+PROGRAMS = ("deeppoly", "crown", "deeppoly2", "deeppoly_efficient", "zono", "zono2", "ibp", "polyzono", "crownibp")
 
 # name -> (program, workload id, batch, eps)
 CASES = {
@@ -97,6 +97,12 @@ CASES = {
     "pz_w1_b8_e5e-4": ("polyzono", 1, 8, 0.0005),
     "pz_w2_b4_e2e-3": ("polyzono", 2, 4, 0.002),
     "pz_w2_b4_e2e-4": ("polyzono", 2, 4, 0.0002),
+    # crownibp.cf: interval bounds for every layer, backsubstitution for the property only
+    "cibp_w0_b4_e1e-3": ("crownibp", 0, 4, 0.001),
+    "cibp_w0_b4_e1e-2": ("crownibp", 0, 4, 0.01),
+    "cibp_w1_b8_e5e-4": ("crownibp", 1, 8, 0.0005),
+    "cibp_w2_b4_e2e-4": ("crownibp", 2, 4, 0.0002),
+    "cibp_w3_b2_e2e-3": ("crownibp", 3, 2, 0.002),
 }
 
 

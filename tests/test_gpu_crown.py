@@ -1,5 +1,7 @@
 """GPU parity of the network driver running the reference's CROWN program
-(DeepPolyEngine(certifier='crown') -> cf_deeppoly_run with CF_RELAX_CROWN).
+(DeepPolyEngine(certifier='crown') -> cf_deeppoly_run with CF_RELAX_CROWN), and its
+crownibp.cf program (certifier='crownibp', CF_RELAX_CROWNIBP: interval bounds below the
+property, one backsubstitution of the property rows).
 
 CROWN's ReLU takes one branch per layer for the whole batch (crown.cf:25 as the
 reference compiles it): pass-through and zero run in the fused driver; the all-crossing
@@ -119,3 +121,66 @@ def test_gpu_crown_needs_one_chunk():
                                   torch.cuda.current_stream().cuda_stream)
     assert st == _lib.CF_ERR_WORKSPACE
     assert b"whole batch" in _lib.lib.cf_last_error()
+
+
+CIBP_CASES = names("crownibp")
+
+
+def _cibp_run(wl, l0, u0, W, budget=None):
+    from cfgpu.engine import DeepPolyEngine
+    eng = DeepPolyEngine(wl.layers, wl.input_size, "cuda:0", certifier="crownibp")
+    dev = torch.device("cuda:0")
+    kw = {} if budget is None else {"workspace_budget": eng.workspace_bytes(budget)}
+    lb, ub, sl, su = eng.run(torch.from_numpy(l0).to(dev), torch.from_numpy(u0).to(dev),
+                             torch.from_numpy(W).to(dev), want_state=True, check_device=True, **kw)
+    torch.cuda.synchronize()
+    return lb.cpu().numpy(), ub.cpu().numpy(), sl.cpu().numpy(), su.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", CIBP_CASES)
+def test_gpu_crownibp_matches_reference(name):
+    c = Case(name)
+    lb, ub, sl, su = _cibp_run(c.wl, c.l0, c.u0, c.spec_W)
+    n0 = c.wl.input_size
+    assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+    np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
+    bounds, _, _, _ = C.crownibp(c.wl.layers, c.l0, c.u0, c.spec_W)
+    ol, ou = O.flatten_bounds(n0, bounds, c.B)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
+
+
+def test_gpu_crownibp_full_batch_and_chunks():
+    """The default workload's full batch: the first regions agree with the oracle, a
+    workspace of one region at a time gives the same bounds, and the property bounds are
+    no tighter than DeepPoly's (interval bounds below the property are looser)."""
+    from cfgpu.engine import DeepPolyEngine
+    wl = nets.workload(2)
+    B = 256
+    X = nets.centres(wl, B)
+    y = nets.labels(wl, X)
+    l0, u0 = (t.numpy() for t in nets.input_box(X, 0.002, wl.dataset))
+    W = nets.spec_weight(y).numpy()
+    lb, ub, sl, su = _cibp_run(wl, l0, u0, W)
+    lb1, ub1, _, _ = _cibp_run(wl, l0, u0, W, budget=1)
+    assert np.array_equal(lb, lb1) and np.array_equal(ub, ub1)
+    nb = 2
+    bounds, _, _, _ = C.crownibp(wl.layers, l0[:nb], u0[:nb], W[:nb])
+    n0 = wl.input_size
+    ol, ou = O.flatten_bounds(n0, bounds, nb)
+    worst, where = parity.continuous_errors(sl[:nb, n0:], su[:nb, n0:], ol, ou, [L.n_out for L in wl.layers] + [9])
+    assert worst <= 1.0, f"GPU vs oracle {worst:.3g}x tolerance at {where}"
+    dev = torch.device("cuda:0")
+    eng = DeepPolyEngine(wl.layers, wl.input_size, dev)
+    lbd, _ = eng.run(torch.from_numpy(l0).to(dev), torch.from_numpy(u0).to(dev), torch.from_numpy(W).to(dev))
+    lbd = lbd.cpu().numpy()
+    assert (lb <= lbd + 1e-4 * np.abs(lbd).max()).all()
+
+
+def test_gpu_crownibp_refuses_dag():
+    from cfgpu.engine import DeepPolyEngine
+    with pytest.raises(NotImplementedError):
+        DeepPolyEngine(nets.workload(5).layers, nets.workload(5).input_size, "cuda:0", certifier="crownibp")

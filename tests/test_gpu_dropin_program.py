@@ -1,5 +1,5 @@
 """The reference compiler's own output for examples/compiler_examples/{deeppoly,crown,
-deeppoly_efficient,zono,ibp,polyzono}.cf (tests/golden/generated/<program>/{main.py,transformers.py}, saved
+deeppoly_efficient,zono,ibp,polyzono,crownibp}.cf (tests/golden/generated/<program>/{main.py,transformers.py}, saved
 by tests/golden/gen_golden.py) runs UNCHANGED on this runtime's constraintflow package:
 main.run(...) -> (lb, ub) float64, matching the reference's golden bounds (chain, residual
 Add and Concat networks)."""
@@ -50,7 +50,8 @@ PROGRAM_CASES = [("deeppoly", n) for n in ("dp_w0_b4_e1e-3", "dp_w1_b16_e5e-4", 
     [("crown", n) for n in ("crown_w5_b2_e2e-3", "crown_w6_b2_e1e-1")] + \
     [("zono", n) for n in ("zono_w0_b4_e1e-3", "zono_w2_b4_e2e-4")] + \
     [("ibp", n) for n in ("ibp_w0_b4_e1e-3", "ibp_w3_b2_e2e-3")] + \
-    [("polyzono", n) for n in ("pz_w0_b4_e1e-2", "pz_w2_b4_e2e-4")]
+    [("polyzono", n) for n in ("pz_w0_b4_e1e-2", "pz_w2_b4_e2e-4")] + \
+    [("crownibp", n) for n in ("cibp_w0_b4_e1e-3", "cibp_w3_b2_e2e-3")]
 
 
 @pytest.mark.parametrize("program,name", PROGRAM_CASES)
@@ -78,10 +79,10 @@ def test_generated_program_runs_unchanged(program, name):
 def test_programs_are_recognised():
     from constraintflow.lib.flow_sparse import certifier_of
     for program, expect in (("deeppoly", "deeppoly"), ("deeppoly_efficient", "deeppoly"), ("crown", "crown"),
-                            ("zono", "zono"), ("ibp", "ibp"), ("polyzono", "polyzono")):
+                            ("zono", "zono"), ("ibp", "ibp"), ("polyzono", "polyzono"), ("crownibp", "crownibp")):
         main = _load_program(program)
-        assert certifier_of(getattr(main, program if program in ("zono", "ibp", "polyzono") else "deeppoly")()) \
-            == expect
+        cls = program if program in ("zono", "ibp", "polyzono", "crownibp") else "deeppoly"
+        assert certifier_of(getattr(main, cls)()) == expect
 
     class Other:   # some other certifier program: a ReLU without a recognised relaxation
         def Affine(self, abs_elem, prev, curr):

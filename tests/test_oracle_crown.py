@@ -1,5 +1,6 @@
 """The CROWN oracle (oracle/crown_oracle.py) against the reference's own CROWN outputs,
-and deeppoly_efficient.cf's reference outputs against the DeepPoly oracle.
+deeppoly_efficient.cf's reference outputs against the DeepPoly oracle, and the crownibp.cf
+oracle (interval bounds below the property) against the reference's crownibp outputs.
 
 The reference cases (tests/golden/crown_*.npz, dpe_*.npz, made by gen_golden.py) cover
 CROWN's pass-through branch (eps 1e-3 .. 1e-2) and its all-crossing branch (eps >= 0.1,
@@ -20,6 +21,7 @@ from cfgpu import nets
 
 CROWN_CASES = names("crown")
 DPE_CASES = names("deeppoly_efficient")
+CIBP_CASES = names("crownibp")
 
 
 def _crown(c, **kw):
@@ -80,3 +82,27 @@ def test_deeppoly_efficient_is_deeppoly(name):
     worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
     assert worst <= 1.0, f"{name}: DeepPoly oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+
+
+@pytest.mark.parametrize("name", CIBP_CASES)
+def test_crownibp_oracle_matches_reference(name):
+    c = Case(name)
+    bounds, lb, ub, _ = C.crownibp(c.wl.layers, c.l0, c.u0, c.spec_W)
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+
+
+def test_crownibp_cases_present():
+    assert len(CIBP_CASES) >= 5 and {Case(n).wid for n in CIBP_CASES} >= {0, 1, 2, 3}
+
+
+def test_crownibp_planted_backsubstitution_fails():
+    """A mistake planted in the oracle (every layer backsubstituted, i.e. DeepPoly) breaks
+    the crownibp cases: the reference's intermediate bounds are the interval ones."""
+    c = Case("cibp_w2_b4_e2e-4")
+    bounds, _, _, _ = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, "deeppoly")
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+    worst, _ = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst > 10.0
