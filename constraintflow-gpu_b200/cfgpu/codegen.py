@@ -16,6 +16,10 @@ own definitions, which fused kernel family implements each transformer operation
           interval          map(E, G_low), map(E, G_up) without a traversal
           backsubstitution  max(zonotope low, backsubstitution low), min(... up), E, E, Ez
           + zonotope        over the shape (l, u, L, U, Z) (polyzono.cf), either order
+          interval, then    curr[last_layer] == 1 ? backsubstitution tuple : (map(E, G_low),
+          backsubstitution  map(E, G_up), E, E) (crownibp.cf); its traversal may take the
+                            highest layer first (the runtime runs it on chains, where the
+                            order does not change the bounds)
   Relu    DeepPoly          (relu(l), relu(u), 1[l+u>=0] x, l>=0 ? x : u<=0 ? 0 :
                             lam (x - l)), lam = u/(u-l), x the neuron (prev, prev[L] and
                             prev[U] all denote the affine input of the ReLU)
@@ -415,7 +419,7 @@ def _sign_choice(prog, fname, pos, neg):
     return True
 
 
-def _check_backsub_member(prog, n, lower):
+def _check_backsub_member(prog, n, lower, any_order=False):
     n = _inline_call(prog, n)
     if _kind(n) != "MapNode" or _kind(n.expr) != "TraverseNode":
         return False
@@ -426,7 +430,7 @@ def _check_backsub_member(prog, n, lower):
     # the lowest layer first: priority decreases with the layer index
     p1 = ev.call(_name(t.priority), [Neuron(0, 1, layer=1), 1.0])
     p2 = ev.call(_name(t.priority), [Neuron(0, 1, layer=2), 1.0])
-    if not (isinstance(p1, float) and isinstance(p2, float) and p1 > p2):
+    if not (isinstance(p1, float) and isinstance(p2, float) and (p1 > p2 or (any_order and p1 < p2))):
         return False
     if ev.call(_name(t.stop), [Neuron(0, 1, layer=1), 1.0]) is not False:
         return False
@@ -459,7 +463,37 @@ def _met_bound(prog, n, lower):
     return any(_zono_bound(prog, x, lower) and _check_backsub_member(prog, y, lower) for x, y in ((a, b), (b, a)))
 
 
+def _is_last_layer_test(n):
+    """n is curr[last_layer] == 1."""
+    return (_kind(n) == "BinOpNode" and n.op == "==" and _kind(n.left) == "GetMetadataNode"
+            and _name(n.left.expr) == "curr" and getattr(n.left.metadata, "name", None) == "last_layer"
+            and _kind(n.right) in ("ConstIntNode", "ConstFloatNode") and float(n.right.value) == 1.0)
+
+
+def _classify_interval_then_backsub(prog, ret):
+    """curr[last_layer] == 1 ? (backsubstitution bounds, E, E) : (map(E, G_low), map(E, G_up),
+    E, E) over the shape (l, u, L, U)."""
+    if [m for _, m in prog.shape] != ["l", "u", "L", "U"] or not _is_last_layer_test(ret.cond):
+        return None
+    t, f = _ret_tuple(ret.tret), _ret_tuple(ret.fret)
+    if t is None or f is None or len(t) != 4 or len(f) != 4:
+        return None
+    if not (_check_backsub_member(prog, t[0], True, any_order=True)
+            and _check_backsub_member(prog, t[1], False, any_order=True)
+            and _affine_expr_ok(prog, t[2], "") and _affine_expr_ok(prog, t[3], "")):
+        return None
+    m0, m1 = _inline_call(prog, f[0]), _inline_call(prog, f[1])
+    if (_kind(m0) == "MapNode" and _kind(m1) == "MapNode" and _affine_expr_ok(prog, m0.expr, "")
+            and _affine_expr_ok(prog, m1.expr, "") and _sign_choice(prog, _name(m0.func), "l", "u")
+            and _sign_choice(prog, _name(m1.func), "u", "l") and _affine_expr_ok(prog, f[2], "")
+            and _affine_expr_ok(prog, f[3], "")):
+        return "interval+backsub"
+    return None
+
+
 def _classify_affine(prog, ret):
+    if _kind(ret) == "TransRetIfNode":
+        return _classify_interval_then_backsub(prog, ret)
     exprs = _ret_tuple(ret)
     if exprs is None or len(exprs) != len(prog.shape):
         return None
@@ -511,7 +545,7 @@ def _classify_relu(prog, ret):
 # certifier = (Affine family, Relu family)
 _CERTIFIERS = {("backsub", "deeppoly"): "deeppoly", ("backsub", "crown"): "crown",
                ("zonotope", "zonotope"): "zono", ("interval", "interval"): "ibp",
-               ("backsub+zonotope", "deeppoly+zonotope"): "polyzono"}
+               ("backsub+zonotope", "deeppoly+zonotope"): "polyzono", ("interval+backsub", "deeppoly"): "crownibp"}
 
 
 class Analysis:
@@ -557,6 +591,7 @@ _DOC = {"backsub": "backsubstitution of the layer's coefficient rows down to the
         "deeppoly": "DeepPoly triangle relaxation", "crown": "CROWN whole-layer branches",
         "backsub+zonotope": "backsubstitution and zonotope step, bounds met (max / min)",
         "deeppoly+zonotope": "DeepPoly and zonotope relaxations from the met bounds",
+        "interval+backsub": "interval bound; backsubstitution for the property layer only",
         None: "no fused kernel"}
 
 

@@ -26,8 +26,8 @@ REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 # the programs the backend runs, then programs it must refuse (other traversal order,
 # ReLU relaxation or domain), then programs the reference front end itself refuses
-PROGRAMS = ("deeppoly", "deeppoly_efficient", "crown", "zono", "ibp",
-            "deeppoly_priority", "deeppolyh", "zono2", "ibp2", "polyzono",
+PROGRAMS = ("deeppoly", "deeppoly_efficient", "crown", "zono", "ibp", "polyzono", "crownibp",
+            "deeppoly_priority", "deeppolyh", "zono2", "ibp2",
             "deeppoly2", "hybrid_zono")
 
 

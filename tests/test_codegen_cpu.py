@@ -18,7 +18,7 @@ sys.path.insert(0, GOLDEN)
 import ast_json  # noqa: E402
 
 RUNS = {"deeppoly": "deeppoly", "deeppoly_efficient": "deeppoly", "crown": "crown", "zono": "zono", "ibp": "ibp",
-        "polyzono": "polyzono"}
+        "polyzono": "polyzono", "crownibp": "crownibp"}
 REFUSED = ("deeppoly_priority", "deeppolyh", "zono2", "ibp2")
 
 
@@ -31,7 +31,8 @@ def _ast(prog):
 def test_backend_recognises_program(prog):
     a = codegen.analyse(_ast(prog))
     assert a.certifier == RUNS[prog]
-    assert a.ops["Affine"] in ("backsub", "zonotope", "interval", "backsub+zonotope") and a.ops["Relu"] is not None
+    assert a.ops["Affine"] in ("backsub", "zonotope", "interval", "backsub+zonotope", "interval+backsub")
+    assert a.ops["Relu"] is not None
 
 
 @pytest.mark.parametrize("prog", sorted(RUNS))
@@ -129,3 +130,23 @@ def test_planted_polyzono_mistakes_are_refused(mistake):
     with pytest.raises(codegen.CodegenError) as e:
         codegen.analyse(ast)
     assert ("Relu (unrecognised)" if mistake == "zono_relu_scale" else "Affine (unrecognised)") in str(e.value)
+
+
+@pytest.mark.parametrize("mistake", ["interval_sign", "last_layer_test", "property_replace"])
+def test_planted_crownibp_mistakes_are_refused(mistake):
+    """Mistakes planted in crownibp.cf's AST make the backend refuse it: the interval lower
+    bound concretising a positive coefficient with u; the branch taken for a layer other
+    than the last one; the property traversal substituting U for a positive coefficient
+    of the lower bound."""
+    ast = copy.deepcopy(_ast("crownibp"))
+    f = _funcs(ast)
+    if mistake == "interval_sign":         # simplify_lower(n, c) = c >= 0 ? n[u] * c : c * n[u]
+        f["simplify_lower"].expr.texpr.left.elem.name = "u"
+    elif mistake == "last_layer_test":     # curr[last_layer] == 0
+        _nodes(ast.stmt, "TransRetIfNode")[0].cond.right.value = 0
+    elif mistake == "property_replace":    # replace_lower(n, c) = c >= 0 ? c * n[U] : c * n[U]
+        f["replace_lower"].expr.texpr.right.elem.name = "U"
+    assert codegen.analyse(copy.deepcopy(_ast("crownibp"))).certifier == "crownibp"
+    with pytest.raises(codegen.CodegenError) as e:
+        codegen.analyse(ast)
+    assert "Affine (unrecognised)" in str(e.value)
