@@ -32,9 +32,15 @@ class DeepPolyEngine:
     (zono.cf, DeepZ: forward zonotope pass, linear chains), 'ibp' (ibp.cf: interval
     bounds) or 'crownibp' (crownibp.cf: interval bounds below the property, DeepPoly's
     ReLU relaxation from them, one backsubstitution of the property rows; chains).
+    stop_depth: the custom-stop DeepPoly programs (deeppoly_custom_stop.cf, custom_stops/)
+    with get_start = stop_depth: the traversal bounding a neuron of list layer m stops below
+    layer m - stop_depth and concretises there with those neurons' own bounds (linear chains;
+    None: every traversal reaches the input).  relu_strict: the lower ReLU slope is 1 where
+    l + u > 0 (those programs' relu_n) instead of l + u >= 0.
     """
 
-    def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly"):
+    def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly",
+                 stop_depth=None, relu_strict=False):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("DeepPolyEngine runs on a CUDA device only (no CPU fallback)")
@@ -46,6 +52,7 @@ class DeepPolyEngine:
             raise NotImplementedError(f"certifier {certifier!r} (the driver runs deeppoly, crown, zono, ibp and "
                                       "crownibp)")
         self.certifier = certifier
+        self.stop_depth = None
         self._keep = []
         self._general = []        # (kind, W, b, parents) device tensors for cfgpu.general
         widths = []
@@ -95,7 +102,17 @@ class DeepPolyEngine:
         self.kinds = [g[0] for g in self._general]
         if self.chain:
             self._layers = (CfLayer * len(descs))(*descs)
-            self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, relax[certifier])
+            if stop_depth is not None and (certifier != "deeppoly" or int(stop_depth) < 0 or
+                                           any(g[0] == "conv" for g in self._general)):
+                raise NotImplementedError("a custom stop depth applies to the DeepPoly traversal of linear chains")
+            self.stop_depth = None if stop_depth is None else int(stop_depth)
+            code = relax[certifier]
+            if relu_strict:
+                if certifier != "deeppoly":
+                    raise NotImplementedError("the strict lower-slope test applies to the DeepPoly relaxation")
+                code = _lib.CF_RELAX_DEEPPOLY_STRICT
+            self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, code,
+                                 0 if stop_depth is None else int(stop_depth) + 1)
             self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))
             if self.N < 0:
                 check(_lib.CF_ERR_SHAPE, "network description")
@@ -104,6 +121,9 @@ class DeepPolyEngine:
             if certifier not in ("deeppoly", "crown"):
                 raise NotImplementedError(f"{certifier} on a network with Add / Concat layers (the forward "
                                           "drivers run chain networks)")
+            if stop_depth is not None or relu_strict:
+                raise NotImplementedError("a custom stop depth or strict ReLU test on a network with Add / Concat "
+                                          "layers")
             if any(g[0] == "conv" for g in self._general):
                 raise NotImplementedError("conv layers in a network with Add / Concat layers (the general "
                                           "traversal runs linear, relu, add and concat layers)")

@@ -27,11 +27,16 @@ get_new_eps); it runs as cfgpu.polyzono's coupled DeepPoly and zonotope passes.
 crownibp.cf branches its Affine on the last_layer metadata: interval bounds below the
 property (map(simplify_lower) over the previous layer's l / u), the traversal for the
 property rows; its Relu is DeepPoly's.
+The custom-stop DeepPoly programs (deeppoly_custom_stop.cf, custom_stops/) stop their
+traversal at layers below curr[layer] - get_start: the generated Affine subtracts the
+constant get_start from the layer metadata (stop_depth_of), and the driver runs DeepPoly
+with that stop depth.
 A transformer object may also declare itself with a ``cf_certifier`` attribute
 ('deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp').  Other programs (zono2.cf's whole-layer branches
 among them) raise NotImplementedError.
 """
 import inspect
+import re
 
 import torch
 
@@ -61,6 +66,44 @@ _POLYZONO_AFFINE = _AFFINE + ("get_elem('Z', prev", "cf_max(", "cf_min(")
 _POLYZONO_RELU = ("convert_to_poly(", "get_new_eps(", "get_elem('Z', prev", "operator.truediv", "where(")
 
 
+_STOP_DEPTH = re.compile(r"curr\.get_metadata\('layer'[^)]*\), SparseTensor\(\[\], \[\], 0, torch\.tensor\(\[\]\), "
+                         r"dense_const=(\d+), type= type\(\d+\)\)(?:\.\w+\([^()]*(?:\([^()]*\))?[^()]*\))*, "
+                         r"operator\.sub")
+
+
+def stop_depth_of(transformer):
+    """get_start of a custom-stop DeepPoly program (the traversal bounding a neuron of layer
+    k stops below layer k - get_start, deeppoly_custom_stop.cf:12-17), None for a traversal
+    to the input.  Declared by a ``cf_stop_depth`` attribute or read from the generated
+    Affine, which computes curr[layer] - get_start."""
+    declared = getattr(transformer, "cf_stop_depth", None)
+    if declared is not None or getattr(transformer, "cf_certifier", None) is not None:
+        return declared
+    try:
+        affine = inspect.getsource(type(transformer).Affine)
+    except (AttributeError, OSError, TypeError):
+        return None
+    found = {int(m) for m in _STOP_DEPTH.findall(affine)}
+    if len(found) > 1:
+        raise NotImplementedError(f"traversal stops at several depths {sorted(found)}")
+    return found.pop() if found else None
+
+
+def relu_is_strict(transformer):
+    """DeepPoly's Relu with strict comparisons (relu_n: l + u > 0; compute_upper: l > 0,
+    u < 0), as the custom-stop programs write it (deeppoly_custom_stop.cf:22-24)."""
+    declared = getattr(transformer, "cf_relu_strict", None)
+    if declared is not None or getattr(transformer, "cf_certifier", None) is not None:
+        return bool(declared)
+    try:
+        relu = inspect.getsource(type(transformer).Relu)
+    except (AttributeError, OSError, TypeError):
+        return False
+    return ("if(" not in relu and "any(" not in relu and "operator.ge" not in relu and "operator.le" not in relu
+            and all(k in relu for k in ("convert_to_poly(", "operator.truediv", "operator.gt", "operator.lt",
+                                        "where(")))
+
+
 def certifier_of(transformer):
     """'deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp' for a recognised generated
     transformer, else raises."""
@@ -80,6 +123,8 @@ def certifier_of(transformer):
     if all(k in affine for k in _CROWNIBP_AFFINE) and "if(" not in relu and "any(" not in relu and (
             all(k in relu for k in _DEEPPOLY_RELU)):
         return "crownibp"
+    if all(k in affine for k in _AFFINE) and relu_is_strict(transformer):
+        return "deeppoly"
     if all(k in affine for k in _AFFINE):
         branches = "if(" in relu or "any(" in relu or "operator.gt" in relu
         if not branches and (all(k in relu for k in _DEEPPOLY_RELU) or all(k in relu for k in _EFFICIENT_RELU)):
@@ -164,7 +209,9 @@ class Flow:
             from cfgpu.polyzono import PolyZonoEngine
             eng = PolyZonoEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]))
         else:
-            eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier)
+            eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier,
+                                 stop_depth=stop_depth_of(self.transformer) if certifier == "deeppoly" else None,
+                                 relu_strict=certifier == "deeppoly" and relu_is_strict(self.transformer))
         if getattr(self.transformer, "cf_layerwise", False) and eng.net is not None:
             lb, ub, sl, su = self._layer_by_layer(eng, l0, u0, W)
         else:

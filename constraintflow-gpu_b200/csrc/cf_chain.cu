@@ -263,8 +263,8 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   // input box: staged rows (l0 then u0 per slot) or global memory
   const uint32_t box_pos = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? 0 : P.n0));
   const uint32_t box_neg = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? P.n0 : 0));
-  const float* gpos = (lower ? P.l0 : P.u0) + b * P.n0;
-  const float* gneg = (lower ? P.u0 : P.l0) + b * P.n0;
+  const float* gpos = (lower ? P.l0 : P.u0) + b * P.ld_box;
+  const float* gneg = (lower ? P.u0 : P.l0) + b * P.ld_box;
   uint32_t g = 0, nacc = 0;
   bool ok = true;
   for (int s = 0; s < P.S && ok; ++s) {
@@ -508,8 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         mbar_arrive_expect_tx(box_full, 2u * rb * (uint32_t)n_pairs);
         for (int j = 0; j < n_pairs; ++j) {
           const int64_t b = (p0 + j) % P.B;
-          bulk_g2s(box_region + (size_t)j * 2 * P.n0, P.l0 + b * P.n0, rb, box_full);
-          bulk_g2s(box_region + (size_t)j * 2 * P.n0 + P.n0, P.u0 + b * P.n0, rb, box_full);
+          bulk_g2s(box_region + (size_t)j * 2 * P.n0, P.l0 + b * P.ld_box, rb, box_full);
+          bulk_g2s(box_region + (size_t)j * 2 * P.n0 + P.n0, P.u0 + b * P.ld_box, rb, box_full);
         }
       }
       for (int s = 0; s < P.S; ++s) {
@@ -637,6 +637,9 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   }
   CF_REQUIRE(P.st[P.S - 1].N == P.n0, CF_ERR_SHAPE, "chain: last step does not reach the input");
   ChainParams Q = P;
+  if (Q.ld_box == 0) Q.ld_box = Q.n0;
+  CF_REQUIRE(Q.ld_box >= Q.n0, CF_ERR_SHAPE, "chain: box row stride %lld < %lld", (long long)Q.ld_box,
+             (long long)Q.n0);
   // weight stage: hi plane then lo plane, each tn_max rows x 128 bytes (1024-aligned)
   Q.w_lo_off = (uint32_t)tn_max * 128u;
   Q.stage_bytes = 2u * (uint32_t)tn_max * 128u;
@@ -654,7 +657,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
                        (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 128 * 4;
   // input-box rows of up to kCoefSlots (bound, region) pairs, when they fit
   const size_t box_bytes = (size_t)kCoefSlots * 2 * P.n0 * 4;
-  const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && a16(P.l0) && a16(P.u0) &&
+  const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && Q.ld_box % 4 == 0 && a16(P.l0) && a16(P.u0) &&
                       fixed + box_bytes <= 227 * 1024;
   Q.box_smem_bytes = box_ok ? (uint32_t)box_bytes : 0u;
   size_t smem = fixed + Q.box_smem_bytes;

@@ -30,9 +30,10 @@ struct ChainParams {
   const float* A0;                      // first coefficient rows (row (s,b,i) at s*a_ss + b*a_bs + i*a_rs)
   int64_t a_ss, a_bs, a_rs;
   const float* c0;                      // [R] constant of the bounded layer (its bias) or nullptr
-  const float* l0;                      // [B, n0] input box
+  const float* l0;                      // [B, n0] box of the last step's input (rows at b*ld_box; ld_box 0: n0)
   const float* u0;
   int64_t n0;
+  int64_t ld_box;
   float* out_l;                         // bound of row (0,b,i) -> out_l[b*ld_out + i]
   float* out_u;
   int64_t ld_out;

@@ -19,7 +19,8 @@ namespace cf {
 // float32 IEEE division, same operation order as the generated code.
 __global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
                              int64_t ld_in, float* __restrict__ lo, float* __restrict__ uo, int64_t ld_out,
-                             float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu) {
+                             float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu,
+                             bool strict) {
   int64_t total = B * n;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = t / n, k = t - b * n;
@@ -31,23 +32,48 @@ __global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, 
     float mu_u = 0.0f - __fdiv_rn(__fmul_rn(uv, lv), den);
     if (lo) lo[b * ld_out + k] = pos ? lv : 0.0f;
     if (uo) uo[b * ld_out + k] = (uv >= 0.0f) ? uv : 0.0f;
-    alpha[t] = (__fadd_rn(lv, uv) >= 0.0f) ? 1.0f : 0.0f;
+    const float s = __fadd_rn(lv, uv);
+    alpha[t] = (strict ? s > 0.0f : s >= 0.0f) ? 1.0f : 0.0f;
     lam[t] = pos ? 1.0f : (dead ? 0.0f : lam_u);
     mu[t] = (pos || dead) ? 0.0f : mu_u;
   }
 }
 
 cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
-                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st) {
+                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st,
+                            bool strict) {
   int64_t total = B * n;
   if (total == 0) return CF_OK;
   int threads = 256;
   int64_t blocks = ceil_div(total, threads);
   if (blocks > 148 * 16) blocks = 148 * 16;
   prof_mem_begin(st);
-  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu);
+  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu, strict);
   prof_mem_end(st, 28.0 * total);   // l, u in; l', u', alpha, lambda, mu out
   return check_launch("k_relu_relax");
+}
+
+// The box of a ReLU layer seen through its DeepPoly relaxation, for a traversal that
+// substitutes the ReLU and then stops (custom-stop programs): a coefficient a on the ReLU
+// output concretises to a * lo for the lower bound when a >= 0 (a * alpha * l of the input)
+// and to a * hi when a < 0 (a * (lambda * u + mu)); the upper bound the other way round.
+__global__ void k_relu_box(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
+                           int64_t ld_in, const float* __restrict__ alpha, const float* __restrict__ lam,
+                           const float* __restrict__ mu, float* __restrict__ lo, float* __restrict__ hi) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= B * n) return;
+  const int64_t b = t / n, k = t - b * n;
+  lo[t] = alpha[t] * l[b * ld_in + k];
+  hi[t] = fmaf(lam[t], u[b * ld_in + k], mu[t]);
+}
+
+cf_status launch_relu_box(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, const float* alpha,
+                          const float* lam, const float* mu, float* lo, float* hi, cudaStream_t st) {
+  if (B * n == 0) return CF_OK;
+  prof_mem_begin(st);
+  k_relu_box<<<(unsigned)ceil_div(B * n, 256), 256, 0, st>>>(B, n, l, u, ld_in, alpha, lam, mu, lo, hi);
+  prof_mem_end(st, 28.0 * B * n);
+  return check_launch("k_relu_box");
 }
 
 // ------------------------------------------------------------------ CROWN ReLU

@@ -83,8 +83,12 @@ static void window_sizing(const cf_network* net, Plan& p);
 cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
   CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
-  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_CROWNIBP, CF_ERR_UNSUPPORTED,
+  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_DEEPPOLY_STRICT, CF_ERR_UNSUPPORTED,
              "network: relaxation %d", net->relaxation);
+  CF_REQUIRE(net->stop_depth >= 0, CF_ERR_SHAPE, "network: stop_depth %d", net->stop_depth);
+  CF_REQUIRE(net->stop_depth == 0 || net->relaxation == CF_RELAX_DEEPPOLY ||
+                 net->relaxation == CF_RELAX_DEEPPOLY_STRICT, CF_ERR_UNSUPPORTED,
+             "network: a custom stop depth applies to the DeepPoly traversal only");
   int64_t pos = net->n_input, prev_width = net->n_input;
   p.col.assign(net->n_layers, 0);
   p.relu_after.clear();
@@ -140,6 +144,8 @@ cf_status make_plan(const cf_network* net, Plan& p) {
   }
   CF_REQUIRE(net->layers[net->n_layers - 1].kind != CF_LAYER_RELU, CF_ERR_UNSUPPORTED,
              "network must end with an affine layer");
+  CF_REQUIRE(net->stop_depth == 0 || !p.has_conv, CF_ERR_UNSUPPORTED,
+             "network: a custom stop depth on conv layers is not supported");
   p.n_out_last = prev_width;
   p.spec_col = pos;
   p.N = pos + net->n_spec;
@@ -226,7 +232,7 @@ static void window_sizing(const cf_network* net, Plan& p) {
 static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
-  size_t err, wimg, A[2], C[2], X[2], relu, state, total;
+  size_t err, wimg, A[2], C[2], X[2], relu, box, state, total;
   std::vector<size_t> wimg_off;  // per affine index
 };
 
@@ -238,9 +244,9 @@ static bool use_chain() {
 
 // The chain keeps the coefficient rows in TMEM: every substitution except the last must
 // be at most 256 wide, and every layer below the bounded one must be linear.
-static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below) {
-  if (!use_chain() || p.has_conv || n_below < 1 || n_below > (size_t)kChainMaxSteps) return false;
-  for (size_t j = 0; j < n_below; ++j) {
+static bool chain_applicable(const cf_network* net, const Plan& p, size_t n_below, size_t j_first = 0) {
+  if (!use_chain() || p.has_conv || n_below < j_first + 1 || n_below - j_first > (size_t)kChainMaxSteps) return false;
+  for (size_t j = j_first; j < n_below; ++j) {
     const cf_layer& L = net->layers[p.affine[j]];
     if (L.kind != CF_LAYER_LINEAR) return false;
     if (j + 2 <= n_below && L.n_out > 256) return false;
@@ -287,6 +293,8 @@ static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
     w.C[1] = off; off += cw_bytes;
   }
   w.relu = off; off += align256((size_t)3 * Bc * p.relu_total * sizeof(float));
+  // custom stop: the relaxed box of a ReLU substituted last (lower and upper rows)
+  w.box = off; off += net->stop_depth > 0 ? align256((size_t)2 * Bc * p.n_max * sizeof(float)) : 0;
   w.state = off; off += align256((size_t)2 * Bc * p.N * sizeof(float));
   off += step_scratch_bytes(Bc, p.r_max);
   w.total = off;
@@ -314,10 +322,11 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
                                     size_t n_below, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs,
                                     const float* c0, const float* l0, const float* u0, float* out_l, float* out_u,
                                     const std::vector<float*>& ra, const std::vector<float*>& rl,
-                                    const std::vector<float*>& rm, cudaStream_t st) {
+                                    const std::vector<float*>& rm, cudaStream_t st, size_t j_first = 0,
+                                    int64_t ld_box = 0) {
   ChainParams P;
   memset(&P, 0, sizeof(P));
-  P.S = (int32_t)n_below;
+  P.S = (int32_t)(n_below - j_first);
   for (int s = 0; s < P.S; ++s) {
     const size_t j = n_below - 1 - s;
     const cf_layer& L = net->layers[p.affine[j]];
@@ -342,21 +351,22 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
   P.c0 = c0;
   P.l0 = l0;
   P.u0 = u0;
-  P.n0 = net->n_input;
+  P.n0 = net->layers[p.affine[j_first]].n_in;  // width of the box: the last step's input
+  P.ld_box = ld_box ? ld_box : P.n0;
   P.out_l = out_l;
   P.out_u = out_u;
   P.ld_out = p.N;
   P.err = reinterpret_cast<int*>(ws + w.err);
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   P.a0_vec = (a_bs % 4 == 0) && (a_rs % 4 == 0) && al16(A0);
-  P.box_vec = (net->n_input % 4 == 0) && al16(l0) && al16(u0);
+  P.box_vec = (P.n0 % 4 == 0) && (P.ld_box % 4 == 0) && al16(l0) && al16(u0);
   const double rows = 2.0 * Bc * R;
   double flops = 0.0, bytes = 4.0 * rows;
   for (int s = 0; s < P.S; ++s) {
     flops += 2.0 * rows * P.st[s].K * P.st[s].N;
     bytes += (double)P.st[s].n_tiles * chain_wimg_bytes(P.st[s].K, P.st[s].N) + (P.st[s].alpha ? 12.0 * Bc * P.st[s].K : 0);
   }
-  bytes += 8.0 * Bc * net->n_input;
+  bytes += 8.0 * Bc * P.n0;
   prof_step_begin(st);
   cf_status s = chain_launch(P, st);
   prof_step_end(st, flops, bytes);
@@ -416,6 +426,69 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       c_bs = R;
     }
     return launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + col, st_u + col, N, st);
+  };
+
+  // custom-stop traversal (stop_depth = get_start + 1 > 0, linear chains): bounding list
+  // layer li_m (affine index ma; ma == affine.size(): the property layer) substitutes list
+  // layers li_m-1 .. li_stop = li_m-get_start.  Full steps (ReLU_j, affine j) for affine
+  // j >= j_first; the expression is then over list layer `below`, concretised with its state
+  // bounds, or, when `below` is a ReLU that is itself substituted, with the box of its
+  // relaxation over the bounds of its input.
+  auto bound_stopped = [&](size_t ma, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs, const float* c0,
+                           int64_t col) -> cf_status {
+    const int li_m = ma == p.affine.size() ? net->n_layers : p.affine[ma];
+    const int li_stop = li_m - (net->stop_depth - 1);
+    size_t j_first = ma;
+    while (j_first > 0 && p.affine[j_first - 1] >= li_stop) --j_first;
+    const float *bl = l0, *bu = u0;
+    int64_t ld = n0, nb = n0;
+    if (j_first > 0) {
+      const int below = (j_first < ma ? p.affine[j_first] : li_m) - 1;
+      nb = net->layers[below].n_out;
+      if (below >= li_stop) {
+        CF_REQUIRE(p.relu_after[j_first - 1] == below, CF_ERR_UNSUPPORTED, "custom stop: layer %d", below);
+        float* lo = reinterpret_cast<float*>(ws + w.box);
+        float* hi = lo + Bc * nb;
+        const int64_t acol = p.col[p.affine[j_first - 1]];
+        CF_TRY(launch_relu_box(Bc, nb, st_l + acol, st_u + acol, N, ra[j_first - 1], rl[j_first - 1],
+                               rm[j_first - 1], lo, hi, st));
+        bl = lo;
+        bu = hi;
+        ld = nb;
+      } else {
+        bl = st_l + p.col[below];
+        bu = st_u + p.col[below];
+        ld = N;
+      }
+    }
+    if (j_first == ma)
+      return launch_concretize_box(Bc, R, nb, A0, 0, a_bs, a_rs, c0, 0, 0, bl, bu, ld, st_l + col, st_u + col, N,
+                                   st);
+    if (chain_applicable(net, p, ma, j_first))
+      return launch_chain_layer(net, p, w, ws, Bc, ma, R, A0, a_bs, a_rs, c0, bl, bu, st_l + col, st_u + col, ra,
+                                rl, rm, st, j_first, ld);
+    const float* cur = A0;
+    int64_t ss = 0, bs = a_bs, rs = a_rs;
+    const float* c = c0;
+    int64_t c_ss = 0, c_bs = 0;
+    int t = 0;
+    for (int64_t j = (int64_t)ma - 1; j >= (int64_t)j_first; --j, ++t) {
+      const cf_layer& Lj = net->layers[p.affine[j]];
+      const int64_t K = Lj.n_out, Nn = Lj.n_in;
+      float* Aout = Abuf[t & 1];
+      float* cout_ = Cbuf[t & 1];
+      CF_TRY(timed_step(Bc, R, K, Nn, cur, ss, bs, rs, c, c_ss, c_bs, ra[j], rl[j], rm[j], Lj.W_dev, Lj.b_dev, Aout,
+                        cout_, scratch, st));
+      cur = Aout;
+      ss = Bc * R * Nn;
+      bs = R * Nn;
+      rs = Nn;
+      c = cout_;
+      c_ss = Bc * R;
+      c_bs = R;
+    }
+    return launch_concretize_box(Bc, R, nb, cur, ss, bs, rs, c, c_ss, c_bs, bl, bu, ld, st_l + col, st_u + col, N,
+                                 st);
   };
 
   // receptive-field windows (conv networks): bound layer a (a == affine.size(): property)
@@ -481,7 +554,9 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
         else
           CF_TRY(launch_concretize_box(Bc, L.n_out, L.n_in, L.W_dev, 0, 0, L.n_in, L.b_dev, 0, 0, st_l + in_col,
                                        st_u + in_col, N, st_l + col, st_u + col, N, st));
-      } else if (p.has_conv)
+      } else if (net->stop_depth > 0)
+        CF_TRY(bound_stopped(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
+      else if (p.has_conv)
         CF_TRY(bound_window(a, col));
       else if (chain_applicable(net, p, a))
         CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
@@ -498,13 +573,18 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
                                   rl[a], rm[a], err + 16 + 2 * a, err, st));
       } else {
         CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a],
-                                 rl[a], rm[a], st));
+                                 rl[a], rm[a], st, net->relaxation == CF_RELAX_DEEPPOLY_STRICT));
       }
     }
   }
   if (net->n_layers < li_begin || net->n_layers >= li_end) return CF_OK;
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
-  if (p.has_conv) {
+  if (net->stop_depth > 0) {
+    const int64_t R = net->n_spec, K = p.n_out_last;
+    CF_TRY(bound_stopped(p.affine.size(), R, specW, R * K, K, nullptr, p.spec_col));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
+    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+  } else if (p.has_conv) {
     const int64_t R = net->n_spec;
     CF_TRY(bound_window(p.affine.size(), p.spec_col));
     CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));

@@ -5,7 +5,7 @@
 namespace cf {
 
 cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
-                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st);
+                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st, bool strict = false);
 
 // CROWN ReLU (whole-layer branch): flags = 2 device ints of scratch, err = device error word.
 cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
@@ -15,6 +15,9 @@ cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* 
 cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
                             const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
+// box (alpha l, lambda u + mu) [B, n] of a ReLU substituted last by a custom-stop traversal
+cf_status launch_relu_box(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, const float* alpha,
+                          const float* lam, const float* mu, float* lo, float* hi, cudaStream_t st);
 // the same with the box rows of region b at l0 + b*ld_box (e.g. a layer's state columns)
 cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                                 int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,

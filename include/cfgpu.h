@@ -87,9 +87,19 @@ enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
  *                      interval bound of its expression over the previous layer's l / u
  *                      (no traversal); the ReLU relaxation is DeepPoly's, from those
  *                      bounds; only the property rows are backsubstituted to the input.
+ *   CF_RELAX_DEEPPOLY_STRICT  deeppoly.cf with the strict lower-slope test of the custom-stop
+ *                      programs (relu_n: l + u > 0, deeppoly_custom_stop.cf:24); the
+ *                      other strict comparisons there give DeepPoly's values.
  * CF_RELAX_ZONO and CF_RELAX_IBP run forward through cf_deeppoly_run as well; their
  * regions are independent (any chunk size). */
-enum { CF_RELAX_DEEPPOLY = 0, CF_RELAX_CROWN = 1, CF_RELAX_ZONO = 2, CF_RELAX_IBP = 3, CF_RELAX_CROWNIBP = 4 };
+enum {
+  CF_RELAX_DEEPPOLY = 0,
+  CF_RELAX_CROWN = 1,
+  CF_RELAX_ZONO = 2,
+  CF_RELAX_IBP = 3,
+  CF_RELAX_CROWNIBP = 4,
+  CF_RELAX_DEEPPOLY_STRICT = 5
+};
 
 /* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
  * Conv: W_dev [cout, cin, kh, kw], b_dev [cout]; neurons in (c, y, x) order,
@@ -112,6 +122,12 @@ typedef struct cf_network {
   int32_t n_input;
   int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
   int32_t relaxation;      /* CF_RELAX_DEEPPOLY, _CROWN, _ZONO, _IBP or _CROWNIBP */
+  int32_t stop_depth;      /* 0: every traversal reaches the input.  d > 0 (CF_RELAX_DEEPPOLY
+                              or _DEEPPOLY_STRICT, linear layers): the custom-stop programs with get_start = d - 1
+                              (examples/compiler_examples/deeppoly_custom_stop.cf:12-17,
+                              custom_stops/): bounding list layer m substitutes list layers
+                              m-1 .. m-(d-1) only and concretises the rest with the bounds
+                              of the layer the expression is then over */
 } cf_network;
 
 /* Total neuron count N of the abstract state: input + every layer + property rows

@@ -80,7 +80,7 @@ def _substitute(blocks, c, t, P, N_poly, lower):
     return new, ((dc + F32(0.0)) + c).astype(F32)
 
 
-def _traverse(blocks, c, polys, lower, order=min):
+def _traverse(blocks, c, polys, lower, order=min, stop_below=None, bnd=None):
     """Backward traversal, lowest live layer first, until no coefficient is left.
 
     The input layer is live from the start (constraintflow/lib/spec.py:134-135) and
@@ -89,14 +89,26 @@ def _traverse(blocks, c, polys, lower, order=min):
     whenever input columns are the lowest live layer, their current coefficients are
     concretised there and then.  The final concretisation (generated ``l_new``) then
     sees an empty matrix and returns the constant.
+
+    stop_below (the custom-stop programs, deeppoly_custom_stop.cf:12-17): neurons of
+    layers below it are not substituted; what remains on them is concretised at the end
+    with their own bounds bnd[t] (map(simplify_lower / simplify_upper)).
     """
     while True:
-        live = [t for t, M in blocks.items() if np.any(M)]
+        live = [t for t, M in blocks.items() if np.any(M) and (stop_below is None or t >= stop_below)]
         if not live:
             break
         t = order(live)
         L, U = polys[t]
         blocks, c = _substitute(blocks, c, t, L, U, lower)
+    if stop_below is not None:
+        for t, M in blocks.items():
+            if t >= stop_below or not np.any(M):
+                continue
+            lo, hi = bnd[t]
+            pos, neg = (lo, hi) if lower else (hi, lo)
+            c = (c + np.einsum('brn,bn->br', np.maximum(M, F32(0)), pos, dtype=F32)
+                 + np.einsum('brn,bn->br', np.minimum(M, F32(0)), neg, dtype=F32)).astype(F32)
     return c
 
 
@@ -180,7 +192,7 @@ def _stack_poly(P, Q, B):
     return blocks, np.concatenate([P[1], Q[1]], axis=1).astype(F32)
 
 
-def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=False):
+def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=False, stop_depth=None):
     """Run the reference's DeepPoly or CROWN program over a network of linear / conv / relu /
     add / concat layers listed in the reference reader's breadth-first order.
 
@@ -193,6 +205,8 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=F
     interval : crownibp.cf -- every affine layer below the property gets the interval
              bound of its polyexp over the previous layer's l / u (``map(simplify_lower)``
              without a traversal); only the property layer is backsubstituted.
+    stop_depth : the custom-stop programs' get_start: the traversal bounding layer k stops at
+             neurons of layers below k - stop_depth and concretises there with their l / u.
     Returns (bounds, lb, ub, branches): bounds per layer (excluding input, including
     the property layer) of (l [B,n], u [B,n]); lb/ub float64 [B, 9]; branches the
     BRANCH_* code of every ReLU layer (CROWN).
@@ -246,13 +260,21 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=F
             res = []
             for lower in (True, False):
                 res.append(_traverse({t: np.array(np.broadcast_to(M, (B,) + M.shape[-2:]), F32)
-                                      for t, M in W_prev.items()}, c0.copy(), polys, lower, order))
+                                      for t, M in W_prev.items()}, c0.copy(), polys, lower, order,
+                                     None if stop_depth is None else k - stop_depth, bnd))
             bnd[k] = (res[0], res[1])
         poly = (W_prev, c0)
         polys[k] = (poly, poly)
     bounds = [bnd[k] for k in range(1, len(layers) + 2)]
     lb, ub = bounds[-1]
     return bounds, lb.astype(np.float64), ub.astype(np.float64), branches
+
+
+def custom_stop(layers, l0, u0, spec_W, depth):
+    """The reference's deeppoly_custom_stop.cf / custom_stops/deeppoly_custom_stopNN.cf:
+    DeepPoly whose traversal for a neuron of layer k stops at layers below k - depth
+    (get_start = depth) and concretises there with those neurons' own bounds."""
+    return certify(layers, l0, u0, spec_W, "deeppoly", min, stop_depth=depth)
 
 
 def crownibp(layers, l0, u0, spec_W, order=max):

@@ -103,6 +103,15 @@ CASES = {
     "cibp_w1_b8_e5e-4": ("crownibp", 1, 8, 0.0005),
     "cibp_w2_b4_e2e-4": ("crownibp", 2, 4, 0.0002),
     "cibp_w3_b2_e2e-3": ("crownibp", 3, 2, 0.002),
+    # deeppoly_custom_stop.cf and custom_stops/: the traversal stops get_start layers below the
+    # bounded neuron and concretises there with those neurons' l / u
+    "cs3_w0_b4_e1e-2": ("deeppoly_custom_stop", 0, 4, 0.01),
+    "cs3_w2_b4_e2e-4": ("deeppoly_custom_stop", 2, 4, 0.0002),
+    "cs0_w0_b4_e1e-3": ("custom_stops/deeppoly_custom_stop00", 0, 4, 0.001),
+    "cs1_w0_b4_e1e-3": ("custom_stops/deeppoly_custom_stop01", 0, 4, 0.001),
+    "cs2_w1_b8_e5e-4": ("custom_stops/deeppoly_custom_stop02", 1, 8, 0.0005),
+    "cs5_w2_b4_e2e-4": ("custom_stops/deeppoly_custom_stop05", 2, 4, 0.0002),
+    "cs8_w2_b4_e2e-4": ("custom_stops/deeppoly_custom_stop08", 2, 4, 0.0002),
 }
 
 

@@ -129,3 +129,32 @@ def test_onnx_reader_orders_breadth_first():
     for a, b in zip(eng, bfs):
         if b.W is not None:
             np.testing.assert_array_equal(a.W.numpy(), b.W)
+
+
+def test_custom_stop_programs_are_recognised():
+    """The reference compiler's output for deeppoly_custom_stop.cf and custom_stops/ runs as
+    DeepPoly with the program's stop depth (get_start) and its strict lower-slope test."""
+    import importlib.util
+    import os
+    import sys
+    from constraintflow.lib.flow_sparse import certifier_of, relu_is_strict, stop_depth_of
+    here = os.path.dirname(os.path.abspath(__file__))
+    for program, depth in (("deeppoly_custom_stop", 3), ("custom_stops/deeppoly_custom_stop00", 0),
+                           ("custom_stops/deeppoly_custom_stop05", 5), ("custom_stops/deeppoly_custom_stop08", 8),
+                           ("deeppoly", None), ("crownibp", None)):
+        path = os.path.join(here, "golden", "generated", program, "transformers.py")
+        saved = sys.modules.pop("transformers", None)
+        try:
+            spec = importlib.util.spec_from_file_location("transformers", path)
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules["transformers"] = mod
+            spec.loader.exec_module(mod)
+            obj = getattr(mod, "crownibp" if program == "crownibp" else "deeppoly")()
+            assert stop_depth_of(obj) == depth
+            assert relu_is_strict(obj) == (depth is not None)
+            if depth is not None:
+                assert certifier_of(obj) == "deeppoly"
+        finally:
+            sys.modules.pop("transformers", None)
+            if saved is not None:
+                sys.modules["transformers"] = saved

@@ -106,3 +106,32 @@ def test_crownibp_planted_backsubstitution_fails():
     xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
     worst, _ = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
     assert worst > 10.0
+
+
+CS_CASES = sorted(n for p in ("deeppoly_custom_stop",) + tuple(f"custom_stops/deeppoly_custom_stop{d:02d}"
+                                                                for d in range(19)) for n in names(p))
+
+
+def _cs_depth(name):
+    return int(name[2:name.index("_")])
+
+
+@pytest.mark.parametrize("name", CS_CASES)
+def test_custom_stop_oracle_matches_reference(name):
+    c = Case(name)
+    bounds, lb, ub, _ = C.custom_stop(c.wl.layers, c.l0, c.u0, c.spec_W, _cs_depth(name))
+    xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
+    assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
+
+
+def test_custom_stop_depth_is_pinned():
+    """The depth is pinned by the reference's outputs: one layer more (a mistake planted in
+    the oracle) breaks every custom-stop case."""
+    assert len(CS_CASES) >= 7 and {_cs_depth(n) for n in CS_CASES} >= {0, 1, 2, 3, 5, 8}
+    for name in CS_CASES:
+        c = Case(name)
+        bounds, _, _, _ = C.custom_stop(c.wl.layers, c.l0, c.u0, c.spec_W, _cs_depth(name) + 1)
+        xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+        assert parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)[0] > 10.0, name
