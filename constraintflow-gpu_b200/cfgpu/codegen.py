@@ -16,6 +16,8 @@ own definitions, which fused kernel family implements each transformer operation
           interval          map(E, G_low), map(E, G_up) without a traversal
           backsubstitution  max(zonotope low, backsubstitution low), min(... up), E, E, Ez
           + zonotope        over the shape (l, u, L, U, Z) (polyzono.cf), either order
+          backsubstitution  the backsubstitution tuple with S(n1, c) = n1[layer] < curr[layer] - d
+          stopped           (the custom-stop programs): the traversal stops d layers down
           interval, then    curr[last_layer] == 1 ? backsubstitution tuple : (map(E, G_low),
           backsubstitution  map(E, G_up), E, E) (crownibp.cf); its traversal may take the
                             highest layer first (the runtime runs it on chains, where the
@@ -26,6 +28,7 @@ own definitions, which fused kernel family implements each transformer operation
           CROWN             if l>=0 pass-through, elif u<=0 zero, else the all-crossing
                             tuple (whole-layer branches, crown.cf:25)
           zonotope          (0, 0, l>=0 ? Z : u<=0 ? 0 : lam Z + (u l / (2 (u-l))) (eps-1))
+          DeepPoly, strict  the same with the lower slope where l + u > 0 (custom-stop programs)
           interval          (relu(l), relu(u))
           DeepPoly          DeepPoly's four members followed by the zonotope's Z member
           + zonotope        over the shape (l, u, L, U, Z)
@@ -315,6 +318,14 @@ def _deeppoly_relu(l, u):
     return [max(l, 0.0), max(u, 0.0), x if lu else Form(), up]
 
 
+def _deeppoly_relu_strict(l, u):
+    """DeepPoly's Relu with relu_n testing l + u > 0 (the custom-stop programs)."""
+    out = _deeppoly_relu(l, u)
+    if l + u == 0.0:
+        out[2] = Form()
+    return out
+
+
 def _zono_relu(l, u):
     z = Form({"Z": 1.0})
     if l >= 0.0:
@@ -419,7 +430,39 @@ def _sign_choice(prog, fname, pos, neg):
     return True
 
 
-def _check_backsub_member(prog, n, lower, any_order=False):
+_BAD = object()
+
+
+def _stop_depth(prog, stop):
+    """None when the traversal's stop is false for every neuron; d when it is a partial
+    application stop_f(curr-dependent arguments) whose value for a neuron n1 is
+    n1[layer] < curr[layer] - d (the custom-stop programs, deeppoly_custom_stop.cf:12-17);
+    _BAD otherwise."""
+    if _kind(stop) == "VarNode":
+        return None if _Eval(prog, {}).call(_name(stop), [Neuron(0, 1, layer=1), 1.0]) is False else _BAD
+    if _kind(stop) != "FuncCallNode":
+        return _BAD
+    depths = set()
+    for K in (200, 233):   # layers of the bounded neuron; depths below K are identified
+        bound = [_val(_Eval(prog, {"curr": Neuron(0, 1, layer=float(K))}).ev(a)) for a in stop.arglist.exprlist]
+        flags = [_Eval(prog, {}).call(_name(stop.name), bound + [Neuron(0, 1, layer=float(L)), 1.0])
+                 for L in range(K)]
+        if not all(isinstance(f, bool) for f in flags):
+            return _BAD
+        d = K - sum(flags)
+        if flags != [L < K - d for L in range(K)]:
+            return _BAD
+        depths.add(d)
+    if len(depths) != 1:
+        return _BAD
+    return int(depths.pop())
+
+
+def _check_backsub_member(prog, n, lower, any_order=False, depth_out=None):
+    """n is map(traverse(E; backward, P, S, R), G) with E = prev . weight + bias, P taking
+    the lowest layer first (or either order with any_order), R / G choosing L / U and l / u
+    by the coefficient sign, and S never stopping -- or, when depth_out is given, stopping
+    below curr[layer] - d (d appended to depth_out)."""
     n = _inline_call(prog, n)
     if _kind(n) != "MapNode" or _kind(n.expr) != "TraverseNode":
         return False
@@ -432,8 +475,11 @@ def _check_backsub_member(prog, n, lower, any_order=False):
     p2 = ev.call(_name(t.priority), [Neuron(0, 1, layer=2), 1.0])
     if not (isinstance(p1, float) and isinstance(p2, float) and (p1 > p2 or (any_order and p1 < p2))):
         return False
-    if ev.call(_name(t.stop), [Neuron(0, 1, layer=1), 1.0]) is not False:
+    depth = _stop_depth(prog, t.stop)
+    if depth is _BAD or (depth is not None and depth_out is None):
         return False
+    if depth_out is not None:
+        depth_out.append(depth)
     pos, neg = ("L", "U") if lower else ("U", "L")
     bpos, bneg = ("l", "u") if lower else ("u", "l")
     return _sign_choice(prog, _name(t.func), pos, neg) and _sign_choice(prog, _name(n.func), bpos, bneg)
@@ -505,9 +551,15 @@ def _classify_affine(prog, ret):
             return "backsub+zonotope"
         return None
     if names == ["l", "u", "L", "U"]:
-        if (_check_backsub_member(prog, exprs[0], True) and _check_backsub_member(prog, exprs[1], False)
-                and _affine_expr_ok(prog, exprs[2], "") and _affine_expr_ok(prog, exprs[3], "")):
-            return "backsub"
+        depths = []
+        if (_check_backsub_member(prog, exprs[0], True, depth_out=depths)
+                and _check_backsub_member(prog, exprs[1], False, depth_out=depths)
+                and _affine_expr_ok(prog, exprs[2], "") and _affine_expr_ok(prog, exprs[3], "")
+                and depths[0] == depths[1]):
+            if depths[0] is None:
+                return "backsub"
+            prog.stop_depth = depths[0]
+            return "backsub-stop"
         return None
     if names == ["l", "u", "Z"]:
         if (_zono_bound(prog, exprs[0], True) and _zono_bound(prog, exprs[1], False)
@@ -529,7 +581,9 @@ def _classify_relu(prog, ret):
         if names == ["l", "u", "L", "U"]:
             if _kind(ret) == "TransRetIfNode":
                 return "crown" if _check_crown_relu(prog, ret) else None
-            return "deeppoly" if _check_relu_basic(prog, ret, _deeppoly_relu, merge=True) else None
+            if _check_relu_basic(prog, ret, _deeppoly_relu, merge=True):
+                return "deeppoly"
+            return "deeppoly-strict" if _check_relu_basic(prog, ret, _deeppoly_relu_strict, merge=True) else None
         if names == ["l", "u", "Z"]:
             return "zonotope" if _check_relu_basic(prog, ret, _zono_relu, merge=False) else None
         if names == ["l", "u", "L", "U", "Z"]:
@@ -545,12 +599,15 @@ def _classify_relu(prog, ret):
 # certifier = (Affine family, Relu family)
 _CERTIFIERS = {("backsub", "deeppoly"): "deeppoly", ("backsub", "crown"): "crown",
                ("zonotope", "zonotope"): "zono", ("interval", "interval"): "ibp",
-               ("backsub+zonotope", "deeppoly+zonotope"): "polyzono", ("interval+backsub", "deeppoly"): "crownibp"}
+               ("backsub+zonotope", "deeppoly+zonotope"): "polyzono", ("interval+backsub", "deeppoly"): "crownibp",
+               ("backsub", "deeppoly-strict"): "deeppoly", ("backsub-stop", "deeppoly"): "deeppoly",
+               ("backsub-stop", "deeppoly-strict"): "deeppoly"}
 
 
 class Analysis:
-    def __init__(self, name, certifier, shape, ops):
+    def __init__(self, name, certifier, shape, ops, stop_depth=None, relu_strict=False):
         self.name, self.certifier, self.shape, self.ops = name, certifier, shape, ops
+        self.stop_depth, self.relu_strict = stop_depth, relu_strict
 
 
 def analyse(ast):
@@ -578,7 +635,8 @@ def analyse(ast):
     kinds = {"Affine": affine, "Relu": relu}
     for op in ops:
         kinds.setdefault(op, None)
-    return Analysis(name, cert, prog.shape, kinds)
+    return Analysis(name, cert, prog.shape, kinds, stop_depth=getattr(prog, "stop_depth", None)
+                    if affine == "backsub-stop" else None, relu_strict=relu == "deeppoly-strict")
 
 
 # ------------------------------------------------------------------ emission
@@ -592,6 +650,8 @@ _DOC = {"backsub": "backsubstitution of the layer's coefficient rows down to the
         "backsub+zonotope": "backsubstitution and zonotope step, bounds met (max / min)",
         "deeppoly+zonotope": "DeepPoly and zonotope relaxations from the met bounds",
         "interval+backsub": "interval bound; backsubstitution for the property layer only",
+        "backsub-stop": "backsubstitution stopped below curr[layer] - get_start, concretised there",
+        "deeppoly-strict": "DeepPoly triangle relaxation, lower slope where l + u > 0",
         None: "no fused kernel"}
 
 
@@ -605,7 +665,12 @@ def generate(ast, source_name="program.cf"):
              "from cfgpu import layerwise", "", "",
              f"class {a.name}:",
              f"    cf_certifier = {a.certifier!r}",
-             "    cf_layerwise = True", ""]
+             "    cf_layerwise = True"]
+    if a.stop_depth is not None:
+        lines.append(f"    cf_stop_depth = {a.stop_depth!r}")
+    if a.relu_strict:
+        lines.append("    cf_relu_strict = True")
+    lines.append("")
     for op, kind in a.ops.items():
         lines.append(f"    def {op}({_SIG}):")
         lines.append(f"        # {_DOC.get(kind, kind)}")

@@ -26,7 +26,7 @@ REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 # the programs the backend runs, then programs it must refuse (other traversal order,
 # ReLU relaxation or domain), then programs the reference front end itself refuses
-PROGRAMS = ("deeppoly", "deeppoly_efficient", "crown", "zono", "ibp", "polyzono", "crownibp",
+PROGRAMS = ("deeppoly", "deeppoly_efficient", "crown", "zono", "ibp", "polyzono", "crownibp", "deeppoly_custom_stop",
             "deeppoly_priority", "deeppolyh", "zono2", "ibp2",
             "deeppoly2", "hybrid_zono")
 

@@ -18,7 +18,7 @@ sys.path.insert(0, GOLDEN)
 import ast_json  # noqa: E402
 
 RUNS = {"deeppoly": "deeppoly", "deeppoly_efficient": "deeppoly", "crown": "crown", "zono": "zono", "ibp": "ibp",
-        "polyzono": "polyzono", "crownibp": "crownibp"}
+        "polyzono": "polyzono", "crownibp": "crownibp", "deeppoly_custom_stop": "deeppoly"}
 REFUSED = ("deeppoly_priority", "deeppolyh", "zono2", "ibp2")
 
 
@@ -31,7 +31,8 @@ def _ast(prog):
 def test_backend_recognises_program(prog):
     a = codegen.analyse(_ast(prog))
     assert a.certifier == RUNS[prog]
-    assert a.ops["Affine"] in ("backsub", "zonotope", "interval", "backsub+zonotope", "interval+backsub")
+    assert a.ops["Affine"] in ("backsub", "zonotope", "interval", "backsub+zonotope", "interval+backsub",
+                               "backsub-stop")
     assert a.ops["Relu"] is not None
 
 
@@ -147,6 +148,24 @@ def test_planted_crownibp_mistakes_are_refused(mistake):
     elif mistake == "property_replace":    # replace_lower(n, c) = c >= 0 ? c * n[U] : c * n[U]
         f["replace_lower"].expr.texpr.right.elem.name = "U"
     assert codegen.analyse(copy.deepcopy(_ast("crownibp"))).certifier == "crownibp"
+    with pytest.raises(codegen.CodegenError) as e:
+        codegen.analyse(ast)
+    assert "Affine (unrecognised)" in str(e.value)
+
+
+def test_custom_stop_depth_and_strict_relu():
+    """deeppoly_custom_stop.cf: the traversal stops get_start = 3 layers down and relu_n tests
+    l + u > 0; the emitted transformer declares both.  With the stop's comparison planted
+    the other way (the top layers stop instead) the backend refuses the program."""
+    a = codegen.analyse(_ast("deeppoly_custom_stop"))
+    assert (a.certifier, a.stop_depth, a.relu_strict) == ("deeppoly", 3, True)
+    text = codegen.generate(_ast("deeppoly_custom_stop"))["transformers.py"]
+    assert "cf_stop_depth = 3" in text and "cf_relu_strict = True" in text
+    plain = codegen.analyse(_ast("deeppoly"))
+    assert (plain.stop_depth, plain.relu_strict) == (None, False)
+    ast = copy.deepcopy(_ast("deeppoly_custom_stop"))
+    f = _funcs(ast)
+    f["stop_traverse"].expr.op = ">"
     with pytest.raises(codegen.CodegenError) as e:
         codegen.analyse(ast)
     assert "Affine (unrecognised)" in str(e.value)

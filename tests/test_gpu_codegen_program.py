@@ -42,7 +42,8 @@ CASES = [("deeppoly", "dp_w0_b4_e1e-3"), ("deeppoly", "dp_w2_b8_e2e-4"), ("deepp
          ("deeppoly_efficient", "dpe_w2_b4_e2e-4"), ("crown", "crown_w0_b4_e1e-3"), ("crown", "crown_w1_b2_e1e-1"),
          ("zono", "zono_w2_b4_e2e-3"), ("zono", "zono_w3_b2_e2e-3"), ("ibp", "ibp_w3_b2_e2e-3"),
          ("deeppoly", "dp_w5_b4_e2e-3"), ("polyzono", "pz_w0_b4_e1e-2"), ("polyzono", "pz_w2_b4_e2e-3"),
-         ("crownibp", "cibp_w1_b8_e5e-4"), ("crownibp", "cibp_w3_b2_e2e-3")]
+         ("crownibp", "cibp_w1_b8_e5e-4"), ("crownibp", "cibp_w3_b2_e2e-3"),
+         ("deeppoly_custom_stop", "cs3_w2_b4_e2e-4"), ("deeppoly_custom_stop", "cs3_w0_b4_e1e-2")]
 
 
 @pytest.mark.parametrize("program,name", CASES)
