@@ -2,7 +2,8 @@
 """Benchmark: certified input regions/sec (DeepPoly, whole input box) on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cfgpu|reference] [--workload 2]
-                    [--certifier deeppoly|crown|zono|ibp|polyzono|crownibp] [--batch B]
+                    [--certifier deeppoly|crown|zono|ibp|polyzono|crownibp|custom_stop]
+                    [--stop-depth D] [--batch B]
 
 One step = one whole DeepPoly pass (input box, property matrix, every layer's
 backsubstitution down to the input, final bounds) over one batch of regions of the
@@ -52,8 +53,11 @@ def parse():
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
     ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp", "polyzono",
-                                                                  "crownibp"],
-                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf, crownibp.cf)")
+                                                                  "crownibp", "custom_stop"],
+                    help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf, crownibp.cf, "
+                         "deeppoly_custom_stop.cf)")
+    ap.add_argument("--stop-depth", type=int, default=3,
+                    help="get_start of --certifier custom_stop (3: deeppoly_custom_stop.cf)")
     return ap.parse_args()
 
 
@@ -169,14 +173,15 @@ CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
 
 
 METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)",
-          "polyzono": "polyzono (DeepPoly met with the zonotope)", "crownibp": "CROWN-IBP (crownibp.cf)"}
+          "polyzono": "polyzono (DeepPoly met with the zonotope)", "crownibp": "CROWN-IBP (crownibp.cf)",
+          "custom_stop": "DeepPoly with a custom traversal stop"}
 
 
 def _metric(certifier):
     return f"certified input regions/sec ({METRIC[certifier]}, whole box)"
 
 
-def _oracle_fn(wl, certifier="deeppoly"):
+def _oracle_fn(wl, certifier="deeppoly", stop_depth=3):
     """The oracle for the workload and program: the chain DeepPoly oracle, the general one
     (CROWN, or a network with Add / Concat layers), or the zonotope / interval one."""
     if certifier in ("zono", "ibp", "polyzono"):
@@ -192,6 +197,9 @@ def _oracle_fn(wl, certifier="deeppoly"):
     if certifier == "crownibp":
         from oracle import crown_oracle as C
         return lambda l0, u0, W: C.crownibp(wl.layers, l0, u0, W)
+    if certifier == "custom_stop":
+        from oracle import crown_oracle as C
+        return lambda l0, u0, W: C.custom_stop(wl.layers, l0, u0, W, stop_depth)
     if nets.is_chain(wl.layers):
         from oracle import deeppoly_oracle as O
         return lambda l0, u0, W: O.deeppoly(wl.layers, l0, u0, W)
@@ -199,9 +207,9 @@ def _oracle_fn(wl, certifier="deeppoly"):
     return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "deeppoly")
 
 
-def cpu_baseline(wl, sample, reps=3, certifier="deeppoly"):
+def cpu_baseline(wl, sample, reps=3, certifier="deeppoly", stop_depth=3):
     """Oracle (numpy float32, all host threads) on `sample` regions of the workload: regions/s."""
-    fn = _oracle_fn(wl, certifier)
+    fn = _oracle_fn(wl, certifier, stop_depth)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
@@ -225,7 +233,7 @@ def run_reference(args, rank, world):
                           "net (dense conv rows), beyond a bounded per-step sample"}))
         return
     sample = CPU_SAMPLE[args.workload]
-    fn = _oracle_fn(wl, args.certifier)
+    fn = _oracle_fn(wl, args.certifier, args.stop_depth)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
@@ -246,7 +254,8 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": _metric(args.certifier), "value": val,
         "unit": "regions/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_step": sample, "eps": wl.eps},
+        "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_step": sample, "eps": wl.eps,
+                   **({"stop_depth": args.stop_depth} if args.certifier == "custom_stop" else {})},
         "cpu_baseline": {"value": val, "unit": "regions/s", "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": val, "unit": "regions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
@@ -266,6 +275,8 @@ def run_cfgpu(args, rank, world, local):
     if args.certifier == "polyzono":
         from cfgpu.polyzono import PolyZonoEngine
         eng = PolyZonoEngine(wl.layers, wl.input_size, dev)
+    elif args.certifier == "custom_stop":
+        eng = DeepPolyEngine(wl.layers, wl.input_size, dev, stop_depth=args.stop_depth, relu_strict=True)
     else:
         eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=args.certifier)
     Xd, yd = X.to(dev), y.to(dev)
@@ -371,6 +382,7 @@ def run_cfgpu(args, rank, world, local):
         "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_gpu": B,
+                   **({"stop_depth": args.stop_depth} if args.certifier == "custom_stop" else {}),
                    "global_regions": B * world, "eps": wl.eps,
                    "parallelism": f"regions sharded over {world} GPU(s)", "l2": "flushed between timed steps",
                    "certified": int(certified.item())},
@@ -412,7 +424,7 @@ def run_cfgpu(args, rank, world, local):
                                "sample": "not timed: the oracle port needs ~385 s per region of this net"}
     elif world == 1:
         sample = CPU_SAMPLE[args.workload]
-        v, t1 = cpu_baseline(wl, sample, certifier=args.certifier)
+        v, t1 = cpu_baseline(wl, sample, certifier=args.certifier, stop_depth=args.stop_depth)
         out["cpu_baseline"] = {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
                                "sample": f"oracle numpy float32, {sample} regions of {wl.name}, median of 3 "
                                          f"({t1:.2f} s each)"}
