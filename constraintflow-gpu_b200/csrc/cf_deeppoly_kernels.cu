@@ -177,10 +177,10 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
 // each region's box) are two sign-split GEMMs [B, n0] x [n0, R]:
 //   out_l[b,i] = c[i] + sum_n W+[i,n] l0[b,n] + W-[i,n] u0[b,n]
 //   out_u[b,i] = c[i] + sum_n W+[i,n] u0[b,n] + W-[i,n] l0[b,n]
-// CTA tile: 32 rows x 32 regions (a 200-row layer and 256 regions give 56 CTAs), 32-wide
+// CTA tile: 16 rows x 16 regions (a 200-row layer and 256 regions give 208 CTAs), 32-wide
 // k slices of W (split into W+ / W-) and of both boxes in shared memory; 16x16 threads,
-// 2 rows x 2 regions x 2 bounds each.
-constexpr int kCbT = 32, kCbK = 32, kCbM = kCbT / 16;
+// one row x one region x 2 bounds each.
+constexpr int kCbT = 16, kCbK = 32, kCbM = kCbT / 16;
 __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
                                                           int64_t a_rs, const float* __restrict__ c,
                                                           const float* __restrict__ l0, const float* __restrict__ u0,
