@@ -53,9 +53,9 @@ def parse():
     ap.add_argument("--workload", type=int, default=2)
     ap.add_argument("--batch", type=int, default=0, help="regions per GPU (default: the workload's batch)")
     ap.add_argument("--certifier", default="deeppoly", choices=["deeppoly", "crown", "zono", "ibp", "polyzono",
-                                                                  "crownibp", "custom_stop"],
+                                                                  "crownibp", "custom_stop", "zid"],
                     help="certifier program (deeppoly.cf, crown.cf, zono.cf, ibp.cf, polyzono.cf, crownibp.cf, "
-                         "deeppoly_custom_stop.cf)")
+                         "deeppoly_custom_stop.cf, zid.cf)")
     ap.add_argument("--stop-depth", type=int, default=3,
                     help="get_start of --certifier custom_stop (3: deeppoly_custom_stop.cf)")
     return ap.parse_args()
@@ -174,7 +174,7 @@ CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
 
 METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)",
           "polyzono": "polyzono (DeepPoly met with the zonotope)", "crownibp": "CROWN-IBP (crownibp.cf)",
-          "custom_stop": "DeepPoly with a custom traversal stop"}
+          "custom_stop": "DeepPoly with a custom traversal stop", "zid": "zid (zonotope, interval, DeepPoly)"}
 
 
 def _metric(certifier):
@@ -184,10 +184,12 @@ def _metric(certifier):
 def _oracle_fn(wl, certifier="deeppoly", stop_depth=3):
     """The oracle for the workload and program: the chain DeepPoly oracle, the general one
     (CROWN, or a network with Add / Concat layers), or the zonotope / interval one."""
-    if certifier in ("zono", "ibp", "polyzono"):
+    if certifier in ("zono", "ibp", "polyzono", "zid"):
         from oracle import zono_oracle as Z
         if certifier == "polyzono":
             return lambda l0, u0, W: Z.polyzono(wl.layers, l0, u0, W)
+        if certifier == "zid":
+            return lambda l0, u0, W: Z.zid(wl.layers, l0, u0, W)
         if certifier == "zono":
             return lambda l0, u0, W: Z.zono(wl.layers, l0, u0, W)
         return lambda l0, u0, W: Z.ibp(wl.layers, l0, u0, W)
@@ -275,6 +277,9 @@ def run_cfgpu(args, rank, world, local):
     if args.certifier == "polyzono":
         from cfgpu.polyzono import PolyZonoEngine
         eng = PolyZonoEngine(wl.layers, wl.input_size, dev)
+    elif args.certifier == "zid":
+        from cfgpu.zid import ZidEngine
+        eng = ZidEngine(wl.layers, wl.input_size, dev)
     elif args.certifier == "custom_stop":
         eng = DeepPolyEngine(wl.layers, wl.input_size, dev, stop_depth=args.stop_depth, relu_strict=True)
     else:

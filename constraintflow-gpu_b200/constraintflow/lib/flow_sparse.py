@@ -27,6 +27,8 @@ get_new_eps); it runs as cfgpu.polyzono's coupled DeepPoly and zonotope passes.
 crownibp.cf branches its Affine on the last_layer metadata: interval bounds below the
 property (map(simplify_lower) over the previous layer's l / u), the traversal for the
 property rows; its Relu is DeepPoly's.
+zid.cf branches on last_layer and on curr[layer] <= 4: zonotope bounds up to layer 4,
+interval bounds above, the traversal for the property rows (cfgpu.zid).
 The custom-stop DeepPoly programs (deeppoly_custom_stop.cf, custom_stops/) stop their
 traversal at layers below curr[layer] - get_start: the generated Affine subtracts the
 constant get_start from the layer metadata (stop_depth_of), and the driver runs DeepPoly
@@ -71,6 +73,23 @@ _STOP_DEPTH = re.compile(r"curr\.get_metadata\('layer'[^)]*\), SparseTensor\(\[\
                          r"operator\.sub")
 
 
+_ZID_UPTO = re.compile(r"curr\.get_metadata\('layer'[^)]*\), SparseTensor\(\[\], \[\], 0, torch\.tensor\(\[\]\), "
+                       r"dense_const=(\d+), type= type\(\d+\)\)(?:\.\w+\([^()]*(?:\([^()]*\))?[^()]*\))*, "
+                       r"operator\.le")
+
+
+def zid_upto_of(transformer):
+    """The layer up to which zid.cf bounds neurons by the zonotope (curr[layer] <= 4,
+    zid.cf:38): declared by ``cf_zono_upto`` or read from the generated Affine."""
+    declared = getattr(transformer, "cf_zono_upto", None)
+    if declared is not None:
+        return int(declared)
+    found = {int(m) for m in _ZID_UPTO.findall(inspect.getsource(type(transformer).Affine))}
+    if len(found) != 1:
+        raise NotImplementedError(f"zid-style program with layer thresholds {sorted(found)}")
+    return found.pop()
+
+
 def stop_depth_of(transformer):
     """get_start of a custom-stop DeepPoly program (the traversal bounding a neuron of layer
     k stops below layer k - get_start, deeppoly_custom_stop.cf:12-17), None for a traversal
@@ -105,8 +124,8 @@ def relu_is_strict(transformer):
 
 
 def certifier_of(transformer):
-    """'deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp' for a recognised generated
-    transformer, else raises."""
+    """'deeppoly', 'crown', 'zono', 'ibp', 'polyzono', 'crownibp' or 'zid' for a recognised
+    generated transformer, else raises."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
@@ -116,6 +135,11 @@ def certifier_of(transformer):
         affine = inspect.getsource(cls.Affine)
     except (AttributeError, OSError, TypeError) as e:
         raise NotImplementedError(f"cannot read the generated transformer: {e}")
+    if (all(k in affine for k in ("get_metadata('last_layer'", "get_metadata('layer'", "get_elem('Z', prev",
+                                   "get_max_priority(", "clamp(", "inner_prod("))
+            and all(k in relu for k in ("get_metadata('last_layer'", "get_new_eps(", "convert_to_poly(",
+                                        "get_elem('Z', prev"))):
+        return "zid"
     if all(k in affine for k in _POLYZONO_AFFINE) and all(k in relu for k in _POLYZONO_RELU):
         if "if(" in relu or "any(" in relu:
             raise NotImplementedError("a polyzono-style program with whole-layer branches")
@@ -138,7 +162,7 @@ def certifier_of(transformer):
             and "get_new_eps(" not in relu and "convert_to_poly(" not in relu and not branches):
         return "ibp"
     raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf), interval (ibp.cf), "
-                              "polyzono.cf and crownibp.cf certifier programs; the given "
+                              "polyzono.cf, crownibp.cf and zid.cf certifier programs; the given "
                               f"transformer ({cls.__name__}) is a different program")
 
 
@@ -208,6 +232,10 @@ class Flow:
         if certifier == "polyzono":
             from cfgpu.polyzono import PolyZonoEngine
             eng = PolyZonoEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]))
+        elif certifier == "zid":
+            from cfgpu.zid import ZidEngine
+            eng = ZidEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]),
+                            zono_upto=zid_upto_of(self.transformer))
         else:
             eng = DeepPolyEngine(engine_layers(self.model), n0, dev, n_spec=int(W.shape[1]), certifier=certifier,
                                  stop_depth=stop_depth_of(self.transformer) if certifier == "deeppoly" else None,
@@ -235,7 +263,8 @@ class Flow:
         layer in order (as flow_sparse.py:27-228 does), each one fused libcfgpu call."""
         from cfgpu.layerwise import LayerRun
         from cfgpu.polyzono import PolyZonoRun
-        run = PolyZonoRun(eng, l0, u0, W) if eng.certifier == "polyzono" else LayerRun(eng, l0, u0, W)
+        from cfgpu.zid import ZidRun
+        run = {"polyzono": PolyZonoRun, "zid": ZidRun}.get(eng.certifier, LayerRun)(eng, l0, u0, W)
         self.abs_elem.cf_run = run
         B = self.batch_size
         try:

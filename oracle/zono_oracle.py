@@ -280,3 +280,55 @@ def polyzono(layers, l0, u0, spec_W):
     bounds = [bnd[k] for k in range(1, len(layers) + 2)]
     lb, ub = bounds[-1]
     return bounds, lb.astype(np.float64), ub.astype(np.float64)
+
+
+def zid(layers, l0, u0, spec_W, zono_upto=4):
+    """Run zid.cf over a chain network (examples/compiler_examples/zid.cf:30-78): list layers
+    with reference index <= 4 (the input is 0) bound their neurons by the zonotope (the
+    affine's concretisation; the ReLU carries Z as zono.cf does), layers above by the
+    interval over the previous layer's l / u (map(simplify_lower)), and the property rows
+    by the DeepPoly traversal (priority2 = -layer) through the polyexps of every layer.
+    Every ReLU layer takes DeepPoly's relaxation from its input's bounds; relu_n tests
+    l + u > 0 there, which differs from the l + u >= 0 used here only at l + u == 0.
+    Returns (bounds, lb, ub)."""
+    from .crown_oracle import _deeppoly_relu, _traverse
+    from .deeppoly_oracle import _affine_rows
+    l0 = np.asarray(l0, F32)
+    u0 = np.asarray(u0, F32)
+    B = l0.shape[0]
+    polys = {0: (({}, l0), ({}, u0))}
+    bnd = {0: (l0, u0)}
+    M, c = create_z(l0, u0)
+    E = M.shape[2]
+    for idx, L in enumerate(list(layers) + ['spec']):
+        k = idx + 1
+        kind = 'spec' if L == 'spec' else L.kind
+        pl, pu = bnd[k - 1]
+        if kind == 'relu':
+            polys[k], bnd[k] = _deeppoly_relu(pl, pu, k - 1, B)
+            if k <= zono_upto:
+                M, c = zono_relu(pl, pu, _widen(M, E), c)
+                E = M.shape[2]
+            continue
+        if kind == 'spec':
+            A0 = np.asarray(spec_W, F32)
+            c0 = np.zeros((B, A0.shape[1]), F32)
+            W_prev = {k - 1: A0}
+            res = [_traverse({t: np.array(np.broadcast_to(X, (B,) + X.shape[-2:]), F32) for t, X in W_prev.items()},
+                             c0.copy(), polys, lower) for lower in (True, False)]
+            bnd[k] = (res[0], res[1])
+            continue
+        A0 = np.ascontiguousarray(_affine_rows(L, 0, L.n_out, B)[0])
+        c0 = np.broadcast_to(layer_bias(L), (B, L.n_out)).astype(F32)
+        if k <= zono_upto:
+            lz, uz, M, c = zono_affine(_widen(M, E), c, weight_matrix(L), _bias(L))
+            E = M.shape[2]
+            bnd[k] = (lz, uz)
+        else:
+            Wp, Wn = np.maximum(A0, F32(0)), np.minimum(A0, F32(0))
+            bnd[k] = ((pl @ Wp.T + pu @ Wn.T + c0).astype(F32), (pu @ Wp.T + pl @ Wn.T + c0).astype(F32))
+        poly = ({k - 1: A0[None]}, c0)
+        polys[k] = (poly, poly)
+    bounds = [bnd[k] for k in range(1, len(layers) + 2)]
+    lb, ub = bounds[-1]
+    return bounds, lb.astype(np.float64), ub.astype(np.float64)

@@ -112,6 +112,12 @@ CASES = {
     "cs2_w1_b8_e5e-4": ("custom_stops/deeppoly_custom_stop02", 1, 8, 0.0005),
     "cs5_w2_b4_e2e-4": ("custom_stops/deeppoly_custom_stop05", 2, 4, 0.0002),
     "cs8_w2_b4_e2e-4": ("custom_stops/deeppoly_custom_stop08", 2, 4, 0.0002),
+    # zid.cf: zonotope bounds for list layers up to 4, interval bounds above, DeepPoly for the
+    # property rows
+    "zid_w0_b4_e1e-2": ("zid", 0, 4, 0.01),
+    "zid_w2_b4_e2e-3": ("zid", 2, 4, 0.002),
+    "zid_w1_b8_e5e-4": ("zid", 1, 8, 0.0005),
+    "zid_w3_b2_e2e-3": ("zid", 3, 2, 0.002),
 }
 
 

@@ -47,7 +47,7 @@ def test_generated_programs_are_recognised():
     here = os.path.dirname(os.path.abspath(__file__))
     for program, expect in (("deeppoly", "deeppoly"), ("deeppoly_efficient", "deeppoly"), ("crown", "crown"),
                             ("zono", "zono"), ("ibp", "ibp"), ("polyzono", "polyzono"), ("crownibp", "crownibp"),
-                            ("zono2", None)):
+                            ("zid", "zid"), ("zono2", None)):
         path = os.path.join(here, "golden", "generated", program, "transformers.py")
         saved = sys.modules.pop("transformers", None)
         try:
@@ -55,7 +55,7 @@ def test_generated_programs_are_recognised():
             mod = importlib.util.module_from_spec(spec)
             sys.modules["transformers"] = mod
             spec.loader.exec_module(mod)
-            cls = getattr(mod, program if program in ("ibp", "polyzono", "crownibp") else
+            cls = getattr(mod, program if program in ("ibp", "polyzono", "crownibp", "zid") else
                           "zono" if program.startswith("zono") else "deeppoly")
             if expect is None:
                 with pytest.raises(NotImplementedError):

@@ -52,7 +52,8 @@ PROGRAM_CASES = [("deeppoly", n) for n in ("dp_w0_b4_e1e-3", "dp_w1_b16_e5e-4", 
     [("ibp", n) for n in ("ibp_w0_b4_e1e-3", "ibp_w3_b2_e2e-3")] + \
     [("polyzono", n) for n in ("pz_w0_b4_e1e-2", "pz_w2_b4_e2e-4")] + \
     [("crownibp", n) for n in ("cibp_w0_b4_e1e-3", "cibp_w3_b2_e2e-3")] + \
-    [("deeppoly_custom_stop", "cs3_w2_b4_e2e-4"), ("custom_stops/deeppoly_custom_stop05", "cs5_w2_b4_e2e-4")]
+    [("deeppoly_custom_stop", "cs3_w2_b4_e2e-4"), ("custom_stops/deeppoly_custom_stop05", "cs5_w2_b4_e2e-4")] + \
+    [("zid", "zid_w2_b4_e2e-3"), ("zid", "zid_w3_b2_e2e-3")]
 
 
 @pytest.mark.parametrize("program,name", PROGRAM_CASES)

@@ -20,6 +20,7 @@ pytestmark = pytest.mark.gpu
 CHAIN_ZONO = [n for n in names("zono", max_wid=9) if nets.is_chain(Case(n).wl.layers)]
 CHAIN_IBP = [n for n in names("ibp", max_wid=9) if nets.is_chain(Case(n).wl.layers)]
 PZ = names("polyzono", max_wid=9)
+ZID = names("zid", max_wid=9)
 
 
 def _engine(wl, certifier):
@@ -27,6 +28,9 @@ def _engine(wl, certifier):
     if certifier == "polyzono":
         from cfgpu.polyzono import PolyZonoEngine
         return PolyZonoEngine(wl.layers, wl.input_size, "cuda:0")
+    if certifier == "zid":
+        from cfgpu.zid import ZidEngine
+        return ZidEngine(wl.layers, wl.input_size, "cuda:0")
     return DeepPolyEngine(wl.layers, wl.input_size, "cuda:0", certifier=certifier)
 
 
@@ -43,10 +47,12 @@ def _oracle(program, layers, l0, u0, W):
         return Z.ibp(layers, l0, u0, W)[0]
     if program == "polyzono":
         return Z.polyzono(layers, l0, u0, W)[0]
+    if program == "zid":
+        return Z.zid(layers, l0, u0, W)[0]
     return Z.zono(layers, l0, u0, W)[0]
 
 
-@pytest.mark.parametrize("name", CHAIN_ZONO + CHAIN_IBP + PZ)
+@pytest.mark.parametrize("name", CHAIN_ZONO + CHAIN_IBP + PZ + ZID)
 def test_gpu_forward_matches_reference(name):
     c = Case(name)
     lb, ub, sl, su = _run(_engine(c.wl, c.program), c.l0, c.u0, c.spec_W)
@@ -65,7 +71,8 @@ def test_gpu_forward_matches_reference(name):
 
 @pytest.mark.parametrize("certifier,wid,B,eps", [("zono", 2, 256, 0.002), ("zono", 1, 64, 0.005),
                                                  ("ibp", 4, 8, 2.0 / 255.0), ("zono", 3, 128, 0.02),
-                                                 ("polyzono", 1, 64, 0.005), ("polyzono", 3, 32, 0.02)])
+                                                 ("polyzono", 1, 64, 0.005), ("polyzono", 3, 32, 0.02),
+                                                 ("zid", 2, 256, 0.002), ("zid", 3, 32, 0.02)])
 def test_gpu_forward_full_size_sound(certifier, wid, B, eps):
     """The workload's full batch: concrete points of every box (its corners included) stay
     inside the bounds of every affine layer and of the property rows; the first regions

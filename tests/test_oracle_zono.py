@@ -16,6 +16,7 @@ from cfgpu import nets
 ZONO_CASES = names("zono", max_wid=9) + names("zono2", max_wid=9)
 IBP_CASES = names("ibp", max_wid=9)
 PZ_CASES = names("polyzono", max_wid=9)
+ZID_CASES = names("zid", max_wid=9)
 
 
 def _run(c, program=None, relu=None):
@@ -25,6 +26,9 @@ def _run(c, program=None, relu=None):
         br = None
     elif program == "polyzono":
         bounds, lb, ub = Z.polyzono(c.wl.layers, c.l0, c.u0, c.spec_W)
+        br = None
+    elif program == "zid":
+        bounds, lb, ub = Z.zid(c.wl.layers, c.l0, c.u0, c.spec_W)
         br = None
     else:
         saved = Z.zono_relu
@@ -44,7 +48,7 @@ def test_cases_present():
     assert len(PZ_CASES) >= 4 and {Case(n).wid for n in PZ_CASES} >= {0, 1, 2}
 
 
-@pytest.mark.parametrize("name", ZONO_CASES + IBP_CASES + PZ_CASES)
+@pytest.mark.parametrize("name", ZONO_CASES + IBP_CASES + PZ_CASES + ZID_CASES)
 def test_oracle_matches_reference(name):
     c = Case(name)
     xl, xu, lb, ub, br = _run(c)
@@ -152,3 +156,15 @@ def test_soundness_by_sampling(program, wid, eps):
             scale = max(1.0, float(np.abs(acts[k]).max()))
             assert (acts[k] >= lo[b].astype(np.float64) - 1e-4 * scale).all(), (program, k, kind)
             assert (acts[k] <= hi[b].astype(np.float64) + 1e-4 * scale).all(), (program, k, kind)
+
+
+def test_zid_layer_threshold_is_pinned():
+    """zid.cf switches from zonotope to interval bounds above layer 4; a threshold planted
+    one layer pair lower or higher in the oracle breaks every zid case."""
+    assert len(ZID_CASES) >= 4 and {Case(n).wid for n in ZID_CASES} >= {0, 1, 2, 3}
+    for name in ZID_CASES:
+        c = Case(name)
+        for upto in (2, 6):
+            bounds, _, _ = Z.zid(c.wl.layers, c.l0, c.u0, c.spec_W, upto)
+            xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+            assert parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)[0] > 10.0, (name, upto)
