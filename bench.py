@@ -58,6 +58,9 @@ def parse():
                          "deeppoly_custom_stop.cf, zid.cf)")
     ap.add_argument("--stop-depth", type=int, default=3,
                     help="get_start of --certifier custom_stop (3: deeppoly_custom_stop.cf)")
+    ap.add_argument("--cifar", default="auto", choices=["auto", "skip"],
+                    help="auto: add the 'cifar' sub-record (DeepPoly, 3x32x32 conv net, 1024 regions split "
+                         "over the GPUs) to the default DeepPoly line")
     return ap.parse_args()
 
 
@@ -168,8 +171,13 @@ class Clocks:
                 "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
-# regions per CPU sample of the oracle port, per workload id (about 0.5-1 s each)
-CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 5: 16, 6: 256}
+# regions per CPU sample of the oracle port, per workload id (about 0.5-1 s each; the
+# CIFAR-shaped conv net: one region, 10-30 s)
+CPU_SAMPLE = {0: 1, 1: 16, 2: 8, 3: 4, 4: 1, 5: 16, 6: 256}
+CPU_REPS = {4: 1}
+# the CIFAR sub-record: regions in all (split over the GPUs), timed steps, warm-up steps
+CIFAR_REGIONS, CIFAR_STEPS, CIFAR_WARMUP = 1024, 2, 1
+CIFAR_WORKSPACE = 32 << 30   # bytes of engine workspace: regions run in chunks that fit
 
 
 METRIC = {"deeppoly": "DeepPoly", "crown": "CROWN", "zono": "zonotope (DeepZ)", "ibp": "interval (IBP)",
@@ -204,6 +212,9 @@ def _oracle_fn(wl, certifier="deeppoly", stop_depth=3):
         return lambda l0, u0, W: C.custom_stop(wl.layers, l0, u0, W, stop_depth)
     if nets.is_chain(wl.layers):
         from oracle import deeppoly_oracle as O
+        if any(L.kind == "conv" for L in wl.layers):
+            # conv networks: the receptive-field-window restatement (dense rows take minutes)
+            return lambda l0, u0, W: O.deeppoly_windows(wl.layers, l0, u0, W)
         return lambda l0, u0, W: O.deeppoly(wl.layers, l0, u0, W)
     from oracle import crown_oracle as C
     return lambda l0, u0, W: C.certify(wl.layers, l0, u0, W, "deeppoly")
@@ -217,7 +228,8 @@ def cpu_baseline(wl, sample, reps=3, certifier="deeppoly", stop_depth=3):
     l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
     W = nets.spec_weight(y).numpy()
     l0, u0 = l0.numpy(), u0.numpy()
-    fn(l0[:1], u0[:1], W[:1])  # warm
+    if reps > 1:
+        fn(l0[:1], u0[:1], W[:1])  # warm
     ts = []
     for _ in range(reps):
         t = time.perf_counter()
@@ -230,11 +242,10 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     wl = nets.workload(args.workload)
-    if args.workload == 4:
-        print(json.dumps({"impl": "reference", "unavailable": "the oracle port needs ~385 s per region of this "
-                          "net (dense conv rows), beyond a bounded per-step sample"}))
-        return
     sample = CPU_SAMPLE[args.workload]
+    if args.workload in CPU_REPS:
+        # a step of this workload is 10-30 s of CPU work: at most two, no warm-up
+        args.steps, args.warmup = min(args.steps, 2), 0
     fn = _oracle_fn(wl, args.certifier, args.stop_depth)
     X = nets.centres(wl, sample)
     y = nets.labels(wl, X)
@@ -262,54 +273,74 @@ def run_reference(args, rank, world):
         "e2e": {"value": val, "unit": "regions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
-def run_cfgpu(args, rank, world, local):
+def _make_engine(wl, certifier, stop_depth, dev):
+    from cfgpu.engine import DeepPolyEngine
+    if certifier == "polyzono":
+        from cfgpu.polyzono import PolyZonoEngine
+        return PolyZonoEngine(wl.layers, wl.input_size, dev)
+    if certifier == "zid":
+        from cfgpu.zid import ZidEngine
+        return ZidEngine(wl.layers, wl.input_size, dev)
+    if certifier == "custom_stop":
+        return DeepPolyEngine(wl.layers, wl.input_size, dev, stop_depth=stop_depth, relu_strict=True)
+    return DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=certifier)
+
+
+def measure(wl, B_total, per_rank, steps, warmup, certifier, stop_depth, rank, world, dev, workspace_budget):
+    """Time `steps` certifier passes of this rank's regions (after `warmup`), device-timed with
+    CUDA events; every step also all-gathers every rank's bounds (NCCL) and counts the
+    certified regions on the device, inside the timed region.  Then the same end to end
+    through the public API with host buffers.  Returns a dict of the figures (max over ranks)."""
     import torch.distributed as dist
-    from cfgpu.engine import DeepPolyEngine, profile_enable, profile_collect
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    wl = nets.workload(args.workload)
-    B = args.batch or wl.B
     from cfgpu import dist as cdist
-    Xall = nets.centres(wl, B * world)
-    lo, hi = cdist.shard_range(B * world, rank, world)
+    from cfgpu.engine import profile_enable, profile_collect
+    Xall = nets.centres(wl, B_total)
+    lo, hi = cdist.shard_range(B_total, rank, world) if not per_rank else (rank * per_rank, (rank + 1) * per_rank)
+    if per_rank:
+        Xall = nets.centres(wl, per_rank * world)
     X = Xall[lo:hi].contiguous()
     y = nets.labels(wl, X)
-    if args.certifier == "polyzono":
-        from cfgpu.polyzono import PolyZonoEngine
-        eng = PolyZonoEngine(wl.layers, wl.input_size, dev)
-    elif args.certifier == "zid":
-        from cfgpu.zid import ZidEngine
-        eng = ZidEngine(wl.layers, wl.input_size, dev)
-    elif args.certifier == "custom_stop":
-        eng = DeepPolyEngine(wl.layers, wl.input_size, dev, stop_depth=args.stop_depth, relu_strict=True)
-    else:
-        eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier=args.certifier)
+    B = int(X.shape[0])
+    n_regions = int(Xall.shape[0])
+    eng = _make_engine(wl, certifier, stop_depth, dev)
+    if workspace_budget:
+        eng.workspace_budget = workspace_budget
     Xd, yd = X.to(dev), y.to(dev)
     lb = torch.empty(B, 9, dtype=torch.float64, device=dev)
     ub = torch.empty_like(lb)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    n_cert = torch.zeros((), dtype=torch.int64, device=dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    def gather_and_count():
+        # the one collective of the path: every rank's bounds to every rank, then the
+        # reference's verdict rule (all property lower bounds >= 0, constraintflow/cli.py:118-121)
+        if world > 1:
+            lb_all, _ = cdist.gather_bounds(lb, ub, n_regions, rank, world)
+        else:
+            lb_all = lb
+        n_cert.copy_((lb_all >= 0).all(dim=1).sum())
+
     def step():
         eng.certify(Xd, yd, wl.eps, wl.dataset, out=(lb, ub))
+        gather_and_count()
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    # ---- timed region: device events per step, L2 flushed between steps
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     clk_dir = os.environ.get("CF_CLOCKS_DIR", "/tmp")   # where the per-rank clock samples are written
-    clk = Clocks(local, os.path.join(clk_dir, f"cf_clocks_r{rank}.csv"), device=dev)
+    clk = Clocks(int(dev.index or 0), os.path.join(clk_dir, f"cf_clocks_{wl.wid}_r{rank}.csv"), device=dev)
     barrier()
     torch.cuda.synchronize()
     profile_enable(True)
-    replay0 = eng.replayed_launches
+    replay0 = getattr(eng, "replayed_launches", 0)
     wall = time.perf_counter()
-    for k in range(args.steps):
+    for k in range(steps):
         flush.zero_()
         starts[k].record()
         step()
@@ -320,21 +351,15 @@ def run_cfgpu(args, rank, world, local):
     profile_enable(False)
     # kernels replayed from the CUDA graph of a general traversal are not counted by the
     # library's launch counter
-    prof["kernel_launches"] += eng.replayed_launches - replay0
+    prof["kernel_launches"] += getattr(eng, "replayed_launches", 0) - replay0
     barrier()
     clocks = clk.stop()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = B * world * args.steps / (ms_max / 1000.0)
-    # the one collective of the path, after the timed region: gather every region's bounds
-    if world > 1:
-        lb_all, _ = cdist.gather_bounds(lb, ub, B * world, rank, world)
-    else:
-        lb_all = lb
-    certified = (lb_all >= 0).all(dim=1).sum()
+    certified = int(n_cert.item())
     # ---- end-to-end through the public API with host buffers
     Xh = X.pin_memory()
     yh = y.pin_memory()
@@ -347,92 +372,138 @@ def run_cfgpu(args, rank, world, local):
         Xe.copy_(Xh, non_blocking=True)
         ye.copy_(yh, non_blocking=True)
         eng.certify(Xe, ye, wl.eps, wl.dataset, out=(lb, ub))
+        gather_and_count()
         lbh.copy_(lb, non_blocking=True)
         ubh.copy_(ub, non_blocking=True)
 
-    for _ in range(3):
+    for _ in range(warmup):
         e2e_step()
     torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_val = B * world * args.steps / (float(te.item()) / 1000.0)
-    if rank != 0:
-        return
+    return {"eng": eng, "B": B, "n_regions": n_regions, "ms_max": ms_max, "ms_local": ms, "prof": prof,
+            "clocks": clocks, "wall": wall, "certified": certified,
+            "value": n_regions * steps / (ms_max / 1000.0),
+            "e2e": {"value": n_regions * steps / (float(te.item()) / 1000.0), "unit": "regions/s",
+                    "h2d_bytes_per_step": int(X.numel() * 4 + y.numel() * 8),
+                    "d2h_bytes_per_step": int(2 * B * 9 * 8)}}
+
+
+def _roofline(m, wl, certifier, steps, dev):
     bf16, hbm, src = peaks()
+    prof, ms, eng = m["prof"], m["ms_local"], m["eng"]
     achieved = prof["step_flops"] / (prof["step_ms"] / 1000.0) / 1e12 if prof["step_ms"] > 0 else None
     conv = any(L.kind == "conv" for L in wl.layers)
-    zono_tc = args.certifier in ("zono", "polyzono") and os.environ.get("CF_STEP_IMPL") != "simt"
-    if conv or not eng.chain or (args.certifier in ("zono", "ibp") and not zono_tc):
+    chain = getattr(eng, "chain", True)
+    zono_tc = certifier in ("zono", "polyzono") and os.environ.get("CF_STEP_IMPL") != "simt"
+    if conv or not chain or (certifier in ("zono", "ibp") and not zono_tc):
         # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
         # with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass: k_zono_gemm
         # over the noise-symbol rows -- all on the FP32 pipe.
         # MEASURED_PEAKS holds no FP32-pipe figure, so the nominal one: SMs x 128 lanes x 2 x max clock
         props = torch.cuda.get_device_properties(dev)
-        mhz = clocks.get("sm_max_mhz") or 1965.0
+        mhz = m["clocks"].get("sm_max_mhz") or 1965.0
         peak, bound, peak_src = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12, "fp32", \
             "nominal FP32 FMA pipe (SMs x 128 x 2 x max SM clock); no measured figure"
     else:
         peak, bound, peak_src = bf16 / 2.0 / 3.0, "tensor", f"3xTF32 = bf16/2/3 of {src} MEASURED_PEAKS"
+    key = (wl.wid, certifier)
+    roof = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": (achieved / peak) if achieved else None,
+            "traffic": NCU_TRAFFIC.get(key),
+            "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
+                               "CTAs) from one ncu --set full capture of this command") if key in NCU_TRAFFIC else None,
+            "kernel": {"zono": "k_zono_persist" if zono_tc else "k_zono_gemm", "ibp": None,
+                       "polyzono": "k_chain (backsubstitution) + k_zono_persist"}.get(
+                           certifier, ("transposed convolution of the receptive-field windows" if conv else
+                                       "backsubstitution step") if chain else "k_bmm (general traversal)"),
+            "peak_source": peak_src,
+            "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
+            "step_launches": prof["step_launches"]}
+    mem = {"kernels": {"zono": "k_zono_bounds, k_zono_relu", "polyzono": "k_relu_relax, k_zono_bounds, "
+                       "k_zono_relu, k_to_f64, k_prep_wimg", "ibp": None}.get(
+                           certifier, "k_relu_relax / k_crown_relax, k_concretize, k_to_f64, k_prep_wimg"),
+           "launches": int(prof["mem_launches"]),
+           "bytes_per_pass": prof["mem_bytes"] / steps,
+           "ms_per_pass": prof["mem_ms"] / steps,
+           "achieved": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 if prof["mem_ms"] > 0 else None,
+           "peak": hbm, "unit": "GB/s",
+           "frac": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 / hbm if prof["mem_ms"] > 0 else None,
+           "peak_source": f"{src} MEASURED_PEAKS hbm_gbs",
+           "share_of_pass": prof["mem_ms"] / ms if ms > 0 else None}
+    return roof, mem
+
+
+def _cpu_baseline_record(wl, certifier, stop_depth):
+    sample = CPU_SAMPLE[wl.wid]
+    reps = CPU_REPS.get(wl.wid, 3)
+    v, t1 = cpu_baseline(wl, sample, reps=reps, certifier=certifier, stop_depth=stop_depth)
+    how = "receptive-field windows" if any(L.kind == "conv" for L in wl.layers) else "dense rows"
+    return {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle numpy float32 ({how}, {os.cpu_count()} host threads), {sample} region(s) of "
+                      f"{wl.name}, median of {reps} ({t1:.2f} s each)"}
+
+
+def run_cfgpu(args, rank, world, local):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl = nets.workload(args.workload)
+    B = args.batch or wl.B
+    warm = max(3, args.warmup)
+    m = measure(wl, 0, B, args.steps, warm, args.certifier, args.stop_depth, rank, world, dev, None)
+    cifar = None
+    if args.cifar == "auto" and args.workload == 2 and args.certifier == "deeppoly" and not args.batch:
+        # the CIFAR-shaped conv net (3x32x32, 4 conv + 3 FC layers): 1024 regions in all, split
+        # over the GPUs (strong scaling), chunked inside the engine to fit its workspace
+        wl4 = nets.workload(4)
+        cifar = measure(wl4, CIFAR_REGIONS, 0, CIFAR_STEPS, CIFAR_WARMUP, "deeppoly", 0, rank, world, dev,
+                        CIFAR_WORKSPACE)
+    if rank != 0:
+        return
+    roof, mem = _roofline(m, wl, args.certifier, args.steps, dev)
     out = {
-        "metric": _metric(args.certifier), "value": value, "unit": "regions/s",
-        "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps,
+        "metric": _metric(args.certifier), "value": m["value"], "unit": "regions/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warm, "ms_per_step": m["ms_max"] / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl.name, "certifier": args.certifier, "regions_per_gpu": B,
                    **({"stop_depth": args.stop_depth} if args.certifier == "custom_stop" else {}),
-                   "global_regions": B * world, "eps": wl.eps,
-                   "parallelism": f"regions sharded over {world} GPU(s)", "l2": "flushed between timed steps",
-                   "certified": int(certified.item())},
-        "e2e": {"value": e2e_val, "unit": "regions/s",
-                "h2d_bytes_per_step": int(X.numel() * 4 + y.numel() * 8),
-                "d2h_bytes_per_step": int(2 * B * 9 * 8)},
-        "gpu_launches": int(prof["kernel_launches"]),
-        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None,
-                     "traffic": NCU_TRAFFIC.get((args.workload, args.certifier)),
-                     "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
-                                        "CTAs) from one ncu --set full capture of this command")
-                     if (args.workload, args.certifier) in NCU_TRAFFIC else None,
-                     "kernel": {"zono": "k_zono_persist" if zono_tc else "k_zono_gemm", "ibp": None,
-                                "polyzono": "k_chain (backsubstitution) + k_zono_persist"}.get(
-                         args.certifier, "backsubstitution step" if eng.chain else "k_bmm (general traversal)"),
-                     "peak_source": peak_src,
-                     "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
-                     "step_launches": prof["step_launches"]},
-        "memory_bound": {
-            "kernels": {"zono": "k_zono_bounds, k_zono_relu", "polyzono": "k_relu_relax, k_zono_bounds, "
-                        "k_zono_relu, k_to_f64, k_prep_wimg", "ibp": None}.get(
-                            args.certifier, "k_relu_relax / k_crown_relax, k_concretize, k_to_f64, k_prep_wimg"),
-            "launches": int(prof["mem_launches"]),
-            "bytes_per_pass": prof["mem_bytes"] / args.steps,
-            "ms_per_pass": prof["mem_ms"] / args.steps,
-            "achieved": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 if prof["mem_ms"] > 0 else None,
-            "peak": hbm, "unit": "GB/s",
-            "frac": prof["mem_bytes"] / (prof["mem_ms"] / 1000.0) / 1e9 / hbm if prof["mem_ms"] > 0 else None,
-            "peak_source": f"{src} MEASURED_PEAKS hbm_gbs",
-            "share_of_pass": prof["mem_ms"] / ms if ms > 0 else None},
-        "clocks": clocks,
-        "wall_s_timed": wall,
+                   "global_regions": m["n_regions"], "eps": wl.eps,
+                   "parallelism": f"regions sharded over {world} GPU(s); bounds all-gathered and verdicts counted "
+                                  "every step inside the timed region",
+                   "l2": "flushed between timed steps", "certified": m["certified"]},
+        "e2e": m["e2e"],
+        "gpu_launches": int(m["prof"]["kernel_launches"]),
+        "roofline": roof,
+        "memory_bound": mem,
+        "clocks": m["clocks"],
+        "wall_s_timed": m["wall"],
     }
-    if world == 1 and args.workload == 4:
-        # one region of this net takes the numpy port ~6 minutes (its dense conv rows), far past a
-        # bounded sample, and ~45x longer than the reference's own torch CPU path
-        out["cpu_baseline"] = {"value": None, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
-                               "sample": "not timed: the oracle port needs ~385 s per region of this net"}
-    elif world == 1:
-        sample = CPU_SAMPLE[args.workload]
-        v, t1 = cpu_baseline(wl, sample, certifier=args.certifier, stop_depth=args.stop_depth)
-        out["cpu_baseline"] = {"value": v, "unit": "regions/s", "cores": os.cpu_count(), "kind": "port",
-                               "sample": f"oracle numpy float32, {sample} regions of {wl.name}, median of 3 "
-                                         f"({t1:.2f} s each)"}
+    if world == 1:
+        out["cpu_baseline"] = _cpu_baseline_record(wl, args.certifier, args.stop_depth)
+    if cifar is not None:
+        croof, cmem = _roofline(cifar, wl4, "deeppoly", CIFAR_STEPS, dev)
+        rec = {"metric": _metric("deeppoly"), "value": cifar["value"], "unit": "regions/s", "n_gpus": world,
+               "steps": CIFAR_STEPS, "warmup": CIFAR_WARMUP, "ms_per_step": cifar["ms_max"] / CIFAR_STEPS,
+               "scaling": "strong",
+               "config": {"workload": wl4.name, "certifier": "deeppoly", "global_regions": cifar["n_regions"],
+                          "regions_per_gpu": cifar["B"], "eps": wl4.eps,
+                          "parallelism": f"{CIFAR_REGIONS} regions split over {world} GPU(s)",
+                          "workspace_bytes": CIFAR_WORKSPACE, "certified": cifar["certified"],
+                          "l2": "flushed between timed steps (the windows far exceed L2)"},
+               "e2e": cifar["e2e"], "gpu_launches": int(cifar["prof"]["kernel_launches"]),
+               "roofline": croof, "memory_bound": cmem, "clocks": cifar["clocks"], "wall_s_timed": cifar["wall"]}
+        if world == 1:
+            rec["cpu_baseline"] = _cpu_baseline_record(wl4, "deeppoly", 0)
+        out["cifar"] = rec
     print(json.dumps(out))
 
 

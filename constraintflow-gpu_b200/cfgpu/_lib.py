@@ -66,6 +66,9 @@ def _load():
         "cf_signscale": (_i32, [_i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
         "cf_deeppoly_check": (_i32, [_vp, _vp]),
         "cf_deeppoly_run_static": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+        "cf_deeppoly_check_static": (_i32, [_vp]),
+        "cf_deeppoly_run_replay": (_i32, [P(CfNetwork), _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                                          _vp]),
         "cf_relu_relax": (_i32, [_i64, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _vp]),
         "cf_backsub_step": (_i32, [_i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -98,7 +101,7 @@ lib = _load()
 # Every symbol the C header declares (checked by the CPU test suite).
 EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_run", "cf_deeppoly_check",
             "cf_deeppoly_layer", "cf_signscale", "cf_bounds_meet",
-            "cf_deeppoly_run_static",
+            "cf_deeppoly_run_static", "cf_deeppoly_check_static", "cf_deeppoly_run_replay",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",
             "cf_ew_any", "cf_bmm", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",

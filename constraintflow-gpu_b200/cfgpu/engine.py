@@ -147,7 +147,12 @@ class DeepPolyEngine:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def run(self, l0, u0, spec_W, want_state=False, workspace_budget=8 << 30, out=None, check_device=False):
+    # device bytes the fused driver's workspace may take; DeepPoly regions beyond what fits
+    # run in further chunks of the same call
+    workspace_budget = 8 << 30
+
+    def run(self, l0, u0, spec_W, want_state=False, workspace_budget=None, out=None, check_device=False,
+            replay=None):
         """Bounds for B regions.
 
         l0, u0: [B, n_input] float32 device tensors (normalised input box);
@@ -155,6 +160,8 @@ class DeepPolyEngine:
         Returns (lb, ub) float64 [B, n_spec] and, if want_state, (state_l, state_u)
         float32 [B, N] with every neuron's bounds in the reference's neuron order.
         check_device=True synchronises and raises if a bounded device wait gave up.
+        replay=(dec_l, dec_u): [B, N] float32 device tensors (state layout) from which every
+        ReLU branch decision is taken (cf_deeppoly_run_replay; DeepPoly chains only).
         """
         B = int(l0.shape[0])
         for t, shp in ((l0, (B, self.input_size)), (u0, (B, self.input_size)),
@@ -178,13 +185,26 @@ class DeepPolyEngine:
                 su.copy_(su_g)
                 return lb, ub, sl, su
             return lb, ub
-        ws = self._workspace(B, workspace_budget)
+        ws = self._workspace(B, self.workspace_budget if workspace_budget is None else workspace_budget)
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        st = lib.cf_deeppoly_run(ctypes.byref(self.net), B, l0.data_ptr(), u0.data_ptr(), spec_W.data_ptr(),
-                                 sl.data_ptr() if sl is not None else None,
-                                 su.data_ptr() if su is not None else None,
-                                 lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
-        check(st, "cf_deeppoly_run")
+        if replay is not None:
+            dl, du = replay
+            for t in (dl, du):
+                if tuple(t.shape) != (B, self.N) or t.dtype != torch.float32 or not t.is_contiguous() or \
+                        t.device != self.device:
+                    raise Exception(f"SHAPE MISMATCH: replay bounds must be contiguous float32 {(B, self.N)}")
+            st = lib.cf_deeppoly_run_replay(ctypes.byref(self.net), B, l0.data_ptr(), u0.data_ptr(),
+                                            spec_W.data_ptr(), dl.data_ptr(), du.data_ptr(),
+                                            sl.data_ptr() if sl is not None else None,
+                                            su.data_ptr() if su is not None else None,
+                                            lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+            check(st, "cf_deeppoly_run_replay")
+        else:
+            st = lib.cf_deeppoly_run(ctypes.byref(self.net), B, l0.data_ptr(), u0.data_ptr(), spec_W.data_ptr(),
+                                     sl.data_ptr() if sl is not None else None,
+                                     su.data_ptr() if su is not None else None,
+                                     lb.data_ptr(), ub.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+            check(st, "cf_deeppoly_run")
         if self.certifier == "crown":
             st = lib.cf_deeppoly_check(ws.data_ptr(), stream)
             if st == _lib.CF_ERR_UNSUPPORTED:

@@ -17,22 +17,25 @@ namespace cf {
 //   L' = 1[l+u>=0] * x
 //   U' = x if l>=0; 0 if u<=0; else lam*x + mu, lam = u/(u-l), mu = -(u*l)/(u-l)
 // float32 IEEE division, same operation order as the generated code.
+// Decision replay (parity tests): with dl / du given, the three branch decisions (l >= 0,
+// u <= 0, l + u >= 0) and the ReLU outputs' cases are taken from (dl, du) instead of (l, u).
 __global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
                              int64_t ld_in, float* __restrict__ lo, float* __restrict__ uo, int64_t ld_out,
                              float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu,
-                             bool strict) {
+                             bool strict, const float* __restrict__ dl, const float* __restrict__ du) {
   int64_t total = B * n;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = t / n, k = t - b * n;
     float lv = l[b * ld_in + k], uv = u[b * ld_in + k];
-    bool pos = lv >= 0.0f;
-    bool dead = (!pos) && (uv <= 0.0f);
+    const float ld = dl ? dl[b * ld_in + k] : lv, ud = du ? du[b * ld_in + k] : uv;
+    bool pos = ld >= 0.0f;
+    bool dead = (!pos) && (ud <= 0.0f);
     float den = uv - lv;
     float lam_u = __fdiv_rn(uv, den);
     float mu_u = 0.0f - __fdiv_rn(__fmul_rn(uv, lv), den);
     if (lo) lo[b * ld_out + k] = pos ? lv : 0.0f;
-    if (uo) uo[b * ld_out + k] = (uv >= 0.0f) ? uv : 0.0f;
-    const float s = __fadd_rn(lv, uv);
+    if (uo) uo[b * ld_out + k] = (ud >= 0.0f) ? uv : 0.0f;
+    const float s = __fadd_rn(ld, ud);
     alpha[t] = (strict ? s > 0.0f : s >= 0.0f) ? 1.0f : 0.0f;
     lam[t] = pos ? 1.0f : (dead ? 0.0f : lam_u);
     mu[t] = (pos || dead) ? 0.0f : mu_u;
@@ -41,14 +44,15 @@ __global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, 
 
 cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
                             float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st,
-                            bool strict) {
+                            bool strict, const float* dl, const float* du) {
   int64_t total = B * n;
   if (total == 0) return CF_OK;
   int threads = 256;
   int64_t blocks = ceil_div(total, threads);
   if (blocks > 148 * 16) blocks = 148 * 16;
   prof_mem_begin(st);
-  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu, strict);
+  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu, strict, dl,
+                                                     du);
   prof_mem_end(st, 28.0 * total);   // l, u in; l', u', alpha, lambda, mu out
   return check_launch("k_relu_relax");
 }

@@ -376,9 +376,12 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
 // Network layers li_begin .. li_end-1 (li == n_layers: the property layer) of one chunk of
 // Bc regions.  All pointers already offset to the chunk.  Layer 0 also writes the input
 // columns of the state.
+// dec_l / dec_u (optional, [Bc, N] in the state's layout): decision replay -- every ReLU's
+// branch decisions are taken from these bounds of its input layer (cf_deeppoly_run_replay).
 static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
                             const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
-                            const WsLayout& w, cudaStream_t st, int li_begin, int li_end) {
+                            const WsLayout& w, cudaStream_t st, int li_begin, int li_end,
+                            const float* dec_l = nullptr, const float* dec_u = nullptr) {
   (void)w.wimg;
   const int64_t N = p.N, n0 = net->n_input;
   float* Abuf[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
@@ -573,7 +576,8 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
                                   rl[a], rm[a], err + 16 + 2 * a, err, st));
       } else {
         CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a],
-                                 rl[a], rm[a], st, net->relaxation == CF_RELAX_DEEPPOLY_STRICT));
+                                 rl[a], rm[a], st, net->relaxation == CF_RELAX_DEEPPOLY_STRICT,
+                                 dec_l ? dec_l + col : nullptr, dec_u ? dec_u + col : nullptr));
       }
     }
   }
@@ -643,11 +647,10 @@ extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chu
   return ws_layout(net, p, chunk).total;
 }
 
-extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
-                                     const float* specW, float* state_l, float* state_u, double* lb, double* ub,
-                                     void* workspace, size_t ws_bytes, void* stream) {
-  clear_error();
-  CF_INJECT("deeppoly_run");
+static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
+                              const float* specW, float* state_l, float* state_u, double* lb, double* ub,
+                              void* workspace, size_t ws_bytes, void* stream, const float* dec_l,
+                              const float* dec_u) {
   Plan p;
   CF_TRY(make_plan(net, p));
   CF_REQUIRE(B >= 0, CF_ERR_SHAPE, "B < 0");
@@ -689,9 +692,31 @@ extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const flo
     float* sl = state_l ? state_l + b0 * N : reinterpret_cast<float*>(ws + w.state);
     float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
     CF_TRY(run_layers(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su,
-                      lb + b0 * ns, ub + b0 * ns, ws, w, st, 0, net->n_layers + 1));
+                      lb + b0 * ns, ub + b0 * ns, ws, w, st, 0, net->n_layers + 1,
+                      dec_l ? dec_l + b0 * N : nullptr, dec_u ? dec_u + b0 * N : nullptr));
   }
   return CF_OK;
+}
+
+extern "C" cf_status cf_deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
+                                     const float* specW, float* state_l, float* state_u, double* lb, double* ub,
+                                     void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  CF_INJECT("deeppoly_run");
+  return deeppoly_run(net, B, l0, u0, specW, state_l, state_u, lb, ub, workspace, ws_bytes, stream, nullptr,
+                      nullptr);
+}
+
+extern "C" cf_status cf_deeppoly_run_replay(const cf_network* net, int64_t B, const float* l0, const float* u0,
+                                            const float* specW, const float* dec_l, const float* dec_u,
+                                            float* state_l, float* state_u, double* lb, double* ub,
+                                            void* workspace, size_t ws_bytes, void* stream) {
+  clear_error();
+  CF_INJECT("deeppoly_run_replay");
+  CF_REQUIRE(net && (net->relaxation == CF_RELAX_DEEPPOLY || net->relaxation == CF_RELAX_DEEPPOLY_STRICT),
+             CF_ERR_UNSUPPORTED, "deeppoly_run_replay: DeepPoly relaxations only");
+  CF_REQUIRE(dec_l && dec_u, CF_ERR_NULL, "deeppoly_run_replay: NULL decision bounds");
+  return deeppoly_run(net, B, l0, u0, specW, state_l, state_u, lb, ub, workspace, ws_bytes, stream, dec_l, dec_u);
 }
 
 extern "C" cf_status cf_deeppoly_layer(const cf_network* net, int32_t layer, int64_t B, const float* l0,

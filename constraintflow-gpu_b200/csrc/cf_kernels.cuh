@@ -4,8 +4,11 @@
 
 namespace cf {
 
+// dl / du (optional, rows at b*ld_in like l / u): the bounds the three branch decisions are
+// taken from (decision replay); the relaxation's values still come from l / u.
 cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
-                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st, bool strict = false);
+                            float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, cudaStream_t st,
+                            bool strict = false, const float* dl = nullptr, const float* du = nullptr);
 
 // CROWN ReLU (whole-layer branch): flags = 2 device ints of scratch, err = device error word.
 cf_status launch_crown_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,

@@ -67,3 +67,20 @@ extern "C" cf_status cf_deeppoly_run_static(const cf_network* net, int64_t B, co
   return cf_deeppoly_run(net, B, l0, u0, specW, state_l, state_u, lb, ub, ptr, (size_t)CF_STATIC_SCRATCH_BYTES,
                          stream);
 }
+
+extern "C" cf_status cf_deeppoly_check_static(void* stream) {
+  clear_error();
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 128) {
+    set_error("deeppoly_check_static: cudaGetDevice: %s", cudaGetErrorString(e));
+    return CF_ERR_CUDA;
+  }
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    ptr = g_static_ptr[dev];
+  }
+  CF_REQUIRE(ptr != nullptr, CF_ERR_NULL, "deeppoly_check_static: no cf_deeppoly_run_static call on device %d", dev);
+  return cf_deeppoly_check(ptr, stream);
+}

@@ -153,6 +153,23 @@ cf_status cf_deeppoly_run(const cf_network* net, int64_t B,
                           double* lb_dev, double* ub_dev,
                           void* workspace_dev, size_t workspace_bytes, void* stream);
 
+/* Decision replay, for parity testing against another implementation of the same program.
+ * cf_deeppoly_run, except that every ReLU branch decision of the generated deeppoly.Relu
+ * (l >= 0, u <= 0, l + u >= 0; examples/compiler_examples/deeppoly.cf:20-24) is taken from
+ * the given bounds dec_l_dev / dec_u_dev [B, N] (state layout, e.g. another run's every-neuron
+ * l / u) of the ReLU's input layer instead of this run's own; the relaxation's values
+ * (lambda = u/(u-l), mu, l', u') still come from this run's bounds.  Two float32
+ * implementations that sum in different orders can take different branches on a bound a few
+ * ulps from 0, after which every later layer differs by far more than rounding; replaying
+ * one side's decisions makes their bounds comparable on every layer.  CF_RELAX_DEEPPOLY and
+ * CF_RELAX_DEEPPOLY_STRICT only. */
+cf_status cf_deeppoly_run_replay(const cf_network* net, int64_t B,
+                                 const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
+                                 const float* dec_l_dev, const float* dec_u_dev,
+                                 float* state_l_dev, float* state_u_dev,
+                                 double* lb_dev, double* ub_dev,
+                                 void* workspace_dev, size_t workspace_bytes, void* stream);
+
 /* One layer of the pass, for callers that drive the layer loop themselves as Flow.flow does
  * (constraintflow/lib/flow_sparse.py:27-228 calls the transformer once per layer; code
  * emitted by cfgpu.codegen calls this once per layer).  layer = 0 .. n_layers-1 runs that
@@ -204,13 +221,22 @@ cf_status cf_profile_collect(cf_profile_stats* out);
  * call on a device looks the array up (cudaGetSymbolAddress with that device current):
  * make it before any stream capture.  All calls share the array, so calls that overlap
  * on the GPU race and must be serialised by the caller.  A network whose scratch for one
- * region exceeds the array is rejected with CF_ERR_WORKSPACE; larger batches are run in
- * region chunks that fit. */
+ * region exceeds the array is rejected with CF_ERR_WORKSPACE; larger DeepPoly, zono and ibp
+ * batches are run in region chunks that fit.  CROWN (CF_RELAX_CROWN) decides each ReLU branch
+ * over the whole batch, so its whole batch must fit the array in one chunk
+ * (cf_deeppoly_workspace_bytes(net, B) <= CF_STATIC_SCRATCH_BYTES); otherwise the call
+ * returns CF_ERR_WORKSPACE.  cf_deeppoly_check_static reports the device status of the
+ * last call on the current device. */
 #define CF_STATIC_SCRATCH_BYTES (32u << 20)
 cf_status cf_deeppoly_run_static(const cf_network* net, int64_t B,
                                  const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
                                  float* state_l_dev, float* state_u_dev,
                                  double* lb_dev, double* ub_dev, void* stream);
+/* cf_deeppoly_check on the fixed array of the current device: synchronises `stream` and
+ * reports whether a bounded device wait of the last cf_deeppoly_run_static call gave up
+ * (CF_ERR_TIMEOUT) or a CROWN ReLU layer took the all-crossing branch (CF_ERR_UNSUPPORTED).
+ * CF_ERR_NULL if no static call was made on this device yet. */
+cf_status cf_deeppoly_check_static(void* stream);
 
 /* Synchronise `stream` and report whether a bounded device-side wait of the last
  * cf_deeppoly_run that used `workspace_dev` gave up (CF_ERR_TIMEOUT) instead of hanging,

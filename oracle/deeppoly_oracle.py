@@ -236,3 +236,247 @@ def flatten_bounds(wl_input_size, bounds, B):
     ls = [b[0] for b in bounds]
     us = [b[1] for b in bounds]
     return np.concatenate(ls, axis=1), np.concatenate(us, axis=1)
+
+
+# ---------------------------------------------------------------- receptive-field windows
+# The same DeepPoly arithmetic for conv networks without dense rows.  A coefficient row of
+# a conv neuron (co, oy, ox) is nonzero at every level j below it only inside its
+# receptive field: C_j x Ph x Pw positions of level j's image whose origin is
+# (oy*sig - pi, ox*sig - pi) (the reference keeps the same information in PatchesBlock,
+# constraintflow/gbcsr/sparse_block.py:2576-3100, and its Dense@Kernel products run
+# conv_transpose2d, :839-928).  Rows of a linear or property layer use the whole image
+# (sig = 0).  Entries at positions outside the level image are exact zeros, so every sum
+# below equals the dense one up to float32 summation order.
+
+class _Win:
+    """Window geometry at one level: image (C, H, W), window Ph x Pw, origin step sig and
+    offset pi (origin of row position (oy, ox) = (oy*sig - pi, ox*sig - pi))."""
+
+    def __init__(self, C, H, W, Ph, Pw, sig, pi):
+        self.C, self.H, self.W, self.Ph, self.Pw, self.sig, self.pi = C, H, W, Ph, Pw, sig, pi
+
+    @property
+    def size(self):
+        return self.C * self.Ph * self.Pw
+
+
+def _img(layer, side):
+    shp = layer.in_shape if side == 'in' else layer.out_shape
+    if shp is None or len(shp) == 1:
+        n = layer.n_in if side == 'in' else layer.n_out
+        return (n, 1, 1)
+    return tuple(int(x) for x in shp)
+
+
+def _window_chain(affine, m):
+    """Windows of the rows of affine layer m (m == len(affine): the property layer) at the
+    input of affine layers m-1 .. 0 ... (list index k: the window over affine[m-1-k]'s
+    output, i.e. before substituting it), then over the network input."""
+    spec = m == len(affine)
+
+    def level(j):   # the image at the input of affine layer j: the output image of affine j-1
+        return _img(affine[j - 1], 'out') if j > 0 else _img(affine[0], 'in')
+    lvl = level(m)
+    if not spec and affine[m].kind == 'conv':
+        L = affine[m]
+        g = _Win(lvl[0], lvl[1], lvl[2], L.W.shape[2], L.W.shape[3], L.stride, L.pad)
+    else:
+        g = _Win(lvl[0], lvl[1], lvl[2], lvl[1], lvl[2], 0, 0)
+    out = [g]
+    for j in range(m - 1, -1, -1):
+        Lj = affine[j]
+        C, H, W = level(j)
+        if Lj.kind == 'conv' and g.sig > 0:
+            kh, kw = Lj.W.shape[2], Lj.W.shape[3]
+            h = _Win(C, H, W, (g.Ph - 1) * Lj.stride + kh, (g.Pw - 1) * Lj.stride + kw,
+                     g.sig * Lj.stride, g.pi * Lj.stride + Lj.pad)
+        else:
+            h = _Win(C, H, W, H, W, 0, 0)
+        out.append(h)
+        g = h
+    return out
+
+
+def _win_view(img, g, Hm, Wm):
+    """[B, C, H, W] -> view [B, Hm, Wm, C, Ph, Pw] of every row position's window (zeros
+    outside the image)."""
+    B = img.shape[0]
+    top = g.pi
+    bot = max(0, (Hm - 1) * g.sig - g.pi + g.Ph - g.H)
+    left = g.pi
+    right = max(0, (Wm - 1) * g.sig - g.pi + g.Pw - g.W)
+    pad = np.zeros((B, g.C, g.H + top + bot, g.W + left + right), img.dtype)
+    pad[:, :, top:top + g.H, left:left + g.W] = img
+    sb, sc, sh, sw = pad.strides
+    return np.lib.stride_tricks.as_strided(
+        pad, shape=(B, Hm, Wm, g.C, g.Ph, g.Pw),
+        strides=(sb, g.sig * sh, g.sig * sw, sc, sh, sw), writeable=False)
+
+
+def _in_image(g, Hm, Wm):
+    """[Hm, Wm, 1, Ph, Pw] mask of window positions inside the level image."""
+    oy = np.arange(Hm)[:, None, None, None, None]
+    ox = np.arange(Wm)[None, :, None, None, None]
+    u = np.arange(g.Ph)[None, None, None, :, None]
+    v = np.arange(g.Pw)[None, None, None, None, :]
+    Y = oy * g.sig - g.pi + u
+    X = ox * g.sig - g.pi + v
+    return ((Y >= 0) & (Y < g.H) & (X >= 0) & (X < g.W)).astype(F32)
+
+
+def _win_conv_T(X, layer, g, h):
+    """Transposed convolution of window rows X [M, Cout, g.Ph, g.Pw] (over the conv's output)
+    into windows [M, Cin, h.Ph, h.Pw] over its input: out[u*s + ky - D, v*s + kx - D] +=
+    X[u, v] W[:, :, ky, kx], D = g.pi*s + pad - h.pi (0 for receptive-field windows, pad for
+    whole-image ones); the caller zeroes positions outside the image."""
+    Cout, Cin, kh, kw = layer.W.shape
+    s = layer.stride
+    D = g.pi * s + layer.pad - h.pi
+    M = X.shape[0]
+    Xhw = np.ascontiguousarray(X.transpose(0, 2, 3, 1)).reshape(M * g.Ph * g.Pw, Cout)
+    Hp = max((g.Ph - 1) * s + kh, D + h.Ph)
+    Wp = max((g.Pw - 1) * s + kw, D + h.Pw)
+    outp = np.zeros((M, Hp, Wp, Cin), F32)
+    for i in range(kh):
+        for j in range(kw):
+            contrib = (Xhw @ layer.W[:, :, i, j].astype(F32)).reshape(M, g.Ph, g.Pw, Cin)
+            outp[:, i:i + s * (g.Ph - 1) + 1:s, j:j + s * (g.Pw - 1) + 1:s, :] += contrib
+    out = outp[:, D:D + h.Ph, D:D + h.Pw, :]
+    return np.ascontiguousarray(out.transpose(0, 3, 1, 2))
+
+
+def _win_bound(affine, relax, m, A0, c0, Hm, Wm, l0img, u0img, lower):
+    """Bound of rows A0 [B, r, C, Ph, Pw] (windows over layer m's input, row i at position
+    (oy, ox) = divmod(i % (Hm*Wm), Wm)), constants c0 [B, r].  Rows are all of layer m's
+    rows for the given positions (r = Cm * Hm * Wm, or the linear rows with Hm = Wm = 1).
+
+    An affine layer's L and U are the same expression W x + b, so the two products of the
+    sign split (clamp(A,0,True) @ W + clamp(A,0,False) @ W) are one product A @ W here: the
+    same sum, with float32 rounding of a different order."""
+    gs = _window_chain(affine, m)
+    B, r = A0.shape[:2]
+    k_ = r // (Hm * Wm)
+    A, c = A0, c0
+    zero = F32(0.0)
+    for k, j in enumerate(range(m - 1, -1, -1)):
+        g, h = gs[k], gs[k + 1]
+        Lj = affine[j]
+        A6 = A.reshape(B, k_, Hm, Wm, g.C, g.Ph, g.Pw)
+        if j in relax:   # substitute ReLU_j with the region's relaxation at absolute positions
+            alpha, lam, mu = (_win_view(v.reshape(B, g.C, g.H, g.W), g, Hm, Wm) for v in relax[j])
+            neg = A6 < zero
+            # lower bound: a >= 0 -> a*alpha (L), a < 0 -> a*lam + a*mu (U); upper the other way
+            fac = np.where(neg, lam[:, None], alpha[:, None]) if lower else np.where(neg, alpha[:, None], lam[:, None])
+            side = np.where(neg, A6, zero) if lower else np.where(neg, zero, A6)
+            dc = np.einsum('bkhwcuv,bhwcuv->bkhw', side, mu, dtype=F32, optimize=True).reshape(B, r)
+            A6 = np.multiply(A6, fac, dtype=F32)
+            c = ((dc + zero) + c).astype(F32)
+        # substitute affine j: A W, c + A b
+        if Lj.kind == 'conv':
+            dc = np.einsum('bkhwcuv,c->bkhw', A6, Lj.b.astype(F32), dtype=F32, optimize=True).reshape(B, r)
+        else:
+            dc = (A6.reshape(B, r, -1) @ Lj.b.astype(F32)).astype(F32)
+        c = ((dc + zero) + c).astype(F32)
+        Mr = B * r
+        if Lj.kind == 'conv':
+            A = _win_conv_T(A6.reshape(Mr, g.C, g.Ph, g.Pw), Lj, g, h).reshape(B, k_, Hm, Wm, h.C, h.Ph, h.Pw)
+            if h.sig > 0 or h.Ph != h.H or h.Pw != h.W:
+                A *= _in_image(h, Hm, Wm)[None, None]
+        else:
+            A = (A6.reshape(Mr, -1) @ Lj.W.astype(F32)).reshape(B, k_, Hm, Wm, h.C, h.Ph, h.Pw)
+    # fold the input box in (input layer L / U = constant l0 / u0)
+    g = gs[-1]
+    A6 = A.reshape(B, k_, Hm, Wm, g.C, g.Ph, g.Pw)
+    lw = _win_view(l0img, g, Hm, Wm)
+    uw = _win_view(u0img, g, Hm, Wm)
+    neg = A6 < zero
+    box = np.where(neg, uw[:, None], lw[:, None]) if lower else np.where(neg, lw[:, None], uw[:, None])
+    dc = np.einsum('bkhwcuv,bkhwcuv->bkhw', A6, box, dtype=F32, optimize=True).reshape(B, r)
+    return ((dc.astype(F32) + zero) + c).astype(F32)
+
+
+def _win_rows(layer, g, Hm, Wm, rows_c, B):
+    """Initial windows [B, r, C, Ph, Pw] of the rows of output channels rows_c (conv) or of
+    rows rows_c (linear): the conv kernel placed at each position's origin, zero outside
+    the image; a linear row over the whole image."""
+    if layer.kind == 'conv':
+        K = layer.W.astype(F32)[rows_c]                              # [rc, Cin, kh, kw]
+        mask = _in_image(g, Hm, Wm)                                  # [Hm, Wm, 1, Ph, Pw]
+        A = K[:, None, None] * mask[None]                            # [rc, Hm, Wm, Cin, kh, kw]
+        A = A.reshape((-1,) + A.shape[3:])
+    else:
+        A = layer.W.astype(F32)[rows_c].reshape(-1, g.C, g.Ph, g.Pw)
+    return np.broadcast_to(A, (B,) + A.shape)
+
+
+def deeppoly_windows(layers, l0, u0, spec_W, force=None, chunk_floats=1 << 22, threads=None):
+    """DeepPoly over a chain network with conv layers on receptive-field windows.
+
+    Same contract as deeppoly(): layers (property layer excluded), l0 / u0 [B, n0], spec_W
+    [B, 9, 10], optional force = (l_all, u_all) replaying ReLU decisions; returns (bounds, lb,
+    ub).  Rows are processed in chunks of whole output channels (conv) or rows (linear)
+    holding about chunk_floats window entries, on `threads` host threads (default: all;
+    numpy releases the interpreter lock inside its array loops and BLAS calls)."""
+    import concurrent.futures
+    import os
+    pool = concurrent.futures.ThreadPoolExecutor(threads or os.cpu_count() or 1)
+    l0 = np.asarray(l0, F32)
+    u0 = np.asarray(u0, F32)
+    B = l0.shape[0]
+    first = next(L for L in layers if L.kind != 'relu')
+    C0, H0, W0 = _img(first, 'in')
+    l0img, u0img = l0.reshape(B, C0, H0, W0), u0.reshape(B, C0, H0, W0)
+    affine, bounds, relax = [], [], {}
+    pos = 0
+    for L in layers + ['spec']:
+        kind = 'spec' if L == 'spec' else L.kind
+        if kind == 'relu':
+            l_prev, u_prev = bounds[-1]
+            n = l_prev.shape[1]
+            fz = None if force is None else (force[0][:, pos - n:pos], force[1][:, pos - n:pos])
+            ln, un, alpha, lam, mu = relu_relax(l_prev, u_prev, fz)
+            pos += n
+            relax[len(affine) - 1] = (alpha, lam, mu)
+            bounds.append((ln, un))
+            continue
+        m = len(affine)
+        aff = affine + ([] if kind == 'spec' else [L])
+        gs = _window_chain(aff, m)
+        if kind == 'conv':
+            _, Hm, Wm = L.out_shape
+            groups = L.W.shape[0]
+            per = Hm * Wm
+        else:
+            Hm = Wm = 1
+            groups = 9 if kind == 'spec' else L.n_out
+            per = 1
+        n_rows = groups * per
+        lo_all = np.empty((B, n_rows), F32)
+        up_all = np.empty((B, n_rows), F32)
+        wsize = max(g.size for g in gs)
+        step = max(1, int(chunk_floats // max(1, B * per * wsize)))
+
+        def work(g0, lower, L=L, kind=kind, gs=gs, aff=aff, m=m, Hm=Hm, Wm=Wm, per=per, step=step,
+                 groups=groups, lo_all=lo_all, up_all=up_all):
+            g1 = min(groups, g0 + step)
+            rr = slice(g0 * per, g1 * per)
+            if kind == 'spec':
+                g = gs[0]
+                A0 = spec_W[:, g0:g1, :].astype(F32).reshape(B, g1 - g0, g.C, g.Ph, g.Pw)
+                c0 = np.zeros((B, g1 - g0), F32)
+            else:
+                A0 = _win_rows(L, gs[0], Hm, Wm, slice(g0, g1), B)
+                c0 = np.broadcast_to(layer_bias(L)[rr], (B, (g1 - g0) * per)).astype(F32)
+            res = _win_bound(aff, relax, m, np.array(A0, F32), np.array(c0, F32), Hm, Wm, l0img, u0img, lower)
+            (lo_all if lower else up_all)[:, rr] = res
+
+        futs = [pool.submit(work, g0, lower) for g0 in range(0, groups, step) for lower in (True, False)]
+        for f in futs:
+            f.result()
+        bounds.append((lo_all, up_all))
+        pos += n_rows
+        if kind != 'spec':
+            affine.append(L)
+    pool.shutdown()
+    lb, ub = bounds[-1]
+    return bounds, lb.astype(np.float64), ub.astype(np.float64)

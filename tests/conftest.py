@@ -21,3 +21,18 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "slow" in it.keywords:
             it.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Worst observed parity ratios (error / tolerance) of this session, per case and check."""
+    try:
+        import parity
+    except Exception:
+        return
+    if not parity.OBSERVED:
+        return
+    parity.dump_observed()
+    tr = terminalreporter
+    tr.section("parity: worst observed error / tolerance")
+    for key in sorted(parity.OBSERVED):
+        tr.write_line(f"{parity.OBSERVED[key]:10.4f}  {key}")

@@ -22,7 +22,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 # the programs the backend runs, then programs it must refuse (other traversal order,
 # ReLU relaxation or domain), then programs the reference front end itself refuses
@@ -70,6 +70,8 @@ def worker(out_json):
 
 
 def main():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "constraintflow")):
+        sys.exit("set CF_REFERENCE_ROOT to the reference checkout (the directory holding constraintflow/)")
     import tempfile
     with tempfile.TemporaryDirectory() as tmp:
         out = os.path.join(tmp, "asts.json")

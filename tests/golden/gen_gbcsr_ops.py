@@ -18,13 +18,15 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "")
 
 BIN_OPS = ["add", "sub", "mul", "truediv", "ge", "gt", "le", "lt", "eq", "ne"]
 BOOL_OPS = ["and_", "or_"]
 
 
 def main():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "constraintflow")):
+        sys.exit("set CF_REFERENCE_ROOT to the reference checkout (the directory holding constraintflow/)")
     sys.argv = ["x"]
     sys.path.insert(0, os.path.join(HERE, "refshim", "stubs"))
     sys.path.insert(0, REF_ROOT)

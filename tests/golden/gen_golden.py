@@ -4,8 +4,8 @@ This script is test infrastructure.  It runs only in a container that has the
 reference checkout (ConstraintFlow, pure Python + PyTorch) at REF_ROOT; the GPU
 box never runs it.  Usage::
 
-    python tests/golden/gen_golden.py            # all cases
-    python tests/golden/gen_golden.py dp_w0      # cases whose name starts with dp_w0
+    CF_REFERENCE_ROOT=<reference checkout> python tests/golden/gen_golden.py          # all cases
+    CF_REFERENCE_ROOT=<reference checkout> python tests/golden/gen_golden.py dp_w0    # names starting dp_w0
 
 For every case it
   1. compiles the reference's own certifier program
@@ -34,7 +34,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("CF_REFERENCE_ROOT", "")
 PKG = os.path.join(REPO, "constraintflow-gpu_b200")
 
 # certifier programs of examples/compiler_examples/ whose generated code is kept and run
@@ -56,6 +56,11 @@ CASES = {
     "dp_w3_b4_e2e-4": ("deeppoly", 3, 4, 0.0002),
     "dp_w4_b1_e2o255": ("deeppoly", 4, 1, 2.0 / 255.0),
     "dp_w4_b1_e2o2550": ("deeppoly", 4, 1, 2.0 / 2550.0),
+    # the benchmark batch of the 9x200 MLP and an 8-region batch of the CIFAR conv net, stored
+    # compactly (COMPACT below)
+    "dp_w2_b256_e2e-3": ("deeppoly", 2, 256, 0.002),
+    "dp_w4_b8_e2o255": ("deeppoly", 4, 8, 2.0 / 255.0),
+    "dp_w4_b8_e2o2550": ("deeppoly", 4, 8, 2.0 / 2550.0),
     "crown_w0_b4_e1e-2": ("crown", 0, 4, 0.01),
     "crown_w0_b4_e1e-3": ("crown", 0, 4, 0.001),
     "crown_w2_b4_e2e-3": ("crown", 2, 4, 0.002),
@@ -121,6 +126,14 @@ CASES = {
 }
 
 
+# Cases stored compactly: the per-neuron l/u of the affine layers and the property rows only
+# (l_aff / u_aff), the input box of the first COMPACT_INPUT_ROWS regions (l_in / u_in); a
+# ReLU layer's columns are where(x >= 0, x, 0) of the affine layer below it (deeppoly.cf:20-24:
+# l' = l if l >= 0 else 0, u' likewise), which the generator checks before dropping them.
+COMPACT = {"dp_w2_b256_e2e-3", "dp_w4_b8_e2o255", "dp_w4_b8_e2o2550"}
+COMPACT_INPUT_ROWS = 2
+
+
 def _load_nets():
     spec = importlib.util.spec_from_file_location("cfgpu_nets", os.path.join(PKG, "cfgpu", "nets.py"))
     mod = importlib.util.module_from_spec(spec)
@@ -174,6 +187,28 @@ def _onnx_graph(nets, wl):
               node=nodes, initializer=inits)
 
 
+def _compact(wl, l_all, u_all):
+    """Affine-layer and property columns, and the first regions' input box (COMPACT)."""
+    import numpy as np
+    n0 = wl.input_size
+    keep, pos, prev = [], n0, None
+    for L in wl.layers:
+        sl = slice(pos, pos + L.n_out)
+        if L.kind == "relu":
+            for a in (l_all, u_all):
+                x = a[:, prev]
+                assert np.array_equal(a[:, sl], np.where(x >= 0, x, np.float32(0))), "ReLU columns not derivable"
+        else:
+            keep.append(sl)
+        prev = sl
+        pos += L.n_out
+    keep.append(slice(pos, l_all.shape[1]))  # property rows
+    cols = np.concatenate([np.arange(s.start, s.stop) for s in keep])
+    r = COMPACT_INPUT_ROWS
+    return {"compact": True, "l_aff": l_all[:, cols], "u_aff": u_all[:, cols],
+            "l_in": l_all[:r, :n0], "u_in": u_all[:r, :n0]}
+
+
 def worker(program, outdir, case_names):
     """Runs inside a fresh interpreter: the reference package on sys.path first."""
     sys.argv = ["x"]
@@ -224,18 +259,23 @@ def worker(program, outdir, case_names):
         l_all = ae.d["l"].get_dense().to(torch.float32).numpy()
         u_all = ae.d["u"].get_dense().to(torch.float32).numpy()
         layout = [(str(layer.type).split(".")[-1], int(layer.start), int(layer.end)) for layer in captured["model"]]
+        state = {"l_all": l_all, "u_all": u_all}
+        if name in COMPACT:
+            state = _compact(wl, l_all, u_all)
         np.savez_compressed(
             os.path.join(HERE, f"{name}.npz"),
             program=program, wid=wid, B=B, eps=eps, dataset=wl.dataset,
             X=X.numpy(), y=y.numpy().astype(np.int64),
             weights_digest=nets.weights_digest(wl.layers),
-            lb=lb.numpy(), ub=ub.numpy(), l_all=l_all, u_all=u_all,
+            lb=lb.numpy(), ub=ub.numpy(), **state,
             layout=json.dumps(layout), ref_seconds=dt)
         print(json.dumps({"case": name, "seconds": round(dt, 2), "lb_dtype": str(lb.dtype),
                           "certified": int((lb >= 0).all(dim=1).sum()), "B": B}), flush=True)
 
 
 def main():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "constraintflow")):
+        sys.exit("set CF_REFERENCE_ROOT to the reference checkout (the directory holding constraintflow/)")
     sel = sys.argv[1:]
     if sel == ["--programs-only"]:
         for prog in PROGRAMS:

@@ -20,11 +20,41 @@ Floating-point parity (float32 everywhere, as in the reference):
 * Never looser: lb >= lb_ref - tol and ub <= ub_ref + tol on every neuron whose
   upstream decisions agree.
 """
+import json
+import os
+
 import numpy as np
 
 RTOL = 1e-5
 ATOL = 1e-4
 TIE = 1e-4
+
+# Worst observed ratio (error / tolerance) per (case, check), printed at the end of the
+# session (tests/conftest.py) and written to $CF_PARITY_LOG as JSON when that is set.
+OBSERVED = {}
+
+
+def record(case, check, ratio):
+    """Keep the worst ratio seen for (case, check); returns the ratio."""
+    key = f"{case}::{check}"
+    r = float(ratio)
+    if key not in OBSERVED or r > OBSERVED[key]:
+        OBSERVED[key] = r
+    return r
+
+
+def dump_observed():
+    path = os.environ.get("CF_PARITY_LOG")
+    if path and OBSERVED:
+        old = {}
+        if os.path.exists(path):
+            try:
+                old = json.load(open(path))
+            except Exception:
+                old = {}
+        old.update(OBSERVED)
+        with open(path, "w") as fh:
+            json.dump(old, fh, indent=1, sort_keys=True)
 
 
 def layer_slices(layout_sizes):
@@ -35,8 +65,9 @@ def layer_slices(layout_sizes):
     return out
 
 
-def continuous_errors(x_l, x_u, r_l, r_u, sizes):
-    """Max of |x-ref| / (RTOL|ref| + ATOL*S) over all neurons (<= 1 passes)."""
+def continuous_errors(x_l, x_u, r_l, r_u, sizes, label=None):
+    """Max of |x-ref| / (RTOL|ref| + ATOL*S) over all neurons (<= 1 passes); recorded under
+    label = (case, check) when given."""
     worst = 0.0
     where = None
     for li, sl in enumerate(layer_slices(sizes)):
@@ -50,6 +81,29 @@ def continuous_errors(x_l, x_u, r_l, r_u, sizes):
             if m > worst:
                 worst = m
                 where = (li, np.unravel_index(int(np.argmax(q)), q.shape))
+    if label is not None:
+        record(label[0], label[1], worst)
+    return worst, where
+
+
+def looser_errors(x_l, x_u, r_l, r_u, sizes, label=None):
+    """Never looser: how far x's lower bounds lie below, and its upper bounds above, the
+    reference's, in units of the tolerance RTOL|ref| + ATOL*S.  Returns the worst ratio
+    (<= 1 passes; 0 when x is nowhere looser) and where it occurs."""
+    worst = 0.0
+    where = None
+    for li, sl in enumerate(layer_slices(sizes)):
+        rl, ru = r_l[:, sl].astype(np.float64), r_u[:, sl].astype(np.float64)
+        S = np.maximum(np.abs(rl).max(axis=1, keepdims=True), np.abs(ru).max(axis=1, keepdims=True))
+        S = np.maximum(S, 1e-30)
+        for over, r in ((rl - x_l[:, sl].astype(np.float64), rl), (x_u[:, sl].astype(np.float64) - ru, ru)):
+            q = np.maximum(over, 0.0) / (RTOL * np.abs(r) + ATOL * S)
+            m = float(q.max()) if q.size else 0.0
+            if m > worst:
+                worst = m
+                where = (li, np.unravel_index(int(np.argmax(q)), q.shape))
+    if label is not None:
+        record(label[0], label[1], worst)
     return worst, where
 
 

@@ -57,7 +57,7 @@ def test_gpu_crown_matches_reference(name):
     lb, ub, sl, su = _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
     n0 = c.wl.input_size
     assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     assert _against_oracle(c.wl, c.l0, c.u0, c.spec_W, lb, sl, su) == [C.BRANCH_PASS] * len(c.relu_layers)
@@ -79,7 +79,7 @@ def test_gpu_crown_crossing_branch_matches_reference(name):
     c = Case(name)
     lb, ub, sl, su = _run(_engine(c.wl), c.l0, c.u0, c.spec_W)
     n0 = c.wl.input_size
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     assert _against_oracle(c.wl, c.l0, c.u0, c.spec_W, lb, sl, su) == [C.BRANCH_CROSS] * len(c.relu_layers)
@@ -143,13 +143,13 @@ def test_gpu_crownibp_matches_reference(name):
     lb, ub, sl, su = _cibp_run(c.wl, c.l0, c.u0, c.spec_W)
     n0 = c.wl.input_size
     assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
     bounds, _, _, _ = C.crownibp(c.wl.layers, c.l0, c.u0, c.spec_W)
     ol, ou = O.flatten_bounds(n0, bounds, c.B)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes, label=(c.name, "gpu vs oracle"))
     assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
 
 

@@ -36,13 +36,13 @@ def _run(wl, l0, u0, W, depth, budget=None):
 
 def _check(c, sl, su, lb, depth):
     n0 = c.wl.input_size
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{c.name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
     bounds, _, _, _ = C.custom_stop(c.wl.layers, c.l0, c.u0, c.spec_W, depth)
     ol, ou = O.flatten_bounds(n0, bounds, c.B)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes, label=(c.name, "gpu vs oracle"))
     assert worst <= 1.0, f"{c.name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
 
 

@@ -38,14 +38,14 @@ def test_gpu_dag_matches_reference(name):
     n0 = c.wl.input_size
     assert sl.shape[1] == n0 + sum(c.sizes)
     assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
     np.testing.assert_array_equal(ub, su[:, -9:].astype(np.float64))
     bounds, _, _, _ = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, rel)
     ol, ou = O.flatten_bounds(n0, bounds, c.B)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes, label=(c.name, "gpu vs oracle"))
     assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
 
 

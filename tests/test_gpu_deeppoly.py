@@ -17,6 +17,8 @@ pytestmark = pytest.mark.gpu
 
 MLP_CASES = [n for n in names() if Case(n).wid <= 2]
 CONV_CASES = [n for n in names() if Case(n).wid >= 3]
+# the 3x32x32 net at 8 regions: compared with the reference (own and replayed decisions); the
+# oracle's window restatement needs tens of seconds per region of it
 
 
 def _engine(wl):
@@ -54,9 +56,10 @@ def _check_case(c, lb, ub, sl, su, with_oracle=True):
     np.testing.assert_array_equal(lb, xl[:, -9:].astype(np.float64))
     if with_oracle:
         # (1) against the oracle replaying the GPU's decisions
-        bounds, _, _ = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W, force=(xl, xu))
+        run = O.deeppoly_windows if c.wid >= 3 else O.deeppoly
+        bounds, _, _ = run(c.wl.layers, c.l0, c.u0, c.spec_W, force=(xl, xu))
         ol, ou = O.flatten_bounds(n0, bounds, c.B)
-        worst, where = parity.continuous_errors(xl, xu, ol, ou, c.sizes)
+        worst, where = parity.continuous_errors(xl, xu, ol, ou, c.sizes, label=(c.name, "gpu vs oracle"))
         assert worst <= 1.0, f"{c.name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
         ok, flips, ratio = parity.decision_flips_are_ties(ol, ou, xl, xu, c.sizes, c.relu_layers)
         assert ok, f"{c.name}: oracle would branch differently off-tie ({flips}, {ratio:.3g})"
@@ -65,8 +68,11 @@ def _check_case(c, lb, ub, sl, su, with_oracle=True):
     upto = len(c.sizes) if ff is None else ff + 1
     cut = sum(c.sizes[:upto])
     worst, where = parity.continuous_errors(xl[:, :cut], xu[:, :cut], c.l_all[:, :cut], c.u_all[:, :cut],
-                                            c.sizes[:upto])
+                                            c.sizes[:upto], label=(c.name, "gpu vs reference (own decisions)"))
     assert worst <= 1.0, f"{c.name}: GPU vs reference {worst:.3g}x tolerance at {where}"
+    loose, where = parity.looser_errors(xl[:, :cut], xu[:, :cut], c.l_all[:, :cut], c.u_all[:, :cut],
+                                        c.sizes[:upto], label=(c.name, "gpu looser than reference (own decisions)"))
+    assert loose <= 1.0, f"{c.name}: GPU looser than the reference by {loose:.3g}x tolerance at {where}"
     if ff is not None:
         # the first differing branch must be a tie of the reference's own bounds
         sizes_cut = c.sizes[:ff + 1]
@@ -75,6 +81,7 @@ def _check_case(c, lb, ub, sl, su, with_oracle=True):
         assert ok, f"{c.name}: first branch difference is not a tie ({ratio:.3g})"
     same, nd = parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))
     assert same, f"{c.name}: {nd} verdicts differ from the reference"
+    parity.record(c.name, "verdicts differing from the reference", nd)
 
 
 @pytest.mark.parametrize("name", MLP_CASES)
@@ -86,9 +93,51 @@ def test_deeppoly_mlp_matches_reference(name):
 @pytest.mark.parametrize("name", CONV_CASES)
 def test_deeppoly_conv_matches_reference(name):
     """Conv networks (receptive-field windows).  The 3x32x32 net is compared with the
-    reference's golden bounds directly: its dense CPU oracle takes minutes per region."""
+    reference's golden bounds directly (its CPU oracle takes tens of seconds per region) and,
+    with the reference's decisions replayed, on every layer (test_replay_matches_reference)."""
     c = Case(name)
     _check_case(c, *_gpu_run(c), with_oracle=c.wid <= 3)
+
+
+@pytest.mark.parametrize("name", MLP_CASES + CONV_CASES)
+def test_replay_matches_reference(name):
+    """The GPU replaying the reference's own ReLU decisions (cf_deeppoly_run_replay): every
+    neuron of every layer, including the layers below a tie-induced branch difference of the
+    GPU's own run, agrees with the reference within the tolerance and is never looser than
+    it; the verdicts are identical."""
+    c = Case(name)
+    eng = _engine(c.wl)
+    dev = torch.device("cuda:0")
+    n0 = c.wl.input_size
+    dl = torch.from_numpy(np.concatenate([c.l0, c.l_all], axis=1)).to(dev).contiguous()
+    du = torch.from_numpy(np.concatenate([c.u0, c.u_all], axis=1)).to(dev).contiguous()
+    lb, ub, sl, su = eng.run(torch.from_numpy(c.l0).to(dev), torch.from_numpy(c.u0).to(dev),
+                             torch.from_numpy(c.spec_W).to(dev), want_state=True, replay=(dl, du))
+    xl, xu = sl.cpu().numpy()[:, n0:], su.cpu().numpy()[:, n0:]
+    lb = lb.cpu().numpy()
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes,
+                                            label=(c.name, "gpu vs reference (reference decisions)"))
+    assert worst <= 1.0, f"{c.name}: replayed GPU vs reference {worst:.3g}x tolerance at {where}"
+    loose, where = parity.looser_errors(xl, xu, c.l_all, c.u_all, c.sizes,
+                                        label=(c.name, "gpu looser than reference (reference decisions)"))
+    assert loose <= 1.0, f"{c.name}: replayed GPU looser than the reference by {loose:.3g}x tolerance at {where}"
+    # with the same decisions every branch of the GPU's own bounds agrees except on ties
+    ok, flips, ratio = parity.decision_flips_are_ties(xl, xu, c.l_all, c.u_all, c.sizes, c.relu_layers)
+    assert ok, f"{c.name}: replayed GPU would branch differently off-tie ({flips}, {ratio:.3g})"
+    same, nd = parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))
+    assert same, f"{c.name}: {nd} verdicts differ from the reference"
+
+
+def test_replay_of_own_decisions_is_identity():
+    """Replaying the GPU's own decisions reproduces its bounds bit for bit."""
+    c = Case([n for n in MLP_CASES if n.startswith("dp_w1")][0])
+    eng = _engine(c.wl)
+    lb, ub, sl, su = _gpu_run(c, eng)
+    dev = torch.device("cuda:0")
+    lb2, ub2, sl2, su2 = eng.run(torch.from_numpy(c.l0).to(dev), torch.from_numpy(c.u0).to(dev),
+                                 torch.from_numpy(c.spec_W).to(dev), want_state=True,
+                                 replay=(torch.from_numpy(sl).to(dev), torch.from_numpy(su).to(dev)))
+    assert np.array_equal(sl2.cpu().numpy(), sl) and np.array_equal(su2.cpu().numpy(), su)
 
 
 def test_batch_independence_and_determinism():

@@ -58,14 +58,14 @@ def test_gpu_forward_matches_reference(name):
     lb, ub, sl, su = _run(_engine(c.wl, c.program), c.l0, c.u0, c.spec_W)
     n0 = c.wl.input_size
     assert np.array_equal(sl[:, :n0], c.l0) and np.array_equal(su[:, :n0], c.u0)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"{name}: GPU vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     np.testing.assert_array_equal(lb, sl[:, -9:].astype(np.float64))
     np.testing.assert_array_equal(ub, su[:, -9:].astype(np.float64))
     bounds = _oracle(c.program, c.wl.layers, c.l0, c.u0, c.spec_W)
     ol, ou = O.flatten_bounds(n0, bounds, c.B)
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], ol, ou, c.sizes, label=(c.name, "gpu vs oracle"))
     assert worst <= 1.0, f"{name}: GPU vs oracle {worst:.3g}x tolerance at {where}"
 
 
@@ -133,7 +133,7 @@ def test_gpu_ibp_conv_matches_reference():
     c = Case("ibp_w3_b2_e2e-3")
     lb, ub, sl, su = _run(_engine(c.wl, "ibp"), c.l0, c.u0, c.spec_W)
     n0 = c.wl.input_size
-    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(sl[:, n0:], su[:, n0:], c.l_all, c.u_all, c.sizes, label=(c.name, "gpu vs reference"))
     assert worst <= 1.0, f"GPU vs reference {worst:.3g}x tolerance at {where}"
 
 

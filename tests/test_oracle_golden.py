@@ -12,24 +12,29 @@ import parity
 from golden_cases import Case, names
 from oracle import deeppoly_oracle as O
 
-FAST = [n for n in names() if Case(n).wid <= 3]
-SLOW = [n for n in names() if Case(n).wid == 4]
+FAST = [n for n in names() if Case(n).wid <= 3 and Case(n).B <= 16]
+SLOW = [n for n in names() if Case(n).wid == 4 or Case(n).B > 16]
+CONV_FAST = [n for n in FAST if Case(n).wid == 3]
 
 
-def _check(name):
+def _check(name, run=O.deeppoly):
     c = Case(name)
     # input layer: bit-identical to the reference's clip + normalisation
-    assert np.array_equal(c.l0, c.l0_ref) and np.array_equal(c.u0, c.u0_ref)
+    r = c.l0_ref.shape[0]
+    assert np.array_equal(c.l0[:r], c.l0_ref) and np.array_equal(c.u0[:r], c.u0_ref)
     # replay the reference's decisions: continuous agreement on every neuron
-    bounds, lb, ub = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W, force=(c.l_all, c.u_all))
+    bounds, lb, ub = run(c.wl.layers, c.l0, c.u0, c.spec_W, force=(c.l_all, c.u_all))
     xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
     worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    parity.record(name, f"oracle[{run.__name__}] vs reference", worst)
     assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
+    loose, where = parity.looser_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    assert loose <= 1.0, f"{name}: oracle looser than the reference by {loose:.3g}x tolerance at {where}"
     # with the same upstream decisions, the oracle would decide differently only on ties
     ok, flips, ratio = parity.decision_flips_are_ties(xl, xu, c.l_all, c.u_all, c.sizes, c.relu_layers)
     assert ok, f"{name}: {flips} decision flips, worst at {ratio:.3g} of layer scale"
     # verdicts of the oracle's own (unforced) run
-    bounds2, lb2, ub2 = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W)
+    bounds2, lb2, ub2 = run(c.wl.layers, c.l0, c.u0, c.spec_W)
     scale = np.abs(c.lb).max(axis=1)
     same, nd = parity.verdicts_match(lb2, c.lb, scale)
     assert same, f"{name}: {nd} verdicts differ"
@@ -42,9 +47,35 @@ def test_oracle_matches_reference(name):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("name", SLOW)
-def test_oracle_matches_reference_cifar_conv(name):
+@pytest.mark.parametrize("name", [n for n in SLOW if Case(n).wid <= 3])
+def test_oracle_matches_reference_large_batch(name):
     _check(name)
+
+
+@pytest.mark.parametrize("name", CONV_FAST)
+def test_window_oracle_matches_reference(name):
+    """The receptive-field-window restatement (deeppoly_windows) on the 1x28x28 conv net."""
+    _check(name, O.deeppoly_windows)
+
+
+def test_window_oracle_matches_dense_oracle():
+    """Windows and dense rows give the same bounds on an MLP (whole-image windows) and on the
+    1x28x28 conv net (receptive-field windows), decisions replayed."""
+    for name in (FAST[0], CONV_FAST[0]):
+        c = Case(name)
+        b1, _, _ = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W, force=(c.l_all, c.u_all))
+        b2, _, _ = O.deeppoly_windows(c.wl.layers, c.l0, c.u0, c.spec_W, force=(c.l_all, c.u_all))
+        x1 = O.flatten_bounds(c.wl.input_size, b1, c.B)
+        x2 = O.flatten_bounds(c.wl.input_size, b2, c.B)
+        worst, where = parity.continuous_errors(x2[0], x2[1], x1[0], x1[1], c.sizes)
+        assert worst <= 1.0, f"{name}: windows vs dense {worst:.3g}x tolerance at {where}"
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", [n for n in SLOW if Case(n).wid == 4])
+def test_window_oracle_matches_reference_cifar_conv(name):
+    """The 3x32x32 CIFAR-shaped conv net (dense rows would take minutes per region)."""
+    _check(name, O.deeppoly_windows)
 
 
 def test_relu_relax_formulae():

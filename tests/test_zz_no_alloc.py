@@ -4,8 +4,10 @@ Callers such as a plugin running inside another framework's allocator, or a serv
 that must not touch the allocator while serving, cannot pass a workspace.  This entry
 point uses a fixed device array inside libcfgpu instead.  The test calls it through the
 C ABI twice in a row and checks both results against cf_deeppoly_run with a caller
-workspace, using the parity tolerance of the other GPU tests; it also checks that a
-network too large for the fixed array is rejected with a clear error.
+workspace: bit for bit, since the region chunking of the driver does not change any
+region's arithmetic; after each call cf_deeppoly_check_static reports the device status of
+the fixed array.  It also checks that a network too large for the fixed array, and a CROWN
+batch that does not fit it in one chunk, are rejected with a clear error.
 
 The file name sorts last so that a run stopping at the first failure has already run
 every other test; it also passes alone in a fresh process.
@@ -51,17 +53,38 @@ def test_static_scratch_matches_workspace_entry_point(wid, B):
         st = _lib.lib.cf_deeppoly_run_static(ctypes.byref(eng.net), B, l0.data_ptr(), u0.data_ptr(), W.data_ptr(),
                                              sl.data_ptr(), su.data_ptr(), lb.data_ptr(), ub.data_ptr(), stream)
         _lib.check(st, f"cf_deeppoly_run_static call {call}")
+        _lib.check(_lib.lib.cf_deeppoly_check_static(stream), f"device status after static call {call}")
         torch.cuda.synchronize()
         x_l, x_u = sl.cpu().numpy(), su.cpu().numpy()
         r_l, r_u = sl_ref.cpu().numpy(), su_ref.cpu().numpy()
         assert np.isfinite(x_l).all() and np.isfinite(x_u).all(), f"call {call}: unwritten outputs"
-        assert np.array_equal(x_l[:, :n0], r_l[:, :n0])
         worst, where = parity.continuous_errors(x_l[:, n0:], x_u[:, n0:], r_l[:, n0:], r_u[:, n0:], sizes)
         assert worst <= 1.0, f"call {call}: static vs workspace entry point {worst:.3g}x tolerance at {where}"
-        np.testing.assert_allclose(lb.cpu().numpy(), lb_ref.cpu().numpy(), rtol=parity.RTOL,
-                                   atol=parity.ATOL * float(np.abs(lb_ref.cpu().numpy()).max()))
-        np.testing.assert_allclose(ub.cpu().numpy(), ub_ref.cpu().numpy(), rtol=parity.RTOL,
-                                   atol=parity.ATOL * float(np.abs(ub_ref.cpu().numpy()).max()))
+        # chunking does not change a region's arithmetic: the same bits
+        assert np.array_equal(x_l, r_l) and np.array_equal(x_u, r_u), f"call {call}: state differs"
+        assert np.array_equal(lb.cpu().numpy(), lb_ref.cpu().numpy())
+        assert np.array_equal(ub.cpu().numpy(), ub_ref.cpu().numpy())
+
+
+def test_static_scratch_rejects_crown_batch_beyond_one_chunk():
+    """CROWN decides each ReLU branch over the whole batch, so its batch must fit the fixed
+    array in one chunk; a larger batch is refused before any launch."""
+    from cfgpu import _lib, nets
+    from cfgpu.engine import DeepPolyEngine
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    wl = nets.workload(2)
+    eng = DeepPolyEngine(wl.layers, wl.input_size, dev, certifier="crown")
+    B = 1024
+    assert eng.workspace_bytes(B) > _lib.CF_STATIC_SCRATCH_BYTES >= eng.workspace_bytes(1)
+    l0 = torch.zeros(B, wl.input_size, device=dev)
+    W = torch.zeros(B, 9, 10, device=dev)
+    lb = torch.zeros(B, 9, dtype=torch.float64, device=dev)
+    st = _lib.lib.cf_deeppoly_run_static(ctypes.byref(eng.net), B, l0.data_ptr(), l0.data_ptr(), W.data_ptr(),
+                                         None, None, lb.data_ptr(), lb.data_ptr(),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+    assert st == _lib.CF_ERR_WORKSPACE
+    assert b"whole batch" in _lib.lib.cf_last_error()
 
 
 def test_static_scratch_rejects_oversized_network():
