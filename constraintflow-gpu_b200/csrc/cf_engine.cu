@@ -233,6 +233,7 @@ static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct WsLayout {
   size_t err, wimg, A[2], C[2], X[2], relu, box, state, total;
+  size_t conv_wimg;  // weight image of one conv phase for the tensor-core transposed convolution
   std::vector<size_t> wimg_off;  // per affine index
 };
 
@@ -240,6 +241,14 @@ struct WsLayout {
 static bool use_chain() {
   const char* e = getenv("CF_STEP_IMPL");
   return !(e && strcmp(e, "simt") == 0);
+}
+
+// Tensor-core transposed convolution of the conv windows (cf_window_tc.cu) for a conv layer
+// where it applies, unless CF_CONV_IMPL=simt selects the CUDA-core implicit GEMM.
+static bool use_conv_tc(const cf_layer& L) {
+  const char* e = getenv("CF_CONV_IMPL");
+  if (e && strcmp(e, "simt") == 0) return false;
+  return win_convT_tc_applicable(ConvGeom{L.cin, L.kh, L.kw, L.stride, L.pad}, L.cout);
 }
 
 // The chain keeps the coefficient rows in TMEM: every substitution except the last must
@@ -291,6 +300,14 @@ static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   if (p.has_conv) {
     w.C[0] = off; off += cw_bytes;
     w.C[1] = off; off += cw_bytes;
+  }
+  w.conv_wimg = off;
+  for (size_t a = 0; a < p.affine.size(); ++a) {
+    const cf_layer& L = net->layers[p.affine[a]];
+    if (L.kind == CF_LAYER_CONV && use_conv_tc(L)) {
+      const size_t b = align256(win_convT_tc_scratch_bytes(ConvGeom{L.cin, L.kh, L.kw, L.stride, L.pad}, L.cout));
+      if (off < w.conv_wimg + b) off = w.conv_wimg + b;
+    }
   }
   w.relu = off; off += align256((size_t)3 * Bc * p.relu_total * sizeof(float));
   // custom stop: the relaxed box of a ReLU substituted last (lower and upper rows)
@@ -523,7 +540,11 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       CF_TRY(win_relu_bias(rg, g, X, c, Bc * rg.R, rg.R, ra[j], rl[j], rm[j], Lj.b_dev, c2, st));
       if (Lj.kind == CF_LAYER_CONV) {
         ConvGeom cv{Lj.cin, Lj.kh, Lj.kw, Lj.stride, Lj.pad};
-        CF_TRY(win_convT(rg, g, h, cv, X, Lj.W_dev, Y, st));
+        if (use_conv_tc(Lj))
+          CF_TRY(win_convT_tc(rg, g, h, cv, Lj.cout, X, Lj.W_dev, Y, reinterpret_cast<uint8_t*>(ws + w.conv_wimg),
+                              reinterpret_cast<int*>(ws + w.err), st));
+        else
+          CF_TRY(win_convT(rg, g, h, cv, X, Lj.W_dev, Y, st));
       } else {
         const int64_t K = Lj.n_out, Nn = Lj.n_in;
         CF_TRY(launch_step_gemm_simt(Bc, rg.R, K, Nn, X, Bc * rg.R * K, rg.R * K, K, nullptr, nullptr, Lj.W_dev, Y,

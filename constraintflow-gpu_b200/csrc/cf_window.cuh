@@ -37,6 +37,13 @@ struct ConvPhase {
 
 cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
                     const float* W, float* out, cudaStream_t st);
+// The same transposed convolution as tcgen05 implicit GEMMs (cf_window_tc.cu): applicable
+// when cin >= 8 and the phase's weight image fits in shared memory; `scratch` holds one
+// phase's weight image (win_convT_tc_scratch_bytes), `err` is the device error word.
+bool win_convT_tc_applicable(const ConvGeom& cv, int cout);
+size_t win_convT_tc_scratch_bytes(const ConvGeom& cv, int cout);
+cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout,
+                       const float* in, const float* W, float* out, uint8_t* scratch, int* err, cudaStream_t st);
 cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, const float* c, const float* l0,
                          const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
 

@@ -194,3 +194,30 @@ def test_full_size_batch_against_oracle(wid, B, sample):
     assert worst <= 1.0, f"workload {wid}: {worst:.3g}x tolerance at {where}"
     assert np.isfinite(sl).all() and np.isfinite(su).all()
     assert (sl <= su + 1e-4 * np.abs(su).max()).all(), "lower bound above upper bound"
+
+
+@pytest.mark.parametrize("wid,B", [(3, 16), (4, 2)])
+def test_conv_tensor_core_matches_cuda_core(wid, B, monkeypatch):
+    """The tcgen05 transposed convolution of the conv windows (3xTF32) against the CUDA-core
+    float32 implicit GEMM (CF_CONV_IMPL=simt) on the same regions: every neuron within the
+    parity tolerance, decisions replayed so that a tie cannot make the two runs diverge."""
+    from cfgpu import nets
+    wl = nets.workload(wid)
+    X = nets.centres(wl, B)
+    y = nets.labels(wl, X)
+    l0, u0 = nets.input_box(X, wl.eps, wl.dataset)
+    W = nets.spec_weight(y)
+    dev = torch.device("cuda:0")
+    eng = _engine(wl)
+    l0d, u0d, Wd = l0.to(dev), u0.to(dev), W.to(dev)
+    lb, ub, sl, su = eng.run(l0d, u0d, Wd, want_state=True, check_device=True)
+    monkeypatch.setenv("CF_CONV_IMPL", "simt")
+    lb2, ub2, sl2, su2 = eng.run(l0d, u0d, Wd, want_state=True, check_device=True, replay=(sl, su))
+    n0 = wl.input_size
+    sizes = [L.n_out for L in wl.layers] + [9]
+    x = sl.cpu().numpy()[:, n0:], su.cpu().numpy()[:, n0:]
+    r = sl2.cpu().numpy()[:, n0:], su2.cpu().numpy()[:, n0:]
+    worst, where = parity.continuous_errors(x[0], x[1], r[0], r[1], sizes,
+                                            label=(f"w{wid}_b{B}", "tensor-core vs CUDA-core conv"))
+    assert worst <= 1.0, f"workload {wid}: tensor-core conv vs CUDA-core conv {worst:.3g}x tolerance at {where}"
+    assert np.isfinite(x[0]).all() and np.isfinite(x[1]).all()
