@@ -243,6 +243,14 @@ static bool use_chain() {
   return !(e && strcmp(e, "simt") == 0);
 }
 
+// The fused first-layer kernel (win_convT_first) for the last substitution of a traversal,
+// unless CF_CONV_IMPL=simt or =tc selects the unfused transposed convolution.
+static bool use_conv_first(const WinGeom& g, const WinGeom& h, const cf_layer& L) {
+  const char* e = getenv("CF_CONV_IMPL");
+  if (e && (strcmp(e, "simt") == 0 || strcmp(e, "tc") == 0)) return false;
+  return win_convT_first_applicable(g, h, ConvGeom{L.cin, L.kh, L.kw, L.stride, L.pad}, L.cout);
+}
+
 // Tensor-core transposed convolution of the conv windows (cf_window_tc.cu) for a conv layer
 // where it applies, unless CF_CONV_IMPL=simt selects the CUDA-core implicit GEMM.
 static bool use_conv_tc(const cf_layer& L) {
@@ -538,6 +546,17 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       const WinGeom& h = gs[k + 1];
       prof_step_begin(st);
       CF_TRY(win_relu_bias(rg, g, X, c, Bc * rg.R, rg.R, ra[j], rl[j], rm[j], Lj.b_dev, c2, st));
+      const double rows = 2.0 * Bc * rg.R;
+      const double macs = Lj.kind == CF_LAYER_CONV ? (double)h.C * h.Ph * h.Pw * g.C * Lj.kh * Lj.kw /
+                                                         ((double)Lj.stride * Lj.stride)
+                                                   : (double)Lj.n_out * Lj.n_in;
+      if (j == 0 && Lj.kind == CF_LAYER_CONV && use_conv_first(g, h, Lj)) {
+        // the last substitution, fused with the concretisation (the input-level window is not stored)
+        ConvGeom cv{Lj.cin, Lj.kh, Lj.kw, Lj.stride, Lj.pad};
+        CF_TRY(win_convT_first(rg, g, h, cv, Lj.cout, X, Lj.W_dev, c2, l0, u0, st_l + col, st_u + col, N, st));
+        prof_step_end(st, 2.0 * rows * macs, 4.0 * rows * ((double)g.C * g.Ph * g.Pw * 2));
+        return CF_OK;
+      }
       if (Lj.kind == CF_LAYER_CONV) {
         ConvGeom cv{Lj.cin, Lj.kh, Lj.kw, Lj.stride, Lj.pad};
         if (use_conv_tc(Lj))
@@ -550,10 +569,6 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
         CF_TRY(launch_step_gemm_simt(Bc, rg.R, K, Nn, X, Bc * rg.R * K, rg.R * K, K, nullptr, nullptr, Lj.W_dev, Y,
                                      st));
       }
-      const double rows = 2.0 * Bc * rg.R;
-      const double macs = Lj.kind == CF_LAYER_CONV ? (double)h.C * h.Ph * h.Pw * g.C * Lj.kh * Lj.kw /
-                                                         ((double)Lj.stride * Lj.stride)
-                                                   : (double)Lj.n_out * Lj.n_in;
       prof_step_end(st, 2.0 * rows * macs, 4.0 * rows * ((double)g.C * g.Ph * g.Pw * 2 + (double)h.C * h.Ph * h.Pw));
       float* tX = X;
       X = Y;

@@ -81,50 +81,148 @@ __global__ void k_win_init(RowGeom rg, WinGeom g, const float* __restrict__ W, i
 }
 
 // ------------------------------------------------------------------ relu + bias
-// One block per row.  T(a) = a>=0 ? a*pf : a*nf at in-image positions (0 elsewhere),
-// c_out = c_in + sum mu-terms + sum T(a)*bias[c].  Block tree reduction (deterministic).
+// kT threads per row (a warp for small windows, the whole block for large ones), 256 / kT
+// rows per block.  T(a) = a>=0 ? a*pf : a*nf at in-image positions (0 elsewhere),
+// c_out = c_in + sum mu-terms + sum T(a)*bias[c].  A thread owns one window position p of
+// the Ph x Pw plane (several when the plane is larger than kT) and a fixed subset of the
+// channels, so the plane coordinates and the relaxation offsets are computed once per
+// position; the row sum is a fixed-order shuffle (and, for kT = 256, shared-memory) tree.
+template <int kT>
 __global__ void __launch_bounds__(256) k_win_relu_bias(RowGeom rg, WinGeom g, float* __restrict__ A,
                                                        const float* __restrict__ c_in, int64_t c_ss, int64_t c_bs,
                                                        const float* __restrict__ alpha, const float* __restrict__ lam,
                                                        const float* __restrict__ mu, const float* __restrict__ bias,
                                                        float* __restrict__ c_out) {
-  __shared__ float red[256];
-  const int64_t per = (int64_t)g.C * g.Ph * g.Pw;
-  const int64_t HW = (int64_t)g.H * g.W;
+  __shared__ float red[8];
+  constexpr int kRowsPerBlock = 256 / kT;
+  const int pp = g.Ph * g.Pw;
+  const int HW = g.H * g.W;
+  const int64_t per = (int64_t)g.C * pp;
   const int64_t n_level = (int64_t)g.C * HW;
+  const int64_t rows = 2 * rg.B * rg.R;
+  const int t = threadIdx.x % kT, slot = threadIdx.x / kT;
+  // channel lanes: threads t = cl*pp + p when the plane is smaller than kT
+  const int cstep = pp >= kT ? 1 : kT / pp;
+  const int c0 = pp >= kT ? 0 : t / pp;
+  const int p_first = pp >= kT ? t : t - (t / pp) * pp;
+  const int p_step = pp >= kT ? kT : pp;
+  const bool active = c0 < cstep;
+  for (int64_t r0 = (int64_t)blockIdx.x * kRowsPerBlock; r0 < rows; r0 += (int64_t)gridDim.x * kRowsPerBlock) {
+    const int64_t r = r0 + slot;
+    float acc = 0.0f;
+    int64_t s = 0, b = 0, i = 0;
+    if (r < rows && active) {
+      int oy, ox;
+      row_coords(rg, r, s, b, i, oy, ox);
+      float* a = A + r * per;
+      const float* pf = nullptr;
+      const float* nf = nullptr;
+      if (alpha) {
+        pf = s == 0 ? alpha : lam;
+        nf = s == 0 ? lam : alpha;
+      }
+      for (int p = p_first; p < pp; p += p_step) {
+        const int u = p / g.Pw, v = p - (p / g.Pw) * g.Pw;
+        const int Y = oy * g.sig_h - g.pi_h + u, X = ox * g.sig_w - g.pi_w + v;
+        const bool in = Y >= 0 && Y < g.H && X >= 0 && X < g.W;
+        if (!in) {
+          for (int c = c0; c < g.C; c += cstep) a[(int64_t)c * pp + p] = 0.0f;
+          continue;
+        }
+        const int64_t k0 = b * n_level + (int64_t)Y * g.W + X;
+        for (int c = c0; c < g.C; c += cstep) {
+          const int64_t e = (int64_t)c * pp + p;
+          const float x = a[e];
+          float tr = x;
+          if (alpha) {
+            const int64_t k = k0 + (int64_t)c * HW;
+            tr = x >= 0.0f ? x * pf[k] : x * nf[k];
+            if (s == 0 ? (x < 0.0f) : (x > 0.0f)) acc = fmaf(x, mu[k], acc);
+          }
+          if (bias) acc = fmaf(tr, bias[c], acc);
+          a[e] = tr;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (kT == 256) {
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        acc = tot;
+      }
+      __syncthreads();
+    }
+    if (t == 0 && r < rows) {
+      int64_t ss, bb, ii;
+      int oy, ox;
+      row_coords(rg, r, ss, bb, ii, oy, ox);
+      const float cv = c_in ? c_in[ss * c_ss + bb * c_bs + ii] : 0.0f;
+      c_out[r] = cv + acc;
+    }
+  }
+}
+
+// Whole-image windows (origin 0, the window is the level image: rows of linear layers and
+// of the property): window element e of region b is relaxation index b*n_level + e, so the
+// row is processed in 16-byte pieces.  Same arithmetic as k_win_relu_bias; block per row.
+__global__ void __launch_bounds__(256) k_win_relu_bias_whole(RowGeom rg, WinGeom g, float* __restrict__ A,
+                                                             const float* __restrict__ c_in, int64_t c_ss,
+                                                             int64_t c_bs, const float* __restrict__ alpha,
+                                                             const float* __restrict__ lam,
+                                                             const float* __restrict__ mu,
+                                                             const float* __restrict__ bias,
+                                                             float* __restrict__ c_out) {
+  __shared__ float red[8];
+  const int pp = g.Ph * g.Pw;
+  const int64_t per = (int64_t)g.C * pp;   // == n_level, a multiple of 4
   const int64_t rows = 2 * rg.B * rg.R;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     int64_t s, b, i;
     int oy, ox;
     row_coords(rg, r, s, b, i, oy, ox);
-    float* a = A + r * per;
+    float4* a = reinterpret_cast<float4*>(A + r * per);
+    const float4* pf = nullptr;
+    const float4* nf = nullptr;
+    const float4* m4 = nullptr;
+    if (alpha) {
+      pf = reinterpret_cast<const float4*>((s == 0 ? alpha : lam) + b * per);
+      nf = reinterpret_cast<const float4*>((s == 0 ? lam : alpha) + b * per);
+      m4 = reinterpret_cast<const float4*>(mu + b * per);
+    }
     float acc = 0.0f;
-    for (int64_t e = threadIdx.x; e < per; e += blockDim.x) {
-      const WinPos p = win_pos(g, e, oy, ox);
-      float v = a[e];
-      float tr = 0.0f;
-      if (p.in) {
-        tr = v;
-        if (alpha) {
-          const int64_t k = b * n_level + (int64_t)p.c * HW + (int64_t)p.Y * g.W + p.X;
-          const float al = alpha[k], la = lam[k], m = mu[k];
-          const float pf = s == 0 ? al : la, nf = s == 0 ? la : al;
-          tr = v >= 0.0f ? v * pf : v * nf;
-          if (s == 0 ? (v < 0.0f) : (v > 0.0f)) acc = fmaf(v, m, acc);
+    for (int64_t q = threadIdx.x; q < per / 4; q += blockDim.x) {
+      float4 x = a[q];
+      float xs[4] = {x.x, x.y, x.z, x.w};
+      float tr[4] = {x.x, x.y, x.z, x.w};
+      if (alpha) {
+        const float4 p4 = __ldg(pf + q), n4 = __ldg(nf + q), u4 = __ldg(m4 + q);
+        const float ps[4] = {p4.x, p4.y, p4.z, p4.w}, ns[4] = {n4.x, n4.y, n4.z, n4.w};
+        const float ms[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          tr[e] = xs[e] >= 0.0f ? xs[e] * ps[e] : xs[e] * ns[e];
+          if (s == 0 ? (xs[e] < 0.0f) : (xs[e] > 0.0f)) acc = fmaf(xs[e], ms[e], acc);
         }
-        if (bias) acc = fmaf(tr, bias[p.c], acc);
       }
-      a[e] = tr;
+      if (bias) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc = fmaf(tr[e], __ldg(bias + (4 * q + e) / pp), acc);
+      }
+      a[q] = make_float4(tr[0], tr[1], tr[2], tr[3]);
     }
-    red[threadIdx.x] = acc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
     __syncthreads();
-    for (int o = 128; o > 0; o >>= 1) {
-      if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-      __syncthreads();
-    }
     if (threadIdx.x == 0) {
+      float tot = 0.0f;
+      for (int w = 0; w < 8; ++w) tot += red[w];
       const float cv = c_in ? c_in[s * c_ss + b * c_bs + i] : 0.0f;
-      c_out[r] = cv + red[0];
+      c_out[r] = cv + tot;
     }
     __syncthreads();
   }
@@ -304,6 +402,175 @@ static unsigned grid_for(int64_t work, int64_t per_block, int64_t cap) {
   return (unsigned)(g < 1 ? 1 : g);
 }
 
+// ------------------------------------------------------------------ first layer, fused
+// The last substitution of a traversal through a stride-1 conv layer with at most 4 input
+// channels (the first layer of an image network), fused with the concretisation against the
+// input box, so that the input-level window of a row is never stored.  A block takes rb
+// rows at a time; their windows are staged in shared memory cc channels at a time (each
+// row's channels are contiguous, so the copy is coalesced); a thread computes 4 consecutive
+// output columns of one output row for every input channel, accumulating over channels and
+// taps in registers (the row segment it reads is shared by the kw taps), folds its outputs
+// into the box bound (a >= 0 ? a * box_s : a * box_{1-s} at in-image positions) and the
+// block adds each row's partial bounds in a fixed order.
+template <int NCI, int KW>
+__global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGeom go, int kh, int cout, int Dy,
+                                                   int Dx, int rb, int cc, const float* __restrict__ in,
+                                                   const float* __restrict__ W, const float* __restrict__ c,
+                                                   const float* __restrict__ l0, const float* __restrict__ u0,
+                                                   float* __restrict__ out_l, float* __restrict__ out_u,
+                                                   int64_t ld_out) {
+  extern __shared__ float sm[];
+  const int wn = cout * NCI * kh * KW;
+  float* wsm = sm;                                  // [cout][NCI][kh][KW]
+  const int plane = gi.Ph * gi.Pw;
+  float* xs = sm + ((wn + 3) & ~3);                 // [rb][cc][Ph][Pw]
+  float* part = xs + (size_t)rb * cc * plane;       // [256] partial bounds
+  for (int e = threadIdx.x; e < wn; e += blockDim.x) wsm[e] = W[e];
+  const int XG = (go.Pw + 3) / 4, TPR = go.Ph * XG;
+  const int64_t per_in = (int64_t)gi.C * plane;
+  const int64_t rows = 2 * rg.B * rg.R;
+  const int64_t HW0 = (int64_t)go.H * go.W, n0 = (int64_t)NCI * HW0;
+  const int slot = threadIdx.x / TPR, task = threadIdx.x - (threadIdx.x / TPR) * TPR;
+  const int up = task / XG, xg = task - (task / XG) * XG;
+  for (int64_t r0 = (int64_t)blockIdx.x * rb; r0 < rows; r0 += (int64_t)gridDim.x * rb) {
+    const int64_t r = r0 + slot;
+    const bool active = slot < rb && r < rows;
+    float acc[4][NCI];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int ci = 0; ci < NCI; ++ci) acc[j][ci] = 0.0f;
+    for (int co0 = 0; co0 < cout; co0 += cc) {
+      const int nc = cout - co0 < cc ? cout - co0 : cc;
+      __syncthreads();  // the previous chunk (and the previous rows' partials) are consumed
+      const int per_chunk = nc * plane;
+      for (int e = threadIdx.x; e < rb * per_chunk; e += blockDim.x) {
+        const int rs = e / per_chunk, rem = e - rs * per_chunk;
+        const int64_t row = r0 + rs;
+        xs[(size_t)rs * cc * plane + rem] = row < rows ? in[row * per_in + (int64_t)co0 * plane + rem] : 0.0f;
+      }
+      __syncthreads();
+      if (active) {
+        for (int cix = 0; cix < nc; ++cix) {
+          const float* xp = xs + ((size_t)slot * cc + cix) * plane;
+          const float* wc = wsm + (size_t)(co0 + cix) * NCI * kh * KW;
+          for (int ky = 0; ky < kh; ++ky) {
+            const int u = up + Dy - ky;
+            if (u < 0 || u >= gi.Ph) continue;
+            const float* xr = xp + u * gi.Pw;
+            float xv[4 + KW - 1];
+#pragma unroll
+            for (int q = 0; q < 4 + KW - 1; ++q) {
+              const int v = xg * 4 + Dx - (KW - 1) + q;
+              xv[q] = (v >= 0 && v < gi.Pw) ? xr[v] : 0.0f;
+            }
+#pragma unroll
+            for (int kx = 0; kx < KW; ++kx) {
+#pragma unroll
+              for (int ci = 0; ci < NCI; ++ci) {
+                const float w = wc[(ci * kh + ky) * KW + kx];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[j][ci] = fmaf(xv[j + (KW - 1) - kx], w, acc[j][ci]);
+              }
+            }
+          }
+        }
+      }
+    }
+    float partial = 0.0f;
+    if (active) {
+      int64_t s, b, i;
+      int oy, ox;
+      row_coords(rg, r, s, b, i, oy, ox);
+      const float* pb = (s == 0 ? l0 : u0) + b * n0;
+      const float* nb = (s == 0 ? u0 : l0) + b * n0;
+      const int Y = oy * go.sig_h - go.pi_h + up;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int vo = xg * 4 + j;
+        const int X = ox * go.sig_w - go.pi_w + vo;
+        if (vo >= go.Pw || Y < 0 || Y >= go.H || X < 0 || X >= go.W) continue;
+#pragma unroll
+        for (int ci = 0; ci < NCI; ++ci) {
+          const int64_t k = (int64_t)ci * HW0 + (int64_t)Y * go.W + X;
+          const float a = acc[j][ci];
+          partial = fmaf(a, a >= 0.0f ? pb[k] : nb[k], partial);
+        }
+      }
+    }
+    part[threadIdx.x] = partial;
+    __syncthreads();
+    if (threadIdx.x < rb && r0 + threadIdx.x < rows) {
+      const int64_t rr = r0 + threadIdx.x;
+      float tot = 0.0f;
+      for (int t = 0; t < TPR; ++t) tot += part[threadIdx.x * TPR + t];
+      int64_t s, b, i;
+      int oy, ox;
+      row_coords(rg, rr, s, b, i, oy, ox);
+      const float res = tot + c[rr];
+      if (s == 0) out_l[b * ld_out + i] = res;
+      else out_u[b * ld_out + i] = res;
+    }
+  }
+}
+
+// shared-memory floats of the staged windows per block
+constexpr int kFirstStageFloats = 8192;
+
+static bool first_geometry(const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout, int& rb, int& cc) {
+  if (cv.s != 1 || cv.cin < 1 || cv.cin > 4 || !(cv.kw == 3 || cv.kw == 5) || cv.kh > 7 || go.C != cv.cin)
+    return false;
+  const int TPR = go.Ph * ((go.Pw + 3) / 4);
+  const int plane = gi.Ph * gi.Pw;
+  if (TPR > 256 || plane > kFirstStageFloats || cout * cv.cin * cv.kh * cv.kw > 4096) return false;
+  rb = 256 / TPR;
+  while (rb > 1 && rb * plane > kFirstStageFloats) --rb;
+  cc = kFirstStageFloats / (rb * plane);
+  if (cc > cout) cc = cout;
+  return cc >= 1;
+}
+
+bool win_convT_first_applicable(const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout) {
+  int rb, cc;
+  return first_geometry(gi, go, cv, cout, rb, cc);
+}
+
+cf_status win_convT_first(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout,
+                          const float* in, const float* W, const float* c, const float* l0, const float* u0,
+                          float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
+  int rb, cc;
+  CF_REQUIRE(first_geometry(gi, go, cv, cout, rb, cc), CF_ERR_UNSUPPORTED, "win_convT_first: geometry");
+  const int64_t rows = 2 * rg.B * rg.R;
+  if (rows == 0) return CF_OK;
+  const int Dy = gi.pi_h + cv.pad - go.pi_h, Dx = gi.pi_w + cv.pad - go.pi_w;
+  const int wn = cout * cv.cin * cv.kh * cv.kw;
+  const size_t smem = (size_t)(((wn + 3) & ~3) + rb * cc * gi.Ph * gi.Pw + 256) * sizeof(float);
+  const unsigned grid = grid_for(rows, rb, 148 * 16);
+#define CF_FIRST(NCI, KW)                                                                                          \
+  do {                                                                                                             \
+    cudaFuncSetAttribute(k_win_first<NCI, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);            \
+    k_win_first<NCI, KW><<<grid, 256, smem, st>>>(rg, gi, go, cv.kh, cout, Dy, Dx, rb, cc, in, W, c, l0, u0, out_l, \
+                                                  out_u, ld_out);                                                  \
+  } while (0)
+  if (cv.kw == 3) {
+    switch (cv.cin) {
+      case 1: CF_FIRST(1, 3); break;
+      case 2: CF_FIRST(2, 3); break;
+      case 3: CF_FIRST(3, 3); break;
+      default: CF_FIRST(4, 3); break;
+    }
+  } else {
+    switch (cv.cin) {
+      case 1: CF_FIRST(1, 5); break;
+      case 2: CF_FIRST(2, 5); break;
+      case 3: CF_FIRST(3, 5); break;
+      default: CF_FIRST(4, 5); break;
+    }
+  }
+#undef CF_FIRST
+  return check_launch("k_win_first");
+}
+
 cf_status win_init(const RowGeom& rg, const WinGeom& g, const float* W, int64_t w_bs, bool conv, float* out,
                    cudaStream_t st) {
   const int64_t total = 2 * rg.B * rg.R * (int64_t)g.C * g.Ph * g.Pw;
@@ -334,8 +601,19 @@ cf_status win_relu_bias(const RowGeom& rg, const WinGeom& g, float* A, const flo
                         cudaStream_t st) {
   const int64_t rows = 2 * rg.B * rg.R;
   if (rows == 0) return CF_OK;
-  k_win_relu_bias<<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c_in, c_ss, c_bs, alpha, lam, mu, bias,
-                                                                c_out);
+  const int64_t per = (int64_t)g.C * g.Ph * g.Pw;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  const bool whole = g.sig_h == 0 && g.sig_w == 0 && g.pi_h == 0 && g.pi_w == 0 && g.Ph == g.H && g.Pw == g.W;
+  if (whole && per % 4 == 0 && a16(A) && (!alpha || (a16(alpha) && a16(lam) && a16(mu)))) {
+    k_win_relu_bias_whole<<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c_in, c_ss, c_bs, alpha, lam, mu,
+                                                                       bias, c_out);
+  } else if (per <= 2048) {   // a warp per row, 8 rows per block
+    k_win_relu_bias<32><<<grid_for(rows, 8, 148 * 64), 256, 0, st>>>(rg, g, A, c_in, c_ss, c_bs, alpha, lam, mu,
+                                                                     bias, c_out);
+  } else {
+    k_win_relu_bias<256><<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c_in, c_ss, c_bs, alpha, lam, mu,
+                                                                      bias, c_out);
+  }
   return check_launch("k_win_relu_bias");
 }
 

@@ -37,13 +37,21 @@ struct ConvPhase {
 
 cf_status win_convT(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, const float* in,
                     const float* W, float* out, cudaStream_t st);
-// The same transposed convolution as tcgen05 implicit GEMMs (cf_window_tc.cu): applicable
-// when cin >= 8 and the phase's weight image fits in shared memory; `scratch` holds one
-// phase's weight image (win_convT_tc_scratch_bytes), `err` is the device error word.
+// The same transposed convolution as tcgen05 implicit GEMMs (cf_window_tc.cu), all stride
+// phases in one launch: applicable when a phase's weight image (Cin padded to 16 columns)
+// fits in shared memory and the stride is at most 3; `scratch` holds every phase's weight
+// image (win_convT_tc_scratch_bytes), `err` is the device error word.
 bool win_convT_tc_applicable(const ConvGeom& cv, int cout);
 size_t win_convT_tc_scratch_bytes(const ConvGeom& cv, int cout);
 cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout,
                        const float* in, const float* W, float* out, uint8_t* scratch, int* err, cudaStream_t st);
+// The last substitution of a traversal (into the network input) through a stride-1 conv
+// layer with at most 4 input channels, fused with the concretisation: writes the bounds of
+// rows (s, b, i) to out_l / out_u[b*ld_out + i] = c + box sum of the input-level window.
+bool win_convT_first_applicable(const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout);
+cf_status win_convT_first(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout,
+                          const float* in, const float* W, const float* c, const float* l0, const float* u0,
+                          float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
 cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, const float* c, const float* l0,
                          const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st);
 

@@ -11,9 +11,10 @@
 // written to out[r, ci, u0 + iy*s, v0 + ix*s] (0 where that position lies outside the
 // level image: the conv's zero padding).
 //
-// Persistent CTAs loop over 128-row M tiles.  The phase's weight image B (tf32 hi and lo
-// planes of B^T, K-major, 128-byte swizzle; N = Cin padded to 16) is copied into shared
-// memory once per CTA and stays there.  Warps 0-7 gather the A operand chunk by chunk
+// One launch covers all stride phases; each persistent CTA works on one phase and loops over
+// that phase's 128-row M tiles.  The phase's weight image B (tf32 hi and lo planes of B^T,
+// K-major, 128-byte swizzle; N = Cin padded to 16) is copied into shared memory once per CTA
+// and stays there.  Warps 0-7 gather the A operand chunk by chunk
 // (32 k columns; thread <-> tile row, the two halves take 16 columns each; a per-thread tap
 // mask replaces the window bounds test), split it into tf32 hi + lo and store it at its
 // SW128 position; warp 8 allocates TMEM and loads the weights, warp 9 issues the
@@ -38,18 +39,28 @@ constexpr int kWMmaWarp = 9;
 constexpr int kWThreads = 448;           // + 4 drain warps (10-13)
 constexpr int kWMaxTaps = 31;            // tap index 31 marks padded k columns
 
+constexpr int kWMaxPhases = 9;          // stride <= 3
+
+// One launch covers every stride phase of the step.  CTA c works on phase c % S2 only (the
+// grid is a multiple of S2), on that phase's tiles c / S2, + gridDim.x / S2, ...: the S2
+// phase tiles of the same output block run at the same time on neighbouring CTAs, so the
+// interleaved output elements of a 32-byte sector are written together (merged in L2) and
+// the input window every phase reads is fetched from DRAM once.
 struct WinTcParams {
   RowGeom rg;
   WinGeom gi, go;
   ConvGeom cv;
-  ConvPhase ph;
+  int32_t S2;                      // number of phases
+  ConvPhase phs[kWMaxPhases];
+  int32_t Ks[kWMaxPhases], kch[kWMaxPhases], tapsv[kWMaxPhases];
+  uint32_t woff[kWMaxPhases], wbytes[kWMaxPhases];   // weight image of each phase in `wimg`
+  int64_t Mp[kWMaxPhases];         // M of each phase
   const float* in;
   float* out;
-  const uint8_t* wimg;   // kchunks x (hi plane, lo plane) of n_pad rows x 128 B
-  int32_t N, n_pad, K, kchunks, taps;
-  int64_t M;
+  const uint8_t* wimg;   // per phase: kchunks x (hi plane, lo plane) of n_pad rows x 128 B
+  int32_t N, n_pad, kchunks_max;
   int32_t a_stages;
-  uint32_t wimg_bytes;
+  uint32_t wimg_max;     // shared-memory bytes reserved for one phase's image
   int* err;
 };
 
@@ -94,9 +105,9 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* w_region = smem;                                        // resident weight image
-  uint8_t* a_region = smem + ((P.wimg_bytes + 1023u) & ~1023u);    // A stages (hi, lo planes)
+  uint8_t* a_region = smem + ((P.wimg_max + 1023u) & ~1023u);      // A stages (hi, lo planes)
   int2* ktab = reinterpret_cast<int2*>(a_region + (size_t)P.a_stages * 2 * kWAImg);  // per k: (offset, tap)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ktab + P.kchunks * 32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ktab + P.kchunks_max * 32);
   uint64_t* full_a = bars;                 // [a_stages]
   uint64_t* empty_a = bars + 4;            // [a_stages]
   uint64_t* w_full = bars + 8;
@@ -106,8 +117,16 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = P.err;
-  const int64_t n_tiles = (P.M + 127) / 128;
-  const int64_t my_tiles = (int64_t)blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // this CTA's phase and its tiles first, + stride, + 2*stride, ...
+  const int phase = (int)(blockIdx.x % (unsigned)P.S2);
+  const ConvPhase ph = P.phs[phase];
+  const int K = P.Ks[phase], kchunks = P.kch[phase], taps = P.tapsv[phase];
+  const int64_t M = P.Mp[phase];
+  const uint8_t* wimg = P.wimg + P.woff[phase];
+  const uint32_t wimg_bytes = P.wbytes[phase];
+  const int64_t first = blockIdx.x / P.S2, stride = gridDim.x / P.S2;
+  const int64_t n_tiles = (M + 127) / 128;
+  const int64_t my_tiles = first < n_tiles ? (n_tiles - 1 - first) / stride + 1 : 0;
   // two accumulators of n_pad columns, each at a power-of-two column stride >= 32
   uint32_t acc_cols = 32;
   while (acc_cols < (uint32_t)P.n_pad) acc_cols <<= 1;
@@ -128,10 +147,10 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
     fence_mbar_init();
   }
   // k table: k -> (window offset co*plane - ty*Pw - tx, tap index; 31 for padded columns)
-  for (int k = threadIdx.x; k < P.kchunks * 32; k += blockDim.x) {
+  for (int k = threadIdx.x; k < kchunks * 32; k += blockDim.x) {
     int2 e = make_int2(0, kWMaxTaps);
-    if (k < P.K) {
-      const int co = k / P.taps, t = k - co * P.taps, ty = t / P.ph.txn, tx = t - ty * P.ph.txn;
+    if (k < K) {
+      const int co = k / taps, t = k - co * taps, ty = t / ph.txn, tx = t - ty * ph.txn;
       e = make_int2(co * plane_in - ty * P.gi.Pw - tx, t);
     }
     ktab[k] = e;
@@ -156,11 +175,11 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
   if (warp == kWProducerWarp) {
     // ---------------------------------------------------------------- weights, once
     if (lane == 0) {
-      mbar_arrive_expect_tx(w_full, P.wimg_bytes);
+      mbar_arrive_expect_tx(w_full, wimg_bytes);
       // bulk copies of at most 64 KB each (the image is a multiple of 16 bytes)
-      for (uint32_t o = 0; o < P.wimg_bytes; o += 65536u) {
-        const uint32_t nb = P.wimg_bytes - o < 65536u ? P.wimg_bytes - o : 65536u;
-        bulk_g2s(w_region + o, P.wimg + o, nb, w_full);
+      for (uint32_t o = 0; o < wimg_bytes; o += 65536u) {
+        const uint32_t nb = wimg_bytes - o < 65536u ? wimg_bytes - o : 65536u;
+        bulk_g2s(w_region + o, wimg + o, nb, w_full);
       }
       mbar_wait_drain(w_full, 0, err, 61);
     }
@@ -175,8 +194,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
         if (i >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)((i >> 1) & 1) ^ 1u, err, 63)) goto done_m;
         tc_fence_after();
         const uint32_t acc = tbase + buf * acc_cols;
-        for (int c = 0; c < P.kchunks; ++c, ++g) {
-          const int nks = min(4, (P.K - c * 32 + 7) / 8);
+        for (int c = 0; c < kchunks; ++c, ++g) {
+          const int nks = min(4, (K - c * 32 + 7) / 8);
           const uint32_t stage = g % (uint32_t)P.a_stages, round = g / (uint32_t)P.a_stages;
           if (!mbar_wait(&full_a[stage], round & 1u, err, 64)) goto done_m;
           tc_fence_after();
@@ -207,40 +226,56 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
     uint32_t soff[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) soff[q] = (uint32_t)r * 128u + ((((uint32_t)(half * 4 + q)) ^ ((uint32_t)r & 7u)) << 4);
-    const int pos = P.ph.ny * P.ph.nx;
+    const int pos = ph.ny * ph.nx;
     const int64_t per_in = (int64_t)P.gi.C * plane_in;
     uint32_t g = 0;
     bool ok = true;
-    for (int64_t i = 0; i < my_tiles && ok; ++i) {
-      const int64_t m = ((int64_t)blockIdx.x + i * gridDim.x) * 128 + r;
-      // this row's window base (at its phase position) and the taps whose input position
-      // lies inside the input window
-      const float* base = P.in;
-      uint32_t tapmask = 0;
-      if (m < P.M) {
+    // this row's window base (at its phase position) and the taps whose input position lies
+    // inside the input window, for tile i
+    const float* base = P.in;
+    uint32_t tapmask = 0;
+    auto tile_row = [&](int64_t i) {
+      const int64_t m = (first + i * stride) * 128 + r;
+      base = P.in;
+      tapmask = 0;
+      if (m < M) {
         const int64_t rr = m / pos;
         const int rem = (int)(m - rr * pos);
-        const int iy = rem / P.ph.nx, ix = rem - iy * P.ph.nx;
-        const int qy = P.ph.q0y + iy, qx = P.ph.q0x + ix;
+        const int iy = rem / ph.nx, ix = rem - iy * ph.nx;
+        const int qy = ph.q0y + iy, qx = ph.q0x + ix;
         base = P.in + rr * per_in + (int64_t)qy * P.gi.Pw + qx;
-        for (int t = 0; t < P.taps; ++t) {
-          const int ty = t / P.ph.txn, tx = t - ty * P.ph.txn;
+        for (int t = 0; t < taps; ++t) {
+          const int ty = t / ph.txn, tx = t - ty * ph.txn;
           const int u = qy - ty, v = qx - tx;
           if (u >= 0 && u < P.gi.Ph && v >= 0 && v < P.gi.Pw) tapmask |= 1u << t;
         }
       }
-      for (int c = 0; c < P.kchunks; ++c, ++g) {
-        const uint32_t stage = g % (uint32_t)P.a_stages, round = g / (uint32_t)P.a_stages;
-        float v[16];
-        const int kb = c * 32 + half * 16;
+    };
+    // the 16 values of chunk c of the current tile row (loaded one chunk ahead, so that their
+    // latency overlaps the split and the store of the chunk before)
+    auto load_chunk = [&](int c, float (&v)[16]) {
+      const int kb = c * 32 + half * 16;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int2 te = ktab[kb + e];
-          v[e] = ((tapmask >> te.y) & 1u) ? __ldg(base + te.x) : 0.0f;
-        }
+      for (int e = 0; e < 16; ++e) {
+        const int2 te = ktab[kb + e];
+        v[e] = ((tapmask >> te.y) & 1u) ? __ldg(base + te.x) : 0.0f;
+      }
+    };
+    float vnext[16];
+    tile_row(0);
+    load_chunk(0, vnext);
+    for (int64_t i = 0; i < my_tiles && ok; ++i) {
+      for (int c = 0; c < kchunks; ++c, ++g) {
+        const uint32_t stage = g % (uint32_t)P.a_stages, round = g / (uint32_t)P.a_stages;
         float hi[16], lo[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) split_tf32(v[e], hi[e], lo[e]);
+        for (int e = 0; e < 16; ++e) split_tf32(vnext[e], hi[e], lo[e]);
+        if (c + 1 < kchunks) {
+          load_chunk(c + 1, vnext);
+        } else if (i + 1 < my_tiles) {
+          tile_row(i + 1);
+          load_chunk(0, vnext);
+        }
         if (!warp_wait(&empty_a[stage], (round & 1u) ^ 1u, err, 66)) {
           ok = false;
           break;
@@ -263,20 +298,20 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
     // ---------------------------------------------------------------- drain (warps 10-13)
     const int q4 = warp & 3;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const int pos = P.ph.ny * P.ph.nx;
+    const int pos = ph.ny * ph.nx;
     const int plane_out = P.go.Ph * P.go.Pw;
     const int64_t per_out = (int64_t)P.go.C * plane_out;
     for (int64_t i = 0; i < my_tiles; ++i) {
       const uint32_t buf = (uint32_t)(i & 1);
-      const int64_t m = ((int64_t)blockIdx.x + i * gridDim.x) * 128 + q4 * 32 + lane;
-      const bool valid = m < P.M;
+      const int64_t m = (first + i * stride) * 128 + q4 * 32 + lane;
+      const bool valid = m < M;
       float* o = nullptr;
       bool inside = false;
       if (valid) {
         const int64_t rr = m / pos;
         const int rem = (int)(m - rr * pos);
-        const int iy = rem / P.ph.nx, ix = rem - iy * P.ph.nx;
-        const int uo = P.ph.u0 + iy * P.cv.s, vo = P.ph.v0 + ix * P.cv.s;
+        const int iy = rem / ph.nx, ix = rem - iy * ph.nx;
+        const int uo = ph.u0 + iy * P.cv.s, vo = ph.v0 + ix * P.cv.s;
         // row rr = (bound, region, i); i's position (oy, ox) in the bounded layer's image
         const int64_t BR = P.rg.B * P.rg.R;
         const int64_t rem2 = rr - (rr / BR) * BR;
@@ -321,10 +356,10 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
 static size_t phase_wimg_bytes(int K, int n_pad) { return (size_t)((K + 31) / 32) * 2 * n_pad * 128; }
 
 size_t win_convT_tc_scratch_bytes(const ConvGeom& cv, int cout) {
-  // the largest phase: taps ceil(kh/s) x ceil(kw/s)
+  // every phase's image, each at most the largest one (taps ceil(kh/s) x ceil(kw/s))
   const int tyn = (cv.kh + cv.s - 1) / cv.s, txn = (cv.kw + cv.s - 1) / cv.s;
   const int n_pad = ((cv.cin + 15) / 16) * 16;
-  return (phase_wimg_bytes(cout * tyn * txn, n_pad) + 1023) & ~(size_t)1023;
+  return (size_t)cv.s * cv.s * ((phase_wimg_bytes(cout * tyn * txn, n_pad) + 1023) & ~(size_t)1023);
 }
 
 bool win_convT_tc_applicable(const ConvGeom& cv, int cout) {
@@ -333,7 +368,7 @@ bool win_convT_tc_applicable(const ConvGeom& cv, int cout) {
   const size_t wb = phase_wimg_bytes(cout * tyn * txn, n_pad);
   const size_t smem = 1024 + ((wb + 1023) & ~(size_t)1023) + (size_t)2 * 2 * kWAImg +
                       (size_t)((cout * tyn * txn + 31) / 32) * 32 * 8 + 16 * 8 + 16;
-  return cv.cin >= 8 && n_pad <= 256 && tyn * txn <= kWMaxTaps && smem <= 227 * 1024;
+  return cv.cin >= 1 && cv.s * cv.s <= kWMaxPhases && n_pad <= 256 && tyn * txn <= kWMaxTaps && smem <= 227 * 1024;
 }
 
 cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout,
@@ -354,8 +389,23 @@ cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, 
     return CF_ERR_CUDA;
   }
   const int s = cv.s;
+  CF_REQUIRE(s * s <= kWMaxPhases, CF_ERR_UNSUPPORTED, "convT_tc: stride %d", s);
   const int Dy = gi.pi_h * s + cv.pad - go.pi_h, Dx = gi.pi_w * s + cv.pad - go.pi_w;
   const int n_pad = ((cv.cin + 15) / 16) * 16;
+  WinTcParams P;
+  memset(&P, 0, sizeof(P));
+  P.rg = rg;
+  P.gi = gi;
+  P.go = go;
+  P.cv = cv;
+  P.in = in;
+  P.out = out;
+  P.N = cv.cin;
+  P.n_pad = n_pad;
+  P.wimg = scratch;
+  P.err = err;
+  int64_t t_max = 0;
+  uint32_t off = 0;
   for (int py = 0; py < s; ++py) {
     const int u0 = ((py - Dy) % s + s) % s;
     const int ny = u0 < go.Ph ? (go.Ph - u0 + s - 1) / s : 0;
@@ -366,40 +416,41 @@ cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, 
       const int txn = cv.kw > px ? (cv.kw - px + s - 1) / s : 0;
       if (ny == 0 || nx == 0) continue;
       CF_REQUIRE(tyn >= 1 && txn >= 1, CF_ERR_UNSUPPORTED, "convT_tc: a phase without taps");
-      ConvPhase ph{py, px, ny, nx, tyn, txn, u0, v0, (u0 + Dy - py) / s, (v0 + Dx - px) / s};
-      WinTcParams P;
-      P.rg = rg;
-      P.gi = gi;
-      P.go = go;
-      P.cv = cv;
-      P.ph = ph;
-      P.in = in;
-      P.out = out;
-      P.N = cv.cin;
-      P.n_pad = n_pad;
-      P.taps = tyn * txn;
-      P.K = cout * P.taps;
-      P.kchunks = (P.K + 31) / 32;
-      P.M = rows * ny * nx;
-      P.wimg = scratch;
-      P.wimg_bytes = (uint32_t)phase_wimg_bytes(P.K, n_pad);
-      P.err = err;
-      const size_t fixed = 1024 + ((P.wimg_bytes + 1023u) & ~1023u) + (size_t)P.kchunks * 32 * 8 + 16 * 8 + 16;
-      P.a_stages = fixed + (size_t)4 * 2 * kWAImg <= 227 * 1024 ? 4
-                   : (fixed + (size_t)3 * 2 * kWAImg <= 227 * 1024 ? 3 : 2);
-      const size_t smem = fixed + (size_t)P.a_stages * 2 * kWAImg;
-      CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "convT_tc: %zu bytes of shared memory", smem);
-      // the phase's weight image (stream-ordered before the GEMM that reads it)
-      const int64_t total = (int64_t)P.kchunks * n_pad * 32;
-      k_win_prep_wimg<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(W, cv, ph, P.N, n_pad, P.K, P.kchunks, scratch);
-      CF_TRY(check_launch("k_win_prep_wimg"));
-      const int64_t tiles = (P.M + 127) / 128;
-      const int64_t grid = tiles < sms ? tiles : sms;
-      k_win_convT_tc<<<(unsigned)grid, kWThreads, smem, st>>>(P);
-      CF_TRY(check_launch("k_win_convT_tc"));
+      const int q = P.S2++;
+      P.phs[q] = ConvPhase{py, px, ny, nx, tyn, txn, u0, v0, (u0 + Dy - py) / s, (v0 + Dx - px) / s};
+      P.tapsv[q] = tyn * txn;
+      P.Ks[q] = cout * P.tapsv[q];
+      P.kch[q] = (P.Ks[q] + 31) / 32;
+      P.Mp[q] = rows * ny * nx;
+      P.woff[q] = off;
+      P.wbytes[q] = (uint32_t)phase_wimg_bytes(P.Ks[q], n_pad);
+      off += (P.wbytes[q] + 1023u) & ~1023u;
+      if (P.wbytes[q] > P.wimg_max) P.wimg_max = P.wbytes[q];
+      if (P.kch[q] > P.kchunks_max) P.kchunks_max = P.kch[q];
+      const int64_t tiles = (P.Mp[q] + 127) / 128;
+      if (tiles > t_max) t_max = tiles;
     }
   }
-  return CF_OK;
+  if (P.S2 == 0) return CF_OK;
+  const size_t fixed = 1024 + ((P.wimg_max + 1023u) & ~1023u) + (size_t)P.kchunks_max * 32 * 8 + 16 * 8 + 16;
+  P.a_stages = fixed + (size_t)4 * 2 * kWAImg <= 227 * 1024 ? 4
+               : (fixed + (size_t)3 * 2 * kWAImg <= 227 * 1024 ? 3 : 2);
+  const size_t smem = fixed + (size_t)P.a_stages * 2 * kWAImg;
+  CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "convT_tc: %zu bytes of shared memory", smem);
+  // every phase's weight image (stream-ordered before the GEMM that reads them)
+  for (int q = 0; q < P.S2; ++q) {
+    const int64_t total = (int64_t)P.kch[q] * n_pad * 32;
+    k_win_prep_wimg<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(W, cv, P.phs[q], P.N, n_pad, P.Ks[q], P.kch[q],
+                                                                     scratch + P.woff[q]);
+    CF_TRY(check_launch("k_win_prep_wimg"));
+  }
+  // a multiple of S2 CTAs (each CTA works on one phase), at most one per SM
+  int64_t per_phase = sms / P.S2;
+  if (per_phase < 1) per_phase = 1;
+  if (per_phase > t_max) per_phase = t_max;
+  const int64_t grid = per_phase * P.S2;
+  k_win_convT_tc<<<(unsigned)grid, kWThreads, smem, st>>>(P);
+  return check_launch("k_win_convT_tc");
 }
 
 }  // namespace cf
