@@ -47,12 +47,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait.  On timeout sets *err (if not already set) and returns false.  The error
-// word (global memory, an L2 round trip) is read only every 16th poll so that a barrier
-// that completes mid-wait is seen at mbarrier latency.
+// word (global memory: a volatile load is an L2 round trip of several hundred cycles, during
+// which a barrier that completes is not seen) is read only every kErrPollInterval polls, so
+// that the common short waits run at mbarrier latency.
+constexpr uint32_t kErrPollInterval = 4096;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 15u && *(volatile int*)err != 0) return false;  // another role already gave up
+    if ((i & (kErrPollInterval - 1)) == kErrPollInterval - 1 && *(volatile int*)err != 0)
+      return false;  // another role already gave up
   }
   atomicCAS(err, 0, site);
   return false;
