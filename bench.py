@@ -405,10 +405,16 @@ def _roofline(m, wl, certifier, steps, dev):
     conv = any(L.kind == "conv" for L in wl.layers)
     chain = getattr(eng, "chain", True)
     zono_tc = certifier in ("zono", "polyzono") and os.environ.get("CF_STEP_IMPL") != "simt"
-    if conv or not chain or (certifier in ("zono", "ibp") and not zono_tc):
-        # receptive-field windows: transposed-conv GEMMs on the CUDA cores (float32 FMA pipe); a network
-        # with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass: k_zono_gemm
-        # over the noise-symbol rows -- all on the FP32 pipe.
+    conv_tc = conv and certifier == "deeppoly" and os.environ.get("CF_CONV_IMPL") != "simt"
+    if conv_tc:
+        # receptive-field windows: the transposed convolutions of the windows run as tcgen05 3xTF32
+        # GEMMs (k_win_convT_tc); the first layer's (3 input channels) is fused with the
+        # concretisation on the CUDA cores (k_win_first); both count as backsubstitution steps
+        peak, bound, peak_src = bf16 / 2.0 / 3.0, "tensor", f"3xTF32 = bf16/2/3 of {src} MEASURED_PEAKS"
+    elif conv or not chain or (certifier in ("zono", "ibp") and not zono_tc):
+        # transposed-conv GEMMs on the CUDA cores (CF_CONV_IMPL=simt) or the zonotope conv kernels; a
+        # network with Add / Concat layers: the general traversal's k_bmm GEMMs; the zonotope pass:
+        # k_zono_gemm over the noise-symbol rows -- all on the FP32 pipe.
         # MEASURED_PEAKS holds no FP32-pipe figure, so the nominal one: SMs x 128 lanes x 2 x max clock
         props = torch.cuda.get_device_properties(dev)
         mhz = m["clocks"].get("sm_max_mhz") or 1965.0
@@ -424,14 +430,17 @@ def _roofline(m, wl, certifier, steps, dev):
                                "CTAs) from one ncu --set full capture of this command") if key in NCU_TRAFFIC else None,
             "kernel": {"zono": "k_zono_persist" if zono_tc else "k_zono_gemm", "ibp": None,
                        "polyzono": "k_chain (backsubstitution) + k_zono_persist"}.get(
-                           certifier, ("transposed convolution of the receptive-field windows" if conv else
+                           certifier, ("k_win_convT_tc (tcgen05 3xTF32) + k_win_first (CUDA cores, first layer), "
+                                       "the transposed convolutions of the receptive-field windows" if conv_tc
+                                       else "transposed convolution of the receptive-field windows" if conv else
                                        "backsubstitution step") if chain else "k_bmm (general traversal)"),
             "peak_source": peak_src,
             "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
             "step_launches": prof["step_launches"]}
     mem = {"kernels": {"zono": "k_zono_bounds, k_zono_relu", "polyzono": "k_relu_relax, k_zono_bounds, "
                        "k_zono_relu, k_to_f64, k_prep_wimg", "ibp": None}.get(
-                           certifier, "k_relu_relax / k_crown_relax, k_concretize, k_to_f64, k_prep_wimg"),
+                           certifier, "k_win_relu_bias (ReLU window pass), k_relu_relax, k_to_f64" if conv else
+                           "k_relu_relax / k_crown_relax, k_concretize, k_to_f64, k_prep_wimg"),
            "launches": int(prof["mem_launches"]),
            "bytes_per_pass": prof["mem_bytes"] / steps,
            "ms_per_pass": prof["mem_ms"] / steps,

@@ -544,8 +544,12 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       const cf_layer& Lj = net->layers[p.affine[j]];
       const WinGeom& g = gs[k];
       const WinGeom& h = gs[k + 1];
-      prof_step_begin(st);
+      // the ReLU window pass is memory-bound: the window read and written, the relaxation of the
+      // level read once per region
+      prof_mem_begin(st);
       CF_TRY(win_relu_bias(rg, g, X, c, Bc * rg.R, rg.R, ra[j], rl[j], rm[j], Lj.b_dev, c2, st));
+      prof_mem_end(st, 8.0 * 2 * Bc * rg.R * g.C * g.Ph * g.Pw + 12.0 * Bc * g.C * g.H * g.W);
+      prof_step_begin(st);
       const double rows = 2.0 * Bc * rg.R;
       const double macs = Lj.kind == CF_LAYER_CONV ? (double)h.C * h.Ph * h.Pw * g.C * Lj.kh * Lj.kw /
                                                          ((double)Lj.stride * Lj.stride)
