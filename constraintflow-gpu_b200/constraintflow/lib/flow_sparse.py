@@ -7,87 +7,65 @@ of the B200 network driver (cf_deeppoly_run through cfgpu.engine), which compute
 same abstract state: every neuron's l/u is written back into abs_elem.d['l'|'u'] and the
 property layer's bounds are returned as float64 (lb, ub), as Flow.flow returns them.
 
-Recognition: the compiler emits a class with Affine and Relu methods; the program is
-identified from the operations its generated code performs.  Every supported program
-has the same Affine (the backward traversal with priority2 = -layer: clamp sign split,
-inner_prod, get_max_priority over the negated layer index) and one of three Relu bodies:
-  * deeppoly.cf: per-neuron triangle relaxation over the neuron itself (convert_to_poly,
-    the u/(u-l) slope, where() on l>=0 / u<=0);
-  * deeppoly_efficient.cf: the same relaxation applied to the affine's L/U polyexps
-    (get_elem('L'/'U', prev)); it composes to exactly DeepPoly's bounds;
-  * crown.cf: whole-layer if(any(...)) branches with the -l > u lower-slope choice.
-Two forward programs are recognised by their own Affine / Relu:
-  * zono.cf (DeepZ): the Affine maps the previous layer's symbolic expression Z and
-    concretises sum |coefficient|; the Relu opens fresh noise symbols (get_new_eps);
-  * ibp.cf: interval arithmetic on the previous layer's l / u (clamp sign split, no
-    traversal); the Relu clamps l and u.
-polyzono.cf carries both states: its Affine is DeepPoly's traversal met (cf_max / cf_min)
-with the zonotope's concretisation, its Relu both relaxations (convert_to_poly and
-get_new_eps); it runs as cfgpu.polyzono's coupled DeepPoly and zonotope passes.
-crownibp.cf branches its Affine on the last_layer metadata: interval bounds below the
-property (map(simplify_lower) over the previous layer's l / u), the traversal for the
-property rows; its Relu is DeepPoly's.
-zid.cf branches on last_layer and on curr[layer] <= 4: zonotope bounds up to layer 4,
-interval bounds above, the traversal for the property rows (cfgpu.zid).
-The custom-stop DeepPoly programs (deeppoly_custom_stop.cf, custom_stops/) stop their
-traversal at layers below curr[layer] - get_start: the generated Affine subtracts the
-constant get_start from the layer metadata (stop_depth_of), and the driver runs DeepPoly
-with that stop depth.
-A transformer object may also declare itself with a ``cf_certifier`` attribute
-('deeppoly', 'crown', 'zono', 'ibp', 'polyzono' or 'crownibp').  Other programs (zono2.cf's whole-layer branches
-among them) raise NotImplementedError.
+Recognition: the compiler emits a class with Affine and Relu methods.  The program is
+identified by the semantic fingerprint of those two methods (program_fingerprint.py: a
+hash of their syntax trees with the compiler's variable names canonicalised), which must be
+the fingerprint of the reference compiler's own output for one of the example programs the
+runtime implements: deeppoly.cf, deeppoly_efficient.cf (composes to DeepPoly's bounds),
+crown.cf, crownibp.cf, zono.cf, ibp.cf, polyzono.cf, zid.cf and the custom-stop DeepPoly
+programs (deeppoly_custom_stop.cf, custom_stops/*.cf).  A program that differs from those
+in any threshold, slope, operator or control flow raises NotImplementedError; the two
+constants the runtime takes as parameters are read from the source first: the custom-stop
+programs' get_start (the generated Affine computes curr[layer] - get_start) and zid.cf's
+zonotope layer bound (curr[layer] <= K, in its Affine and its Relu alike).
+A transformer object may also declare itself with a ``cf_certifier`` attribute (the code
+that cfgpu.codegen emits, after its own semantic checks of the program).
 """
 import inspect
-import re
 
 import torch
 
 from constraintflow.gbcsr.sparse_block import DenseBlock
 from constraintflow.gbcsr.sparse_tensor import SparseTensor
 
+from . import program_fingerprint as PF
 from .network import LayerType
 
-_AFFINE = ("clamp(", "inner_prod(", "get_max_priority(", "filter_trav_exp_not_stop(",
-           "get_metadata('layer'", "operator.neg")
-_DEEPPOLY_RELU = ("convert_to_poly(", "operator.truediv", "operator.le", "operator.ge", "where(")
-_EFFICIENT_RELU = ("get_elem('L', prev", "get_elem('U', prev", "operator.truediv", "operator.le", "operator.ge",
-                   "where(")
-_CROWN_RELU = ("if(", "any(", "operator.gt", "convert_to_poly(", "operator.truediv", "get_elem('U', prev")
-# zono.cf: forward symbol algebra (Affine concretises sum |coefficient|, Relu opens fresh symbols)
-_ZONO_AFFINE = ("get_elem('Z', prev", "get_mat(SymExpSparse.count", "inner_prod(", "clamp(", ".sum(2")
-_ZONO_RELU = ("get_new_eps(", "get_elem('Z', prev", "operator.truediv", "operator.le", "operator.ge", "where(")
-# ibp.cf: interval arithmetic over the previous layer's l / u
-_IBP_AFFINE = ("inner_prod(", "clamp(", "get_elem('l'", "get_elem('u'")
-_IBP_RELU = ("convert_to_float(", "operator.ge", "get_elem('l', prev", "get_elem('u', prev")
-# crownibp.cf: interval bounds below the property (a branch on the last_layer metadata), the
-# traversal only for the property rows; DeepPoly's Relu
-_CROWNIBP_AFFINE = ("get_metadata('last_layer'", "if(", "clamp(", "inner_prod(", "get_max_priority(",
-                    "get_metadata('layer'", "get_elem('l'", "get_elem('u'")
-# polyzono.cf: DeepPoly's traversal met with the zonotope bound; both relaxations in the Relu
-_POLYZONO_AFFINE = _AFFINE + ("get_elem('Z', prev", "cf_max(", "cf_min(")
-_POLYZONO_RELU = ("convert_to_poly(", "get_new_eps(", "get_elem('Z', prev", "operator.truediv", "where(")
+def _methods_source(transformer):
+    cls = type(transformer)
+    try:
+        return inspect.getsource(cls.Affine), inspect.getsource(cls.Relu)
+    except (AttributeError, OSError, TypeError) as e:
+        raise NotImplementedError(f"cannot read the generated transformer: {e}")
 
 
-_STOP_DEPTH = re.compile(r"curr\.get_metadata\('layer'[^)]*\), SparseTensor\(\[\], \[\], 0, torch\.tensor\(\[\]\), "
-                         r"dense_const=(\d+), type= type\(\d+\)\)(?:\.\w+\([^()]*(?:\([^()]*\))?[^()]*\))*, "
-                         r"operator\.sub")
-
-
-_ZID_UPTO = re.compile(r"curr\.get_metadata\('layer'[^)]*\), SparseTensor\(\[\], \[\], 0, torch\.tensor\(\[\]\), "
-                       r"dense_const=(\d+), type= type\(\d+\)\)(?:\.\w+\([^()]*(?:\([^()]*\))?[^()]*\))*, "
-                       r"operator\.le")
+def _known(transformer):
+    """(certifier, strict ReLU test) of a generated transformer from its fingerprint."""
+    _methods_source(transformer)
+    fp = PF.fingerprint(type(transformer))
+    hit = PF.KNOWN.get(fp)
+    if hit is None:
+        raise NotImplementedError(
+            "this runtime runs the reference compiler's output for deeppoly.cf, deeppoly_efficient.cf, "
+            "crown.cf, crownibp.cf, zono.cf, ibp.cf, polyzono.cf, zid.cf and the custom-stop DeepPoly "
+            f"programs; the given transformer ({type(transformer).__name__}, fingerprint {fp}) computes "
+            "something else")
+    return hit
 
 
 def zid_upto_of(transformer):
     """The layer up to which zid.cf bounds neurons by the zonotope (curr[layer] <= 4,
-    zid.cf:38): declared by ``cf_zono_upto`` or read from the generated Affine."""
+    zid.cf:38): declared by ``cf_zono_upto`` or read from the generated Affine and Relu, which
+    must both test the same bound."""
     declared = getattr(transformer, "cf_zono_upto", None)
     if declared is not None:
         return int(declared)
-    found = {int(m) for m in _ZID_UPTO.findall(inspect.getsource(type(transformer).Affine))}
-    if len(found) != 1:
-        raise NotImplementedError(f"zid-style program with layer thresholds {sorted(found)}")
-    return found.pop()
+    affine, relu = _methods_source(transformer)
+    found_a, found_r = PF.params(affine, "zono_upto"), PF.params(relu, "zono_upto")
+    if len(found_a) != 1 or found_a != found_r:
+        raise NotImplementedError(f"zid-style program with layer bounds {sorted(found_a)} (Affine) and "
+                                  f"{sorted(found_r)} (Relu)")
+    return found_a.pop()
 
 
 def stop_depth_of(transformer):
@@ -102,7 +80,7 @@ def stop_depth_of(transformer):
         affine = inspect.getsource(type(transformer).Affine)
     except (AttributeError, OSError, TypeError):
         return None
-    found = {int(m) for m in _STOP_DEPTH.findall(affine)}
+    found = PF.params(affine, "stop_depth")
     if len(found) > 1:
         raise NotImplementedError(f"traversal stops at several depths {sorted(found)}")
     return found.pop() if found else None
@@ -115,55 +93,18 @@ def relu_is_strict(transformer):
     if declared is not None or getattr(transformer, "cf_certifier", None) is not None:
         return bool(declared)
     try:
-        relu = inspect.getsource(type(transformer).Relu)
-    except (AttributeError, OSError, TypeError):
+        return _known(transformer)[1]
+    except NotImplementedError:
         return False
-    return ("if(" not in relu and "any(" not in relu and "operator.ge" not in relu and "operator.le" not in relu
-            and all(k in relu for k in ("convert_to_poly(", "operator.truediv", "operator.gt", "operator.lt",
-                                        "where(")))
 
 
 def certifier_of(transformer):
     """'deeppoly', 'crown', 'zono', 'ibp', 'polyzono', 'crownibp' or 'zid' for a recognised
-    generated transformer, else raises."""
+    generated transformer, else raises NotImplementedError."""
     declared = getattr(transformer, "cf_certifier", None)
     if declared is not None:
         return declared
-    cls = type(transformer)
-    try:
-        relu = inspect.getsource(cls.Relu)
-        affine = inspect.getsource(cls.Affine)
-    except (AttributeError, OSError, TypeError) as e:
-        raise NotImplementedError(f"cannot read the generated transformer: {e}")
-    if (all(k in affine for k in ("get_metadata('last_layer'", "get_metadata('layer'", "get_elem('Z', prev",
-                                   "get_max_priority(", "clamp(", "inner_prod("))
-            and all(k in relu for k in ("get_metadata('last_layer'", "get_new_eps(", "convert_to_poly(",
-                                        "get_elem('Z', prev"))):
-        return "zid"
-    if all(k in affine for k in _POLYZONO_AFFINE) and all(k in relu for k in _POLYZONO_RELU):
-        if "if(" in relu or "any(" in relu:
-            raise NotImplementedError("a polyzono-style program with whole-layer branches")
-        return "polyzono"
-    if all(k in affine for k in _CROWNIBP_AFFINE) and "if(" not in relu and "any(" not in relu and (
-            all(k in relu for k in _DEEPPOLY_RELU)):
-        return "crownibp"
-    if all(k in affine for k in _AFFINE) and relu_is_strict(transformer):
-        return "deeppoly"
-    if all(k in affine for k in _AFFINE):
-        branches = "if(" in relu or "any(" in relu or "operator.gt" in relu
-        if not branches and (all(k in relu for k in _DEEPPOLY_RELU) or all(k in relu for k in _EFFICIENT_RELU)):
-            return "deeppoly"
-        if all(k in relu for k in _CROWN_RELU):
-            return "crown"
-    branches = "if(" in relu or "any(" in relu
-    if all(k in affine for k in _ZONO_AFFINE) and all(k in relu for k in _ZONO_RELU) and not branches:
-        return "zono"
-    if (all(k in affine for k in _IBP_AFFINE) and all(k in relu for k in _IBP_RELU) and "get_max_priority(" not in affine
-            and "get_new_eps(" not in relu and "convert_to_poly(" not in relu and not branches):
-        return "ibp"
-    raise NotImplementedError("this runtime runs the DeepPoly, CROWN, zonotope (zono.cf), interval (ibp.cf), "
-                              "polyzono.cf, crownibp.cf and zid.cf certifier programs; the given "
-                              f"transformer ({cls.__name__}) is a different program")
+    return _known(transformer)[0]
 
 
 class _EngineLayer:

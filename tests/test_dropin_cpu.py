@@ -158,3 +158,101 @@ def test_custom_stop_programs_are_recognised():
             sys.modules.pop("transformers", None)
             if saved is not None:
                 sys.modules["transformers"] = saved
+
+
+def _load_transformer(src, clsname, tmp_path, tag):
+    import importlib.util
+    import sys
+    path = tmp_path / f"transformers_{tag}.py"
+    path.write_text(src)
+    saved = sys.modules.pop("transformers", None)
+    try:
+        spec = importlib.util.spec_from_file_location("transformers", str(path))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["transformers"] = mod
+        spec.loader.exec_module(mod)
+        return getattr(mod, clsname)()
+    finally:
+        sys.modules.pop("transformers", None)
+        if saved is not None:
+            sys.modules["transformers"] = saved
+
+
+def _generated(program):
+    import os
+    here = os.path.dirname(os.path.abspath(__file__))
+    with open(os.path.join(here, "golden", "generated", program, "transformers.py")) as fh:
+        return fh.read()
+
+
+def _relu_part(src):
+    i = src.index("def Relu(")
+    return src[:i], src[i:]
+
+
+def test_fingerprints_of_generated_programs():
+    """The table of known fingerprints is what the reference compiler's output hashes to."""
+    from constraintflow.lib import program_fingerprint as PF
+    import tempfile
+    import pathlib
+    with tempfile.TemporaryDirectory() as d:
+        for program, cls, expect in (("deeppoly", "deeppoly", ("deeppoly", False)),
+                                     ("deeppoly_efficient", "deeppoly", ("deeppoly", False)),
+                                     ("crown", "deeppoly", ("crown", False)), ("zono", "zono", ("zono", False)),
+                                     ("ibp", "ibp", ("ibp", False)), ("polyzono", "polyzono", ("polyzono", False)),
+                                     ("crownibp", "crownibp", ("crownibp", False)), ("zid", "zid", ("zid", False)),
+                                     ("deeppoly_custom_stop", "deeppoly", ("deeppoly", True)),
+                                     ("custom_stops/deeppoly_custom_stop05", "deeppoly", ("deeppoly", True))):
+            obj = _load_transformer(_generated(program), cls, pathlib.Path(d), program.replace("/", "_"))
+            assert PF.KNOWN.get(PF.fingerprint(type(obj))) == expect, program
+
+
+def test_dropin_recognition_survives_renaming(tmp_path):
+    """The compiler's CSE variable names do not enter the fingerprint."""
+    import re
+    from constraintflow.lib.flow_sparse import certifier_of
+    src = re.sub(r"\bcse_var_(\d+)\b", lambda m: f"tmp_{int(m.group(1)) * 7 + 3}", _generated("deeppoly"))
+    assert certifier_of(_load_transformer(src, "deeppoly", tmp_path, "renamed")) == "deeppoly"
+
+
+@pytest.mark.parametrize("program,cls,mistake", [
+    # the lower-slope test l + u >= 0 made strict (one comparison only)
+    ("deeppoly", "deeppoly", lambda a, r: (a, r.replace("operator.add, layer_index = layer_index, counter = -1, "
+                                                        "inside_while = False, while_number = -1), cse_var_39, "
+                                                        "operator.ge", "operator.add, layer_index = layer_index, "
+                                                        "counter = -1, inside_while = False, while_number = -1), "
+                                                        "cse_var_39, operator.gt", 1))),
+    # a threshold: the ReLU's zero constant made 1
+    ("deeppoly", "deeppoly", lambda a, r: (a, r.replace("dense_const=0.0", "dense_const=1.0", 1))),
+    # a slope: u / (u - l) made u * (u - l)
+    ("deeppoly", "deeppoly", lambda a, r: (a, r.replace("operator.truediv", "operator.mul", 1))),
+    # the traversal: the negated layer priority made positive
+    ("deeppoly", "deeppoly", lambda a, r: (a.replace("operator.neg", "operator.pos", 1), r)),
+    # the sign split threshold of the backsubstitution
+    ("crown", "deeppoly", lambda a, r: (a.replace("dense_const=0.0", "dense_const=0.5", 1), r)),
+    # a zonotope program whose ReLU scales the fresh symbols differently
+    ("zono", "zono", lambda a, r: (a, r.replace("operator.truediv", "operator.mul", 1))),
+])
+def test_dropin_refuses_planted_mistakes(program, cls, mistake, tmp_path):
+    """A generated program that differs from a known one in a threshold, a slope, an
+    operator or its traversal is refused instead of being run as the known program."""
+    from constraintflow.lib.flow_sparse import certifier_of
+    affine, relu = _relu_part(_generated(program))
+    a2, r2 = mistake(affine, relu)
+    assert (a2, r2) != (affine, relu), "the planted mistake did not change the program"
+    with pytest.raises(NotImplementedError):
+        certifier_of(_load_transformer(a2 + r2, cls, tmp_path, "planted"))
+
+
+def test_zid_thresholds_must_agree(tmp_path):
+    """zid.cf tests curr[layer] <= K in its Affine and in its Relu; a program whose two
+    bounds differ is refused (each alone would be a valid parameter)."""
+    from constraintflow.lib.flow_sparse import certifier_of, zid_upto_of
+    affine, relu = _relu_part(_generated("zid"))
+    obj = _load_transformer(affine + relu, "zid", tmp_path, "zid_ok")
+    assert certifier_of(obj) == "zid" and zid_upto_of(obj) == 4
+    bad = _load_transformer(affine + relu.replace("dense_const=4, type= type(4)", "dense_const=5, type= type(5)"),
+                            "zid", tmp_path, "zid_bad")
+    assert certifier_of(bad) == "zid"      # the bound itself is a parameter
+    with pytest.raises(NotImplementedError):
+        zid_upto_of(bad)
