@@ -7,11 +7,13 @@ Floating-point parity (float32 everywhere, as in the reference):
   of the layer's bound magnitude, not of each bound.  A neuron bound passes when
       |x - ref| <= RTOL * |ref| + ATOL * S
   with S = max |bound| over that layer for that region (l and u together),
-  RTOL = 1e-5 and ATOL = 6e-5.  The absolute floor is the measured disagreement of two
-  float32 implementations with identical decisions: the oracle and the reference differ
-  by up to 4.4e-5*S on the 9x200 MLP (256 regions), the GPU and the reference by up to
-  4.2e-5*S, the GPU and the oracle by up to 5.4e-5*S (a custom-stop program).  Every
-  test records its worst ratio (tests/conftest.py prints them; CF_PARITY_LOG keeps them).
+  RTOL = 1e-5 and ATOL = 8e-5.  The absolute floor is the measured disagreement of two
+  float32 implementations with identical decisions: on the 9x200 MLP (256 regions) the
+  oracle and the reference differ by up to 4.4e-5*S and the GPU and the reference by up to
+  4.2e-5*S; the largest is the custom-stop program at depth 5, whose property rows are
+  concretised against a hidden layer's bounds (much larger than S): oracle vs reference
+  7.3e-5*S, GPU vs oracle 5.1e-5*S.  Every test records its worst ratio (tests/conftest.py
+  prints them; CF_PARITY_LOG keeps them).
 * Discrete decisions.  The ReLU transformer branches on l>=0, u<=0 and l+u>=0
   (deeppoly.cf:20-24).  A bound a few ulps from 0 can take either branch and every
   later layer then differs by far more than rounding.  The continuous comparison is
@@ -30,7 +32,7 @@ import os
 import numpy as np
 
 RTOL = 1e-5
-ATOL = 6e-5
+ATOL = 8e-5
 TIE = 1e-4
 
 # Worst observed ratio (error / tolerance) per (case, check), printed at the end of the

@@ -34,7 +34,7 @@ def _crown(c, **kw):
 def test_crown_oracle_matches_reference(name):
     c = Case(name)
     xl, xu, lb, ub, br = _crown(c)
-    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes, label=(c.name, "oracle vs reference"))
     assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     # the branch taken is visible in the reference's ReLU bounds
@@ -79,7 +79,7 @@ def test_deeppoly_efficient_is_deeppoly(name):
     c = Case(name)
     bounds, lb, _ = O.deeppoly(c.wl.layers, c.l0, c.u0, c.spec_W)
     xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
-    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes, label=(c.name, "oracle vs reference"))
     assert worst <= 1.0, f"{name}: DeepPoly oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
 
@@ -89,7 +89,7 @@ def test_crownibp_oracle_matches_reference(name):
     c = Case(name)
     bounds, lb, ub, _ = C.crownibp(c.wl.layers, c.l0, c.u0, c.spec_W)
     xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
-    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes, label=(c.name, "oracle vs reference"))
     assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
 
@@ -121,7 +121,7 @@ def test_custom_stop_oracle_matches_reference(name):
     c = Case(name)
     bounds, lb, ub, _ = C.custom_stop(c.wl.layers, c.l0, c.u0, c.spec_W, _cs_depth(name))
     xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
-    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes, label=(c.name, "oracle vs reference"))
     assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
 

@@ -52,7 +52,7 @@ def test_cases_present():
 def test_oracle_matches_reference(name):
     c = Case(name)
     xl, xu, lb, ub, br = _run(c)
-    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)
+    worst, where = parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes, label=(c.name, "oracle vs reference"))
     assert worst <= 1.0, f"{name}: oracle vs reference {worst:.3g}x tolerance at {where}"
     assert parity.verdicts_match(lb, c.lb, np.abs(c.lb).max(axis=1))[0]
     if c.program == "zono2":
