@@ -123,8 +123,9 @@ __device__ __forceinline__ void load16g(const float* __restrict__ p, int k0, int
 
 // Bounded wait by every lane of a warp with a warp-uniform result, so that warp-collective
 // code after it (__syncwarp, tcgen05.ld) is reached by all lanes or by none.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
-  const bool ok = mbar_wait(bar, parity, err, site);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int site,
+                                          uint32_t max_polls = kMaxPolls) {
+  const bool ok = mbar_wait(bar, parity, err, site, max_polls);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -272,7 +273,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
     const int K = S.K;
     const bool cvec = (K & 3) == 0;
     if (s > 0) {
-      if (!warp_wait(M.acc_full, nacc & 1, err, 31)) { ok = false; break; }
+      if (!warp_wait(M.acc_full, nacc & 1, err, 31, P.max_polls)) { ok = false; break; }
       ++nacc;
       tc_fence_after();
     }
@@ -280,7 +281,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
     uint32_t s_pf = 0, s_nf = 0, s_mu = 0, s_bias = 0;
     const float *g_pf = nullptr, *g_nf = nullptr, *g_mu = nullptr, *g_bias = S.bias;
     if (kStaged) {
-      if (!warp_wait(&M.coef_full[s & 1], (s >> 1) & 1, err, 34)) { ok = false; break; }
+      if (!warp_wait(&M.coef_full[s & 1], (s >> 1) & 1, err, 34, P.max_polls)) { ok = false; break; }
       const uint32_t cbuf = M.coef + 4u * (uint32_t)((s & 1) * kCoefBufFloats);
       const uint32_t al = cbuf + 4u * (uint32_t)(slot * 3 * kCoefRow), la = al + 4u * kCoefRow;
       s_pf = lower ? al : la;
@@ -350,7 +351,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
           split_tf32(tr, hi[e], lo[e]);
         }
         // only the stage write waits for the MMAs that read this stage kAStages chunks ago
-        if (!warp_wait(&M.empty_a[stage], (round & 1) ^ 1, err, 32)) return false;
+        if (!warp_wait(&M.empty_a[stage], (round & 1) ^ 1, err, 32, P.max_polls)) return false;
         const uint32_t sbase = M.a_region + stage * 2 * kAImg;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -382,8 +383,8 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
         // drain output tile t straight into the concretisation; halves take alternate
         // 16-column groups
         const int ng = tile_width(S, t) / 16, nlim = valid ? S.N : 0;
-        if (kBox && !warp_wait(M.box_full, 0, err, 35)) { ok = false; break; }
-        if (!warp_wait(M.acc_full, nacc & 1, err, 33)) { ok = false; break; }
+        if (kBox && !warp_wait(M.box_full, 0, err, 35, P.max_polls)) { ok = false; break; }
+        if (!warp_wait(M.acc_full, nacc & 1, err, 33, P.max_polls)) { ok = false; break; }
         ++nacc;
         tc_fence_after();
         const uint32_t dst = tbase + (uint32_t)(s & 1) * 256u + lane_off;
@@ -519,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           // step s's alpha / lambda / mu rows of the CTA's regions and the layer bias, into
           // step buffer s%2 once the transform warps have finished step s-2
           const int cb = s & 1;
-          if (!mbar_wait(&coef_empty[cb], ((s >> 1) & 1) ^ 1, err, 13)) goto done_w;
+          if (!mbar_wait(&coef_empty[cb], ((s >> 1) & 1) ^ 1, err, 13, P.max_polls)) goto done_w;
           const uint32_t kb = (uint32_t)S.K * 4u;
           const bool relu = S.alpha != nullptr;
           float* dst = coef_region + cb * kCoefBufFloats;
@@ -538,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         for (int t = 0; t < S.n_tiles; ++t) {
           for (int c = 0; c < S.kchunks; ++c, ++g) {
             const uint32_t stage = g % kWStages, round = g / kWStages;
-            if (!mbar_wait(&empty_w[stage], (round & 1) ^ 1, err, 11)) goto done_w;
+            if (!mbar_wait(&empty_w[stage], (round & 1) ^ 1, err, 11, P.max_polls)) goto done_w;
             uint8_t* sb = w_region + stage * w_stage_bytes;
             const uint8_t* src = S.wimg + ((size_t)t * S.kchunks + c) * 2 * plane;
             const uint32_t bytes = (uint32_t)tile_width(S, t) * 128u;  // rows the MMAs read
@@ -552,13 +553,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       // copies still in flight (error path) land before the CTA can exit
       for (uint32_t x = 0; x < kWStages && x < g; ++x) {
         const uint32_t gl = g - 1 - x, stage = gl % kWStages, round = gl / kWStages;
-        mbar_wait_drain(&full_w[stage], round & 1, err, 12);
+        mbar_wait_drain(&full_w[stage], round & 1, err, 12, P.max_polls);
       }
       for (int x = 0; x < 2 && x < coef_n; ++x) {
         const int sl = coef_n - 1 - x;
-        mbar_wait_drain(&coef_full[sl & 1], (sl >> 1) & 1, err, 14);
+        mbar_wait_drain(&coef_full[sl & 1], (sl >> 1) & 1, err, 14, P.max_polls);
       }
-      if (box_staged) mbar_wait_drain(box_full, 0, err, 15);
+      if (box_staged) mbar_wait_drain(box_full, 0, err, 15, P.max_polls);
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
@@ -574,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             // k-steps of 8 that reach below K (the rest of the chunk is zero padding)
             const int nks = min(4, (S.K - c * 32 + 7) / 8);
             const uint32_t as = g % kAStages, ar = g / kAStages, ws = g % kWStages, wr = g / kWStages;
-            if (!mbar_wait(&full_a[as], ar & 1, err, 21)) goto done_m;
-            if (!mbar_wait(&full_w[ws], wr & 1, err, 22)) goto done_m;
+            if (!mbar_wait(&full_a[as], ar & 1, err, 21, P.max_polls)) goto done_m;
+            if (!mbar_wait(&full_w[ws], wr & 1, err, 22, P.max_polls)) goto done_m;
             tc_fence_after();
             const uint32_t sa = smem_u32(a_region + as * 2 * kAImg), sw = smem_u32(w_region + ws * w_stage_bytes);
             const uint32_t a_hi = sa, a_lo = sa + kAImg, w_hi = sw, w_lo = sw + P.w_lo_off;
@@ -591,13 +592,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             mma_commit(&empty_a[as]);
             mma_commit(&empty_w[ws]);
           }
-          mma_commit(acc_full);
+          // (failure-path test: the first step's accumulator-ready arrival is withheld, so the
+          // transform warps' bounded wait for it gives up)
+          if (!(P.withhold_acc && s == 0)) mma_commit(acc_full);
         }
       }
     done_m:
       // every MMA issued above has completed before TMEM is released
       mma_commit(mma_done);
-      mbar_wait_drain(mma_done, 0, err, 23);
+      mbar_wait_drain(mma_done, 0, err, 23, P.max_polls);
     }
   } else {
     // ---------------------------------------------------------------- transform warps
@@ -638,6 +641,14 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   CF_REQUIRE(P.st[P.S - 1].N == P.n0, CF_ERR_SHAPE, "chain: last step does not reach the input");
   ChainParams Q = P;
   if (Q.ld_box == 0) Q.ld_box = Q.n0;
+  // bounded-wait limit: kMaxPolls, or CF_WAIT_POLLS (>= 256) for the failure-path test;
+  // CF_FAULT=chain_withhold_acc withholds one arrival so that a wait runs out
+  Q.max_polls = kMaxPolls;
+  if (const char* e = getenv("CF_WAIT_POLLS")) {
+    const long v = strtol(e, nullptr, 10);
+    if (v >= 256 && v < (long)kMaxPolls) Q.max_polls = (uint32_t)v;
+  }
+  Q.withhold_acc = fault_injected("chain_withhold_acc") ? 1 : 0;
   CF_REQUIRE(Q.ld_box >= Q.n0, CF_ERR_SHAPE, "chain: box row stride %lld < %lld", (long long)Q.ld_box,
              (long long)Q.n0);
   // weight stage: hi plane then lo plane, each tn_max rows x 128 bytes (1024-aligned)

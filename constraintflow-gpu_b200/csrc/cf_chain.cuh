@@ -38,6 +38,9 @@ struct ChainParams {
   float* out_u;
   int64_t ld_out;
   int* err;                             // device error word (bounded-wait timeouts)
+  uint32_t max_polls;                   // poll limit of every bounded wait (filled by chain_launch)
+  int32_t withhold_acc;                 // failure-path test: the MMA issuer withholds the first
+                                        // step's accumulator-ready arrival (filled by chain_launch)
   int32_t a0_vec, box_vec;              // 16-byte loads allowed for A0 rows / the input box
   uint32_t stage_bytes, w_lo_off;       // filled by chain_launch
   uint32_t box_smem_bytes;              // input-box staging bytes (0: read from global memory)

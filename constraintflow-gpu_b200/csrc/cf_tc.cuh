@@ -8,7 +8,7 @@
 namespace cf {
 namespace tc {
 
-// Every wait on an mbarrier gives up after this many polls (each try_wait itself
+// Every wait on an mbarrier gives up after this many polls (a kernel may pass a smaller limit) (each try_wait itself
 // suspends for a while), records CF_ERR_TIMEOUT in the device error word and returns
 // false so the caller can unwind instead of hanging the GPU.
 constexpr uint32_t kMaxPolls = 1u << 24;
@@ -51,8 +51,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // which a barrier that completes is not seen) is read only every kErrPollInterval polls, so
 // that the common short waits run at mbarrier latency.
 constexpr uint32_t kErrPollInterval = 4096;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site,
+                                          uint32_t max_polls = kMaxPolls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & (kErrPollInterval - 1)) == kErrPollInterval - 1 && *(volatile int*)err != 0)
       return false;  // another role already gave up
@@ -64,8 +65,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // Bounded wait for work already in flight (bulk copies, MMAs) before the CTA releases what
 // that work writes: unlike mbar_wait it does not give up when another role has recorded
 // an error, only after kMaxPolls polls (then it records `site` if nothing was recorded).
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int site) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i)
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int site,
+                                                uint32_t max_polls = kMaxPolls) {
+  for (uint32_t i = 0; i < max_polls; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   atomicCAS(err, 0, site);
   return false;
