@@ -15,7 +15,7 @@ CF_OK, CF_ERR_SHAPE, CF_ERR_UNSUPPORTED, CF_ERR_CUDA, CF_ERR_TIMEOUT, CF_ERR_NUL
     CF_ERR_INJECTED = range(8)
 CF_LAYER_LINEAR, CF_LAYER_CONV, CF_LAYER_RELU = 1, 2, 3
 CF_RELAX_DEEPPOLY, CF_RELAX_CROWN, CF_RELAX_ZONO, CF_RELAX_IBP, CF_RELAX_CROWNIBP = 0, 1, 2, 3, 4
-CF_RELAX_DEEPPOLY_STRICT = 5
+CF_RELAX_DEEPPOLY_STRICT, CF_RELAX_CROWNIBP_STRICT = 5, 6
 CF_MAX_DIMS = 6
 CF_STATIC_SCRATCH_BYTES = 32 << 20
 CF_F32, CF_BOOL = 0, 1

@@ -36,7 +36,8 @@ class DeepPolyEngine:
     with get_start = stop_depth: the traversal bounding a neuron of list layer m stops below
     layer m - stop_depth and concretises there with those neurons' own bounds (linear chains;
     None: every traversal reaches the input).  relu_strict: the lower ReLU slope is 1 where
-    l + u > 0 (those programs' relu_n) instead of l + u >= 0.
+    l + u > 0 (the relu_n of those programs and of zid.cf) instead of l + u >= 0; deeppoly
+    and crownibp.
     """
 
     def __init__(self, layers, input_size, device="cuda", n_spec=N_CLASSES - 1, certifier="deeppoly",
@@ -108,9 +109,11 @@ class DeepPolyEngine:
             self.stop_depth = None if stop_depth is None else int(stop_depth)
             code = relax[certifier]
             if relu_strict:
-                if certifier != "deeppoly":
-                    raise NotImplementedError("the strict lower-slope test applies to the DeepPoly relaxation")
-                code = _lib.CF_RELAX_DEEPPOLY_STRICT
+                strict = {"deeppoly": _lib.CF_RELAX_DEEPPOLY_STRICT, "crownibp": _lib.CF_RELAX_CROWNIBP_STRICT}
+                if certifier not in strict:
+                    raise NotImplementedError("the strict lower-slope test applies to DeepPoly's relaxation "
+                                              "(deeppoly, crownibp)")
+                code = strict[certifier]
             self.net = CfNetwork(len(descs), self._layers, self.input_size, self.n_spec, code,
                                  0 if stop_depth is None else int(stop_depth) + 1)
             self.N = int(lib.cf_network_neurons(ctypes.byref(self.net)))

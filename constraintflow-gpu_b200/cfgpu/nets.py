@@ -1,4 +1,4 @@
-"""Seeded synthetic networks and input regions for the five certification workloads.
+"""Seeded synthetic networks and input regions for the certification workloads.
 
 No public model or dataset is available offline, so every workload is a seeded
 network built in memory plus uniformly drawn input centres:
@@ -6,7 +6,8 @@ network built in memory plus uniformly drawn input centres:
 * weights: ``torch.nn.init.kaiming_normal_`` (fan_in, gain sqrt(2)) drawn from one
   ``torch.Generator().manual_seed(seed)`` in layer order (weight, then bias);
 * biases: zero, except the 784-(100x6)-10 MLP whose biases are N(0, 0.01);
-* centres: ``torch.rand(B, C, H, W, generator=manual_seed(100 + workload id))``;
+* centres: ``torch.rand(B, C, H, W, generator=manual_seed(100 + workload id))`` (the tied
+  workload copies pixel 2r to pixel 2r+1 for its tied pairs);
 * label: argmax of the float32 forward pass at the *normalised* centre.
 
 The layer list mirrors what the reference's ONNX reader produces
@@ -160,6 +161,22 @@ def _branches(seed):
     return L
 
 
+def _tied(seed, pairs=32):
+    """784-64-50-10 ReLU MLP whose first `pairs` first-layer neurons are x[2r] - x[2r+1]
+    (weights exactly +1 and -1, bias 0).  With the two pixels of each pair equal
+    (``centres`` ties them), such a neuron's lower and upper bounds are exact negatives
+    (l + u == 0) under every certifier: the two products are exact, so the sum is rounded
+    once whatever the order.  That is where the strict lower-slope test of zid.cf and the
+    custom-stop programs (relu_n: l + u > 0) and DeepPoly's (l + u >= 0) part."""
+    layers = _mlp([784, 64, 50, 10], seed, None)
+    W = layers[0].W.copy()
+    W[:pairs] = 0.0
+    for r in range(pairs):
+        W[r, 2 * r], W[r, 2 * r + 1] = 1.0, -1.0
+    layers[0].W = W
+    return layers
+
+
 def parents_of(layers, i):
     """Parent indices of layer i (-1 = the network input)."""
     p = layers[i].parents
@@ -172,8 +189,9 @@ def is_chain(layers):
 
 
 def workload(wid):
-    """The certification workloads: id -> Workload (full batch size).  0-4 are chains;
-    5 (residual blocks) and 6 (concatenated branches) are DAGs."""
+    """The certification workloads: id -> Workload (full batch size).  0-4 and 7 are chains;
+    5 (residual blocks) and 6 (concatenated branches) are DAGs; 7 has exactly tied ReLU
+    inputs (a parity case for the lower-slope tests)."""
     if wid == 0:
         return Workload(0, "mlp_784-50x3-10", (1, 28, 28), _mlp([784, 50, 50, 50, 10], 0, None),
                         1, 0.01, 'mnist', 0, "DeepPoly, ReLU MLP 784-50-50-50-10, 1 region, eps 0.01")
@@ -198,6 +216,10 @@ def workload(wid):
     if wid == 6:
         return Workload(6, "branch_784-60-(40|40)-concat-10", (1, 28, 28), _branches(6),
                         32, 0.002, 'mnist', 6, "DeepPoly, two branches concatenated, 32 regions")
+    if wid == 7:
+        return Workload(7, "tied_784-64-50-10", (1, 28, 28), _tied(7), 16, 0.01, 'mnist', 7,
+                        "ReLU MLP 784-64-50-10 with 32 exactly tied first-layer neurons (l + u == 0), "
+                        "16 regions, eps 0.01", extra={"tied_pairs": 32})
     raise ValueError(f"unknown workload {wid}")
 
 
@@ -206,6 +228,10 @@ def centres(wl, B=None):
     Bfull = wl.B if B is None else max(B, wl.B)
     g = torch.Generator().manual_seed(100 + wl.wid)
     X = torch.rand(Bfull, *wl.input_shape, generator=g)
+    tp = wl.extra.get("tied_pairs", 0)
+    if tp:
+        flat = X.view(Bfull, -1)
+        flat[:, 1:2 * tp:2] = flat[:, 0:2 * tp:2]
     return X[: (wl.B if B is None else B)].contiguous()
 
 

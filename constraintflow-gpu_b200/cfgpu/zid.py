@@ -10,11 +10,10 @@ Per list layer k (the reference's layer index; the input is 0):
   property  the DeepPoly traversal (priority2 = -layer) through every layer's polyexps.
 
 Both halves are libcfgpu's own per-layer drivers: a zonotope pass (CF_RELAX_ZONO) for the
-layers up to 4 and a crownibp.cf pass (CF_RELAX_CROWNIBP: interval layers, DeepPoly
-relaxation, one backsubstitution of the property rows) for all layers, whose affine bounds
+layers up to 4 and a crownibp.cf pass with zid.cf's strict lower-slope test
+(CF_RELAX_CROWNIBP_STRICT: interval layers, DeepPoly relaxation with relu_n's l + u > 0,
+zid.cf:22, one backsubstitution of the property rows) for all layers, whose affine bounds
 up to layer 4 are replaced by the zonotope's before the ReLU above them is relaxed.
-zid.cf's relu_n tests l + u > 0; the relaxation here takes l + u >= 0, which differs only
-where l + u == 0 exactly.
 """
 import torch
 
@@ -33,7 +32,7 @@ class ZidEngine:
     def __init__(self, layers, input_size, device="cuda", n_spec=9, zono_upto=ZONO_UPTO):
         layers = list(layers)
         self.zono_upto = int(zono_upto)
-        self.cb = DeepPolyEngine(layers, input_size, device, n_spec=n_spec, certifier="crownibp")
+        self.cb = DeepPolyEngine(layers, input_size, device, n_spec=n_spec, certifier="crownibp", relu_strict=True)
         if self.cb.net is None:
             raise NotImplementedError("zid on a network with Add / Concat layers (the zonotope driver runs "
                                       "chain networks)")

@@ -125,5 +125,5 @@ KNOWN = {
     "a4c4f34561a0a6a17c5cf2fa7e35f4fa": ("zono", False),       # zono.cf
     "4cca3f85897a5185c8842f23c8a30689": ("ibp", False),        # ibp.cf
     "2bbe373f0ca98b2c7cc83383a47fd82f": ("polyzono", False),   # polyzono.cf
-    "e5770c120f0fa8994e1c40311111ad79": ("zid", False),        # zid.cf
+    "e5770c120f0fa8994e1c40311111ad79": ("zid", True),         # zid.cf
 }

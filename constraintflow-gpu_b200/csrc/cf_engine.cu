@@ -83,7 +83,7 @@ static void window_sizing(const cf_network* net, Plan& p);
 cf_status make_plan(const cf_network* net, Plan& p) {
   CF_REQUIRE(net && net->layers && net->n_layers > 0, CF_ERR_NULL, "network: empty");
   CF_REQUIRE(net->n_input > 0 && net->n_spec > 0, CF_ERR_SHAPE, "network: bad input/spec size");
-  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_DEEPPOLY_STRICT, CF_ERR_UNSUPPORTED,
+  CF_REQUIRE(net->relaxation >= CF_RELAX_DEEPPOLY && net->relaxation <= CF_RELAX_CROWNIBP_STRICT, CF_ERR_UNSUPPORTED,
              "network: relaxation %d", net->relaxation);
   CF_REQUIRE(net->stop_depth >= 0, CF_ERR_SHAPE, "network: stop_depth %d", net->stop_depth);
   CF_REQUIRE(net->stop_depth == 0 || net->relaxation == CF_RELAX_DEEPPOLY ||
@@ -588,7 +588,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
     if (p.affine[a] >= li_begin && p.affine[a] < li_end) {
-      if (net->relaxation == CF_RELAX_CROWNIBP) {
+      if (is_interval_layers(net)) {
         // crownibp.cf: the interval bound over the previous layer's state columns (the
         // input's columns start at 0)
         const int64_t in_col = p.affine[a] == 0 ? 0 : p.col[p.affine[a] - 1];
@@ -616,7 +616,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
                                   rl[a], rm[a], err + 16 + 2 * a, err, st));
       } else {
         CF_TRY(launch_relu_relax(Bc, Rl.n_out, st_l + col, st_u + col, N, st_l + rcol, st_u + rcol, N, ra[a],
-                                 rl[a], rm[a], st, net->relaxation == CF_RELAX_DEEPPOLY_STRICT,
+                                 rl[a], rm[a], st, is_strict_relu(net),
                                  dec_l ? dec_l + col : nullptr, dec_u ? dec_u + col : nullptr));
       }
     }

@@ -33,6 +33,16 @@ inline bool is_forward(const cf_network* net) {
   return net->relaxation == CF_RELAX_ZONO || net->relaxation == CF_RELAX_IBP;
 }
 
+// crownibp.cf's interval layers (CF_RELAX_CROWNIBP, and its strict variant for zid.cf)
+inline bool is_interval_layers(const cf_network* net) {
+  return net->relaxation == CF_RELAX_CROWNIBP || net->relaxation == CF_RELAX_CROWNIBP_STRICT;
+}
+
+// DeepPoly's lower ReLU slope is 1 where l + u > 0 (instead of >= 0)
+inline bool is_strict_relu(const cf_network* net) {
+  return net->relaxation == CF_RELAX_DEEPPOLY_STRICT || net->relaxation == CF_RELAX_CROWNIBP_STRICT;
+}
+
 // Forward programs (zono.cf, ibp.cf): workspace for `chunk` regions, and the whole pass.
 size_t forward_workspace_bytes(const cf_network* net, const Plan& p, int64_t chunk);
 cf_status forward_run(const cf_network* net, const Plan& p, int64_t B, const float* l0, const float* u0,

@@ -90,6 +90,8 @@ enum { CF_LAYER_LINEAR = 1, CF_LAYER_CONV = 2, CF_LAYER_RELU = 3 };
  *   CF_RELAX_DEEPPOLY_STRICT  deeppoly.cf with the strict lower-slope test of the custom-stop
  *                      programs (relu_n: l + u > 0, deeppoly_custom_stop.cf:24); the
  *                      other strict comparisons there give DeepPoly's values.
+ *   CF_RELAX_CROWNIBP_STRICT  CF_RELAX_CROWNIBP with that strict lower-slope test: the
+ *                      interval and ReLU layers of zid.cf (relu_n: l + u > 0, zid.cf:22).
  * CF_RELAX_ZONO and CF_RELAX_IBP run forward through cf_deeppoly_run as well; their
  * regions are independent (any chunk size). */
 enum {
@@ -98,7 +100,8 @@ enum {
   CF_RELAX_ZONO = 2,
   CF_RELAX_IBP = 3,
   CF_RELAX_CROWNIBP = 4,
-  CF_RELAX_DEEPPOLY_STRICT = 5
+  CF_RELAX_DEEPPOLY_STRICT = 5,
+  CF_RELAX_CROWNIBP_STRICT = 6
 };
 
 /* One layer.  Linear: W_dev [n_out, n_in] row-major, b_dev [n_out].
@@ -121,7 +124,7 @@ typedef struct cf_network {
   const cf_layer* layers;  /* host array */
   int32_t n_input;
   int32_t n_spec;          /* rows of the property layer (9 for 10 classes) */
-  int32_t relaxation;      /* CF_RELAX_DEEPPOLY, _CROWN, _ZONO, _IBP or _CROWNIBP */
+  int32_t relaxation;      /* one of the CF_RELAX_* codes */
   int32_t stop_depth;      /* 0: every traversal reaches the input.  d > 0 (CF_RELAX_DEEPPOLY
                               or _DEEPPOLY_STRICT, linear layers): the custom-stop programs with get_start = d - 1
                               (examples/compiler_examples/deeppoly_custom_stop.cf:12-17,

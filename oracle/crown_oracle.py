@@ -117,10 +117,11 @@ def _parents(layers, i):
     return tuple(p) if p is not None else (i - 1,)
 
 
-def _deeppoly_relu(l, u, k_in, B):
+def _deeppoly_relu(l, u, k_in, B, strict=False):
     """Generated deeppoly.Relu (deeppoly.cf:20-24,41) over its input layer k_in:
-    L' = alpha x, U' = lam x + mu as diagonal blocks."""
-    l_new, u_new, alpha, lam, mu = relu_relax(l, u)
+    L' = alpha x, U' = lam x + mu as diagonal blocks.  ``strict``: relu_n's l + u > 0
+    (deeppoly_custom_stop.cf:25, zid.cf:22)."""
+    l_new, u_new, alpha, lam, mu = relu_relax(l, u, strict=strict)
     n = l.shape[1]
     eye = np.eye(n, dtype=F32)[None]
     Lp = ({k_in: (alpha[:, :, None] * eye).astype(F32)}, np.zeros_like(l))
@@ -192,7 +193,8 @@ def _stack_poly(P, Q, B):
     return blocks, np.concatenate([P[1], Q[1]], axis=1).astype(F32)
 
 
-def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=False, stop_depth=None):
+def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=False, stop_depth=None,
+            strict=False):
     """Run the reference's DeepPoly or CROWN program over a network of linear / conv / relu /
     add / concat layers listed in the reference reader's breadth-first order.
 
@@ -207,6 +209,8 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=F
              without a traversal); only the property layer is backsubstituted.
     stop_depth : the custom-stop programs' get_start: the traversal bounding layer k stops at
              neurons of layers below k - stop_depth and concretises there with their l / u.
+    strict : DeepPoly's lower slope is 1 where l + u > 0 (the custom-stop programs' relu_n,
+             deeppoly_custom_stop.cf:25) instead of l + u >= 0.
     Returns (bounds, lb, ub, branches): bounds per layer (excluding input, including
     the property layer) of (l [B,n], u [B,n]); lb/ub float64 [B, 9]; branches the
     BRANCH_* code of every ReLU layer (CROWN).
@@ -229,7 +233,7 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=F
                 br, polys[k], bnd[k] = _crown_relu(l, u, ks[0], polys, B)
                 branches.append(br)
             else:
-                polys[k], bnd[k] = _deeppoly_relu(l, u, ks[0], B)
+                polys[k], bnd[k] = _deeppoly_relu(l, u, ks[0], B, strict)
             continue
         if kind == 'add':
             (l1, u1), (l2, u2) = bnd[ks[0]], bnd[ks[1]]
@@ -273,8 +277,9 @@ def certify(layers, l0, u0, spec_W, relaxation="deeppoly", order=min, interval=F
 def custom_stop(layers, l0, u0, spec_W, depth):
     """The reference's deeppoly_custom_stop.cf / custom_stops/deeppoly_custom_stopNN.cf:
     DeepPoly whose traversal for a neuron of layer k stops at layers below k - depth
-    (get_start = depth) and concretises there with those neurons' own bounds."""
-    return certify(layers, l0, u0, spec_W, "deeppoly", min, stop_depth=depth)
+    (get_start = depth) and concretises there with those neurons' own bounds.  Their relu_n
+    is strict (l + u > 0, deeppoly_custom_stop.cf:25)."""
+    return certify(layers, l0, u0, spec_W, "deeppoly", min, stop_depth=depth, strict=True)
 
 
 def crownibp(layers, l0, u0, spec_W, order=max):

@@ -41,10 +41,16 @@ F32 = np.float32
 
 
 # ---------------------------------------------------------------- relaxation
-def relu_relax(l, u, force=None):
+def relu_relax(l, u, force=None, strict=False):
     """DeepPoly ReLU transformer (deeppoly.cf:20-24,41; generated Relu body).
 
     Returns (l', u', alpha, lam, mu): L' = alpha*x, U' = lam*x + mu.
+
+    ``strict``: the lower slope is 1 where l + u > 0 (relu_n of zid.cf:22 and of the
+    custom-stop programs, deeppoly_custom_stop.cf:25) instead of l + u >= 0; the two differ
+    only where l + u == 0 exactly.  Their other strict comparisons (compute_upper: l > 0,
+    u < 0) give DeepPoly's values: at l == 0 the slope u / (u - l) is 1 and the offset 0,
+    at u == 0 both are 0.
 
     ``force`` = (l_dec, u_dec) optionally supplies the bounds from which the three
     discrete decisions (l>=0, u<=0, l+u>=0) are taken, while the continuous values
@@ -58,7 +64,7 @@ def relu_relax(l, u, force=None):
     zero = F32(0.0)
     l_new = np.where(ld >= zero, l, zero).astype(F32)
     u_new = np.where(ud >= zero, u, zero).astype(F32)
-    alpha = ((ld + ud) >= zero).astype(F32)
+    alpha = (((ld + ud) > zero) if strict else ((ld + ud) >= zero)).astype(F32)
     with np.errstate(divide='ignore', invalid='ignore'):
         den = (u - l).astype(F32)
         lam_unst = (u / den).astype(F32)

@@ -282,14 +282,14 @@ def polyzono(layers, l0, u0, spec_W):
     return bounds, lb.astype(np.float64), ub.astype(np.float64)
 
 
-def zid(layers, l0, u0, spec_W, zono_upto=4):
+def zid(layers, l0, u0, spec_W, zono_upto=4, strict=True):
     """Run zid.cf over a chain network (examples/compiler_examples/zid.cf:30-78): list layers
     with reference index <= 4 (the input is 0) bound their neurons by the zonotope (the
     affine's concretisation; the ReLU carries Z as zono.cf does), layers above by the
     interval over the previous layer's l / u (map(simplify_lower)), and the property rows
     by the DeepPoly traversal (priority2 = -layer) through the polyexps of every layer.
-    Every ReLU layer takes DeepPoly's relaxation from its input's bounds; relu_n tests
-    l + u > 0 there, which differs from the l + u >= 0 used here only at l + u == 0.
+    Every ReLU layer takes DeepPoly's relaxation from its input's bounds with relu_n's
+    strict test l + u > 0 (zid.cf:22; ``strict=False`` plants the non-strict test).
     Returns (bounds, lb, ub)."""
     from .crown_oracle import _deeppoly_relu, _traverse
     from .deeppoly_oracle import _affine_rows
@@ -305,7 +305,7 @@ def zid(layers, l0, u0, spec_W, zono_upto=4):
         kind = 'spec' if L == 'spec' else L.kind
         pl, pu = bnd[k - 1]
         if kind == 'relu':
-            polys[k], bnd[k] = _deeppoly_relu(pl, pu, k - 1, B)
+            polys[k], bnd[k] = _deeppoly_relu(pl, pu, k - 1, B, strict=strict)
             if k <= zono_upto:
                 M, c = zono_relu(pl, pu, _widen(M, E), c)
                 E = M.shape[2]

@@ -123,6 +123,12 @@ CASES = {
     "zid_w2_b4_e2e-3": ("zid", 2, 4, 0.002),
     "zid_w1_b8_e5e-4": ("zid", 1, 8, 0.0005),
     "zid_w3_b2_e2e-3": ("zid", 3, 2, 0.002),
+    # the tied network (32 first-layer neurons with l + u == 0 exactly): zid.cf and the
+    # custom-stop programs test l + u > 0, deeppoly.cf and crownibp.cf l + u >= 0
+    "zid_w7_b4_e1e-2": ("zid", 7, 4, 0.01),
+    "cs3_w7_b4_e1e-2": ("deeppoly_custom_stop", 7, 4, 0.01),
+    "dp_w7_b4_e1e-2": ("deeppoly", 7, 4, 0.01),
+    "cibp_w7_b4_e1e-2": ("crownibp", 7, 4, 0.01),
 }
 
 

@@ -18,6 +18,19 @@ def names(program="deeppoly", max_wid=4):
     return out
 
 
+def chain_names(program="deeppoly"):
+    """Cases of `program` on chain networks (linear / conv / relu only), every workload."""
+    return [n for n in names(program, max_wid=99) if nets.is_chain(nets.workload(_wid(n)).layers)]
+
+
+def has_conv(name):
+    return any(L.kind == "conv" for L in nets.workload(_wid(name)).layers)
+
+
+def _wid(name):
+    return int(np.load(os.path.join(GOLDEN, name + ".npz"))["wid"])
+
+
 def _expand_compact(wl, z, l0, u0):
     """Full [B, N - n0] per-neuron l/u of a compactly stored case (gen_golden.COMPACT): the
     affine and property columns as stored, each ReLU layer's columns where(x >= 0, x, 0) of

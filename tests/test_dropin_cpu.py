@@ -200,7 +200,7 @@ def test_fingerprints_of_generated_programs():
                                      ("deeppoly_efficient", "deeppoly", ("deeppoly", False)),
                                      ("crown", "deeppoly", ("crown", False)), ("zono", "zono", ("zono", False)),
                                      ("ibp", "ibp", ("ibp", False)), ("polyzono", "polyzono", ("polyzono", False)),
-                                     ("crownibp", "crownibp", ("crownibp", False)), ("zid", "zid", ("zid", False)),
+                                     ("crownibp", "crownibp", ("crownibp", False)), ("zid", "zid", ("zid", True)),
                                      ("deeppoly_custom_stop", "deeppoly", ("deeppoly", True)),
                                      ("custom_stops/deeppoly_custom_stop05", "deeppoly", ("deeppoly", True))):
             obj = _load_transformer(_generated(program), cls, pathlib.Path(d), program.replace("/", "_"))

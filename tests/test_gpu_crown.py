@@ -16,7 +16,7 @@ import pytest
 import torch
 
 import parity
-from golden_cases import Case, names
+from golden_cases import Case, chain_names, names
 from oracle import crown_oracle as C
 from oracle import deeppoly_oracle as O
 from cfgpu import nets
@@ -123,7 +123,7 @@ def test_gpu_crown_needs_one_chunk():
     assert b"whole batch" in _lib.lib.cf_last_error()
 
 
-CIBP_CASES = names("crownibp")
+CIBP_CASES = chain_names("crownibp")
 
 
 def _cibp_run(wl, l0, u0, W, budget=None):

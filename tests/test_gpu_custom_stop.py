@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import parity
-from golden_cases import Case, names
+from golden_cases import Case, chain_names, names
 from oracle import crown_oracle as C
 from oracle import deeppoly_oracle as O
 from cfgpu import nets
@@ -16,7 +16,7 @@ from cfgpu import nets
 pytestmark = pytest.mark.gpu
 
 CS_CASES = sorted(n for p in ("deeppoly_custom_stop",) + tuple(f"custom_stops/deeppoly_custom_stop{d:02d}"
-                                                                for d in range(19)) for n in names(p))
+                                                                for d in range(19)) for n in chain_names(p))
 
 
 def _depth(name):

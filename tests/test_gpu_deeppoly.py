@@ -10,13 +10,13 @@ import pytest
 import torch
 
 import parity
-from golden_cases import Case, names
+from golden_cases import Case, chain_names, has_conv, names
 from oracle import deeppoly_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-MLP_CASES = [n for n in names() if Case(n).wid <= 2]
-CONV_CASES = [n for n in names() if Case(n).wid >= 3]
+MLP_CASES = [n for n in chain_names() if not has_conv(n)]
+CONV_CASES = [n for n in chain_names() if has_conv(n)]
 # the 3x32x32 net at 8 regions: compared with the reference (own and replayed decisions); the
 # oracle's window restatement needs tens of seconds per region of it
 

@@ -8,11 +8,18 @@ copies and MMAs are awaited before shared memory and tensor memory are released)
 launches of the pass exit early, and cf_deeppoly_check reports CF_ERR_TIMEOUT.  The context
 stays usable: the next pass, without the fault, gives the usual bounds.
 """
+import re
+
 import numpy as np
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+# k_chain's bounded waits (constraintflow-gpu_b200/csrc/cf_chain.cu): weight producer 11, 13;
+# MMA issuer 21, 22; transform / drain warps 31-35.  With the accumulator commit withheld,
+# whichever of them has waited longest gives up first -- all are downstream of it.
+K_CHAIN_SITES = {11, 13, 21, 22, 31, 32, 33, 34, 35}
 
 
 def _inputs(wl, B, dev):
@@ -38,7 +45,9 @@ def test_withheld_arrival_times_out_and_context_recovers(monkeypatch):
     st = _lib.lib.cf_deeppoly_check(eng._ws.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
     msg = _lib.lib.cf_last_error()
     assert st == _lib.CF_ERR_TIMEOUT, (st, msg)
-    assert b"gave up" in msg
+    m = re.search(rb"gave up \(site (\d+)\)", msg)
+    assert m is not None, msg
+    assert int(m.group(1)) in K_CHAIN_SITES, msg
     monkeypatch.delenv("CF_FAULT")
     monkeypatch.delenv("CF_WAIT_POLLS")
     lb, ub = eng.run(l0, u0, W, check_device=True)

@@ -14,14 +14,14 @@ import pytest
 import torch
 
 import parity
-from golden_cases import Case, names
+from golden_cases import Case, chain_names, names
 from oracle import crown_oracle as C
 from oracle import deeppoly_oracle as O
 from cfgpu import nets
 
 CROWN_CASES = names("crown")
 DPE_CASES = names("deeppoly_efficient")
-CIBP_CASES = names("crownibp")
+CIBP_CASES = chain_names("crownibp")
 
 
 def _crown(c, **kw):
@@ -109,7 +109,7 @@ def test_crownibp_planted_backsubstitution_fails():
 
 
 CS_CASES = sorted(n for p in ("deeppoly_custom_stop",) + tuple(f"custom_stops/deeppoly_custom_stop{d:02d}"
-                                                                for d in range(19)) for n in names(p))
+                                                                for d in range(19)) for n in chain_names(p))
 
 
 def _cs_depth(name):
@@ -135,3 +135,33 @@ def test_custom_stop_depth_is_pinned():
         bounds, _, _, _ = C.custom_stop(c.wl.layers, c.l0, c.u0, c.spec_W, _cs_depth(name) + 1)
         xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
         assert parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)[0] > 10.0, name
+
+
+def test_relu_tie_rule_is_pinned():
+    """The tied network (workload 7) has 32 first-layer neurons with l + u == 0 exactly in
+    every region.  The reference's bounds there follow each program's own relu_n: strict
+    (l + u > 0) for zid.cf and the custom-stop programs, non-strict (l + u >= 0) for
+    deeppoly.cf and crownibp.cf.  The oracle with the other rule planted misses every one of
+    these cases by far more than the tolerance."""
+    from oracle import zono_oracle as Z
+
+    def run(name, strict):
+        c = Case(name)
+        if name.startswith("zid"):
+            bounds = Z.zid(c.wl.layers, c.l0, c.u0, c.spec_W, strict=strict)[0]
+        elif name.startswith("cs3"):
+            bounds = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, "deeppoly", min, stop_depth=3, strict=strict)[0]
+        elif name.startswith("cibp"):
+            bounds = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, "deeppoly", max, interval=True, strict=strict)[0]
+        else:
+            bounds = C.certify(c.wl.layers, c.l0, c.u0, c.spec_W, "deeppoly", min, strict=strict)[0]
+        xl, xu = O.flatten_bounds(c.wl.input_size, bounds, c.B)
+        return c, parity.continuous_errors(xl, xu, c.l_all, c.u_all, c.sizes)[0]
+
+    for name, strict in (("zid_w7_b4_e1e-2", True), ("cs3_w7_b4_e1e-2", True), ("dp_w7_b4_e1e-2", False),
+                         ("cibp_w7_b4_e1e-2", False)):
+        c, worst = run(name, strict)
+        n_tied = int((c.l_all[:, :32] + c.u_all[:, :32] == 0).sum())
+        assert n_tied == 32 * c.B and (c.l_all[:, :32] < 0).all(), name
+        assert worst <= 1.0, (name, worst)
+        assert run(name, not strict)[1] > 100.0, name

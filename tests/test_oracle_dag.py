@@ -13,7 +13,8 @@ from oracle import crown_oracle as C
 from oracle import deeppoly_oracle as O
 from cfgpu import nets
 
-DAG_CASES = [n for p in ("deeppoly", "crown") for n in names(p, max_wid=9) if Case(n).wid >= 5]
+DAG_CASES = [n for p in ("deeppoly", "crown") for n in names(p, max_wid=9)
+             if not nets.is_chain(Case(n).wl.layers)]
 
 
 def _certify(c, layers=None, **kw):

@@ -9,11 +9,11 @@ import numpy as np
 import pytest
 
 import parity
-from golden_cases import Case, names
+from golden_cases import Case, chain_names, names
 from oracle import deeppoly_oracle as O
 
-FAST = [n for n in names() if Case(n).wid <= 3 and Case(n).B <= 16]
-SLOW = [n for n in names() if Case(n).wid == 4 or Case(n).B > 16]
+FAST = [n for n in chain_names() if Case(n).wid != 4 and Case(n).B <= 16]
+SLOW = [n for n in chain_names() if Case(n).wid == 4 or Case(n).B > 16]
 CONV_FAST = [n for n in FAST if Case(n).wid == 3]
 
 
