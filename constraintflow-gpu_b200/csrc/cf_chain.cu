@@ -55,10 +55,24 @@ size_t chain_wimg_bytes(int K, int N) {
 }
 
 // W [K, N] row-major -> per (n tile, k chunk): hi and lo tf32 planes of W^T (tile_n rows x
-// 32 k), K-major with the 128-byte swizzle, zero outside [0,N) x [0,K).
-__global__ void k_prep_wimg(const float* __restrict__ W, int K, int N, int tile_n, int n_tiles, int kchunks,
-                            uint8_t* __restrict__ img) {
-  int64_t total = (int64_t)n_tiles * kchunks * tile_n * 32;
+// 32 k), K-major with the 128-byte swizzle, zero outside [0,N) x [0,K).  One launch prepares
+// the images of several layers: job blockIdx.y of the list.
+struct PrepJob {
+  const float* W;
+  uint8_t* img;
+  int32_t K, N, tile_n, n_tiles, kchunks;
+};
+constexpr int kPrepJobs = 32;
+struct PrepList {
+  PrepJob j[kPrepJobs];
+};
+
+__global__ void k_prep_wimg(const __grid_constant__ PrepList L) {
+  const PrepJob& J = L.j[blockIdx.y];
+  const float* __restrict__ W = J.W;
+  uint8_t* __restrict__ img = J.img;
+  const int K = J.K, N = J.N, tile_n = J.tile_n, kchunks = J.kchunks;
+  int64_t total = (int64_t)J.n_tiles * kchunks * tile_n * 32;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     int kl = (int)(e & 31);
     int64_t q = e >> 5;
@@ -78,17 +92,38 @@ __global__ void k_prep_wimg(const float* __restrict__ W, int K, int N, int tile_
   }
 }
 
+cf_status chain_prep_weights_batch(const float* const* W, const int* K, const int* N, uint8_t* const* img, int n,
+                                   cudaStream_t st) {
+  for (int j0 = 0; j0 < n; j0 += kPrepJobs) {
+    PrepList L;
+    memset(&L, 0, sizeof(L));
+    const int m = n - j0 < kPrepJobs ? n - j0 : kPrepJobs;
+    int64_t most = 0;
+    double bytes = 0.0;
+    for (int j = 0; j < m; ++j) {
+      PrepJob& J = L.j[j];
+      J.W = W[j0 + j];
+      J.img = img[j0 + j];
+      J.K = K[j0 + j];
+      J.N = N[j0 + j];
+      chain_tile(J.N, J.tile_n, J.n_tiles);
+      J.kchunks = (J.K + 31) / 32;
+      const int64_t total = (int64_t)J.n_tiles * J.kchunks * J.tile_n * 32;
+      if (total > most) most = total;
+      bytes += 4.0 * J.K * J.N + (double)chain_wimg_bytes(J.K, J.N);   // W in, the hi / lo image out
+    }
+    int64_t blocks = ceil_div(most, 256);
+    if (blocks > 148 * 8 / m + 1) blocks = 148 * 8 / m + 1;
+    prof_mem_begin(st);
+    k_prep_wimg<<<dim3((unsigned)blocks, (unsigned)m), 256, 0, st>>>(L);
+    prof_mem_end(st, bytes);
+    CF_TRY(check_launch("k_prep_wimg"));
+  }
+  return CF_OK;
+}
+
 cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStream_t st) {
-  int tile_n, n_tiles;
-  chain_tile(N, tile_n, n_tiles);
-  int kchunks = (K + 31) / 32;
-  int64_t total = (int64_t)n_tiles * kchunks * tile_n * 32;
-  int64_t blocks = ceil_div(total, 256);
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  prof_mem_begin(st);
-  k_prep_wimg<<<(unsigned)blocks, 256, 0, st>>>(W, K, N, tile_n, n_tiles, kchunks, img);
-  prof_mem_end(st, 4.0 * K * N + (double)chain_wimg_bytes(K, N));   // W in, the hi / lo image out
-  return check_launch("k_prep_wimg");
+  return chain_prep_weights_batch(&W, &K, &N, &img, 1, st);
 }
 
 // Columns of N tile t of a step: tile_n, except the last tile, which covers the remaining
@@ -238,14 +273,29 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   const int warp = threadIdx.x >> 5;
   int* err = P.err;
   const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
-  const int64_t row = (int64_t)blockIdx.x * 128 + r;
-  const bool valid = row < P.rows;
+  bool valid;
   int64_t sb_ = 0, b = 0, i = 0;
-  if (valid) {
-    sb_ = row / (P.B * P.R);
-    int64_t rem = row - sb_ * P.B * P.R;
-    b = rem / P.R;
-    i = rem - b * P.R;
+  int slot = 0;
+  if constexpr (kZono) {
+    const int64_t row = (int64_t)blockIdx.x * 128 + r;
+    valid = row < P.rows;
+    if (valid) {
+      sb_ = row / (P.B * P.R);
+      int64_t rem = row - sb_ * P.B * P.R;
+      b = rem / P.R;
+      i = rem - b * P.R;
+      slot = (int)(row / P.R - p0);
+    }
+  } else {
+    // pair q of the tile: lane r & 63, lower bound in lanes 0-63, upper in 64-127
+    const int64_t q = (int64_t)blockIdx.x * 64 + (r & 63);
+    valid = q < P.B * P.R;
+    sb_ = r >> 6;
+    if (valid) {
+      b = q / P.R;
+      i = q - b * P.R;
+      slot = (int)(b - p0);
+    }
   }
   const bool lower = sb_ == 0;
   // zonotope mode: does the CTA's row range reach into a second region
@@ -260,7 +310,6 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
 #pragma unroll
   for (int q = 0; q < 4; ++q) soff[q] = (uint32_t)r * 128u + ((((uint32_t)(half * 4 + q)) ^ ((uint32_t)r & 7u)) << 4);
   const float* a0row = P.A0 + sb_ * P.a_ss + b * P.a_bs + i * P.a_rs;
-  const int slot = valid ? (int)(row / P.R - p0) : 0;
   // input box: staged rows (l0 then u0 per slot) or global memory
   const uint32_t box_pos = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? 0 : P.n0));
   const uint32_t box_neg = M.box + 4u * (uint32_t)((size_t)slot * 2 * P.n0 + (lower ? P.n0 : 0));
@@ -424,9 +473,17 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   // combine the two halves of every row
   if (half == 1) M.red[r] = conc + cacc;
   asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
+  float res = 0.0f;
   if (half == 0 && valid && ok) {
-    const float res = (conc + cacc) + M.red[r];
+    res = (conc + cacc) + M.red[r];
     (lower ? P.out_l : P.out_u)[b * P.ld_out + i] = res;
+    if (P.out_l64) (lower ? P.out_l64 : P.out_u64)[b * P.ld_out64 + i] = (double)res;
+  }
+  if (P.relu.alpha != nullptr) {
+    // both bounds of neuron (b, i) are in this tile (lanes r and r + 64): relax the ReLU above
+    if (half == 0) M.red[128 + r] = res;
+    asm volatile("bar.sync 1, %0;" ::"r"(kTransformThreads) : "memory");
+    if (half == 0 && r < 64 && valid && ok) relu_relax_store(P.relu, b, i, M.red[128 + r], M.red[192 + r]);
   }
 }
 
@@ -452,15 +509,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   uint64_t* acc_full = box_full + 1;
   uint64_t* mma_done = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [128] partial sums of the second half
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [256]: second-half sums, then the rows' bounds
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = P.err;
-  // the (bound, region) pairs p = row / R this CTA's rows belong to: p0 .. p0+n_pairs-1.  With
-  // at most kCoefSlots of them, their relaxation vectors and box rows are staged in shared memory.
-  const int64_t row_first = (int64_t)blockIdx.x * 128;
-  const int64_t row_last = (row_first + 127 < P.rows ? row_first + 127 : P.rows - 1);
-  const int64_t p0 = row_first / P.R;
-  const int n_pairs = (int)(row_last / P.R - p0 + 1);
+  // the slots of this CTA's rows: regions p0 .. p0+n_pairs-1 (bounding mode) or (bound,
+  // region) pairs p = row / R (zonotope mode).  With at most kCoefSlots of them, their
+  // relaxation vectors and box rows are staged in shared memory.
+  int64_t p0;
+  int n_pairs;
+  if (kZono) {
+    const int64_t row_first = (int64_t)blockIdx.x * 128;
+    const int64_t row_last = (row_first + 127 < P.rows ? row_first + 127 : P.rows - 1);
+    p0 = row_first / P.R;
+    n_pairs = (int)(row_last / P.R - p0 + 1);
+  } else {
+    const int64_t q_first = (int64_t)blockIdx.x * 64, q_all = P.B * P.R;
+    const int64_t q_last = (q_first + 63 < q_all ? q_first + 63 : q_all - 1);
+    p0 = q_first / P.R;
+    n_pairs = (int)(q_last / P.R - p0 + 1);
+  }
   const bool staged = P.coef_ok && n_pairs <= kCoefSlots;
   const bool box_staged = staged && P.box_smem_bytes > 0;
 
@@ -665,7 +732,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   }
   Q.coef_ok = coef_ok ? 1 : 0;
   const size_t fixed = 1024 + (size_t)kAStages * 2 * kAImg + (size_t)kWStages * Q.stage_bytes +
-                       (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 128 * 4;
+                       (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 256 * 4;
   // input-box rows of up to kCoefSlots (bound, region) pairs, when they fit
   const size_t box_bytes = (size_t)kCoefSlots * 2 * P.n0 * 4;
   const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && Q.ld_box % 4 == 0 && a16(P.l0) && a16(P.u0) &&
@@ -686,7 +753,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
     return CF_ERR_CUDA;
   }
   CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "chain: %zu bytes of shared memory", smem);
-  const int64_t tiles = ceil_div(P.rows, 128);
+  const int64_t tiles = P.zono ? ceil_div(P.rows, 128) : ceil_div(P.B * P.R, 64);
   CF_REQUIRE(tiles <= 0x7fffffff, CF_ERR_SHAPE, "chain: too many rows");
   kern<<<(unsigned)tiles, kThreads, smem, st>>>(Q);
   return check_launch(P.zono ? "k_chain (zonotope)" : "k_chain");

@@ -1,6 +1,7 @@
 // Chained tensor-core backsubstitution (cf_chain.cu): parameters and host entry points.
 #pragma once
 #include "cf_common.cuh"
+#include "cf_relax.cuh"
 
 namespace cf {
 
@@ -26,7 +27,11 @@ struct ChainStep {
 struct ChainParams {
   ChainStep st[kChainMaxSteps];
   int32_t S;
-  int64_t B, R, rows;                   // rows = 2*B*R, row = (bound, region, i)
+  // rows = 2*B*R, one per (bound, region b, row i).  Bounding mode: tile t holds the 64
+  // (b, i) pairs q = 64t .. 64t+63 (q = b*R + i), TMEM lanes 0-63 their lower bounds and
+  // 64-127 their upper bounds, so that both bounds of a neuron end in one CTA.  Zonotope
+  // mode: row = b*R + i, 128 per tile.
+  int64_t B, R, rows;
   const float* A0;                      // first coefficient rows (row (s,b,i) at s*a_ss + b*a_bs + i*a_rs)
   int64_t a_ss, a_bs, a_rs;
   const float* c0;                      // [R] constant of the bounded layer (its bias) or nullptr
@@ -37,6 +42,11 @@ struct ChainParams {
   float* out_l;                         // bound of row (0,b,i) -> out_l[b*ld_out + i]
   float* out_u;
   int64_t ld_out;
+  double* out_l64;                      // optional float64 copies (the property rows):
+  double* out_u64;                      //   out_l64[b*ld_out64 + i]
+  int64_t ld_out64;
+  ReluOut relu;                         // relu.alpha != nullptr: the ReLU above the bounded layer
+                                        // is relaxed in the drain from the two new bounds
   int* err;                             // device error word (bounded-wait timeouts)
   uint32_t max_polls;                   // poll limit of every bounded wait (filled by chain_launch)
   int32_t withhold_acc;                 // failure-path test: the MMA issuer withholds the first
@@ -85,6 +95,9 @@ cf_status zono_tc_launch(const ZonoTcParams& P, cudaStream_t st);
 void chain_tile(int N, int& tile_n, int& n_tiles);
 size_t chain_wimg_bytes(int K, int N);
 cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStream_t st);
+// the images of n weight matrices in one launch (per group of 32)
+cf_status chain_prep_weights_batch(const float* const* W, const int* K, const int* N, uint8_t* const* img, int n,
+                                   cudaStream_t st);
 cf_status chain_launch(const ChainParams& P, cudaStream_t st);
 
 }  // namespace cf

@@ -6,40 +6,41 @@
 // region.  Strides (a_ss, a_bs, a_rs) locate row (s,b,i) of a possibly broadcast input
 // (zero strides), so the first step of every layer reads the shared weight matrix
 // without materialising it per region.
+#include <algorithm>
+
 #include "cf_common.cuh"
 #include "cf_kernels.cuh"
 
 namespace cf {
 
 // ------------------------------------------------------------------ ReLU relaxation
-// Generated deeppoly.Relu (deeppoly.cf:20-24,41):
-//   l' = relu(l), u' = relu(u)
-//   L' = 1[l+u>=0] * x
-//   U' = x if l>=0; 0 if u<=0; else lam*x + mu, lam = u/(u-l), mu = -(u*l)/(u-l)
-// float32 IEEE division, same operation order as the generated code.
-// Decision replay (parity tests): with dl / du given, the three branch decisions (l >= 0,
-// u <= 0, l + u >= 0) and the ReLU outputs' cases are taken from (dl, du) instead of (l, u).
+// The relaxation of a whole layer (relu_relax_store, cf_relax.cuh).  Decision replay
+// (parity tests): with dl / du given, the three branch decisions (l >= 0, u <= 0,
+// l + u >= 0) and the ReLU outputs' cases are taken from (dl, du) instead of (l, u).
 __global__ void k_relu_relax(int64_t B, int64_t n, const float* __restrict__ l, const float* __restrict__ u,
-                             int64_t ld_in, float* __restrict__ lo, float* __restrict__ uo, int64_t ld_out,
-                             float* __restrict__ alpha, float* __restrict__ lam, float* __restrict__ mu,
-                             bool strict, const float* __restrict__ dl, const float* __restrict__ du) {
+                             int64_t ld_in, const ReluOut o) {
   int64_t total = B * n;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = t / n, k = t - b * n;
-    float lv = l[b * ld_in + k], uv = u[b * ld_in + k];
-    const float ld = dl ? dl[b * ld_in + k] : lv, ud = du ? du[b * ld_in + k] : uv;
-    bool pos = ld >= 0.0f;
-    bool dead = (!pos) && (ud <= 0.0f);
-    float den = uv - lv;
-    float lam_u = __fdiv_rn(uv, den);
-    float mu_u = 0.0f - __fdiv_rn(__fmul_rn(uv, lv), den);
-    if (lo) lo[b * ld_out + k] = pos ? lv : 0.0f;
-    if (uo) uo[b * ld_out + k] = (ud >= 0.0f) ? uv : 0.0f;
-    const float s = __fadd_rn(ld, ud);
-    alpha[t] = (strict ? s > 0.0f : s >= 0.0f) ? 1.0f : 0.0f;
-    lam[t] = pos ? 1.0f : (dead ? 0.0f : lam_u);
-    mu[t] = (pos || dead) ? 0.0f : mu_u;
+    relu_relax_store(o, b, k, l[b * ld_in + k], u[b * ld_in + k]);
   }
+}
+
+ReluOut relu_out(int64_t n, float* lo, float* uo, int64_t ld_out, float* alpha, float* lam, float* mu, bool strict,
+                 const float* dl, const float* du, int64_t ld_dec) {
+  ReluOut o;
+  o.lo = lo;
+  o.uo = uo;
+  o.ld_out = ld_out;
+  o.alpha = alpha;
+  o.lam = lam;
+  o.mu = mu;
+  o.n = n;
+  o.dl = dl;
+  o.du = du;
+  o.ld_dec = ld_dec;
+  o.strict = strict ? 1 : 0;
+  return o;
 }
 
 cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u, int64_t ld_in, float* lo,
@@ -51,8 +52,8 @@ cf_status launch_relu_relax(int64_t B, int64_t n, const float* l, const float* u
   int64_t blocks = ceil_div(total, threads);
   if (blocks > 148 * 16) blocks = 148 * 16;
   prof_mem_begin(st);
-  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in, lo, uo, ld_out, alpha, lam, mu, strict, dl,
-                                                     du);
+  k_relu_relax<<<(unsigned)blocks, threads, 0, st>>>(B, n, l, u, ld_in,
+                                                     relu_out(n, lo, uo, ld_out, alpha, lam, mu, strict, dl, du, ld_in));
   prof_mem_end(st, 28.0 * total);   // l, u in; l', u', alpha, lambda, mu out
   return check_launch("k_relu_relax");
 }
@@ -183,13 +184,15 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
 //   out_u[b,i] = c[i] + sum_n W+[i,n] u0[b,n] + W-[i,n] l0[b,n]
 // CTA tile: 16 rows x 16 regions (a 200-row layer and 256 regions give 208 CTAs), 32-wide
 // k slices of W (split into W+ / W-) and of both boxes in shared memory; 16x16 threads,
-// one row x one region x 2 bounds each.
+// one row x one region x 2 bounds each.  With `relu` (alpha != nullptr) the thread also
+// relaxes the ReLU above the layer from the two bounds it has just stored.
 constexpr int kCbT = 16, kCbK = 32, kCbM = kCbT / 16;
 __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
                                                           int64_t a_rs, const float* __restrict__ c,
                                                           const float* __restrict__ l0, const float* __restrict__ u0,
                                                           int64_t ld_box, float* __restrict__ out_l,
-                                                          float* __restrict__ out_u, int64_t ld_out) {
+                                                          float* __restrict__ out_u, int64_t ld_out,
+                                                          const ReluOut relu) {
   __shared__ __align__(16) float Wp[kCbK][kCbT + 4];
   __shared__ __align__(16) float Wn[kCbK][kCbT + 4];
   __shared__ __align__(16) float Ls[kCbK][kCbT + 4];
@@ -241,22 +244,26 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
     for (int q = 0; q < kCbM; ++q) {
       const int64_t b = b0 + tx * kCbM + q;
       if (b >= B) continue;
-      out_l[b * ld_out + i] = lo[a][q] + cv;
-      out_u[b * ld_out + i] = up[a][q] + cv;
+      const float lv = lo[a][q] + cv, uv = up[a][q] + cv;
+      out_l[b * ld_out + i] = lv;
+      out_u[b * ld_out + i] = uv;
+      if (relu.alpha) relu_relax_store(relu, b, i, lv, uv);
     }
   }
 }
 
 cf_status launch_concretize(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                             int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
-                            const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
-  return launch_concretize_box(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, n0, out_l, out_u, ld_out, st);
+                            const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st,
+                            const ReluOut* relu) {
+  return launch_concretize_box(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, n0, out_l, out_u, ld_out, st,
+                               relu);
 }
 
 cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A, int64_t a_ss, int64_t a_bs,
                                 int64_t a_rs, const float* c, int64_t c_ss, int64_t c_bs, const float* l0,
                                 const float* u0, int64_t ld_box, float* out_l, float* out_u, int64_t ld_out,
-                                cudaStream_t st) {
+                                cudaStream_t st, const ReluOut* relu) {
   int64_t rows = 2 * B * R;
   if (rows == 0) return CF_OK;
   const int64_t gx = ceil_div(R, kCbT), gy = ceil_div(B, kCbT);
@@ -265,10 +272,12 @@ cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A
   const double bytes = 4.0 * ((bcast ? (double)R : (double)rows) * n0 + 2.0 * B * n0 + (c ? (bcast ? R : rows) : 0) +
                               2.0 * B * R);
   if (bcast && gx <= 0x7fffffff && gy <= 65535) {
+    ReluOut none;
+    memset(&none, 0, sizeof(none));
     prof_mem_begin(st);
     k_concretize_bcast<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(B, R, n0, A, a_rs, c, l0, u0, ld_box, out_l,
-                                                                         out_u, ld_out);
-    prof_mem_end(st, bytes);
+                                                                         out_u, ld_out, relu ? *relu : none);
+    prof_mem_end(st, bytes + (relu ? 20.0 * B * R : 0.0));
     return check_launch("k_concretize_bcast");
   }
   int threads = 256;
@@ -278,7 +287,14 @@ cf_status launch_concretize_box(int64_t B, int64_t R, int64_t n0, const float* A
   k_concretize<<<(unsigned)blocks, threads, 0, st>>>(B, R, n0, A, a_ss, a_bs, a_rs, c, c_ss, c_bs, l0, u0, ld_box,
                                                       out_l, out_u, ld_out);
   prof_mem_end(st, bytes);
-  return check_launch("k_concretize");
+  CF_TRY(check_launch("k_concretize"));
+  if (!relu) return CF_OK;
+  // the rows of one neuron's two bounds lie in different warps here: relax in a launch of its own
+  prof_mem_begin(st);
+  k_relu_relax<<<(unsigned)std::min<int64_t>(ceil_div(B * R, 256), 148 * 16), 256, 0, st>>>(B, R, out_l, out_u,
+                                                                                            ld_out, *relu);
+  prof_mem_end(st, 28.0 * B * R);
+  return check_launch("k_relu_relax");
 }
 
 // ------------------------------------------------------------------ step constant

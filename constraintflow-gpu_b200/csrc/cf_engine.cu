@@ -47,21 +47,24 @@ bool fault_injected(const char* site) {
 }
 
 // ------------------------------------------------------------------ small kernels
-__global__ void k_to_f64(int64_t B, int64_t n, const float* __restrict__ src, int64_t ld, double* __restrict__ dst) {
+__global__ void k_to_f64(int64_t B, int64_t n, const float* __restrict__ src_l, const float* __restrict__ src_u,
+                         int64_t ld, double* __restrict__ dst_l, double* __restrict__ dst_u) {
   int64_t total = B * n;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = t / n, k = t - b * n;
-    dst[t] = (double)src[b * ld + k];
+    dst_l[t] = (double)src_l[b * ld + k];
+    dst_u[t] = (double)src_u[b * ld + k];
   }
 }
 
-cf_status launch_to_f64(int64_t B, int64_t n, const float* src, int64_t ld_src, double* dst, cudaStream_t st) {
+cf_status launch_to_f64(int64_t B, int64_t n, const float* src_l, const float* src_u, int64_t ld_src, double* dst_l,
+                        double* dst_u, cudaStream_t st) {
   if (B * n == 0) return CF_OK;
   int64_t blocks = ceil_div(B * n, 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
   prof_mem_begin(st);
-  k_to_f64<<<(unsigned)blocks, 256, 0, st>>>(B, n, src, ld_src, dst);
-  prof_mem_end(st, 12.0 * B * n);
+  k_to_f64<<<(unsigned)blocks, 256, 0, st>>>(B, n, src_l, src_u, ld_src, dst_l, dst_u);
+  prof_mem_end(st, 24.0 * B * n);
   return check_launch("k_to_f64");
 }
 
@@ -348,9 +351,14 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
                                     const float* c0, const float* l0, const float* u0, float* out_l, float* out_u,
                                     const std::vector<float*>& ra, const std::vector<float*>& rl,
                                     const std::vector<float*>& rm, cudaStream_t st, size_t j_first = 0,
-                                    int64_t ld_box = 0) {
+                                    int64_t ld_box = 0, const ReluOut* relu = nullptr, double* lb64 = nullptr,
+                                    double* ub64 = nullptr) {
   ChainParams P;
   memset(&P, 0, sizeof(P));
+  if (relu) P.relu = *relu;
+  P.out_l64 = lb64;
+  P.out_u64 = ub64;
+  P.ld_out64 = R;
   P.S = (int32_t)(n_below - j_first);
   for (int s = 0; s < P.S; ++s) {
     const size_t j = n_below - 1 - s;
@@ -432,7 +440,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
 
   // bound one affine-type layer: rows R, coefficient source (A0 strides), bias c0
   auto bound_layer = [&](size_t ma, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs, const float* c0,
-                         int64_t col) -> cf_status {
+                         int64_t col, const ReluOut* relu) -> cf_status {
     const float* cur = A0;
     int64_t ss = 0, bs = a_bs, rs = a_rs;
     const float* c = c0;
@@ -453,7 +461,8 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       c_ss = Bc * R;
       c_bs = R;
     }
-    return launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + col, st_u + col, N, st);
+    return launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + col, st_u + col, N, st,
+                             relu);
   };
 
   // custom-stop traversal (stop_depth = get_start + 1 > 0, linear chains): bounding list
@@ -463,7 +472,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
   // bounds, or, when `below` is a ReLU that is itself substituted, with the box of its
   // relaxation over the bounds of its input.
   auto bound_stopped = [&](size_t ma, int64_t R, const float* A0, int64_t a_bs, int64_t a_rs, const float* c0,
-                           int64_t col) -> cf_status {
+                           int64_t col, const ReluOut* relu) -> cf_status {
     const int li_m = ma == p.affine.size() ? net->n_layers : p.affine[ma];
     const int li_stop = li_m - (net->stop_depth - 1);
     size_t j_first = ma;
@@ -491,10 +500,10 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     }
     if (j_first == ma)
       return launch_concretize_box(Bc, R, nb, A0, 0, a_bs, a_rs, c0, 0, 0, bl, bu, ld, st_l + col, st_u + col, N,
-                                   st);
+                                   st, relu);
     if (chain_applicable(net, p, ma, j_first))
       return launch_chain_layer(net, p, w, ws, Bc, ma, R, A0, a_bs, a_rs, c0, bl, bu, st_l + col, st_u + col, ra,
-                                rl, rm, st, j_first, ld);
+                                rl, rm, st, j_first, ld, relu);
     const float* cur = A0;
     int64_t ss = 0, bs = a_bs, rs = a_rs;
     const float* c = c0;
@@ -516,7 +525,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
       c_bs = R;
     }
     return launch_concretize_box(Bc, R, nb, cur, ss, bs, rs, c, c_ss, c_bs, bl, bu, ld, st_l + col, st_u + col, N,
-                                 st);
+                                 st, relu);
   };
 
   // receptive-field windows (conv networks): bound layer a (a == affine.size(): property)
@@ -587,27 +596,47 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
-    if (p.affine[a] >= li_begin && p.affine[a] < li_end) {
+    const bool affine_here = p.affine[a] >= li_begin && p.affine[a] < li_end;
+    const bool relu_here = p.relu_after[a] >= li_begin && p.relu_after[a] < li_end;
+    // DeepPoly's relaxation of the ReLU above layer a, handed to the launch that bounds layer
+    // a where that launch can apply it (it holds both bounds of a neuron, or relaxes the
+    // layer right after it)
+    ReluOut ro;
+    const ReluOut* fuse = nullptr;
+    if (affine_here && relu_here && net->relaxation != CF_RELAX_CROWN) {
+      const int64_t rcol = p.col[p.relu_after[a]];
+      ro = relu_out(net->layers[p.relu_after[a]].n_out, st_l + rcol, st_u + rcol, N, ra[a], rl[a], rm[a],
+                    is_strict_relu(net), dec_l ? dec_l + col : nullptr, dec_u ? dec_u + col : nullptr, N);
+      fuse = &ro;
+    }
+    bool relaxed = false;
+    if (affine_here) {
       if (is_interval_layers(net)) {
         // crownibp.cf: the interval bound over the previous layer's state columns (the
         // input's columns start at 0)
         const int64_t in_col = p.affine[a] == 0 ? 0 : p.col[p.affine[a] - 1];
         if (L.kind == CF_LAYER_CONV)
           CF_TRY(launch_ibp_conv_state(Bc, L, st_l + in_col, st_u + in_col, N, st_l + col, st_u + col, N, st));
-        else
+        else {
           CF_TRY(launch_concretize_box(Bc, L.n_out, L.n_in, L.W_dev, 0, 0, L.n_in, L.b_dev, 0, 0, st_l + in_col,
-                                       st_u + in_col, N, st_l + col, st_u + col, N, st));
-      } else if (net->stop_depth > 0)
-        CF_TRY(bound_stopped(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
-      else if (p.has_conv)
+                                       st_u + in_col, N, st_l + col, st_u + col, N, st, fuse));
+          relaxed = fuse != nullptr;
+        }
+      } else if (net->stop_depth > 0) {
+        CF_TRY(bound_stopped(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col, fuse));
+        relaxed = fuse != nullptr;
+      } else if (p.has_conv) {
         CF_TRY(bound_window(a, col));
-      else if (chain_applicable(net, p, a))
+      } else if (chain_applicable(net, p, a)) {
         CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
-                                  st_u + col, ra, rl, rm, st));
-      else
-        CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col));
+                                  st_u + col, ra, rl, rm, st, 0, 0, fuse));
+        relaxed = fuse != nullptr;
+      } else {
+        CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col, fuse));
+        relaxed = fuse != nullptr;
+      }
     }
-    if (p.relu_after[a] >= li_begin && p.relu_after[a] < li_end) {
+    if (relu_here && !relaxed) {
       const cf_layer& Rl = net->layers[p.relu_after[a]];
       int64_t rcol = p.col[p.relu_after[a]];
       if (net->relaxation == CF_RELAX_CROWN) {
@@ -625,20 +654,17 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
   // property layer: per-region matrix [Bc, n_spec, n_out_last], zero bias
   if (net->stop_depth > 0) {
     const int64_t R = net->n_spec, K = p.n_out_last;
-    CF_TRY(bound_stopped(p.affine.size(), R, specW, R * K, K, nullptr, p.spec_col));
-    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
-    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+    CF_TRY(bound_stopped(p.affine.size(), R, specW, R * K, K, nullptr, p.spec_col, nullptr));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, st_u + p.spec_col, N, lb, ub, st));
   } else if (p.has_conv) {
     const int64_t R = net->n_spec;
     CF_TRY(bound_window(p.affine.size(), p.spec_col));
-    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
-    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, st_u + p.spec_col, N, lb, ub, st));
   } else if (chain_applicable(net, p, p.affine.size())) {
+    // the drain also writes the float64 bounds
     const int64_t R = net->n_spec, K = p.n_out_last;
     CF_TRY(launch_chain_layer(net, p, w, ws, Bc, p.affine.size(), R, specW, R * K, K, nullptr, l0, u0,
-                              st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st));
-    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
-    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+                              st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st, 0, 0, nullptr, lb, ub));
   } else {
     const int64_t R = net->n_spec, K = p.n_out_last;
     // treat it as affine index affine.size(): substitutes every affine layer below it
@@ -664,8 +690,7 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     }
     CF_TRY(launch_concretize(Bc, R, n0, cur, ss, bs, rs, c, c_ss, c_bs, l0, u0, st_l + p.spec_col,
                              st_u + p.spec_col, N, st));
-    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, N, lb, st));
-    CF_TRY(launch_to_f64(Bc, R, st_u + p.spec_col, N, ub, st));
+    CF_TRY(launch_to_f64(Bc, R, st_l + p.spec_col, st_u + p.spec_col, N, lb, ub, st));
   }
   return CF_OK;
 }
@@ -721,10 +746,17 @@ static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0,
     return CF_ERR_CUDA;
   }
   if (use_chain() && !p.has_conv) {
+    std::vector<const float*> Wl;
+    std::vector<int> Kl, Nl;
+    std::vector<uint8_t*> img;
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
-      CF_TRY(chain_prep_weights(L.W_dev, L.n_out, L.n_in, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
+      Wl.push_back(L.W_dev);
+      Kl.push_back(L.n_out);
+      Nl.push_back(L.n_in);
+      img.push_back(reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]));
     }
+    CF_TRY(chain_prep_weights_batch(Wl.data(), Kl.data(), Nl.data(), img.data(), (int)Wl.size(), st));
   }
   const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
   for (int64_t b0 = 0; b0 < B; b0 += Bc) {
