@@ -47,6 +47,10 @@ class CfProfileStats(ctypes.Structure):
                 ("mem_launches", _i64), ("mem_ms", ctypes.c_double), ("mem_bytes", ctypes.c_double)]
 
 
+class CfConvGeom(ctypes.Structure):
+    _fields_ = [(n, _i32) for n in ("K", "C", "ox", "oy", "ix", "iy", "kx", "ky", "sx", "sy", "px", "py")]
+
+
 class CfNetwork(ctypes.Structure):
     _fields_ = [("n_layers", _i32), ("layers", ctypes.POINTER(CfLayer)), ("n_input", _i32),
                 ("n_spec", _i32), ("relaxation", _i32), ("stop_depth", _i32)]
@@ -84,6 +88,12 @@ def _load():
         "cf_input_box": (_i32, [_i64, _i32, _i64, _vp, _f32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp, _vp,
                                 _vp]),
         "cf_spec_matrix": (_i32, [_i64, _i32, _vp, _vp, _vp]),
+        "cf_conv_densify": (_i32, [P(CfConvGeom), _i64, _vp, _i64, _i64, _i64, _vp, _vp]),
+        "cf_conv_apply": (_i32, [P(CfConvGeom), _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64,
+                                 _i64, _i64, _vp]),
+        "cf_conv_scale": (_i32, [P(CfConvGeom), _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp]),
+        "cf_conv_transpose": (_i32, [P(CfConvGeom), _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _vp, _i64,
+                                     _i64, _i64, _vp]),
         "cf_profile_enable": (_i32, [_i32]),
         "cf_profile_collect": (_i32, [P(CfProfileStats)]),
         "cf_last_error": (ctypes.c_char_p, []),
@@ -104,7 +114,8 @@ EXPORTED = ("cf_network_neurons", "cf_deeppoly_workspace_bytes", "cf_deeppoly_ru
             "cf_deeppoly_run_static", "cf_deeppoly_check_static", "cf_deeppoly_run_replay",
             "cf_relu_relax",
             "cf_backsub_step", "cf_concretize", "cf_ew_binary", "cf_ew_unary", "cf_ew_where", "cf_ew_clamp",
-            "cf_ew_any", "cf_bmm", "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",
+            "cf_ew_any", "cf_bmm", "cf_conv_densify", "cf_conv_apply", "cf_conv_scale", "cf_conv_transpose",
+            "cf_input_box", "cf_spec_matrix", "cf_profile_enable", "cf_profile_collect",
             "cf_last_error", "cf_version")
 
 

@@ -1,10 +1,11 @@
 """Tensor-level wrappers over libcfgpu's block kernels (cf_ew_binary, cf_ew_unary,
-cf_ew_where, cf_ew_clamp, cf_ew_any, cf_bmm), used by the gbcsr mirror
+cf_ew_where, cf_ew_clamp, cf_ew_any, cf_bmm, cf_conv_*), used by the gbcsr mirror
 (constraintflow.gbcsr) and by the general traversal (cfgpu.general).
 
 Operands are CUDA tensors, possibly broadcast views (zero strides); results are new
 contiguous tensors.  PyTorch only allocates the memory and supplies the stream.
 """
+import ctypes
 import operator
 
 import torch
@@ -149,3 +150,44 @@ def bmm(A, B, C=None, accumulate=False):
                          B.stride(0), B.stride(1), B.stride(2), C.data_ptr(), 1 if accumulate else 0, _stream())
     _lib.check(st, "cf_bmm")
     return C
+
+
+# ---------------------------------------------------------------- gbcsr conv blocks
+def conv_geom(K, C, ox, oy, ix, iy, kx, ky, sx, sy, px, py):
+    """The geometry of a conv block (cf_conv_geom)."""
+    return _lib.CfConvGeom(*[int(v) for v in (K, C, ox, oy, ix, iy, kx, ky, sx, sy, px, py)])
+
+
+def conv_densify(g, nb, P, p_bs, p_ks, p_ps):
+    """[nb, K*ox*oy, C*ix*iy]: the matrix a conv block stands for (cf_conv_densify)."""
+    out = torch.empty(nb, g.K * g.ox * g.oy, g.C * g.ix * g.iy, dtype=torch.float32, device=P.device)
+    LAUNCHES[0] += 1
+    _lib.check(_lib.lib.cf_conv_densify(ctypes.byref(g), nb, P.data_ptr(), p_bs, p_ks, p_ps, out.data_ptr(),
+                                        _stream()), "cf_conv_densify")
+    return out
+
+
+def conv_apply(g, nb, per_b, P, pstr, X, xstr, out, ostr):
+    """out = M x for nb*per_b images (cf_conv_apply); pstr = (p_bs, p_ks, p_ps),
+    xstr = (x_bs, x_ss, x_es), ostr = (o_bs, o_ss, o_rs) in elements."""
+    LAUNCHES[0] += 1
+    _lib.check(_lib.lib.cf_conv_apply(ctypes.byref(g), nb, per_b, P.data_ptr(), *pstr, X.data_ptr(), *xstr,
+                                      out.data_ptr(), *ostr, _stream()), "cf_conv_apply")
+    return out
+
+
+def conv_scale(g, nb, P, pstr, X, x_bs, x_es):
+    """[nb, K*ox*oy, C*kx*ky]: patch values times the input values under them (cf_conv_scale)."""
+    out = torch.empty(nb, g.K * g.ox * g.oy, g.C * g.kx * g.ky, dtype=torch.float32, device=P.device)
+    LAUNCHES[0] += 1
+    _lib.check(_lib.lib.cf_conv_scale(ctypes.byref(g), nb, P.data_ptr(), *pstr, X.data_ptr(), x_bs, x_es,
+                                      out.data_ptr(), _stream()), "cf_conv_scale")
+    return out
+
+
+def conv_transpose(g, nb, per_b, Y, ystr, W, OH, OW, out, ostr):
+    """Transposed convolution of nb*per_b rows (cf_conv_transpose)."""
+    LAUNCHES[0] += 1
+    _lib.check(_lib.lib.cf_conv_transpose(ctypes.byref(g), nb, per_b, Y.data_ptr(), *ystr, W.data_ptr(), OH, OW,
+                                          out.data_ptr(), *ostr, _stream()), "cf_conv_transpose")
+    return out

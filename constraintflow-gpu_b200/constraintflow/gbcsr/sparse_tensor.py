@@ -365,6 +365,10 @@ class SparseTensor:
         N = 1 if unequal else ys[2]
         if ys[0] != B or ys[1] != K:
             raise Exception("SHAPE MISMATCH")
+        if any(b.block_type in ("K", "P") for b in self.blocks + y.blocks):
+            res = self._matmul_blocks(y, unequal)
+            if res is not None:
+                return res
         # grid dims: (batch, R, K, N); x covers (0,1,2), y covers (0,2,3) (unequal: (0,2))
         x_map = [0, 1, 2, None]
         y_map = [0, None, 1, None] if unequal else [0, None, 1, 2]
@@ -406,6 +410,42 @@ class SparseTensor:
                 blocks.append(DenseBlock(out))
         total = [B, R] if unequal else [B, R, N]
         return SparseTensor(starts, blocks, len(total), torch.tensor(total), type=float, dense_const=0.0)
+
+    def _matmul_blocks(self, y, unequal):
+        """The reference's block-pair product (sparse_tensor.py:1780-2050) where every pair of
+        blocks that meets does so over the same range of the contracted dim and the products
+        land in disjoint boxes: each pair is one block-level product (so a conv block stays a
+        KernelBlock / PatchesBlock where the reference keeps it so).  None otherwise: the
+        grid refinement then computes the same values on dense cell views."""
+        starts, ends, blocks = [], [], []
+        xb, yb = self._boxes(), y._boxes()
+        for (sx_, ex_), bx in zip(xb, self.blocks):
+            for (sy_, ey_), by in zip(yb, y.blocks):
+                if max(sx_[0], sy_[0]) >= min(ex_[0], ey_[0]):
+                    continue
+                ky = (sy_[1], ey_[1])
+                if max(sx_[2], ky[0]) >= min(ex_[2], ky[1]):
+                    continue
+                if (sx_[2], ex_[2]) != ky:
+                    return None
+                if unequal:
+                    blk = bx.matmul_unequal_dims(by)[0]
+                    st = [min(sx_[0], sy_[0]), sx_[1]]
+                    en = [max(ex_[0], ey_[0]), ex_[1]]
+                else:
+                    blk = bx.matmul_equal_dims(by)[0]
+                    st = [min(sx_[0], sy_[0]), sx_[1], sy_[2]]
+                    en = [max(ex_[0], ey_[0]), ex_[1], ey_[2]]
+                for s0, e0 in zip(starts, ends):
+                    if all(max(a, c) < min(b, d) for a, b, c, d in zip(st, en, s0, e0)):
+                        return None
+                if isinstance(blk, ConstBlock) and blk.block == 0:
+                    continue
+                starts.append(st)
+                ends.append(en)
+                blocks.append(blk)
+        total = self.shape[:2] if unequal else self.shape[:2] + [y.shape[2]]
+        return SparseTensor(starts, blocks, len(total), torch.tensor(total), ends, type=float, dense_const=0.0)
 
     def _bp_union(self, n, pairs):
         pts = {0, n}

@@ -343,6 +343,47 @@ cf_status cf_bounds_meet(int64_t B, int64_t n, float* l_a, float* u_a, int64_t l
 cf_status cf_ew_any(int32_t ndim, const int64_t* shape, const void* x_dev, int32_t x_dtype,
                     const int64_t* x_strides, uint32_t* flag_dev, void* stream);
 
+/* gbcsr conv blocks (constraintflow/gbcsr/sparse_block.py: KernelBlock :1158, PatchesBlock
+ * :2576).  A conv block stands for the matrix M [K*ox*oy, C*ix*iy] of a convolution with K
+ * kernels over C input channels (input ix x iy, output ox x oy, kernel kx x ky, stride
+ * sx / sy, padding px / py; x the first spatial dim, as in the reference): row
+ * r = (k, oxi, oyi) holds a patch placed at input rows oxi*sx - px + dx and columns
+ * oyi*sy - py + dy, positions outside the image dropped.  Patch values are read through
+ * strides: (region b, kernel k, position pos = oxi*oy + oyi, channel c, dx, dy) at
+ * P[b*p_bs + k*p_ks + pos*p_ps + (c*kx + dx)*ky + dy]; a KernelBlock's weights
+ * W [K, C, kx, ky] have p_bs = p_ps = 0, p_ks = C*kx*ky; a PatchesBlock payload
+ * [B, K*ox*oy, C*kx*ky] has p_ks = ox*oy*C*kx*ky, p_ps = C*kx*ky and p_bs = K*ox*oy*C*kx*ky
+ * (0 when shared by every region).  Sums are float32. */
+typedef struct cf_conv_geom {
+  int32_t K, C;            /* kernels (output channels), input channels */
+  int32_t ox, oy, ix, iy;  /* output and input spatial sizes */
+  int32_t kx, ky, sx, sy, px, py;
+} cf_conv_geom;
+/* out [nb, K*ox*oy, C*ix*iy] = M of region b (KernelBlock.get_dense :1195 as
+ * conv_transpose2d of the identity; PatchesBlock.get_dense :3089). */
+cf_status cf_conv_densify(const cf_conv_geom* g, int64_t nb, const float* P, int64_t p_bs, int64_t p_ks,
+                          int64_t p_ps, float* out, void* stream);
+/* For image n = (bb, s), bb = n / per_b < nb: out[bb*o_bs + s*o_ss + r*o_rs] =
+ * sum_j M[bb][r, j] x[j], x element j at X[bb*x_bs + s*x_ss + j*x_es] (F.conv2d of the
+ * columns in KernelBlock.matmul_equal_dims :1364 / matmul_unequal_dims :1631; the unfold
+ * product and sum of PatchesBlock.matmul_unequal_dims :2942). */
+cf_status cf_conv_apply(const cf_conv_geom* g, int64_t nb, int64_t per_b, const float* P, int64_t p_bs,
+                        int64_t p_ks, int64_t p_ps, const float* X, int64_t x_bs, int64_t x_ss, int64_t x_es,
+                        float* out, int64_t o_bs, int64_t o_ss, int64_t o_rs, void* stream);
+/* out [nb, K*ox*oy, C*kx*ky] = every patch value times the input value under it, 0 in the
+ * padding; input element j of region b at X[b*x_bs + j*x_es] (the unfold products of
+ * KernelBlock / PatchesBlock.matmul_equal_dims with a DiagonalBlock, :1364, :2820). */
+cf_status cf_conv_scale(const cf_conv_geom* g, int64_t nb, const float* P, int64_t p_bs, int64_t p_ks,
+                        int64_t p_ps, const float* X, int64_t x_bs, int64_t x_es, float* out, void* stream);
+/* Transposed convolution of rows: for image n = (bb, s), out[bb*o_bs + s*o_ss + e*o_es]
+ * (e = (c, X, Y) of an OH x OW output) = sum over (k, dx, dy) with X = oxi*sx - px + dx,
+ * Y = oyi*sy - py + dy of y[(k, oxi, oyi)] * W[k, c, dx, dy], y element at
+ * Y[bb*x_bs + s*x_ss + i*x_es] (F.conv_transpose2d in DenseBlock.matmul_equal_dims
+ * :839-911 and in PatchesBlock.matmul_equal_dims with a KernelBlock :2740-2818). */
+cf_status cf_conv_transpose(const cf_conv_geom* g, int64_t nb, int64_t per_b, const float* Y, int64_t x_bs,
+                            int64_t x_ss, int64_t x_es, const float* W, int32_t OH, int32_t OW, float* out,
+                            int64_t o_bs, int64_t o_ss, int64_t o_es, void* stream);
+
 /* Message for the last non-OK status on this host thread ("" if none). */
 const char* cf_last_error(void);
 /* Library version string. */
