@@ -80,7 +80,6 @@ class DeepPolyEngine:
                 W = torch.as_tensor(L.W, dtype=torch.float32).to(self.device).contiguous()
                 b = torch.as_tensor(L.b, dtype=torch.float32).to(self.device).contiguous()
                 self._keep += [W, b]
-                self._general.append((L.kind, W, b, parents))
                 d.W_dev, d.b_dev = W.data_ptr(), b.data_ptr()
                 if L.kind == "linear":
                     d.kind = _lib.CF_LAYER_LINEAR
@@ -95,6 +94,8 @@ class DeepPolyEngine:
                     d.n_out = d.cout * d.oh * d.ow
                 else:
                     raise NotImplementedError(f"layer kind {L.kind}")
+                geom = ((d.cin, d.ih, d.iw, d.cout, d.oh, d.ow, d.stride, d.pad) if L.kind == "conv" else None)
+                self._general.append((L.kind, W, b, parents, geom))
                 if d.n_in != pw[0]:
                     raise ValueError(f"layer {i}: {L.kind} reads {d.n_in} neurons, its parent has {pw[0]}")
             widths.append(int(d.n_out))
@@ -127,9 +128,6 @@ class DeepPolyEngine:
             if stop_depth is not None or relu_strict:
                 raise NotImplementedError("a custom stop depth or strict ReLU test on a network with Add / Concat "
                                           "layers")
-            if any(g[0] == "conv" for g in self._general):
-                raise NotImplementedError("conv layers in a network with Add / Concat layers (the general "
-                                          "traversal runs linear, relu, add and concat layers)")
             self.net = None
             self.N = self.input_size + sum(widths) + self.n_spec
         self._ws = None

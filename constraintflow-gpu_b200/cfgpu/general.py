@@ -21,9 +21,13 @@ inner_prod, tensor_ops.py:370,765); the stopped part is added after the substitu
 
 Representation: a polyexp is ({layer t: block}, const [B, r]) on the device; layer 0 is
 the input, then one neuron layer per network layer, in list order.  A block is either
-dense, [1 or B, r, n_t] float32 (a batch-shared layer weight has batch 1), or diagonal,
+dense, [1 or B, r, n_t] float32 (a batch-shared layer weight has batch 1), diagonal,
 [B, n_t] (a ReLU's per-neuron relaxation over its own input layer, r = n_t), so a ReLU
-substitution is a column scaling instead of a product with an n x n matrix.  Every
+substitution is a column scaling instead of a product with an n x n matrix, or a conv
+layer's weights (_Conv, the KernelBlock of constraintflow/gbcsr/sparse_block.py:1158),
+substituted by the transposed convolution of every coefficient row (cf_conv_transpose,
+as DenseBlock @ KernelBlock, :839-911) and densified (cf_conv_densify) only where it
+starts a traversal or meets another block over the same layer.  Every
 arithmetic operation is a libcfgpu kernel (cfgpu.ops: cf_bmm, cf_signscale, cf_ew_binary,
 cf_ew_clamp, cf_ew_any; cf_relu_relax for DeepPoly's relaxation); torch provides memory,
 views and copies.
@@ -38,14 +42,36 @@ BRANCH_PASS, BRANCH_ZERO, BRANCH_CROSS = 0, 1, 2
 F32 = torch.float32
 
 
+class _Conv:
+    """A conv layer's weights W [cout, cin, kh, kw] standing for its matrix
+    [cout*oh*ow, cin*ih*iw] (square stride and padding, as the reference's reader gives)."""
+
+    def __init__(self, W, geom):
+        cin, ih, iw, cout, oh, ow, stride, pad = geom
+        kh, kw = int(W.shape[2]), int(W.shape[3])
+        self.W = W
+        self.g = ops.conv_geom(cout, cin, oh, ow, ih, iw, kh, kw, stride, stride, pad, pad)
+        self.ih, self.iw = ih, iw
+        self.shape = (1, cout * oh * ow, cin * ih * iw)
+        self.ckk = cin * kh * kw
+
+    def dim(self):
+        return 4
+
+    def dense(self):
+        return ops.conv_densify(self.g, 1, self.W, 0, self.ckk, 0)
+
+
 def _full(B, t):
     """[1 or B, r, n] -> a [B, r, n] view (batch stride 0 when shared)."""
+    if isinstance(t, _Conv):
+        t = t.dense()
     return t.expand(B, t.shape[1], t.shape[2]) if t.shape[0] == 1 else t
 
 
 def _dense(B, M):
-    """A block as a dense [B, r, n] (a diagonal block materialised)."""
-    if M.dim() == 3:
+    """A block as a dense [B, r, n] (a diagonal block or conv weights materialised)."""
+    if M.dim() != 2:
         return _full(B, M)
     n = M.shape[1]
     eye = torch.eye(n, dtype=F32, device=M.device).unsqueeze(0).expand(B, n, n)
@@ -66,7 +92,14 @@ def _add_block(B, blocks, t, M):
 
 
 def _apply(B, A, M):
-    """A [B, r, n_t] times block M over layer s: bmm for dense, column scaling for diagonal."""
+    """A [B, r, n_t] times block M over layer s: bmm for dense, column scaling for diagonal,
+    the transposed convolution of every row for conv weights."""
+    if isinstance(M, _Conv):
+        r, cols = A.shape[1], M.shape[2]
+        out = torch.empty(B, r, cols, dtype=F32, device=A.device)
+        ops.conv_transpose(M.g, B, r, A, (A.stride(0), A.stride(1), A.stride(2)), M.W, M.ih, M.iw, out,
+                           (r * cols, cols, 1))
+        return out
     if M.dim() == 3:
         return ops.bmm(A, _full(B, M))
     return ops.binary(operator.mul, A, M.unsqueeze(1).expand(A.shape), F32)
@@ -213,10 +246,11 @@ def _stack_poly(B, P, Q):
 
 
 def run(layers, l0, u0, spec_W, relaxation="deeppoly"):
-    """DeepPoly or CROWN bounds of a network of linear / relu / add / concat layers.
+    """DeepPoly or CROWN bounds of a network of linear / conv / relu / add / concat layers.
 
-    layers: list of (kind, W [n_out, n_in] device float32 or None, b [n_out] or None,
-    parents tuple of layer-list indices, -1 = the network input), in the order of the
+    layers: list of (kind, W [n_out, n_in] (conv: [cout, cin, kh, kw]) device float32 or
+    None, b [n_out] (conv: [cout]) or None, parents tuple of layer-list indices, -1 = the
+    network input[, conv geometry (cin, ih, iw, cout, oh, ow, stride, pad)]), in the order of the
     reference's ONNX reader (breadth first from the input; every parent listed before
     its children).  l0, u0 [B, n0], spec_W [B, n_spec, n_last] device float32; the
     property layer reads the last layer of the list.
@@ -232,7 +266,7 @@ def run(layers, l0, u0, spec_W, relaxation="deeppoly"):
     nl = len(layers)
     for idx, layer in enumerate(list(layers) + [("spec", spec_W, None, (nl - 1,))]):
         k = idx + 1
-        kind, W, bias, parents = layer
+        kind, W, bias, parents = layer[:4]
         ks = [p + 1 for p in parents]
         if any(not 0 <= p < k for p in ks):
             raise ValueError(f"layer {idx}: parents {parents} must precede it in the list")
@@ -267,9 +301,13 @@ def run(layers, l0, u0, spec_W, relaxation="deeppoly"):
         elif kind == "linear":
             A0 = W.unsqueeze(0)
             c0 = bias.unsqueeze(0).expand(B, -1).contiguous()
+        elif kind == "conv":
+            A0 = _Conv(W, layer[4])
+            per = A0.shape[1] // int(W.shape[0])      # output positions per channel
+            c0 = bias.reshape(1, -1, 1).expand(B, int(W.shape[0]), per).reshape(B, A0.shape[1])
         else:
-            raise NotImplementedError(f"a {kind} layer in the general traversal (it runs linear, relu, add and "
-                                      "concat layers; conv chains run in the fused driver)")
+            raise NotImplementedError(f"a {kind} layer in the general traversal (it runs linear, conv, relu, add "
+                                      "and concat layers)")
         res = [_traverse(B, {ks[0]: A0}, c0, polys, lower) for lower in (True, False)]
         bnd[k] = (res[0], res[1])
         poly = ({ks[0]: A0}, c0)

@@ -139,6 +139,31 @@ def _residual(seed):
     return L
 
 
+def _resconv(seed):
+    """1x28x28 -> conv 4x3x3 stride 2 (4x14x14), relu; a residual block [conv 4x3x3, relu,
+    conv 4x3x3] (stride 1, padding 1) + skip, relu; -> 10.  Conv layers inside an Add network."""
+    g = torch.Generator().manual_seed(seed)
+
+    def conv(cin, cout, h, s, parents=None):
+        w = _kaiming((cout, cin, 3, 3), g)
+        b = torch.randn(cout, generator=g) * 0.01
+        oh = (h + 2 - 3) // s + 1
+        return Layer('conv', w.numpy(), b.numpy(), stride=s, pad=1, in_shape=(cin, h, h), out_shape=(cout, oh, oh),
+                     parents=parents)
+
+    def relu(shape, parents=None):
+        return Layer('relu', in_shape=shape, out_shape=shape, parents=parents)
+
+    sh = (4, 14, 14)
+    L = [conv(1, 4, 28, 2), relu(sh)]                                            # 0, 1
+    L += [conv(4, 4, 14, 1), relu(sh), conv(4, 4, 14, 1)]                        # 2, 3, 4
+    L.append(Layer('add', in_shape=sh, out_shape=sh, parents=(4, 1)))           # 5
+    L.append(relu(sh))                                                           # 6
+    L.append(Layer('linear', _kaiming((10, 784), g).numpy(), (torch.randn(10, generator=g) * 0.01).numpy(),
+                   in_shape=(784, 1, 1), out_shape=(10, 1, 1)))                  # 7
+    return L
+
+
 def _branches(seed):
     """784 -> 60 -> relu, two branches 60 -> 40 -> relu, concatenated (80) -> 10.
 
@@ -190,8 +215,8 @@ def is_chain(layers):
 
 def workload(wid):
     """The certification workloads: id -> Workload (full batch size).  0-4 and 7 are chains;
-    5 (residual blocks) and 6 (concatenated branches) are DAGs; 7 has exactly tied ReLU
-    inputs (a parity case for the lower-slope tests)."""
+    5 (residual blocks), 6 (concatenated branches) and 8 (conv layers in a residual block)
+    are DAGs; 7 has exactly tied ReLU inputs (a parity case for the lower-slope tests)."""
     if wid == 0:
         return Workload(0, "mlp_784-50x3-10", (1, 28, 28), _mlp([784, 50, 50, 50, 10], 0, None),
                         1, 0.01, 'mnist', 0, "DeepPoly, ReLU MLP 784-50-50-50-10, 1 region, eps 0.01")
@@ -216,6 +241,9 @@ def workload(wid):
     if wid == 6:
         return Workload(6, "branch_784-60-(40|40)-concat-10", (1, 28, 28), _branches(6),
                         32, 0.002, 'mnist', 6, "DeepPoly, two branches concatenated, 32 regions")
+    if wid == 8:
+        return Workload(8, "resconv_1x28x28_c4s2-(c4,c4,add)-10", (1, 28, 28), _resconv(8), 16, 0.01, 'mnist', 8,
+                        "DeepPoly, conv layers inside a residual block, 16 regions")
     if wid == 7:
         return Workload(7, "tied_784-64-50-10", (1, 28, 28), _tied(7), 16, 0.01, 'mnist', 7,
                         "ReLU MLP 784-64-50-10 with 32 exactly tied first-layer neurons (l + u == 0), "

@@ -129,6 +129,11 @@ CASES = {
     "cs3_w7_b4_e1e-2": ("deeppoly_custom_stop", 7, 4, 0.01),
     "dp_w7_b4_e1e-2": ("deeppoly", 7, 4, 0.01),
     "cibp_w7_b4_e1e-2": ("crownibp", 7, 4, 0.01),
+    # conv layers inside a residual block (workload 8).  crown.cf on a conv network stops in
+    # the reference itself (KernelBlock.matmul_unequal_dims, sparse_block.py:1726, raises
+    # "Unrecognized sparse block type: RepeatBlock"), so it has no golden case.
+    "dp_w8_b4_e1e-2": ("deeppoly", 8, 4, 0.01),
+    "dp_w8_b4_e1e-3": ("deeppoly", 8, 4, 0.001),
 }
 
 

@@ -25,7 +25,7 @@ def _certify(c, layers=None, **kw):
 
 
 def test_dag_cases_present():
-    assert {Case(n).wid for n in DAG_CASES} == {5, 6}
+    assert {Case(n).wid for n in DAG_CASES} == {5, 6, 8}
     assert {Case(n).program for n in DAG_CASES} == {"deeppoly", "crown"}
 
 
