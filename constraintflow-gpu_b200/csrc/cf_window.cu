@@ -130,7 +130,35 @@ __global__ void __launch_bounds__(256) k_win_relu_bias(RowGeom rg, WinGeom g, fl
           continue;
         }
         const int64_t k0 = b * n_level + (int64_t)Y * g.W + X;
-        for (int c = c0; c < g.C; c += cstep) {
+        int c = c0;
+        // four channels at a time: their loads are issued before any of their arithmetic
+        // (the pass is latency-bound otherwise); same summation order as one at a time
+        for (; c + 3 * cstep < g.C; c += 4 * cstep) {
+          float x[4], pv[4], nv[4], mv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int cc = c + q * cstep;
+            x[q] = a[(int64_t)cc * pp + p];
+            if (alpha) {
+              const int64_t k = k0 + (int64_t)cc * HW;
+              pv[q] = __ldg(pf + k);
+              nv[q] = __ldg(nf + k);
+              mv[q] = __ldg(mu + k);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int cc = c + q * cstep;
+            float tr = x[q];
+            if (alpha) {
+              tr = x[q] >= 0.0f ? x[q] * pv[q] : x[q] * nv[q];
+              if (s == 0 ? (x[q] < 0.0f) : (x[q] > 0.0f)) acc = fmaf(x[q], mv[q], acc);
+            }
+            if (bias) acc = fmaf(tr, __ldg(bias + cc), acc);
+            a[(int64_t)cc * pp + p] = tr;
+          }
+        }
+        for (; c < g.C; c += cstep) {
           const int64_t e = (int64_t)c * pp + p;
           const float x = a[e];
           float tr = x;
