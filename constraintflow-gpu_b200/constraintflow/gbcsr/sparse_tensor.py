@@ -447,6 +447,23 @@ class SparseTensor:
         total = self.shape[:2] if unequal else self.shape[:2] + [y.shape[2]]
         return SparseTensor(starts, blocks, len(total), torch.tensor(total), ends, type=float, dense_const=0.0)
 
+    def get_sparse_custom_range(self, start_index, end_index, *args, **kwargs):
+        """The blocks inside the box [start, end), at their own positions in a tensor of the
+        same total size and fill (reference: sparse_tensor.py:873-960): blocks outside the box
+        are left out, a block that straddles its border raises NotImplementedError, as there."""
+        st, en = _ints(start_index), _ints(end_index)
+        starts, ends, blocks = [], [], []
+        for (s, e), blk in zip(self._boxes(), self.blocks):
+            inside = all(a >= c and b <= d for a, b, c, d in zip(s, e, st, en))
+            meets = all(max(a, c) < min(b, d) for a, b, c, d in zip(s, e, st, en))
+            if inside:
+                starts.append(s)
+                ends.append(e)
+                blocks.append(blk)
+            elif meets:
+                raise NotImplementedError("get_sparse_custom_range: a block straddles the range")
+        return SparseTensor(starts, blocks, self.dims, self.total_size, ends, self.type, self.dense_const)
+
     def _bp_union(self, n, pairs):
         pts = {0, n}
         for t, d in pairs:

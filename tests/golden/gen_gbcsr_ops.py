@@ -240,6 +240,17 @@ def main():
     for k in range(2):
         dx = rand_layout([2, 3, 5], "bool", bool(k))
         add(f"convert_to_float_{k}", "convert_to_float", dict(x=dx), T.convert_to_float(build(dx)))
+    # sub-tensor over a box (SparseTensor.get_sparse_custom_range, sparse_tensor.py:873; what
+    # PolyExpSparse.get_mat takes over the live layers' columns, polyexp.py:131-137)
+    for k in range(6):
+        dx = rand_layout([2, 3, 10], "float", float(k % 2), split_rows=True)
+        a = int(rng.integers(0, 5))
+        b = int(rng.integers(a + 1, 11))
+        st, en = [0, 0, a], [2, 3, b]
+        res = attempt(f"custom_range_{k}",
+                      lambda: build(dx).get_sparse_custom_range(torch.tensor(st), torch.tensor(en)))
+        if res is not None:
+            add(f"custom_range_{k}", "custom_range", dict(x=dx, start=st, end=en), res)
 
     with open(os.path.join(HERE, "gbcsr_ops.pkl"), "wb") as fh:
         pickle.dump(cases, fh, protocol=4)

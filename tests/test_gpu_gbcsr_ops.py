@@ -60,6 +60,8 @@ def _run(case):
         return _build(a["x"]).squeeze(a["index"])
     if op == "repeat":
         return T.repeat(_build(a["x"]), torch.tensor(a["dims"]))
+    if op == "custom_range":
+        return _build(a["x"]).get_sparse_custom_range(torch.tensor(a["start"]), torch.tensor(a["end"]))
     if op == "convert_to_float":
         return T.convert_to_float(_build(a["x"]))
     raise ValueError(op)
