@@ -21,6 +21,16 @@
 // thread), so N is what makes the tensor core pay.  The s*s phase outputs of a position
 // are adjacent in memory, so a tile writes whole sectors.
 //
+// A stride-1 layer has one phase, so N would be Cin alone.  There the output positions are
+// blocked f x f (f = 2): with S = s*f and u' + D = i*S + py, py = qy*s + ry (qy < f,
+// ry < s), the taps are ky = ry + ty*s and the input rows u = i*f + (f-1) - ty' with
+// ty' = ty - qy + (f-1) in [0, TY + f - 1) for every phase alike, so
+//   k = (co, ty', tx'), K = Cout * (TY + f - 1) * (TX + f - 1);  n = (py, px, ci), N = S*S*Cin
+//   A[m, k] = in[r, co, i*f + f-1 - ty', j*f + f-1 - tx']
+//   B[k, n] = W[co, ci, ry + (ty' + qy - (f-1))*s, rx + (tx' + qx - (f-1))*s] (0 off the kernel)
+// and the output goes to out[r, ci, i*S + py - D, j*S + px - D].  f = 1 is the phase-stacked
+// form above.  For a 3x3 stride-1 layer this takes 2.25x fewer MMAs and gathered loads.
+//
 // Persistent CTAs loop over 128-row M tiles.  Warps 0-7 gather the A operand chunk by chunk
 // (32 k columns; thread <-> tile row, two threads per row take 16 columns each, two chunks
 // loaded ahead; a per-thread tap mask replaces the window bounds test), split it into tf32
@@ -54,12 +64,13 @@ struct WinTcParams {
   RowGeom rg;
   WinGeom gi, go;
   ConvGeom cv;
-  int32_t TY, TX;        // taps per phase and dimension
+  int32_t TY, TX;        // k taps per dimension (the conv's taps per phase + f - 1)
+  int32_t f, S;          // output blocking factor (1, or 2 for stride 1) and S = s*f
   int32_t i0, j0;        // grid origin: i = i0 + iy
   int32_t ny, nx;        // grid size
   int32_t Dy, Dx;
   int32_t K, kchunks, taps;
-  int32_t N, n_pad;      // N = s*s*Cin
+  int32_t N, n_pad;      // N = S*S*Cin
   int64_t M;
   const float* in;
   float* out;
@@ -78,9 +89,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // B^T image: element (n, k) -> plane c = k / 32 of the hi / lo image at the SW128 position
-// of (n, k % 32); zero outside [0, N) x [0, K) and past the kernel.
-__global__ void k_win_prep_wimg(const float* __restrict__ W, ConvGeom cv, int TY, int TX, int N, int n_pad, int K,
-                                int kchunks, uint8_t* __restrict__ img) {
+// of (n, k % 32); zero outside [0, N) x [0, K) and past the kernel.  TY, TX: k taps per
+// dimension; f: the output blocking factor (S = s*f phases per dimension).
+__global__ void k_win_prep_wimg(const float* __restrict__ W, ConvGeom cv, int TY, int TX, int f, int N, int n_pad,
+                                int K, int kchunks, uint8_t* __restrict__ img) {
   const int64_t total = (int64_t)kchunks * n_pad * 32;
   const int taps = TY * TX;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -91,10 +103,13 @@ __global__ void k_win_prep_wimg(const float* __restrict__ W, ConvGeom cv, int TY
     const int k = c * 32 + kl;
     float v = 0.0f;
     if (nl < N && k < K) {
-      const int co = k / taps, t = k - co * taps, ty = t / TX, tx = t - ty * TX;
-      const int p = nl / cv.cin, ci = nl - p * cv.cin, py = p / cv.s, px = p - py * cv.s;
-      const int ky = py + ty * cv.s, kx = px + tx * cv.s;
-      if (ky < cv.kh && kx < cv.kw) v = W[(((int64_t)co * cv.cin + ci) * cv.kh + ky) * cv.kw + kx];
+      const int S = cv.s * f;
+      const int co = k / taps, t = k - co * taps, tyk = t / TX, txk = t - tyk * TX;
+      const int p = nl / cv.cin, ci = nl - p * cv.cin, py = p / S, px = p - py * S;
+      const int ty = tyk + py / cv.s - (f - 1), tx = txk + px / cv.s - (f - 1);
+      const int ky = py % cv.s + ty * cv.s, kx = px % cv.s + tx * cv.s;
+      if (ty >= 0 && tx >= 0 && ky < cv.kh && kx < cv.kw)
+        v = W[(((int64_t)co * cv.cin + ci) * cv.kh + ky) * cv.kw + kx];
     }
     float hi, lo;
     split_tf32(v, hi, lo);
@@ -277,7 +292,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
         const int64_t rr = m / pos;
         const int rem = (int)(m - rr * pos);
         const int iy = rem / P.nx, ix = rem - iy * P.nx;
-        const int qy = P.i0 + iy, qx = P.j0 + ix;
+        const int qy = (P.i0 + iy) * P.f + P.f - 1, qx = (P.j0 + ix) * P.f + P.f - 1;
         base = P.in + rr * per_in + (int64_t)qy * P.gi.Pw + qx;
         for (int t = 0; t < P.taps; ++t) {
           const int ty = t / P.TX, tx = t - ty * P.TX;
@@ -338,7 +353,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
     const int pos = P.ny * P.nx;
     const int plane_out = P.go.Ph * P.go.Pw;
     const int64_t per_out = (int64_t)P.go.C * plane_out;
-    const int s = P.cv.s, cin = P.cv.cin;
+    const int s = P.S, cin = P.cv.cin;
     // 8-byte pair stores: stride 2, even offsets (output x of phase 0 even), whole 16-column
     // channel groups, even plane and row lengths (8-byte aligned rows)
     const bool pair_ok = s == 2 && cin % 16 == 0 && (P.go.Pw & 1) == 0 && (plane_out & 1) == 0 &&
@@ -479,27 +494,48 @@ __global__ void __launch_bounds__(kWThreads, 1) k_win_convT_tc(const __grid_cons
 
 // Geometry of the phase-stacked GEMM of one conv step.
 struct TcGeom {
-  int TY, TX, i0, j0, ny, nx, Dy, Dx, K, kchunks, N, n_pad;
+  int TY, TX, f, S, i0, j0, ny, nx, Dy, Dx, K, kchunks, N, n_pad;
 };
 
 int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
 
+// output blocking factor: 2x2 output blocks for a stride-1 layer (N = 4*Cin <= 256) unless
+// CF_CONV_BLOCK=0; 1 otherwise
+int tc_blocking(const ConvGeom& cv) {
+  static int off = -1;
+  if (off < 0) {
+    const char* e = getenv("CF_CONV_BLOCK");
+    off = (e && e[0] == '0') ? 1 : 0;
+  }
+  return (!off && cv.s == 1 && cv.kh >= 2 && cv.kw >= 2 && 4 * cv.cin <= 256 &&
+          (cv.kh + 1) * (cv.kw + 1) <= kWMaxTaps)
+             ? 2
+             : 1;
+}
+
+// k taps per dimension, K, N of the GEMM of a conv step
+void tc_dims(const ConvGeom& cv, int cout, int& f, int& TY, int& TX, int& K, int& N, int& n_pad) {
+  f = tc_blocking(cv);
+  TY = (cv.kh + cv.s - 1) / cv.s + f - 1;
+  TX = (cv.kw + cv.s - 1) / cv.s + f - 1;
+  K = cout * TY * TX;
+  N = cv.s * f * cv.s * f * cv.cin;
+  n_pad = ((N + 15) / 16) * 16;
+}
+
 TcGeom tc_geom(const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout) {
   TcGeom t;
   const int s = cv.s;
-  t.TY = (cv.kh + s - 1) / s;
-  t.TX = (cv.kw + s - 1) / s;
+  tc_dims(cv, cout, t.f, t.TY, t.TX, t.K, t.N, t.n_pad);
+  t.S = s * t.f;
   t.Dy = gi.pi_h * s + cv.pad - go.pi_h;
   t.Dx = gi.pi_w * s + cv.pad - go.pi_w;
-  // grid rows i with some phase position u' = i*s + py - D inside [0, Ph)
-  t.i0 = floor_div(t.Dy, s);
-  t.j0 = floor_div(t.Dx, s);
-  t.ny = floor_div(go.Ph - 1 + t.Dy, s) - t.i0 + 1;
-  t.nx = floor_div(go.Pw - 1 + t.Dx, s) - t.j0 + 1;
-  t.K = cout * t.TY * t.TX;
+  // grid rows i with some phase position u' = i*S + py - D inside [0, Ph)
+  t.i0 = floor_div(t.Dy, t.S);
+  t.j0 = floor_div(t.Dx, t.S);
+  t.ny = floor_div(go.Ph - 1 + t.Dy, t.S) - t.i0 + 1;
+  t.nx = floor_div(go.Pw - 1 + t.Dx, t.S) - t.j0 + 1;
   t.kchunks = (t.K + 31) / 32;
-  t.N = s * s * cv.cin;
-  t.n_pad = ((t.N + 15) / 16) * 16;
   return t;
 }
 
@@ -509,15 +545,15 @@ size_t tc_smem_fixed(int kchunks) { return 1024 + (size_t)kchunks * 32 * 8 + (4 
 
 size_t win_convT_tc_scratch_bytes(const ConvGeom& cv, int cout) {
   // the weight image: kchunks x 2 planes x n_pad rows x 128 B
-  const int TY = (cv.kh + cv.s - 1) / cv.s, TX = (cv.kw + cv.s - 1) / cv.s;
-  const int n_pad = ((cv.s * cv.s * cv.cin + 15) / 16) * 16;
-  return (size_t)((cout * TY * TX + 31) / 32) * 2 * n_pad * 128;
+  int f, TY, TX, K, N, n_pad;
+  tc_dims(cv, cout, f, TY, TX, K, N, n_pad);
+  return (size_t)((K + 31) / 32) * 2 * n_pad * 128;
 }
 
 bool win_convT_tc_applicable(const ConvGeom& cv, int cout) {
-  const int TY = (cv.kh + cv.s - 1) / cv.s, TX = (cv.kw + cv.s - 1) / cv.s;
-  const int n_pad = ((cv.s * cv.s * cv.cin + 15) / 16) * 16;
-  const size_t smem = tc_smem_fixed((cout * TY * TX + 31) / 32) + (size_t)2 * (2 * kWAImg + 2 * n_pad * 128);
+  int f, TY, TX, K, N, n_pad;
+  tc_dims(cv, cout, f, TY, TX, K, N, n_pad);
+  const size_t smem = tc_smem_fixed((K + 31) / 32) + (size_t)2 * (2 * kWAImg + 2 * n_pad * 128);
   return cv.cin >= 1 && n_pad <= 256 && TY * TX <= kWMaxTaps && smem <= 227 * 1024;
 }
 
@@ -548,6 +584,8 @@ cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, 
   P.cv = cv;
   P.TY = t.TY;
   P.TX = t.TX;
+  P.f = t.f;
+  P.S = t.S;
   P.i0 = t.i0;
   P.j0 = t.j0;
   P.ny = t.ny;
@@ -585,8 +623,8 @@ cf_status win_convT_tc(const RowGeom& rg, const WinGeom& gi, const WinGeom& go, 
   CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "convT_tc: %zu bytes of shared memory", smem);
   // the phase-stacked weight image (stream-ordered before the GEMM that reads it)
   const int64_t total = (int64_t)t.kchunks * t.n_pad * 32;
-  k_win_prep_wimg<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(W, cv, t.TY, t.TX, t.N, t.n_pad, t.K, t.kchunks,
-                                                                   scratch);
+  k_win_prep_wimg<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(W, cv, t.TY, t.TX, t.f, t.N, t.n_pad, t.K,
+                                                                   t.kchunks, scratch);
   CF_TRY(check_launch("k_win_prep_wimg"));
   const int64_t tiles = (P.M + 127) / 128;
   const int64_t grid = tiles < sms ? tiles : sms;
