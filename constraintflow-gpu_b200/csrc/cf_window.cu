@@ -222,13 +222,14 @@ __global__ void __launch_bounds__(256) k_win_relu_bias_whole(RowGeom rg, WinGeom
       m4 = reinterpret_cast<const float4*>(mu + b * per);
     }
     float acc = 0.0f;
-    for (int64_t q = threadIdx.x; q < per / 4; q += blockDim.x) {
-      float4 x = a[q];
-      float xs[4] = {x.x, x.y, x.z, x.w};
+    const int64_t n4 = per / 4;
+    const bool c_per4 = (pp & 3) == 0;   // the 4 elements of a piece share one channel
+    // one 16-byte piece: transform in place, accumulate in element order
+    auto piece = [&](int64_t q, float4 x, float4 p4, float4 n4v, float4 u4) {
+      const float xs[4] = {x.x, x.y, x.z, x.w};
       float tr[4] = {x.x, x.y, x.z, x.w};
       if (alpha) {
-        const float4 p4 = __ldg(pf + q), n4 = __ldg(nf + q), u4 = __ldg(m4 + q);
-        const float ps[4] = {p4.x, p4.y, p4.z, p4.w}, ns[4] = {n4.x, n4.y, n4.z, n4.w};
+        const float ps[4] = {p4.x, p4.y, p4.z, p4.w}, ns[4] = {n4v.x, n4v.y, n4v.z, n4v.w};
         const float ms[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -237,10 +238,43 @@ __global__ void __launch_bounds__(256) k_win_relu_bias_whole(RowGeom rg, WinGeom
         }
       }
       if (bias) {
+        if (c_per4) {
+          const float bv = __ldg(bias + (4 * q) / pp);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc = fmaf(tr[e], __ldg(bias + (4 * q + e) / pp), acc);
+          for (int e = 0; e < 4; ++e) acc = fmaf(tr[e], bv, acc);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc = fmaf(tr[e], __ldg(bias + (4 * q + e) / pp), acc);
+        }
       }
       a[q] = make_float4(tr[0], tr[1], tr[2], tr[3]);
+    };
+    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    // two pieces per iteration, both loaded before either is transformed
+    int64_t q = threadIdx.x;
+    for (; q + blockDim.x < n4; q += 2 * (int64_t)blockDim.x) {
+      const int64_t q2 = q + blockDim.x;
+      const float4 x1 = a[q], x2 = a[q2];
+      float4 p1 = z4, n1 = z4, u1 = z4, p2 = z4, n2 = z4, u2 = z4;
+      if (alpha) {
+        p1 = __ldg(pf + q);
+        n1 = __ldg(nf + q);
+        u1 = __ldg(m4 + q);
+        p2 = __ldg(pf + q2);
+        n2 = __ldg(nf + q2);
+        u2 = __ldg(m4 + q2);
+      }
+      piece(q, x1, p1, n1, u1);
+      piece(q2, x2, p2, n2, u2);
+    }
+    for (; q < n4; q += blockDim.x) {
+      float4 p1 = z4, n1 = z4, u1 = z4;
+      if (alpha) {
+        p1 = __ldg(pf + q);
+        n1 = __ldg(nf + q);
+        u1 = __ldg(m4 + q);
+      }
+      piece(q, a[q], p1, n1, u1);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
