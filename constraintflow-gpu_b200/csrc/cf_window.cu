@@ -28,11 +28,12 @@ struct WinPos {
   bool in;
 };
 
-__device__ __forceinline__ WinPos win_pos(const WinGeom& g, int64_t e, int oy, int ox) {
+// (a window holds one level image at most: e < C*H*W fits 32 bits)
+__device__ __forceinline__ WinPos win_pos(const WinGeom& g, int e, int oy, int ox) {
   WinPos p;
-  const int64_t pp = (int64_t)g.Ph * g.Pw;
-  p.c = (int)(e / pp);
-  const int rem = (int)(e - (int64_t)p.c * pp);
+  const int pp = g.Ph * g.Pw;
+  p.c = e / pp;
+  const int rem = e - p.c * pp;
   const int u = rem / g.Pw, v = rem - (rem / g.Pw) * g.Pw;
   p.Y = oy * g.sig_h - g.pi_h + u;
   p.X = ox * g.sig_w - g.pi_w + v;
@@ -57,26 +58,25 @@ __device__ __forceinline__ void row_coords(const RowGeom& rg, int64_t r, int64_t
 // Row (s,b,i) of layer m, i = (co, oy, ox): its weights as a window at level m-1.
 // Conv: W[co] [Cin, kh, kw] at origin (oy*s - p, ox*s - p).  Linear: W[i] over the whole
 // level image (origin 0).  Positions outside the image are zero.
+// A warp per row: the row's coordinates once, then its elements in 32-bit arithmetic.
 __global__ void k_win_init(RowGeom rg, WinGeom g, const float* __restrict__ W, int64_t w_bs, int conv,
                            float* __restrict__ out) {
-  const int64_t per = (int64_t)g.C * g.Ph * g.Pw;
-  const int64_t total = 2 * rg.B * rg.R * per;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / per, e = t - r * per;
+  const int per = g.C * g.Ph * g.Pw;
+  const int64_t rows = 2 * rg.B * rg.R;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
     int64_t s, b, i;
     int oy, ox;
     row_coords(rg, r, s, b, i, oy, ox);
-    const WinPos p = win_pos(g, e, oy, ox);
-    float v = 0.0f;
-    if (p.in) {
-      if (conv) {
-        const int64_t co = i / ((int64_t)rg.Hm * rg.Wm);
-        v = W[co * per + e];  // kernel [Cin, kh, kw] matches the window layout
-      } else {
-        v = W[b * w_bs + i * per + e];  // linear row over the whole image (C, H, W) order
-      }
+    // conv: the kernel [Cin, kh, kw] of the row's channel matches the window layout;
+    // linear: the row over the whole image in (C, H, W) order
+    const float* src = conv ? W + (i / ((int64_t)rg.Hm * rg.Wm)) * per : W + b * w_bs + i * per;
+    float* dst = out + r * per;
+    for (int e = lane; e < per; e += 32) {
+      const WinPos p = win_pos(g, e, oy, ox);
+      dst[e] = p.in ? src[e] : 0.0f;
     }
-    out[t] = v;
   }
 }
 
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(256) k_win_concretize(RowGeom rg, WinGeom g, c
     const float* pb = (s == 0 ? l0 : u0) + b * n0;
     const float* nb = (s == 0 ? u0 : l0) + b * n0;
     float acc = 0.0f;
-    for (int64_t e = threadIdx.x; e < per; e += blockDim.x) {
+    for (int e = threadIdx.x; e < (int)per; e += blockDim.x) {
       const WinPos p = win_pos(g, e, oy, ox);
       if (!p.in) continue;
       const int64_t k = (int64_t)p.c * HW + (int64_t)p.Y * g.W + p.X;
@@ -637,7 +637,8 @@ cf_status win_init(const RowGeom& rg, const WinGeom& g, const float* W, int64_t 
                    cudaStream_t st) {
   const int64_t total = 2 * rg.B * rg.R * (int64_t)g.C * g.Ph * g.Pw;
   if (total == 0) return CF_OK;
-  k_win_init<<<grid_for(total, 256, 148 * 32), 256, 0, st>>>(rg, g, W, w_bs, conv ? 1 : 0, out);
+  CF_REQUIRE((int64_t)g.C * g.Ph * g.Pw < 0x7fffffff, CF_ERR_SHAPE, "win_init: window too large");
+  k_win_init<<<grid_for(2 * rg.B * rg.R, 8, 148 * 32), 256, 0, st>>>(rg, g, W, w_bs, conv ? 1 : 0, out);
   return check_launch("k_win_init");
 }
 
@@ -722,6 +723,7 @@ cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, co
                          const float* u0, float* out_l, float* out_u, int64_t ld_out, cudaStream_t st) {
   const int64_t rows = 2 * rg.B * rg.R;
   if (rows == 0) return CF_OK;
+  CF_REQUIRE((int64_t)g.C * g.Ph * g.Pw < 0x7fffffff, CF_ERR_SHAPE, "win_concretize: window too large");
   k_win_concretize<<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c, l0, u0, out_l, out_u, ld_out);
   return check_launch("k_win_concretize");
 }
