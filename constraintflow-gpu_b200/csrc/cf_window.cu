@@ -474,6 +474,15 @@ static unsigned grid_for(int64_t work, int64_t per_block, int64_t cap) {
 // taps in registers (the row segment it reads is shared by the kw taps), folds its outputs
 // into the box bound (a >= 0 ? a * box_s : a * box_{1-s} at in-image positions) and the
 // block adds each row's partial bounds in a fixed order.
+__device__ __forceinline__ void cp_async4(float* dst_smem, const float* src, bool valid) {
+  // 4-byte asynchronous copy global -> shared; zero-filled (nothing read) when !valid
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst_smem)),
+               "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 template <int NCI, int KW>
 __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGeom go, int kh, int cout, int Dy,
                                                    int Dx, int rb, int cc, const float* __restrict__ in,
@@ -485,8 +494,9 @@ __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGe
   const int wn = cout * NCI * kh * KW;
   float* wsm = sm;                                  // [cout][NCI][kh][KW]
   const int plane = gi.Ph * gi.Pw;
-  float* xs = sm + ((wn + 3) & ~3);                 // [rb][cc][Ph][Pw]
-  float* part = xs + (size_t)rb * cc * plane;       // [256] partial bounds
+  const int stage = rb * cc * plane;
+  float* xs = sm + ((wn + 3) & ~3);                 // two stages of [rb][cc][Ph][Pw]
+  float* part = xs + 2 * (size_t)stage;             // [256] partial bounds
   for (int e = threadIdx.x; e < wn; e += blockDim.x) wsm[e] = W[e];
   const int XG = (go.Pw + 3) / 4, TPR = go.Ph * XG;
   const int64_t per_in = (int64_t)gi.C * plane;
@@ -494,90 +504,123 @@ __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGe
   const int64_t HW0 = (int64_t)go.H * go.W, n0 = (int64_t)NCI * HW0;
   const int slot = threadIdx.x / TPR, task = threadIdx.x - (threadIdx.x / TPR) * TPR;
   const int up = task / XG, xg = task - (task / XG) * XG;
-  for (int64_t r0 = (int64_t)blockIdx.x * rb; r0 < rows; r0 += (int64_t)gridDim.x * rb) {
+  const int64_t r_step = (int64_t)gridDim.x * rb;
+  // the (row group, channel chunk) sequence of this block, staged two ahead by cp.async:
+  // chunk (r0, co0) into stage buffer `buf`
+  auto issue = [&](int64_t r0, int co0, int buf) {
+    const int nc = cout - co0 < cc ? cout - co0 : cc;
+    const int per_chunk = nc * plane;
+    float* dst = xs + (size_t)buf * stage;
+    for (int e = threadIdx.x; e < rb * per_chunk; e += blockDim.x) {
+      const int rs = e / per_chunk, rem = e - rs * per_chunk;
+      const int64_t row = r0 + rs;
+      const bool ok = row < rows;
+      cp_async4(dst + (size_t)rs * cc * plane + rem, ok ? in + row * per_in + (int64_t)co0 * plane + rem : in, ok);
+    }
+  };
+  int64_t r0 = (int64_t)blockIdx.x * rb;
+  int co0 = 0, buf = 0;
+  if (r0 < rows) issue(r0, 0, 0);
+  cp_async_commit();
+  float acc[4][NCI];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int ci = 0; ci < NCI; ++ci) acc[j][ci] = 0.0f;
+  while (r0 < rows) {
+    // the next chunk of the sequence into the other buffer (its previous contents were
+    // consumed before the barrier that ended the last iteration)
+    int64_t r1 = r0;
+    int co1 = co0 + cc;
+    if (co1 >= cout) {
+      co1 = 0;
+      r1 = r0 + r_step;
+    }
+    if (r1 < rows) issue(r1, co1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait1();   // this chunk's copies (all but the group just issued) have landed
+    __syncthreads();
     const int64_t r = r0 + slot;
     const bool active = slot < rb && r < rows;
-    float acc[4][NCI];
+    const int nc = cout - co0 < cc ? cout - co0 : cc;
+    if (active) {
+      const float* xb = xs + (size_t)buf * stage;
+      for (int cix = 0; cix < nc; ++cix) {
+        const float* xp = xb + ((size_t)slot * cc + cix) * plane;
+        const float* wc = wsm + (size_t)(co0 + cix) * NCI * kh * KW;
+        for (int ky = 0; ky < kh; ++ky) {
+          const int u = up + Dy - ky;
+          if (u < 0 || u >= gi.Ph) continue;
+          const float* xr = xp + u * gi.Pw;
+          float xv[4 + KW - 1];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+          for (int q = 0; q < 4 + KW - 1; ++q) {
+            const int v = xg * 4 + Dx - (KW - 1) + q;
+            xv[q] = (v >= 0 && v < gi.Pw) ? xr[v] : 0.0f;
+          }
 #pragma unroll
-      for (int ci = 0; ci < NCI; ++ci) acc[j][ci] = 0.0f;
-    for (int co0 = 0; co0 < cout; co0 += cc) {
-      const int nc = cout - co0 < cc ? cout - co0 : cc;
-      __syncthreads();  // the previous chunk (and the previous rows' partials) are consumed
-      const int per_chunk = nc * plane;
-      for (int e = threadIdx.x; e < rb * per_chunk; e += blockDim.x) {
-        const int rs = e / per_chunk, rem = e - rs * per_chunk;
-        const int64_t row = r0 + rs;
-        xs[(size_t)rs * cc * plane + rem] = row < rows ? in[row * per_in + (int64_t)co0 * plane + rem] : 0.0f;
-      }
-      __syncthreads();
-      if (active) {
-        for (int cix = 0; cix < nc; ++cix) {
-          const float* xp = xs + ((size_t)slot * cc + cix) * plane;
-          const float* wc = wsm + (size_t)(co0 + cix) * NCI * kh * KW;
-          for (int ky = 0; ky < kh; ++ky) {
-            const int u = up + Dy - ky;
-            if (u < 0 || u >= gi.Ph) continue;
-            const float* xr = xp + u * gi.Pw;
-            float xv[4 + KW - 1];
+          for (int kx = 0; kx < KW; ++kx) {
 #pragma unroll
-            for (int q = 0; q < 4 + KW - 1; ++q) {
-              const int v = xg * 4 + Dx - (KW - 1) + q;
-              xv[q] = (v >= 0 && v < gi.Pw) ? xr[v] : 0.0f;
-            }
+            for (int ci = 0; ci < NCI; ++ci) {
+              const float w = wc[(ci * kh + ky) * KW + kx];
 #pragma unroll
-            for (int kx = 0; kx < KW; ++kx) {
-#pragma unroll
-              for (int ci = 0; ci < NCI; ++ci) {
-                const float w = wc[(ci * kh + ky) * KW + kx];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[j][ci] = fmaf(xv[j + (KW - 1) - kx], w, acc[j][ci]);
-              }
+              for (int j = 0; j < 4; ++j) acc[j][ci] = fmaf(xv[j + (KW - 1) - kx], w, acc[j][ci]);
             }
           }
         }
       }
     }
-    float partial = 0.0f;
-    if (active) {
-      int64_t s, b, i;
-      int oy, ox;
-      row_coords(rg, r, s, b, i, oy, ox);
-      const float* pb = (s == 0 ? l0 : u0) + b * n0;
-      const float* nb = (s == 0 ? u0 : l0) + b * n0;
-      const int Y = oy * go.sig_h - go.pi_h + up;
+    if (co0 + cc >= cout) {
+      // the row group is complete: fold its outputs into the box bound, add them per row
+      float partial = 0.0f;
+      if (active) {
+        int64_t s, b, i;
+        int oy, ox;
+        row_coords(rg, r, s, b, i, oy, ox);
+        const float* pb = (s == 0 ? l0 : u0) + b * n0;
+        const float* nb = (s == 0 ? u0 : l0) + b * n0;
+        const int Y = oy * go.sig_h - go.pi_h + up;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int vo = xg * 4 + j;
-        const int X = ox * go.sig_w - go.pi_w + vo;
-        if (vo >= go.Pw || Y < 0 || Y >= go.H || X < 0 || X >= go.W) continue;
+        for (int j = 0; j < 4; ++j) {
+          const int vo = xg * 4 + j;
+          const int X = ox * go.sig_w - go.pi_w + vo;
+          if (vo >= go.Pw || Y < 0 || Y >= go.H || X < 0 || X >= go.W) continue;
 #pragma unroll
-        for (int ci = 0; ci < NCI; ++ci) {
-          const int64_t k = (int64_t)ci * HW0 + (int64_t)Y * go.W + X;
-          const float a = acc[j][ci];
-          partial = fmaf(a, a >= 0.0f ? pb[k] : nb[k], partial);
+          for (int ci = 0; ci < NCI; ++ci) {
+            const int64_t k = (int64_t)ci * HW0 + (int64_t)Y * go.W + X;
+            const float a = acc[j][ci];
+            partial = fmaf(a, a >= 0.0f ? pb[k] : nb[k], partial);
+          }
         }
       }
+      part[threadIdx.x] = partial;
+      __syncthreads();
+      if (threadIdx.x < rb && r0 + threadIdx.x < rows) {
+        const int64_t rr = r0 + threadIdx.x;
+        float tot = 0.0f;
+        for (int t = 0; t < TPR; ++t) tot += part[threadIdx.x * TPR + t];
+        int64_t s, b, i;
+        int oy, ox;
+        row_coords(rg, rr, s, b, i, oy, ox);
+        const float res = tot + c[rr];
+        if (s == 0) out_l[b * ld_out + i] = res;
+        else out_u[b * ld_out + i] = res;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int ci = 0; ci < NCI; ++ci) acc[j][ci] = 0.0f;
     }
-    part[threadIdx.x] = partial;
-    __syncthreads();
-    if (threadIdx.x < rb && r0 + threadIdx.x < rows) {
-      const int64_t rr = r0 + threadIdx.x;
-      float tot = 0.0f;
-      for (int t = 0; t < TPR; ++t) tot += part[threadIdx.x * TPR + t];
-      int64_t s, b, i;
-      int oy, ox;
-      row_coords(rg, rr, s, b, i, oy, ox);
-      const float res = tot + c[rr];
-      if (s == 0) out_l[b * ld_out + i] = res;
-      else out_u[b * ld_out + i] = res;
-    }
+    __syncthreads();   // this buffer (and the partials) are consumed
+    r0 = r1;
+    co0 = co1;
+    buf ^= 1;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-// shared-memory floats of the staged windows per block
-constexpr int kFirstStageFloats = 8192;
+// shared-memory floats of one stage of staged windows per block (two stages)
+constexpr int kFirstStageFloats = 4096;
 
 static bool first_geometry(const WinGeom& gi, const WinGeom& go, const ConvGeom& cv, int cout, int& rb, int& cc) {
   if (cv.s != 1 || cv.cin < 1 || cv.cin > 4 || !(cv.kw == 3 || cv.kw == 5) || cv.kh > 7 || go.C != cv.cin)
@@ -606,7 +649,7 @@ cf_status win_convT_first(const RowGeom& rg, const WinGeom& gi, const WinGeom& g
   if (rows == 0) return CF_OK;
   const int Dy = gi.pi_h + cv.pad - go.pi_h, Dx = gi.pi_w + cv.pad - go.pi_w;
   const int wn = cout * cv.cin * cv.kh * cv.kw;
-  const size_t smem = (size_t)(((wn + 3) & ~3) + rb * cc * gi.Ph * gi.Pw + 256) * sizeof(float);
+  const size_t smem = (size_t)(((wn + 3) & ~3) + 2 * rb * cc * gi.Ph * gi.Pw + 256) * sizeof(float);
   const unsigned grid = grid_for(rows, rb, 148 * 16);
 #define CF_FIRST(NCI, KW)                                                                                          \
   do {                                                                                                             \
