@@ -88,7 +88,7 @@ __global__ void k_win_init(RowGeom rg, WinGeom g, const float* __restrict__ W, i
 // channels, so the plane coordinates and the relaxation offsets are computed once per
 // position; the row sum is a fixed-order shuffle (and, for kT = 256, shared-memory) tree.
 template <int kT>
-__global__ void __launch_bounds__(256) k_win_relu_bias(RowGeom rg, WinGeom g, float* __restrict__ A,
+__global__ void __launch_bounds__(256, 4) k_win_relu_bias(RowGeom rg, WinGeom g, float* __restrict__ A,
                                                        const float* __restrict__ c_in, int64_t c_ss, int64_t c_bs,
                                                        const float* __restrict__ alpha, const float* __restrict__ lam,
                                                        const float* __restrict__ mu, const float* __restrict__ bias,
