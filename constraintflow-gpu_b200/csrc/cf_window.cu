@@ -419,42 +419,56 @@ __global__ void __launch_bounds__(256) k_win_convT_gemm(RowGeom rg, WinGeom gi, 
 
 // ------------------------------------------------------------------ concretisation
 // bound = c + sum_{in-image window positions} (a>=0 ? a*box_s : a*box_{1-s}); block per row.
+// kT threads per row (a warp for windows of at most 2048 elements, the block otherwise),
+// 256 / kT rows per block; the row's sum is a fixed-order shuffle (and, for kT = 256,
+// shared-memory) tree.
+template <int kT>
 __global__ void __launch_bounds__(256) k_win_concretize(RowGeom rg, WinGeom g, const float* __restrict__ A,
                                                         const float* __restrict__ c, const float* __restrict__ l0,
                                                         const float* __restrict__ u0, float* __restrict__ out_l,
                                                         float* __restrict__ out_u, int64_t ld_out) {
-  __shared__ float red[256];
-  const int64_t per = (int64_t)g.C * g.Ph * g.Pw;
+  __shared__ float red[8];
+  constexpr int kRowsPerBlock = 256 / kT;
+  const int per = g.C * g.Ph * g.Pw;
   const int64_t HW = (int64_t)g.H * g.W;
   const int64_t n0 = (int64_t)g.C * HW;
   const int64_t rows = 2 * rg.B * rg.R;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    int64_t s, b, i;
-    int oy, ox;
-    row_coords(rg, r, s, b, i, oy, ox);
-    const float* a = A + r * per;
-    const float* pb = (s == 0 ? l0 : u0) + b * n0;
-    const float* nb = (s == 0 ? u0 : l0) + b * n0;
+  const int t = threadIdx.x % kT, slot = threadIdx.x / kT;
+  for (int64_t r0 = (int64_t)blockIdx.x * kRowsPerBlock; r0 < rows; r0 += (int64_t)gridDim.x * kRowsPerBlock) {
+    const int64_t r = r0 + slot;
     float acc = 0.0f;
-    for (int e = threadIdx.x; e < (int)per; e += blockDim.x) {
-      const WinPos p = win_pos(g, e, oy, ox);
-      if (!p.in) continue;
-      const int64_t k = (int64_t)p.c * HW + (int64_t)p.Y * g.W + p.X;
-      const float v = a[e];
-      acc += v >= 0.0f ? v * pb[k] : v * nb[k];
+    int64_t s = 0, b = 0, i = 0;
+    if (r < rows) {
+      int oy, ox;
+      row_coords(rg, r, s, b, i, oy, ox);
+      const float* a = A + r * per;
+      const float* pb = (s == 0 ? l0 : u0) + b * n0;
+      const float* nb = (s == 0 ? u0 : l0) + b * n0;
+      for (int e = t; e < per; e += kT) {
+        const WinPos p = win_pos(g, e, oy, ox);
+        if (!p.in) continue;
+        const int64_t k = (int64_t)p.c * HW + (int64_t)p.Y * g.W + p.X;
+        const float v = a[e];
+        acc += v >= 0.0f ? v * pb[k] : v * nb[k];
+      }
     }
-    red[threadIdx.x] = acc;
-    __syncthreads();
-    for (int o = 128; o > 0; o >>= 1) {
-      if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (kT == 256) {
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        acc = tot;
+      }
       __syncthreads();
     }
-    if (threadIdx.x == 0) {
-      const float res = red[0] + c[r];
+    if (t == 0 && r < rows) {
+      const float res = acc + c[r];
       if (s == 0) out_l[b * ld_out + i] = res;
       else out_u[b * ld_out + i] = res;
     }
-    __syncthreads();
   }
 }
 
@@ -767,7 +781,10 @@ cf_status win_concretize(const RowGeom& rg, const WinGeom& g, const float* A, co
   const int64_t rows = 2 * rg.B * rg.R;
   if (rows == 0) return CF_OK;
   CF_REQUIRE((int64_t)g.C * g.Ph * g.Pw < 0x7fffffff, CF_ERR_SHAPE, "win_concretize: window too large");
-  k_win_concretize<<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c, l0, u0, out_l, out_u, ld_out);
+  if ((int64_t)g.C * g.Ph * g.Pw <= 2048)
+    k_win_concretize<32><<<grid_for(rows, 8, 148 * 64), 256, 0, st>>>(rg, g, A, c, l0, u0, out_l, out_u, ld_out);
+  else
+    k_win_concretize<256><<<grid_for(rows, 1, 148 * 64), 256, 0, st>>>(rg, g, A, c, l0, u0, out_l, out_u, ld_out);
   return check_launch("k_win_concretize");
 }
 
