@@ -442,11 +442,91 @@ __global__ void __launch_bounds__(256) k_step_gemm_simt(int64_t B, int64_t R, in
   }
 }
 
+// The same product for steps whose rows are already transformed (no relaxation on load, as
+// the window traversal calls it): a 128 x 128 tile, 8 x 8 outputs per thread, so each pair of
+// shared-memory loads feeds twice the FMAs.  Every output sums over k in the same order as
+// k_step_gemm_simt.
+constexpr int SL_M = 128, SL_N = 128, SL_K = 16;
+__global__ void __launch_bounds__(256) k_step_gemm_simt_large(int64_t B, int64_t R, int64_t K, int64_t N,
+                                                               const float* __restrict__ A, int64_t a_ss,
+                                                               int64_t a_bs, int64_t a_rs,
+                                                               const float* __restrict__ W, float* __restrict__ out) {
+  __shared__ __align__(16) float As[SL_K][SL_M + 4];
+  __shared__ __align__(16) float Ws[SL_K][SL_N + 4];
+  const int64_t rows = 2 * B * R;
+  const int64_t m0 = (int64_t)blockIdx.y * SL_M;
+  const int64_t n0 = (int64_t)blockIdx.x * SL_N;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  // A loads: rows lr + 16*q (q < 8) at column lk of each k slice
+  const int lk = tid & 15, lr = tid >> 4;
+  int64_t rbase[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int64_t r = m0 + lr + 16 * q;
+    if (r < rows) {
+      const int64_t sb = r / (B * R), rem = r - sb * B * R, b = rem / R, i = rem - b * R;
+      rbase[q] = sb * a_ss + b * a_bs + i * a_rs;
+    } else {
+      rbase[q] = -1;
+    }
+  }
+  for (int64_t k0 = 0; k0 < K; k0 += SL_K) {
+    const int64_t k = k0 + lk;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) As[lk][lr + 16 * q] = (rbase[q] >= 0 && k < K) ? A[rbase[q] + k] : 0.0f;
+    // W slice: 16 x 128, 8 elements per thread
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = tid + 256 * q;
+      const int kk = e >> 7, nn = e & 127;
+      const int64_t kg = k0 + kk, ng = n0 + nn;
+      Ws[kk][nn] = (kg < K && ng < N) ? W[kg * N + ng] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SL_K; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[kk][ty * 8 + 4]);
+      const float4 w0 = *reinterpret_cast<const float4*>(&Ws[kk][tx * 8]);
+      const float4 w1 = *reinterpret_cast<const float4*>(&Ws[kk][tx * 8 + 4]);
+      const float a8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float w8[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a8[i], w8[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = m0 + ty * 8 + i;
+    if (r >= rows) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t n = n0 + tx * 8 + j;
+      if (n < N) out[r * N + n] = acc[i][j];
+    }
+  }
+}
+
 cf_status launch_step_gemm_simt(int64_t B, int64_t R, int64_t K, int64_t N, const float* A, int64_t a_ss,
                                 int64_t a_bs, int64_t a_rs, const float* alpha, const float* lam, const float* W,
                                 float* out, cudaStream_t st) {
   int64_t rows = 2 * B * R;
   if (rows == 0 || N == 0) return CF_OK;
+  if (!alpha && rows >= 4 * SL_M && N >= SL_N) {
+    dim3 grid((unsigned)ceil_div(N, SL_N), (unsigned)ceil_div(rows, SL_M));
+    CF_REQUIRE(grid.y <= 65535u, CF_ERR_SHAPE, "step gemm: %lld rows exceed the grid limit", (long long)rows);
+    k_step_gemm_simt_large<<<grid, 256, 0, st>>>(B, R, K, N, A, a_ss, a_bs, a_rs, W, out);
+    return check_launch("k_step_gemm_simt_large");
+  }
   dim3 grid((unsigned)ceil_div(N, SB_N), (unsigned)ceil_div(rows, SB_M));
   CF_REQUIRE(grid.y <= 65535u, CF_ERR_SHAPE, "step gemm: %lld rows exceed the grid limit", (long long)rows);
   k_step_gemm_simt<<<grid, 256, 0, st>>>(B, R, K, N, A, a_ss, a_bs, a_rs, alpha, lam, W, out);
