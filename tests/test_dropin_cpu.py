@@ -36,6 +36,31 @@ def test_structure_without_device():
     assert T.clamp(-1.5, 0, True) == 0 and T.clamp(-1.5, 0, False) == -1.5
 
 
+def test_generic_runtime_refuses_explicitly():
+    """The op-by-op interpretation of generated transformer bodies is not provided: its entry
+    points raise NotImplementedError (as Flow does for an unrecognised program) instead of
+    returning something else; PolyExpSparse.get_mat keeps the live layers' columns only."""
+    import types
+    from constraintflow.gbcsr.sparse_tensor import SparseTensor
+    from constraintflow.lib.abs_elem import Abs_elem_sparse
+    from constraintflow.lib.llist import Llist
+    from constraintflow.lib.polyexp import PolyExpSparse
+    net = [types.SimpleNamespace(start=0, end=4), types.SimpleNamespace(start=4, end=7),
+           types.SimpleNamespace(start=7, end=9)]
+    d = {"llist": torch.tensor([True, True, False]), "l": None, "u": None}
+    ae = Abs_elem_sparse(d, {"llist": "bool", "l": "Float", "u": "Float"}, net, batch_size=2)
+    assert ae.get_poly_size() == 7 and ae.live_layers() == [0, 1]
+    ll = Llist(net, [1], None, None, [1])
+    assert ll.layers() == [1] and Llist(net, [1], 0, 2).layers() == [0, 1]
+    for call in (lambda: ae.get_elem("l", ll), lambda: ae.update(ll, []), lambda: ll.get_metadata("weight", 2),
+                 lambda: ll.dot(None, 7), lambda: ll.convert_to_poly(ae)):
+        with pytest.raises(NotImplementedError):
+            call()
+    mat = SparseTensor([], [], 3, torch.tensor([2, 3, 9]), dense_const=0.0)
+    got = PolyExpSparse(net, mat, 0.0).get_mat(ae)
+    assert got.shape == [2, 3, 9] and got.num_blocks == 0
+
+
 def test_generated_programs_are_recognised():
     """The reference compiler's own output for deeppoly.cf, deeppoly_efficient.cf,
     crown.cf, zono.cf, ibp.cf and polyzono.cf (tests/golden/generated/) is recognised by the drop-in
