@@ -493,7 +493,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   uint8_t* smem = align1024(smem_raw);
   // shared memory: kAStages A-operand stages (hi, lo planes), kWStages weight stages (hi, lo
   // planes of tile_n rows), two step buffers of relaxation vectors, the input-box rows of
-  // the CTA's regions, then the mbarriers
+  // the CTA's regions, then the mbarriers.  Chunk g uses A stage and W stage g % 2; the
+  // commit after its MMAs (empty_a) releases both.
+  static_assert(kAStages == kWStages, "one barrier releases an A stage and a W stage");
   const uint32_t w_stage_bytes = P.stage_bytes;
   uint8_t* a_region = smem;
   uint8_t* w_region = smem + kAStages * 2 * kAImg;
@@ -502,8 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   uint64_t* full_a = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(box_region) + P.box_smem_bytes);
   uint64_t* empty_a = full_a + kAStages;
   uint64_t* full_w = empty_a + kAStages;
-  uint64_t* empty_w = full_w + kWStages;
-  uint64_t* coef_full = empty_w + kWStages;
+  uint64_t* coef_full = full_w + kWStages;
   uint64_t* coef_empty = coef_full + 2;
   uint64_t* box_full = coef_empty + 2;
   uint64_t* acc_full = box_full + 1;
@@ -536,10 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       mbar_init(&full_a[i], kTransformThreads);
       mbar_init(&empty_a[i], 1);
     }
-    for (int i = 0; i < kWStages; ++i) {
-      mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], 1);
-    }
+    for (int i = 0; i < kWStages; ++i) mbar_init(&full_w[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&coef_full[i], 1);
       mbar_init(&coef_empty[i], kTransformWarps);
@@ -606,7 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         for (int t = 0; t < S.n_tiles; ++t) {
           for (int c = 0; c < S.kchunks; ++c, ++g) {
             const uint32_t stage = g % kWStages, round = g / kWStages;
-            if (!mbar_wait(&empty_w[stage], (round & 1) ^ 1, err, 11, P.max_polls)) goto done_w;
+            // chunk g's A stage and W stage are released together (empty_a, one commit)
+            if (!mbar_wait(&empty_a[stage], (round & 1) ^ 1, err, 11, P.max_polls)) goto done_w;
             uint8_t* sb = w_region + stage * w_stage_bytes;
             const uint8_t* src = S.wimg + ((size_t)t * S.kchunks + c) * 2 * plane;
             const uint32_t bytes = (uint32_t)tile_width(S, t) * 128u;  // rows the MMAs read
@@ -656,8 +655,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
               mma_tf32(acc, dah, dwl, idesc, 1);
               mma_tf32(acc, dah, dwh, idesc, 1);
             }
+            // one commit releases both stages (a second commit per chunk cost ~1% of the launch)
             mma_commit(&empty_a[as]);
-            mma_commit(&empty_w[ws]);
           }
           // (failure-path test: the first step's accumulator-ready arrival is withheld, so the
           // transform warps' bounded wait for it gives up)
@@ -732,7 +731,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   }
   Q.coef_ok = coef_ok ? 1 : 0;
   const size_t fixed = 1024 + (size_t)kAStages * 2 * kAImg + (size_t)kWStages * Q.stage_bytes +
-                       (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + 2 * kWStages + 4 + 3) * 8 + 16 + 256 * 4;
+                       (size_t)2 * kCoefBufFloats * 4 + (2 * kAStages + kWStages + 4 + 3) * 8 + 16 + 256 * 4;
   // input-box rows of up to kCoefSlots (bound, region) pairs, when they fit
   const size_t box_bytes = (size_t)kCoefSlots * 2 * P.n0 * 4;
   const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && Q.ld_box % 4 == 0 && a16(P.l0) && a16(P.u0) &&
@@ -778,12 +777,11 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_region + 2 * P.stage_bytes);
   uint64_t* full_a = bars;
   uint64_t* empty_a = bars + 2;
-  uint64_t* full_w = bars + 4;
-  uint64_t* empty_w = bars + 6;
-  uint64_t* acc_full = bars + 8;
-  uint64_t* acc_empty = bars + 10;
-  uint64_t* mma_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* full_w = bars + 4;     // (chunk g's W stage is released with its A stage: empty_a)
+  uint64_t* acc_full = bars + 6;
+  uint64_t* acc_empty = bars + 8;
+  uint64_t* mma_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = P.err;
   const int64_t n_tiles = (P.rows + 127) / 128;
@@ -794,7 +792,6 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
       mbar_init(&full_a[i], kTransformThreads);
       mbar_init(&empty_a[i], 1);
       mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], 1);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
@@ -823,7 +820,7 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
       for (int64_t i = 0; i < my_tiles; ++i) {
         for (int c = 0; c < P.kchunks; ++c, ++g) {
           const uint32_t stage = g & 1u, round = g >> 1;
-          if (!mbar_wait(&empty_w[stage], (round & 1u) ^ 1u, err, 51)) goto done_w;
+          if (!mbar_wait(&empty_a[stage], (round & 1u) ^ 1u, err, 51)) goto done_w;
           uint8_t* sb = w_region + stage * P.stage_bytes;
           const uint8_t* src = P.wimg + (size_t)c * 2 * plane;
           mbar_arrive_expect_tx(&full_w[stage], 2 * plane);
@@ -864,8 +861,7 @@ __global__ void __launch_bounds__(kZtThreads, 1) k_zono_persist(const __grid_con
             mma_tf32(acc, dah, dwl, idesc, 1);
             mma_tf32(acc, dah, dwh, idesc, 1);
           }
-          mma_commit(&empty_a[stage]);
-          mma_commit(&empty_w[stage]);
+          mma_commit(&empty_a[stage]);   // releases the A stage and the W stage
         }
         mma_commit(&acc_full[buf]);
       }
@@ -999,7 +995,7 @@ cf_status zono_tc_launch(const ZonoTcParams& P, cudaStream_t st) {
   Q.a_vec = (P.K % 4 == 0 && P.a_bs % 4 == 0 && a16(P.A)) ? 1 : 0;
   Q.lam_vec = (P.lam && P.K % 4 == 0 && a16(P.lam)) ? 1 : 0;
   Q.o_vec = (P.N % 4 == 0 && P.o_bs % 4 == 0 && a16(P.out)) ? 1 : 0;
-  size_t smem = 1024 + (size_t)4 * kAImg + (size_t)2 * Q.stage_bytes + 13 * 8 + 16;
+  size_t smem = 1024 + (size_t)4 * kAImg + (size_t)2 * Q.stage_bytes + 11 * 8 + 16;
   if (smem < 116 * 1024) smem = 116 * 1024;  // one CTA per SM: it holds all 512 TMEM columns
   CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "zono_tc: %zu bytes of shared memory", smem);
   static int sms = 0;
