@@ -269,7 +269,7 @@ struct ChainSmem {
 // vectors come from the shared-memory step buffers; kBox: the input box from shared memory.
 template <bool kStaged, bool kBox, bool kZono>
 __device__ __forceinline__ void chain_transform(const ChainParams& P, const ChainSmem& M, uint32_t tbase,
-                                                int64_t p0) {
+                                                int64_t p0, int64_t tile) {
   const int warp = threadIdx.x >> 5;
   int* err = P.err;
   const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
@@ -277,7 +277,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   int64_t sb_ = 0, b = 0, i = 0;
   int slot = 0;
   if constexpr (kZono) {
-    const int64_t row = (int64_t)blockIdx.x * 128 + r;
+    const int64_t row = tile * 128 + r;
     valid = row < P.rows;
     if (valid) {
       sb_ = row / (P.B * P.R);
@@ -288,7 +288,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
     }
   } else {
     // pair q of the tile: lane r & 63, lower bound in lanes 0-63, upper in 64-127
-    const int64_t q = (int64_t)blockIdx.x * 64 + (r & 63);
+    const int64_t q = tile * 64 + (r & 63);
     valid = q < P.B * P.R;
     sb_ = r >> 6;
     if (valid) {
@@ -299,9 +299,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   }
   const bool lower = sb_ == 0;
   // zonotope mode: does the CTA's row range reach into a second region
-  const bool two_slots = kZono && ((P.rows - 1 < (int64_t)blockIdx.x * 128 + 127 ? P.rows - 1
-                                                                                   : (int64_t)blockIdx.x * 128 + 127) /
-                                       P.R) != p0;
+  const bool two_slots = kZono && ((P.rows - 1 < tile * 128 + 127 ? P.rows - 1 : tile * 128 + 127) / P.R) != p0;
   float cacc = (valid && P.c0 && half == 0) ? P.c0[i] : 0.0f;
   float conc = 0.0f;
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -443,7 +441,7 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
             float x[16];
             tmem_ld16(dst + (uint32_t)(q * 16), x);
             tmem_ld_wait();
-            zono_drain(P.zout, P.zo_bs, P.zo_vec, P.zpos, P.zneg, blockIdx.x, S.N, n0, x, valid, b, i, slot,
+            zono_drain(P.zout, P.zo_bs, P.zo_vec, P.zpos, P.zneg, tile, S.N, n0, x, valid, b, i, slot,
                        two_slots);
             continue;
           }
@@ -487,8 +485,11 @@ __device__ __forceinline__ void chain_transform(const ChainParams& P, const Chai
   }
 }
 
-template <bool kZono>
-__global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ ChainParams P) {
+// One CTA of k_chain on parameter set kWhich of the launch (a compile-time choice, so that
+// every parameter is read at a fixed offset of the parameter space), tile `tile` of its rows.
+template <bool kZono, int kWhich>
+__device__ __forceinline__ void chain_cta(const ChainPair& PP, int64_t tile) {
+  const ChainParams& P = PP.p[kWhich];
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   // shared memory: kAStages A-operand stages (hi, lo planes), kWStages weight stages (hi, lo
@@ -519,12 +520,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   int64_t p0;
   int n_pairs;
   if (kZono) {
-    const int64_t row_first = (int64_t)blockIdx.x * 128;
+    const int64_t row_first = tile * 128;
     const int64_t row_last = (row_first + 127 < P.rows ? row_first + 127 : P.rows - 1);
     p0 = row_first / P.R;
     n_pairs = (int)(row_last / P.R - p0 + 1);
   } else {
-    const int64_t q_first = (int64_t)blockIdx.x * 64, q_all = P.B * P.R;
+    const int64_t q_first = tile * 64, q_all = P.B * P.R;
     const int64_t q_last = (q_first + 63 < q_all ? q_first + 63 : q_all - 1);
     p0 = q_first / P.R;
     n_pairs = (int)(q_last / P.R - p0 + 1);
@@ -674,16 +675,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
                       coef_full, coef_empty, box_full, acc_full, red};
     if constexpr (kZono) {
       if (staged)
-        chain_transform<true, false, true>(P, M, tbase, p0);
+        chain_transform<true, false, true>(P, M, tbase, p0, tile);
       else
-        chain_transform<false, false, true>(P, M, tbase, p0);
+        chain_transform<false, false, true>(P, M, tbase, p0, tile);
     } else {
       if (box_staged)
-        chain_transform<true, true, false>(P, M, tbase, p0);
+        chain_transform<true, true, false>(P, M, tbase, p0, tile);
       else if (staged)
-        chain_transform<true, false, false>(P, M, tbase, p0);
+        chain_transform<true, false, false>(P, M, tbase, p0, tile);
       else
-        chain_transform<false, false, false>(P, M, tbase, p0);
+        chain_transform<false, false, false>(P, M, tbase, p0, tile);
     }
   }
 
@@ -693,7 +694,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   if (warp == kProducerWarp) tmem_dealloc(tbase, 512);
 }
 
-cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
+// CTAs [0, split) run parameter set 0, the rest set 1 (two independent layers in one launch;
+// the zonotope mode uses set 0 only)
+template <bool kZono>
+__global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ ChainPair PP) {
+  if constexpr (kZono) {
+    chain_cta<true, 0>(PP, (int64_t)blockIdx.x);
+  } else {
+    if ((int64_t)blockIdx.x < PP.split) chain_cta<false, 0>(PP, (int64_t)blockIdx.x);
+    else chain_cta<false, 1>(PP, (int64_t)blockIdx.x - PP.split);
+  }
+}
+
+// Checks P and fills the launch fields of its copy Q; smem: the dynamic shared memory its
+// CTAs need, tiles: its CTA count.
+static cf_status chain_prepare(const ChainParams& P, ChainParams& Q, size_t& smem, int64_t& tiles) {
   CF_REQUIRE(P.S >= 1 && P.S <= kChainMaxSteps, CF_ERR_UNSUPPORTED, "chain: %d steps", P.S);
   int tn_max = 0;
   for (int s = 0; s < P.S; ++s) {
@@ -705,7 +720,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
     if (S.tile_n > tn_max) tn_max = S.tile_n;
   }
   CF_REQUIRE(P.st[P.S - 1].N == P.n0, CF_ERR_SHAPE, "chain: last step does not reach the input");
-  ChainParams Q = P;
+  Q = P;
   if (Q.ld_box == 0) Q.ld_box = Q.n0;
   // bounded-wait limit: kMaxPolls, or CF_WAIT_POLLS (>= 256) for the failure-path test;
   // CF_FAULT=chain_withhold_acc withholds one arrival so that a wait runs out
@@ -737,7 +752,7 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
   const bool box_ok = !P.zono && coef_ok && P.n0 % 4 == 0 && Q.ld_box % 4 == 0 && a16(P.l0) && a16(P.u0) &&
                       fixed + box_bytes <= 227 * 1024;
   Q.box_smem_bytes = box_ok ? (uint32_t)box_bytes : 0u;
-  size_t smem = fixed + Q.box_smem_bytes;
+  smem = fixed + Q.box_smem_bytes;
   // at least 116 KB so that one CTA (which holds all 512 TMEM columns) runs per SM
   if (smem < 116 * 1024) smem = 116 * 1024;
   if (P.zono) {
@@ -745,17 +760,44 @@ cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
                "chain: zonotope mode needs one step, >= 128 rows per region and its outputs");
     Q.zo_vec = (P.st[0].N % 4 == 0 && a16(P.zout) && (P.zo_bs % 4) == 0) ? 1 : 0;
   }
-  auto kern = P.zono ? k_chain<true> : k_chain<false>;
+  CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "chain: %zu bytes of shared memory", smem);
+  tiles = P.zono ? ceil_div(P.rows, 128) : ceil_div(P.B * P.R, 64);
+  CF_REQUIRE(tiles <= 0x3fffffff, CF_ERR_SHAPE, "chain: too many rows");
+  return CF_OK;
+}
+
+static cf_status chain_run(const ChainPair& PP, bool zono, int64_t grid, size_t smem, cudaStream_t st) {
+  auto kern = zono ? k_chain<true> : k_chain<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) {
     set_error("chain: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     return CF_ERR_CUDA;
   }
-  CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "chain: %zu bytes of shared memory", smem);
-  const int64_t tiles = P.zono ? ceil_div(P.rows, 128) : ceil_div(P.B * P.R, 64);
-  CF_REQUIRE(tiles <= 0x7fffffff, CF_ERR_SHAPE, "chain: too many rows");
-  kern<<<(unsigned)tiles, kThreads, smem, st>>>(Q);
-  return check_launch(P.zono ? "k_chain (zonotope)" : "k_chain");
+  if (grid == 0) return CF_OK;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(PP);
+  return check_launch(zono ? "k_chain (zonotope)" : "k_chain");
+}
+
+cf_status chain_launch(const ChainParams& P, cudaStream_t st) {
+  ChainPair PP;
+  memset(&PP, 0, sizeof(PP));
+  size_t smem = 0;
+  int64_t tiles = 0;
+  CF_TRY(chain_prepare(P, PP.p[0], smem, tiles));
+  PP.split = tiles;
+  return chain_run(PP, P.zono != 0, tiles, smem, st);
+}
+
+cf_status chain_launch_pair(const ChainParams& P0, const ChainParams& P1, cudaStream_t st) {
+  CF_REQUIRE(!P0.zono && !P1.zono, CF_ERR_UNSUPPORTED, "chain: paired launches are bounding-mode only");
+  ChainPair PP;
+  memset(&PP, 0, sizeof(PP));
+  size_t smem0 = 0, smem1 = 0;
+  int64_t tiles0 = 0, tiles1 = 0;
+  CF_TRY(chain_prepare(P0, PP.p[0], smem0, tiles0));
+  CF_TRY(chain_prepare(P1, PP.p[1], smem1, tiles1));
+  PP.split = tiles0;
+  return chain_run(PP, false, tiles0 + tiles1, smem0 > smem1 ? smem0 : smem1, st);
 }
 
 // ------------------------------------------------------------------ persistent zonotope GEMM

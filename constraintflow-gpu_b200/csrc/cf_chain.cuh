@@ -99,5 +99,12 @@ cf_status chain_prep_weights(const float* W, int K, int N, uint8_t* img, cudaStr
 cf_status chain_prep_weights_batch(const float* const* W, const int* K, const int* N, uint8_t* const* img, int n,
                                    cudaStream_t st);
 cf_status chain_launch(const ChainParams& P, cudaStream_t st);
+// Two independent bounding-mode launches as one: CTAs [0, split) run p[0], the rest p[1]
+// (e.g. the output layer and the property rows, neither of which needs the other).
+struct ChainPair {
+  ChainParams p[2];
+  int64_t split;
+};
+cf_status chain_launch_pair(const ChainParams& P0, const ChainParams& P1, cudaStream_t st);
 
 }  // namespace cf

@@ -352,7 +352,10 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
                                     const std::vector<float*>& ra, const std::vector<float*>& rl,
                                     const std::vector<float*>& rm, cudaStream_t st, size_t j_first = 0,
                                     int64_t ld_box = 0, const ReluOut* relu = nullptr, double* lb64 = nullptr,
-                                    double* ub64 = nullptr) {
+                                    double* ub64 = nullptr, ChainParams* defer_to = nullptr,
+                                    const ChainParams* pair_with = nullptr) {
+  // defer_to: fill the parameters only, to be launched later beside an independent layer
+  // (pair_with: launch this layer and that one as one grid)
   ChainParams P;
   memset(&P, 0, sizeof(P));
   if (relu) P.relu = *relu;
@@ -393,15 +396,25 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   P.a0_vec = (a_bs % 4 == 0) && (a_rs % 4 == 0) && al16(A0);
   P.box_vec = (P.n0 % 4 == 0) && (P.ld_box % 4 == 0) && al16(l0) && al16(u0);
-  const double rows = 2.0 * Bc * R;
-  double flops = 0.0, bytes = 4.0 * rows;
-  for (int s = 0; s < P.S; ++s) {
-    flops += 2.0 * rows * P.st[s].K * P.st[s].N;
-    bytes += (double)P.st[s].n_tiles * chain_wimg_bytes(P.st[s].K, P.st[s].N) + (P.st[s].alpha ? 12.0 * Bc * P.st[s].K : 0);
+  if (defer_to) {
+    *defer_to = P;
+    return CF_OK;
   }
-  bytes += 8.0 * Bc * P.n0;
+  // algorithmic flops and bytes of a launch
+  auto cost = [](const ChainParams& Q, double& flops, double& bytes) {
+    const double rows = 2.0 * Q.B * Q.R;
+    bytes += 4.0 * rows + 8.0 * Q.B * Q.n0;
+    for (int s = 0; s < Q.S; ++s) {
+      flops += 2.0 * rows * Q.st[s].K * Q.st[s].N;
+      bytes += (double)Q.st[s].n_tiles * chain_wimg_bytes(Q.st[s].K, Q.st[s].N) +
+               (Q.st[s].alpha ? 12.0 * Q.B * Q.st[s].K : 0);
+    }
+  };
+  double flops = 0.0, bytes = 0.0;
+  cost(P, flops, bytes);
+  if (pair_with) cost(*pair_with, flops, bytes);
   prof_step_begin(st);
-  cf_status s = chain_launch(P, st);
+  cf_status s = pair_with ? chain_launch_pair(*pair_with, P, st) : chain_launch(P, st);
   prof_step_end(st, flops, bytes);
   return s;
 }
@@ -593,6 +606,18 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     return win_concretize(rg, gs.back(), X, c, l0, u0, st_l + col, st_u + col, N, st);
   };
 
+  // The last affine layer (no ReLU above it) and the property rows need nothing from each
+  // other -- the property substitutes through that layer's weights, not its bounds -- so
+  // when both go through the chain they are launched as one grid: each alone fills only
+  // 2*B*R/128 CTAs (40 and 36 for 256 regions of a 10-output net), a quarter of the SMs.
+  const size_t last = p.affine.size() - 1;
+  const auto in_call = [&](int li) { return li >= li_begin && li < li_end; };
+  const bool pair_last = p.affine.size() >= 2 && !p.has_conv && net->stop_depth == 0 && !is_interval_layers(net) &&
+                         net->relaxation != CF_RELAX_CROWN && in_call(p.affine[last]) &&
+                         p.relu_after[last] < 0 && in_call(net->n_layers) &&
+                         chain_applicable(net, p, last) && chain_applicable(net, p, p.affine.size());
+  ChainParams last_params;
+
   for (size_t a = 0; a < p.affine.size(); ++a) {
     const cf_layer& L = net->layers[p.affine[a]];
     int64_t col = p.col[p.affine[a]];
@@ -629,7 +654,8 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
         CF_TRY(bound_window(a, col));
       } else if (chain_applicable(net, p, a)) {
         CF_TRY(launch_chain_layer(net, p, w, ws, Bc, a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, l0, u0, st_l + col,
-                                  st_u + col, ra, rl, rm, st, 0, 0, fuse));
+                                  st_u + col, ra, rl, rm, st, 0, 0, fuse, nullptr, nullptr,
+                                  pair_last && a == last ? &last_params : nullptr));
         relaxed = fuse != nullptr;
       } else {
         CF_TRY(bound_layer(a, L.n_out, L.W_dev, 0, L.n_in, L.b_dev, col, fuse));
@@ -664,7 +690,8 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
     // the drain also writes the float64 bounds
     const int64_t R = net->n_spec, K = p.n_out_last;
     CF_TRY(launch_chain_layer(net, p, w, ws, Bc, p.affine.size(), R, specW, R * K, K, nullptr, l0, u0,
-                              st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st, 0, 0, nullptr, lb, ub));
+                              st_l + p.spec_col, st_u + p.spec_col, ra, rl, rm, st, 0, 0, nullptr, lb, ub, nullptr,
+                              pair_last ? &last_params : nullptr));
   } else {
     const int64_t R = net->n_spec, K = p.n_out_last;
     // treat it as affine index affine.size(): substitutes every affine layer below it
