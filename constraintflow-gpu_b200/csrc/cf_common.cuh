@@ -34,6 +34,11 @@ void prof_step_end(cudaStream_t st, double flops, double bytes);
 // the same around a launch of a memory-bound kernel (relaxation, concretisation, conversions)
 void prof_mem_begin(cudaStream_t st);
 void prof_mem_end(cudaStream_t st, double bytes);
+// One record spanning work that runs on several streams at once (per-launch records there
+// would count overlapping time twice): between span_begin and span_end on the joining
+// stream, step and memory records only add their flops and bytes to the span.
+void prof_span_begin(cudaStream_t st);
+void prof_span_end(cudaStream_t st);
 
 inline cf_status check_launch(const char* what) {
   prof_count_launch();

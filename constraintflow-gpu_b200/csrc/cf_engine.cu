@@ -10,6 +10,7 @@
 // while-loop and Flow.flow (constraintflow/lib/flow_sparse.py:27-228).
 #include <stdarg.h>
 
+#include <mutex>
 #include <vector>
 
 #include "cf_chain.cuh"
@@ -427,23 +428,26 @@ static cf_status launch_chain_layer(const cf_network* net, const Plan& p, const 
 static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, const float* l0, const float* u0,
                             const float* specW, float* st_l, float* st_u, double* lb, double* ub, char* ws,
                             const WsLayout& w, cudaStream_t st, int li_begin, int li_end,
-                            const float* dec_l = nullptr, const float* dec_u = nullptr) {
+                            const float* dec_l = nullptr, const float* dec_u = nullptr, int64_t relu_stride = 0,
+                            int64_t relu_off = 0) {
   (void)w.wimg;
   const int64_t N = p.N, n0 = net->n_input;
   float* Abuf[2] = {reinterpret_cast<float*>(ws + w.A[0]), reinterpret_cast<float*>(ws + w.A[1])};
   float* Cbuf[2] = {reinterpret_cast<float*>(ws + w.C[0]), reinterpret_cast<float*>(ws + w.C[1])};
   float* relu_base = reinterpret_cast<float*>(ws + w.relu);
   char* scratch = ws + w.state + align256((size_t)2 * Bc * N * sizeof(float));
-  // relaxation arrays per affine index
+  // relaxation arrays per affine index: [relu_stride, n] each (relu_stride regions, default
+  // Bc), this call's regions from row relu_off
   std::vector<float*> ra(p.affine.size(), nullptr), rl(p.affine.size(), nullptr), rm(p.affine.size(), nullptr);
   {
+    const int64_t rs = relu_stride > 0 ? relu_stride : Bc;
     float* q = relu_base;
     for (size_t a = 0; a < p.affine.size(); ++a) {
       if (p.relu_after[a] < 0) continue;
       int64_t n = net->layers[p.relu_after[a]].n_out;
-      ra[a] = q; q += Bc * n;
-      rl[a] = q; q += Bc * n;
-      rm[a] = q; q += Bc * n;
+      ra[a] = q + relu_off * n; q += rs * n;
+      rl[a] = q + relu_off * n; q += rs * n;
+      rm[a] = q + relu_off * n; q += rs * n;
     }
   }
   if (li_begin == 0) {
@@ -739,6 +743,45 @@ extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chu
   return ws_layout(net, p, chunk).total;
 }
 
+// A second stream per device for the region lanes of a chained pass (created once, never
+// destroyed: it lives as long as the library).
+static cudaStream_t lane_stream() {
+  static std::mutex mu;
+  static cudaStream_t streams[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
+    streams[dev] = nullptr;
+  return streams[dev];
+}
+
+// Region lanes: when every layer of a whole DeepPoly pass after the first is bounded by the
+// chain kernel and one hidden layer's launch over the nb regions of a chunk spans at least
+// two waves of CTAs, the chunk's regions are split into two halves that run the pass on two
+// streams.  Their launches need nothing from each other, so the CTAs of one half fill the
+// SMs while the last, partial wave of the other half's launch drains (a launch of 800 tiles
+// on 148 SMs leaves 60% of them idle for its last wave).  CF_CHAIN_LANES=0 turns this off.
+static bool use_lanes(const cf_network* net, const Plan& p, int64_t nb) {
+  if (const char* e = getenv("CF_CHAIN_LANES"))
+    if (strcmp(e, "0") == 0) return false;
+  if (!use_chain() || p.has_conv || net->stop_depth != 0 || is_interval_layers(net) || p.affine.size() < 2)
+    return false;
+  if (net->relaxation != CF_RELAX_DEEPPOLY && net->relaxation != CF_RELAX_DEEPPOLY_STRICT) return false;
+  for (size_t a = 1; a <= p.affine.size(); ++a)
+    if (!chain_applicable(net, p, a)) return false;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  int64_t widest = 0;
+  for (size_t a = 0; a + 1 < p.affine.size(); ++a)
+    widest = net->layers[p.affine[a]].n_out > widest ? net->layers[p.affine[a]].n_out : widest;
+  return ceil_div(nb * widest, 64) >= 2 * (int64_t)sms;
+}
+
 static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
                               const float* specW, float* state_l, float* state_u, double* lb, double* ub,
                               void* workspace, size_t ws_bytes, void* stream, const float* dec_l,
@@ -790,9 +833,41 @@ static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0,
     int64_t nb = (B - b0 < Bc) ? (B - b0) : Bc;
     float* sl = state_l ? state_l + b0 * N : reinterpret_cast<float*>(ws + w.state);
     float* su = state_u ? state_u + b0 * N : reinterpret_cast<float*>(ws + w.state) + Bc * N;
-    CF_TRY(run_layers(net, p, nb, l0 + b0 * n0, u0 + b0 * n0, specW + b0 * ns * p.n_out_last, sl, su,
-                      lb + b0 * ns, ub + b0 * ns, ws, w, st, 0, net->n_layers + 1,
-                      dec_l ? dec_l + b0 * N : nullptr, dec_u ? dec_u + b0 * N : nullptr));
+    // lane x: regions [b0 + off, b0 + off + n) of the chunk, rows off.. of the workspace arrays
+    auto lane = [&](int64_t off, int64_t n, cudaStream_t s) {
+      const int64_t b = b0 + off;
+      return run_layers(net, p, n, l0 + b * n0, u0 + b * n0, specW + b * ns * p.n_out_last, sl + off * N,
+                        su + off * N, lb + b * ns, ub + b * ns, ws, w, s, 0, net->n_layers + 1,
+                        dec_l ? dec_l + b * N : nullptr, dec_u ? dec_u + b * N : nullptr, Bc, off);
+    };
+    cudaStream_t side = use_lanes(net, p, nb) ? lane_stream() : nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    if (side && (cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
+                 cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess)) {
+      if (fork) cudaEventDestroy(fork);
+      fork = nullptr;
+      side = nullptr;
+      cudaGetLastError();
+    }
+    if (!side) {
+      CF_TRY(lane(0, nb, st));
+      continue;
+    }
+    // fork: the side lane starts after everything queued on st so far; join: st continues
+    // after both lanes, also when a lane failed to queue
+    const int64_t na = nb / 2;
+    prof_span_begin(st);
+    cudaEventRecord(fork, st);
+    cudaStreamWaitEvent(side, fork, 0);
+    cf_status s0 = lane(0, na, st);
+    cf_status s1 = s0 == CF_OK ? lane(na, nb - na, side) : CF_OK;
+    cudaEventRecord(join, side);
+    cudaStreamWaitEvent(st, join, 0);
+    prof_span_end(st);
+    cudaEventDestroy(fork);
+    cudaEventDestroy(join);
+    CF_TRY(s0);
+    CF_TRY(s1);
   }
   return CF_OK;
 }

@@ -51,6 +51,11 @@ struct ProfState {
   std::vector<cudaEvent_t> pool;
 };
 static thread_local ProfState g_prof;
+struct ProfSpan {
+  bool on = false;
+  double flops = 0, bytes = 0;
+};
+static thread_local ProfSpan g_span;
 
 static cudaEvent_t take_event() {
   if (!g_prof.pool.empty()) {
@@ -68,7 +73,7 @@ void prof_count_launch() {
 }
 bool prof_enabled() { return g_prof.on; }
 static void prof_begin(cudaStream_t st, bool mem) {
-  if (!g_prof.on) return;
+  if (!g_prof.on || g_span.on) return;
   ProfRec r;
   r.a = take_event();
   r.b = take_event();
@@ -82,10 +87,27 @@ void prof_mem_begin(cudaStream_t st) { prof_begin(st, true); }
 void prof_mem_end(cudaStream_t st, double bytes) { prof_step_end(st, 0.0, bytes); }
 void prof_step_end(cudaStream_t st, double flops, double bytes) {
   if (!g_prof.on || g_prof.open.empty()) return;
+  if (g_span.on) {
+    g_span.flops += flops;
+    g_span.bytes += bytes;
+    return;
+  }
   ProfRec& r = g_prof.open.back();
   r.flops = flops;
   r.bytes = bytes;
   cudaEventRecord(r.b, st);
+}
+
+void prof_span_begin(cudaStream_t st) {
+  if (!g_prof.on || g_span.on) return;
+  prof_begin(st, false);
+  g_span.on = true;
+  g_span.flops = g_span.bytes = 0;
+}
+void prof_span_end(cudaStream_t st) {
+  if (!g_span.on) return;
+  g_span.on = false;
+  prof_step_end(st, g_span.flops, g_span.bytes);
 }
 
 }  // namespace cf
