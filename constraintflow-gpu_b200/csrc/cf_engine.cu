@@ -743,33 +743,40 @@ extern "C" size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chu
   return ws_layout(net, p, chunk).total;
 }
 
-// A second stream per device for the region lanes of a chained pass (created once, never
-// destroyed: it lives as long as the library).
-static cudaStream_t lane_stream() {
+constexpr int kMaxLanes = 4;
+// Side stream i (< kMaxLanes - 1) per device for the region lanes of a chained pass (created
+// once, never destroyed: they live as long as the library).
+static cudaStream_t lane_stream(int i) {
   static std::mutex mu;
-  static cudaStream_t streams[64] = {};
+  static cudaStream_t streams[64][kMaxLanes - 1] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
-    streams[dev] = nullptr;
-  return streams[dev];
+  if (!streams[dev][i] && cudaStreamCreateWithFlags(&streams[dev][i], cudaStreamNonBlocking) != cudaSuccess)
+    streams[dev][i] = nullptr;
+  return streams[dev][i];
 }
 
 // Region lanes: when every layer of a whole DeepPoly pass after the first is bounded by the
 // chain kernel and one hidden layer's launch over the nb regions of a chunk spans at least
-// two waves of CTAs, the chunk's regions are split into two halves that run the pass on two
-// streams.  Their launches need nothing from each other, so the CTAs of one half fill the
-// SMs while the last, partial wave of the other half's launch drains (a launch of 800 tiles
-// on 148 SMs leaves 60% of them idle for its last wave).  CF_CHAIN_LANES=0 turns this off.
-static bool use_lanes(const cf_network* net, const Plan& p, int64_t nb) {
-  if (const char* e = getenv("CF_CHAIN_LANES"))
-    if (strcmp(e, "0") == 0) return false;
+// two waves of CTAs, the chunk's regions are split into lanes (consecutive region ranges)
+// that run the pass on separate streams.  Their launches need nothing from each other, so
+// the CTAs of one lane fill the SMs while the last, partial wave of another lane's launch
+// drains (a launch of 800 tiles on 148 SMs leaves 60% of them idle for its last wave).
+// Returns the number of lanes: 1 (no split), else CF_CHAIN_LANES (1..kMaxLanes) or 2.
+static int use_lanes(const cf_network* net, const Plan& p, int64_t nb) {
+  int want = 2;
+  if (const char* e = getenv("CF_CHAIN_LANES")) {
+    want = atoi(e);
+    if (want < 1) want = 1;
+    if (want > kMaxLanes) want = kMaxLanes;
+  }
+  if (want == 1) return 1;
   if (!use_chain() || p.has_conv || net->stop_depth != 0 || is_interval_layers(net) || p.affine.size() < 2)
-    return false;
-  if (net->relaxation != CF_RELAX_DEEPPOLY && net->relaxation != CF_RELAX_DEEPPOLY_STRICT) return false;
+    return 1;
+  if (net->relaxation != CF_RELAX_DEEPPOLY && net->relaxation != CF_RELAX_DEEPPOLY_STRICT) return 1;
   for (size_t a = 1; a <= p.affine.size(); ++a)
-    if (!chain_applicable(net, p, a)) return false;
+    if (!chain_applicable(net, p, a)) return 1;
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;
@@ -779,7 +786,8 @@ static bool use_lanes(const cf_network* net, const Plan& p, int64_t nb) {
   int64_t widest = 0;
   for (size_t a = 0; a + 1 < p.affine.size(); ++a)
     widest = net->layers[p.affine[a]].n_out > widest ? net->layers[p.affine[a]].n_out : widest;
-  return ceil_div(nb * widest, 64) >= 2 * (int64_t)sms;
+  if (ceil_div(nb * widest, 64) < 2 * (int64_t)sms || nb < want) return 1;
+  return want;
 }
 
 static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0, const float* u0,
@@ -840,34 +848,39 @@ static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0,
                         su + off * N, lb + b * ns, ub + b * ns, ws, w, s, 0, net->n_layers + 1,
                         dec_l ? dec_l + b * N : nullptr, dec_u ? dec_u + b * N : nullptr, Bc, off);
     };
-    cudaStream_t side = use_lanes(net, p, nb) ? lane_stream() : nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-    if (side && (cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
-                 cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess)) {
+    int nl = use_lanes(net, p, nb);
+    cudaStream_t side[kMaxLanes - 1] = {};
+    cudaEvent_t fork = nullptr, join[kMaxLanes - 1] = {};
+    bool ok = nl > 1 && cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; ok && i + 1 < nl; ++i)
+      ok = (side[i] = lane_stream(i)) != nullptr &&
+           cudaEventCreateWithFlags(&join[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
       if (fork) cudaEventDestroy(fork);
-      fork = nullptr;
-      side = nullptr;
+      for (cudaEvent_t e : join)
+        if (e) cudaEventDestroy(e);
       cudaGetLastError();
-    }
-    if (!side) {
       CF_TRY(lane(0, nb, st));
       continue;
     }
-    // fork: the side lane starts after everything queued on st so far; join: st continues
-    // after both lanes, also when a lane failed to queue
-    const int64_t na = nb / 2;
+    // fork: the side lanes start after everything queued on st so far; join: st continues
+    // after every lane, also when a lane failed to queue
     prof_span_begin(st);
     cudaEventRecord(fork, st);
-    cudaStreamWaitEvent(side, fork, 0);
-    cf_status s0 = lane(0, na, st);
-    cf_status s1 = s0 == CF_OK ? lane(na, nb - na, side) : CF_OK;
-    cudaEventRecord(join, side);
-    cudaStreamWaitEvent(st, join, 0);
+    for (int i = 0; i + 1 < nl; ++i) cudaStreamWaitEvent(side[i], fork, 0);
+    cf_status s = CF_OK;
+    for (int i = 0; i < nl && s == CF_OK; ++i) {
+      const int64_t from = nb * i / nl, to = nb * (i + 1) / nl;
+      s = lane(from, to - from, i == 0 ? st : side[i - 1]);
+    }
+    for (int i = 0; i + 1 < nl; ++i) {
+      cudaEventRecord(join[i], side[i]);
+      cudaStreamWaitEvent(st, join[i], 0);
+    }
     prof_span_end(st);
     cudaEventDestroy(fork);
-    cudaEventDestroy(join);
-    CF_TRY(s0);
-    CF_TRY(s1);
+    for (int i = 0; i + 1 < nl; ++i) cudaEventDestroy(join[i]);
+    CF_TRY(s);
   }
   return CF_OK;
 }
