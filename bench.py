@@ -41,7 +41,7 @@ from cfgpu import nets  # noqa: E402
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from an ncu capture of
 # the default command (profiles/k_chain_mlp784-200x9_b256.txt); per workload id.
-NCU_TRAFFIC = {(2, "deeppoly"): 10.78e6}
+NCU_TRAFFIC = {(2, "deeppoly"): 7.52e6}
 
 
 def parse():
@@ -426,14 +426,18 @@ def _roofline(m, wl, certifier, steps, dev):
     roof = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": (achieved / peak) if achieved else None,
             "traffic": NCU_TRAFFIC.get(key),
-            "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer, 800 "
-                               "CTAs) from one ncu --set full capture of this command") if key in NCU_TRAFFIC else None,
+            "traffic_source": ("dram read+write of one k_chain launch (a 200-wide hidden layer bounded "
+                               "through 8 substitutions for one lane of 128 regions, 400 CTAs) from one ncu "
+                               "--set full capture of this command") if key in NCU_TRAFFIC else None,
             "kernel": {"zono": "k_zono_persist" if zono_tc else "k_zono_gemm", "ibp": None,
                        "polyzono": "k_chain (backsubstitution) + k_zono_persist"}.get(
                            certifier, ("k_win_convT_tc (tcgen05 3xTF32) + k_win_first (CUDA cores, first layer), "
                                        "the transposed convolutions of the receptive-field windows" if conv_tc
                                        else "transposed convolution of the receptive-field windows" if conv else
-                                       "backsubstitution step") if chain else "k_bmm (general traversal)"),
+                                       "k_chain (tcgen05 3xTF32 backsubstitution); when a pass runs its regions as "
+                                       "two lanes on two streams, the step time is the device-time span of the "
+                                       "lanes (first to last launch), not a sum of overlapping launches")
+                                      if chain else "k_bmm (general traversal)"),
             "peak_source": peak_src,
             "step_share_of_pass": prof["step_ms"] / ms if ms > 0 else None,
             "step_launches": prof["step_launches"]}
