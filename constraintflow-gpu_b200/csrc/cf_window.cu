@@ -505,13 +505,21 @@ __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGe
                                                    float* __restrict__ out_l, float* __restrict__ out_u,
                                                    int64_t ld_out) {
   extern __shared__ float sm[];
-  const int wn = cout * NCI * kh * KW;
-  float* wsm = sm;                                  // [cout][NCI][kh][KW]
+  // weights regrouped as [cout][kh][kWG]: the NCI x KW taps of one (channel, kernel row)
+  // are contiguous and padded to whole 16-byte pieces (vector loads, zero padding)
+  constexpr int kWG = (NCI * KW + 3) / 4 * 4;
+  const int wn = cout * kh * kWG;
+  float* wsm = sm;
   const int plane = gi.Ph * gi.Pw;
   const int stage = rb * cc * plane;
-  float* xs = sm + ((wn + 3) & ~3);                 // two stages of [rb][cc][Ph][Pw]
+  float* xs = sm + wn;                              // two stages of [rb][cc][Ph][Pw]
   float* part = xs + 2 * (size_t)stage;             // [256] partial bounds
-  for (int e = threadIdx.x; e < wn; e += blockDim.x) wsm[e] = W[e];
+  for (int e = threadIdx.x; e < wn; e += blockDim.x) {
+    const int g = e / kWG, j = e - (e / kWG) * kWG;   // g = co * kh + ky
+    const int co = g / kh, ky = g - (g / kh) * kh;
+    const int ci = j / KW, kx = j - (j / KW) * KW;
+    wsm[e] = j < NCI * KW ? W[((co * NCI + ci) * kh + ky) * KW + kx] : 0.0f;
+  }
   const int XG = (go.Pw + 3) / 4, TPR = go.Ph * XG;
   const int64_t per_in = (int64_t)gi.C * plane;
   const int64_t rows = 2 * rg.B * rg.R;
@@ -561,10 +569,19 @@ __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGe
       const float* xb = xs + (size_t)buf * stage;
       for (int cix = 0; cix < nc; ++cix) {
         const float* xp = xb + ((size_t)slot * cc + cix) * plane;
-        const float* wc = wsm + (size_t)(co0 + cix) * NCI * kh * KW;
         for (int ky = 0; ky < kh; ++ky) {
           const int u = up + Dy - ky;
           if (u < 0 || u >= gi.Ph) continue;
+          float wk[kWG];
+          const float4* wv = reinterpret_cast<const float4*>(wsm + ((size_t)(co0 + cix) * kh + ky) * kWG);
+#pragma unroll
+          for (int q = 0; q < kWG / 4; ++q) {
+            const float4 t = wv[q];
+            wk[4 * q] = t.x;
+            wk[4 * q + 1] = t.y;
+            wk[4 * q + 2] = t.z;
+            wk[4 * q + 3] = t.w;
+          }
           const float* xr = xp + u * gi.Pw;
           float xv[4 + KW - 1];
 #pragma unroll
@@ -576,7 +593,7 @@ __global__ void __launch_bounds__(256) k_win_first(RowGeom rg, WinGeom gi, WinGe
           for (int kx = 0; kx < KW; ++kx) {
 #pragma unroll
             for (int ci = 0; ci < NCI; ++ci) {
-              const float w = wc[(ci * kh + ky) * KW + kx];
+              const float w = wk[ci * KW + kx];
 #pragma unroll
               for (int j = 0; j < 4; ++j) acc[j][ci] = fmaf(xv[j + (KW - 1) - kx], w, acc[j][ci]);
             }
@@ -662,8 +679,8 @@ cf_status win_convT_first(const RowGeom& rg, const WinGeom& gi, const WinGeom& g
   const int64_t rows = 2 * rg.B * rg.R;
   if (rows == 0) return CF_OK;
   const int Dy = gi.pi_h + cv.pad - go.pi_h, Dx = gi.pi_w + cv.pad - go.pi_w;
-  const int wn = cout * cv.cin * cv.kh * cv.kw;
-  const size_t smem = (size_t)(((wn + 3) & ~3) + 2 * rb * cc * gi.Ph * gi.Pw + 256) * sizeof(float);
+  const int wn = cout * cv.kh * ((cv.cin * cv.kw + 3) / 4 * 4);   // the regrouped weights (see k_win_first)
+  const size_t smem = (size_t)(wn + 2 * rb * cc * gi.Ph * gi.Pw + 256) * sizeof(float);
   const unsigned grid = grid_for(rows, rb, 148 * 16);
 #define CF_FIRST(NCI, KW)                                                                                          \
   do {                                                                                                             \
