@@ -149,7 +149,13 @@ size_t cf_deeppoly_workspace_bytes(const cf_network* net, int64_t chunk);
  *                    neuron order, input columns included (abs_elem.d['l'|'u'] dense view)
  *   lb_dev, ub_dev   [B, n_spec] float64: the property bounds Flow.flow returns
  *   workspace_dev / workspace_bytes: scratch, >= cf_deeppoly_workspace_bytes(net, chunk)
- *                    for some chunk >= 1 */
+ *                    for some chunk >= 1
+ * A DeepPoly pass whose layers all go through the chain kernel may run half of a chunk's
+ * regions on a second stream that the library owns (created once per device): it waits
+ * for the work queued on `stream` before the call and `stream` waits for it before any
+ * later work, so the call stays stream-ordered (and can be captured in a CUDA graph once
+ * the first such call on the device, which creates that stream, has run uncaptured).
+ * CF_CHAIN_LANES=1 keeps everything on `stream`. */
 cf_status cf_deeppoly_run(const cf_network* net, int64_t B,
                           const float* l0_dev, const float* u0_dev, const float* spec_W_dev,
                           float* state_l_dev, float* state_u_dev,
