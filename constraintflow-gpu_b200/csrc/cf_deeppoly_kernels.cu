@@ -187,6 +187,7 @@ __global__ void k_concretize(int64_t B, int64_t R, int64_t n0, const float* __re
 // one row x one region x 2 bounds each.  With `relu` (alpha != nullptr) the thread also
 // relaxes the ReLU above the layer from the two bounds it has just stored.
 constexpr int kCbT = 16, kCbK = 32, kCbM = kCbT / 16;
+static_assert(kCbT * kCbK % 256 == 0, "a 256-thread block loads the tiles in whole rounds");
 __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, int64_t n0, const float* __restrict__ A,
                                                           int64_t a_rs, const float* __restrict__ c,
                                                           const float* __restrict__ l0, const float* __restrict__ u0,
@@ -204,17 +205,32 @@ __global__ void __launch_bounds__(256) k_concretize_bcast(int64_t B, int64_t R, 
   for (int a = 0; a < kCbM; ++a)
 #pragma unroll
     for (int q = 0; q < kCbM; ++q) lo[a][q] = up[a][q] = 0.0f;
-  for (int64_t k0 = 0; k0 < n0; k0 += kCbK) {
-    for (int e = tid; e < kCbT * kCbK; e += 256) {
-      const int r = e / kCbK, kk = e - r * kCbK;
+  // the tiles' elements of the next K chunk are loaded into registers while the current
+  // chunk's FMAs run (each thread holds kCbE of them per operand)
+  constexpr int kCbE = kCbT * kCbK / 256;
+  float nw[kCbE], nl[kCbE], nu[kCbE];
+  auto fetch = [&](int64_t k0) {
+#pragma unroll
+    for (int j = 0; j < kCbE; ++j) {
+      const int e = tid + 256 * j, r = e / kCbK, kk = e - r * kCbK;
       const int64_t k = k0 + kk, i = i0 + r, b = b0 + r;
-      const float w = (i < R && k < n0) ? A[i * a_rs + k] : 0.0f;
-      Wp[kk][r] = fmaxf(w, 0.0f);
-      Wn[kk][r] = fminf(w, 0.0f);
-      Ls[kk][r] = (b < B && k < n0) ? l0[b * ld_box + k] : 0.0f;
-      Us[kk][r] = (b < B && k < n0) ? u0[b * ld_box + k] : 0.0f;
+      nw[j] = (i < R && k < n0) ? A[i * a_rs + k] : 0.0f;
+      nl[j] = (b < B && k < n0) ? l0[b * ld_box + k] : 0.0f;
+      nu[j] = (b < B && k < n0) ? u0[b * ld_box + k] : 0.0f;
+    }
+  };
+  fetch(0);
+  for (int64_t k0 = 0; k0 < n0; k0 += kCbK) {
+#pragma unroll
+    for (int j = 0; j < kCbE; ++j) {
+      const int e = tid + 256 * j, r = e / kCbK, kk = e - r * kCbK;
+      Wp[kk][r] = fmaxf(nw[j], 0.0f);
+      Wn[kk][r] = fminf(nw[j], 0.0f);
+      Ls[kk][r] = nl[j];
+      Us[kk][r] = nu[j];
     }
     __syncthreads();
+    if (k0 + kCbK < n0) fetch(k0 + kCbK);
 #pragma unroll 8
     for (int kk = 0; kk < kCbK; ++kk) {
       float wpa[kCbM], wna[kCbM], la[kCbM], ua[kCbM];
