@@ -231,7 +231,8 @@ __device__ __forceinline__ void zono_colsums(float* zpos, float* zneg, int64_t c
 }
 
 // Zonotope drain of 16 columns n0 .. n0+15 of this thread's row: store the row's values
-// (columns below N) and the warp's per-slot column sums.
+// (columns below N) and, unless zpos is null (a plain product), the warp's per-slot column
+// sums.
 __device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_vec, float* zpos, float* zneg,
                                            int64_t cta, int N, int n0, const float (&x)[16], bool valid,
                                            int64_t b, int64_t i, int slot, bool two_slots) {
@@ -247,7 +248,7 @@ __device__ __forceinline__ void zono_drain(float* zout, int64_t zo_bs, int zo_ve
         if (n0 + e < N) o[e] = x[e];
     }
   }
-  zono_colsums(zpos, zneg, cta, N, n0, x, valid, slot, two_slots);
+  if (zpos) zono_colsums(zpos, zneg, cta, N, n0, x, valid, slot, two_slots);
 }
 
 // Shared-memory pieces the transform warps use.
@@ -756,8 +757,8 @@ static cf_status chain_prepare(const ChainParams& P, ChainParams& Q, size_t& sme
   // at least 116 KB so that one CTA (which holds all 512 TMEM columns) runs per SM
   if (smem < 116 * 1024) smem = 116 * 1024;
   if (P.zono) {
-    CF_REQUIRE(P.S == 1 && P.R >= 128 && P.rows % P.R == 0 && P.zout && P.zpos && P.zneg, CF_ERR_UNSUPPORTED,
-               "chain: zonotope mode needs one step, >= 128 rows per region and its outputs");
+    CF_REQUIRE(P.S == 1 && P.R >= 128 && P.rows % P.R == 0 && P.zout && (P.zpos != nullptr) == (P.zneg != nullptr),
+               CF_ERR_UNSUPPORTED, "chain: zonotope mode needs one step, >= 128 rows per region and its outputs");
     Q.zo_vec = (P.st[0].N % 4 == 0 && a16(P.zout) && (P.zo_bs % 4) == 0) ? 1 : 0;
   }
   CF_REQUIRE(smem <= 227 * 1024, CF_ERR_UNSUPPORTED, "chain: %zu bytes of shared memory", smem);

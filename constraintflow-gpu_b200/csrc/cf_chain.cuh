@@ -60,6 +60,8 @@ struct ChainParams {
   // drain writes every row of the result to zout[b*zo_bs + i*N + n] and, per warp w = warp%4
   // and region slot (region - first region of the CTA), the column sums of the positive /
   // negative coefficients to zpos / zneg[((cta*4 + w)*2 + slot)*N + n].  No input box.
+  // With zpos = zneg = null and no relaxation (alpha null) it is a plain product
+  // zout = A0 rows x W, e.g. a linear substitution of whole-image coefficient windows.
   int32_t zono;
   int32_t zo_vec;                       // 16-byte stores allowed for zout rows
   float* zout;

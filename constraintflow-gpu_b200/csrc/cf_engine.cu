@@ -284,16 +284,29 @@ static bool needs_step_buffers(const cf_network* net, const Plan& p) {
   return false;
 }
 
+// Conv networks: the substitution of whole-image coefficient windows through linear layer a
+// runs on the tensor cores (the chain kernel's plain-product mode, 128 rows per tile of one
+// bounded layer's rows) when some layer above it, or the property, has >= 128 rows per region.
+static bool linear_window_tc(const cf_network* net, const Plan& p, size_t a) {
+  if (!use_chain() || net->layers[p.affine[a]].kind != CF_LAYER_LINEAR) return false;
+  for (size_t m = a + 1; m <= p.affine.size(); ++m) {
+    const int64_t R = m < p.affine.size() ? net->layers[p.affine[m]].n_out : net->n_spec;
+    if (R >= 128) return true;
+  }
+  return false;
+}
+
 static WsLayout ws_layout(const cf_network* net, const Plan& p, int64_t Bc) {
   WsLayout w;
   size_t off = 0;
   // device error word, then two CROWN branch flags per affine layer
   w.err = off; off += align256(64 + 8 * p.affine.size());
   w.wimg = off;
-  w.wimg_off.assign(p.affine.size(), 0);
-  if (use_chain() && !p.has_conv) {  // weight images for the tensor-core chain
+  w.wimg_off.assign(p.affine.size(), 0);   // 0: no image (the error word sits at offset 0)
+  if (use_chain()) {  // weight images for the tensor-core chain
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
+      if (p.has_conv && !linear_window_tc(net, p, a)) continue;
       w.wimg_off[a] = off;
       off += align256(chain_wimg_bytes(L.n_out, L.n_in));
     }
@@ -594,6 +607,34 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
                               reinterpret_cast<int*>(ws + w.err), st));
         else
           CF_TRY(win_convT(rg, g, h, cv, X, Lj.W_dev, Y, st));
+      } else if (w.wimg_off[j] != 0 && rg.R >= 128) {
+        // the rows times the layer's weights on the tensor cores: the chain kernel's plain
+        // product (one step, no relaxation, no column sums), bound x region as its regions
+        const int64_t K = Lj.n_out, Nn = Lj.n_in;
+        ChainParams P;
+        memset(&P, 0, sizeof(P));
+        P.S = 1;
+        ChainStep& S = P.st[0];
+        S.wimg = reinterpret_cast<const uint8_t*>(ws + w.wimg_off[j]);
+        S.bias = Lj.b_dev;
+        S.K = (int32_t)K;
+        S.N = (int32_t)Nn;
+        chain_tile(S.N, S.tile_n, S.n_tiles);
+        S.kchunks = (S.K + 31) / 32;
+        P.B = 2 * Bc;
+        P.R = rg.R;
+        P.rows = 2 * Bc * rg.R;
+        P.A0 = X;
+        P.a_bs = rg.R * K;
+        P.a_rs = K;
+        P.n0 = Nn;
+        P.ld_box = Nn;
+        P.err = reinterpret_cast<int*>(ws + w.err);
+        P.a0_vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+        P.zono = 1;
+        P.zout = Y;
+        P.zo_bs = rg.R * Nn;
+        CF_TRY(chain_launch(P, st));
       } else {
         const int64_t K = Lj.n_out, Nn = Lj.n_in;
         CF_TRY(launch_step_gemm_simt(Bc, rg.R, K, Nn, X, Bc * rg.R * K, rg.R * K, K, nullptr, nullptr, Lj.W_dev, Y,
@@ -823,18 +864,20 @@ static cf_status deeppoly_run(const cf_network* net, int64_t B, const float* l0,
     set_error("deeppoly_run: cudaMemsetAsync failed");
     return CF_ERR_CUDA;
   }
-  if (use_chain() && !p.has_conv) {
+  if (use_chain()) {
     std::vector<const float*> Wl;
     std::vector<int> Kl, Nl;
     std::vector<uint8_t*> img;
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
+      if (w.wimg_off[a] == 0) continue;
       Wl.push_back(L.W_dev);
       Kl.push_back(L.n_out);
       Nl.push_back(L.n_in);
       img.push_back(reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]));
     }
-    CF_TRY(chain_prep_weights_batch(Wl.data(), Kl.data(), Nl.data(), img.data(), (int)Wl.size(), st));
+    if (!Wl.empty())
+      CF_TRY(chain_prep_weights_batch(Wl.data(), Kl.data(), Nl.data(), img.data(), (int)Wl.size(), st));
   }
   const int64_t N = p.N, n0 = net->n_input, ns = net->n_spec;
   for (int64_t b0 = 0; b0 < B; b0 += Bc) {
