@@ -562,6 +562,10 @@ static cf_status run_layers(const cf_network* net, const Plan& p, int64_t Bc, co
   float* Xbuf[2] = {reinterpret_cast<float*>(ws + w.X[0]), reinterpret_cast<float*>(ws + w.X[1])};
   auto bound_window = [&](size_t a, int64_t col) -> cf_status {
     const bool spec = a == p.affine.size();
+    if (!spec && a == 0 && net->layers[p.affine[0]].kind == CF_LAYER_CONV)
+      // the first layer's rows concretise against the input box with no substitution: the
+      // interval convolution of the box (the input columns of the state), no window built
+      return launch_ibp_conv_state(Bc, net->layers[p.affine[0]], st_l, st_u, N, st_l + col, st_u + col, N, st);
     std::vector<WinGeom> gs;
     window_chain(net, p, a, gs);
     RowGeom rg;
