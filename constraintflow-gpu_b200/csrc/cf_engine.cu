@@ -978,10 +978,12 @@ extern "C" cf_status cf_deeppoly_layer(const cf_network* net, int32_t layer, int
     set_error("deeppoly_layer: cudaMemsetAsync failed");
     return CF_ERR_CUDA;
   }
-  if (use_chain() && !p.has_conv) {
+  if (use_chain()) {
+    // the weight image of this layer (every layer of a chained net; in a conv net the linear
+    // layers whose window substitutions run on the tensor cores), used by the layers above
     for (size_t a = 0; a < p.affine.size(); ++a) {
       const cf_layer& L = net->layers[p.affine[a]];
-      if (p.affine[a] == layer)
+      if (p.affine[a] == layer && w.wimg_off[a] != 0)
         CF_TRY(chain_prep_weights(L.W_dev, L.n_out, L.n_in, reinterpret_cast<uint8_t*>(ws + w.wimg_off[a]), st));
     }
   }

@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
                                                  ("crown", 0, 8, 0.005), ("zono", 1, 16, 0.005),
                                                  ("ibp", 3, 8, 0.02), ("deeppoly", 0, 1, 0.01),
                                                  ("zono", 3, 4, 0.02), ("crownibp", 2, 16, 0.002),
-                                                 ("crownibp", 3, 4, 0.02)])
+                                                 ("crownibp", 3, 4, 0.02), ("deeppoly", 4, 2, 2 / 255)])
 def test_layerwise_equals_whole_pass(certifier, wid, B, eps):
     wl = nets.workload(wid)
     dev = torch.device("cuda:0")
