@@ -1,4 +1,6 @@
-// Chained backsubstitution on tcgen05 tensor cores (3xTF32), one launch per bounded layer.
+// Chained backsubstitution on tcgen05 tensor cores (3xTF32), one launch per bounded layer
+// (or per two independent layers: chain_launch_pair puts the output layer and the property
+// rows in one grid, each CTA running one of the two parameter sets).
 //
 // For an affine layer m the DeepPoly bound of every neuron is obtained by pushing its
 // coefficient row through ReLU_j + affine_j for j = m-1 .. 0 and folding the input box
@@ -22,7 +24,8 @@
 //
 // Warp roles (320 threads): warps 0-7 transform/epilogue (thread t <-> TMEM lane t%128 <->
 // tile row t%128; threads t and t+128 take the two 16-column halves of every chunk),
-// warp 8 allocates TMEM and streams W chunks, warp 9 issues the MMAs.
+// warp 8 allocates TMEM and streams W chunks, warp 9 issues the MMAs.  Chunk g uses A stage
+// and W stage g % 2; one commit after its MMAs releases both.
 // Every mbarrier wait is bounded (cf_tc.cuh); a timeout is recorded in the device error
 // word and all roles unwind.
 #include <type_traits>
